@@ -1,0 +1,94 @@
+"""ada_mla -- B200 (sm_100a) MLA decode engine, drop-in for lechebs/ada-mla's
+``ada_mla`` torch extension.
+
+Same names, signatures, output shapes and dtypes as the reference's pybind
+module (csrc/mla_api.cpp:115-120):
+
+* ``mla_decode_naive(query, cache)``  fp32; softmax(Q C^T / sqrt(D)) C over all
+  D columns, attention matrix materialized (reference csrc/mla_api.cpp:5-32).
+* ``mla_decode_fused(query, cache)``  fp32 -> [n_h, 512] fp32, scale 1/sqrt(192)
+  (reference csrc/mla_api.cpp:34-54).
+* ``mla_decode_split(query, cache, num_splits=-1)``  fp16 -> [n_h, 512] fp16 on
+  the split-KV kernels + LSE combine; fp32 -> the fp32 kernel (reference
+  csrc/mla_api.cpp:86-113, whose fp32 branch is an empty stub).
+
+plus ``mla_decode_batched`` (batch / varlen), ``mla_combine`` (the LSE merge the
+multi-GPU layer uses), ``mla_get_device_error`` and the model constants the
+reference left as a TODO in mla.py:29-34.
+
+Importing never compiles: the native libraries are built in-tree by
+``ada_mla._build.build()`` (or the repository's ``__graft_entry__.build()``).
+If they are missing the import fails loudly -- there is no CPU fallback.
+"""
+from __future__ import annotations
+
+import ctypes
+import importlib.util
+import os
+
+import torch  # noqa: F401  (loads libtorch / libc10 before the extension)
+
+from ._build import EXT_NAME, EXT_PATH, LIB_PATH
+
+__all__ = [
+    "mla_decode_naive", "mla_decode_fused", "mla_decode_split", "mla_decode_batched",
+    "mla_combine", "mla_get_device_error", "NUM_HEADS", "HEAD_DIM", "HEAD_DIM_C",
+    "HEAD_DIM_ROPE", "HEAD_DIM_K", "HEAD_DIM_V", "SOFTMAX_SCALE", "lib_path", "ext_path",
+]
+
+
+def _load_extension():
+    for path in (LIB_PATH, EXT_PATH):
+        if not os.path.isfile(path):
+            raise ImportError(
+                f"ada_mla: native library {path} is missing; build it with "
+                "`python -c 'import __graft_entry__ as g; g.build()'` (repository root) "
+                "or `python ada-mla_b200/ada_mla/_build.py`")
+    # The extension links libmla_b200.so by soname; load it first, globally.
+    ctypes.CDLL(LIB_PATH, mode=ctypes.RTLD_GLOBAL)
+    spec = importlib.util.spec_from_file_location(EXT_NAME, EXT_PATH)
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
+_ext = _load_extension()
+
+mla_decode_naive = _ext.mla_decode_naive
+mla_decode_fused = _ext.mla_decode_fused
+mla_decode_split = _ext.mla_decode_split
+mla_combine = _ext.mla_combine
+mla_get_device_error = _ext.mla_get_device_error
+
+NUM_HEADS = _ext.NUM_HEADS
+HEAD_DIM = _ext.HEAD_DIM
+HEAD_DIM_C = _ext.HEAD_DIM_C
+HEAD_DIM_ROPE = _ext.HEAD_DIM_ROPE
+HEAD_DIM_K = _ext.HEAD_DIM_K
+HEAD_DIM_V = _ext.HEAD_DIM_V
+# The reference's fused/split softmax scale, 1/sqrt(HEAD_DIM + HEAD_DIM_ROPE)
+# (csrc/mla_decode_splitk_fwd.cuh:446-450, mla.py:46).
+SOFTMAX_SCALE = 1.0 / (HEAD_DIM + HEAD_DIM_ROPE) ** 0.5
+
+lib_path = LIB_PATH
+ext_path = EXT_PATH
+
+
+def mla_decode_batched(query, cache, cu_seqlens=None, max_seq_len: int = -1,
+                       softmax_scale: float = SOFTMAX_SCALE, num_splits: int = -1,
+                       return_lse: bool = False, out_dtype=None):
+    """Batched / variable-length fp16 decode.
+
+    query  [B, n_h, 576] fp16.
+    cache  dense [B, N, 576] fp16, or packed [T, 576] fp16 with
+           ``cu_seqlens`` int32 [B+1] (sequence b owns rows
+           cu_seqlens[b]:cu_seqlens[b+1]).  Pass ``max_seq_len`` to avoid a
+           device->host read of the longest length.
+    Returns O* [B, n_h, 512] (fp16, or fp32 when ``out_dtype=torch.float32``)
+    and, with ``return_lse``, the natural-log LSE [B, n_h] fp32 as a tuple.
+    """
+    out_fp32 = out_dtype == torch.float32
+    out, lse = _ext.mla_decode_batched(query, cache, cu_seqlens, int(max_seq_len),
+                                       float(softmax_scale), int(num_splits),
+                                       bool(return_lse), out_fp32)
+    return (out, lse) if return_lse else out

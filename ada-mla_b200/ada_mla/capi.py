@@ -1,0 +1,173 @@
+"""ctypes binding of the C ABI (``include/mla_b200.h``) in ``libmla_b200.so``.
+
+This is the binding a maintainer of the reference would add to call the
+engine without the torch extension: plain pointers, sizes and a
+``cudaStream_t``, every call returning a status.  Buffers here are torch
+CUDA tensors only for convenience (their ``data_ptr()`` crosses the ABI).
+The GPU parity tests call through this module to exercise the ABI itself.
+"""
+from __future__ import annotations
+
+import ctypes
+import os
+
+import torch
+
+from ._build import LIB_PATH
+
+OK = 0
+ERR_INVALID_ARG = 1
+ERR_UNSUPPORTED = 2
+ERR_WORKSPACE = 3
+ERR_CUDA = 4
+ERR_DEVICE_TIMEOUT = 5
+ERR_NO_DEVICE = 6
+OUT_F16 = 0
+OUT_F32 = 1
+
+_c_int, _c_ll, _c_size, _c_float = ctypes.c_int, ctypes.c_longlong, ctypes.c_size_t, ctypes.c_float
+_vp = ctypes.c_void_p
+
+# (name, restype, argtypes) for every symbol declared in include/mla_b200.h
+SIGNATURES = {
+    "mla_b200_status_string": (ctypes.c_char_p, [_c_int]),
+    "mla_b200_version": (ctypes.c_char_p, []),
+    "mla_b200_constant": (_c_int, [ctypes.c_char_p]),
+    "mla_b200_plan": (_c_int, [_c_int, _c_int, _c_ll, _c_int, _c_int,
+                               ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
+    "mla_b200_workspace_size": (_c_size, [_c_int, _c_int, _c_ll, _c_int, _c_int]),
+    "mla_b200_decode_split_f16": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _vp, _c_size, _vp]),
+    "mla_b200_decode_batched_f16": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_ll, _c_int, _c_float,
+                                             _c_int, _vp, _c_int, _vp, _vp, _c_size, _vp]),
+    "mla_b200_decode_fused_f32": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _vp, _c_size, _vp]),
+    "mla_b200_decode_naive_f32": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _vp]),
+    "mla_b200_combine_f32": (_c_int, [_vp, _vp, _c_int, _c_ll, _vp, _c_int, _vp, _vp]),
+    "mla_b200_get_device_error": (_c_int, [ctypes.POINTER(_c_int), _vp]),
+}
+
+_lib: ctypes.CDLL | None = None
+
+
+class MlaError(RuntimeError):
+    def __init__(self, fn: str, status: int):
+        super().__init__(f"{fn}: {status_string(status)} (status {status})")
+        self.status = status
+
+
+def lib() -> ctypes.CDLL:
+    global _lib
+    if _lib is None:
+        if not os.path.isfile(LIB_PATH):
+            raise ImportError(f"{LIB_PATH} missing; run ada_mla._build.build()")
+        l = ctypes.CDLL(LIB_PATH, mode=ctypes.RTLD_GLOBAL)
+        for name, (res, args) in SIGNATURES.items():
+            f = getattr(l, name)
+            f.restype = res
+            f.argtypes = args
+        _lib = l
+    return _lib
+
+
+def status_string(status: int) -> str:
+    return lib().mla_b200_status_string(status).decode()
+
+
+def _check(fn: str, status: int) -> None:
+    if status != OK:
+        raise MlaError(fn, status)
+
+
+def _stream() -> int:
+    return torch.cuda.current_stream().cuda_stream
+
+
+def _ptr(t: torch.Tensor | None) -> int | None:
+    return None if t is None else t.data_ptr()
+
+
+def constant(name: str) -> int:
+    return lib().mla_b200_constant(name.encode())
+
+
+def plan(batch: int, num_heads: int, total_tokens: int, max_seq_len: int, num_sms: int = 0):
+    chunk, splits = _c_int(0), _c_int(0)
+    _check("mla_b200_plan", lib().mla_b200_plan(batch, num_heads, total_tokens, max_seq_len,
+                                                num_sms, ctypes.byref(chunk), ctypes.byref(splits)))
+    return chunk.value, splits.value
+
+
+def workspace_size(batch: int, num_heads: int, total_tokens: int, max_seq_len: int,
+                   num_splits: int = 0) -> int:
+    return int(lib().mla_b200_workspace_size(batch, num_heads, total_tokens, max_seq_len, num_splits))
+
+
+def _workspace(nbytes: int, device) -> torch.Tensor:
+    return torch.empty(max(int(nbytes), 256), dtype=torch.uint8, device=device)
+
+
+def decode_split_f16(query: torch.Tensor, cache: torch.Tensor, num_splits: int = -1,
+                     out: torch.Tensor | None = None, workspace: torch.Tensor | None = None):
+    nh, n = query.shape[0], cache.shape[0]
+    if out is None:
+        out = torch.empty((nh, 512), dtype=torch.float16, device=query.device)
+    if workspace is None:
+        workspace = _workspace(workspace_size(1, nh, n, n, num_splits), query.device)
+    _check("mla_b200_decode_split_f16", lib().mla_b200_decode_split_f16(
+        _ptr(query), _ptr(cache), _ptr(out), nh, n, num_splits, _ptr(workspace),
+        workspace.numel(), _stream()))
+    return out
+
+
+def decode_batched_f16(query: torch.Tensor, cache: torch.Tensor, cu_seqlens: torch.Tensor | None,
+                       max_seq_len: int, softmax_scale: float, num_splits: int = -1,
+                       out_fp32: bool = False, return_lse: bool = False,
+                       workspace: torch.Tensor | None = None):
+    b, nh = query.shape[0], query.shape[1]
+    total = cache.shape[0] if cu_seqlens is not None else b * max_seq_len
+    out = torch.empty((b, nh, 512), dtype=torch.float32 if out_fp32 else torch.float16,
+                      device=query.device)
+    lse = torch.empty((b, nh), dtype=torch.float32, device=query.device) if return_lse else None
+    if workspace is None:
+        workspace = _workspace(workspace_size(b, nh, total, max_seq_len, num_splits), query.device)
+    _check("mla_b200_decode_batched_f16", lib().mla_b200_decode_batched_f16(
+        _ptr(query), _ptr(cache), _ptr(cu_seqlens), b, nh, total, max_seq_len,
+        float(softmax_scale), num_splits, _ptr(out), OUT_F32 if out_fp32 else OUT_F16,
+        _ptr(lse), _ptr(workspace), workspace.numel(), _stream()))
+    return (out, lse) if return_lse else out
+
+
+def decode_fused_f32(query: torch.Tensor, cache: torch.Tensor):
+    nh, d, n = query.shape[0], query.shape[1], cache.shape[0]
+    out = torch.empty((nh, 512), dtype=torch.float32, device=query.device)
+    ws = _workspace(workspace_size(1, nh, n, n, 0), query.device)
+    _check("mla_b200_decode_fused_f32", lib().mla_b200_decode_fused_f32(
+        _ptr(query), _ptr(cache), _ptr(out), nh, d, n, _ptr(ws), ws.numel(), _stream()))
+    return out
+
+
+def decode_naive_f32(query: torch.Tensor, cache: torch.Tensor):
+    nh, d, n = query.shape[0], query.shape[1], cache.shape[0]
+    out = torch.empty((nh, d), dtype=torch.float32, device=query.device)
+    attn = torch.empty((nh, n), dtype=torch.float32, device=query.device)
+    _check("mla_b200_decode_naive_f32", lib().mla_b200_decode_naive_f32(
+        _ptr(query), _ptr(cache), _ptr(attn), _ptr(out), nh, d, n, _stream()))
+    return out
+
+
+def combine_f32(part_o: torch.Tensor, part_lse: torch.Tensor, out_fp32: bool = True):
+    p, rows = part_o.shape[0], part_o.shape[1]
+    out = torch.empty((rows, 512), dtype=torch.float32 if out_fp32 else torch.float16,
+                      device=part_o.device)
+    lse = torch.empty((rows,), dtype=torch.float32, device=part_o.device)
+    _check("mla_b200_combine_f32", lib().mla_b200_combine_f32(
+        _ptr(part_o), _ptr(part_lse), p, rows, _ptr(out), OUT_F32 if out_fp32 else OUT_F16,
+        _ptr(lse), _stream()))
+    return out, lse
+
+
+def get_device_error() -> int:
+    code = _c_int(0)
+    st = lib().mla_b200_get_device_error(ctypes.byref(code), _stream())
+    if st not in (OK, ERR_DEVICE_TIMEOUT):
+        raise MlaError("mla_b200_get_device_error", st)
+    return code.value

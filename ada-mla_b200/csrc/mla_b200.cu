@@ -1,0 +1,388 @@
+// mla_b200.cu -- the C ABI (include/mla_b200.h): argument checks, planning,
+// workspace layout and kernel launches.  Every kernel of the library is in
+// this one translation unit (the .cuh files), so no relocatable device code
+// is needed for the shared device error word.
+#include <math.h>
+#include <string.h>
+
+#include <atomic>
+#include <mutex>
+
+#include "mla_b200.h"
+#include "mla_combine.cuh"
+#include "mla_common.cuh"
+#include "mla_simt.cuh"
+
+using namespace mla;
+
+namespace {
+
+constexpr int kMaxDevices = 64;
+constexpr float kRefScale = 0.07216878364870322f;  // 1/sqrt(HEAD_DIM + HEAD_DIM_ROPE) = 1/sqrt(192)
+
+struct DevInfo {
+    int sms = 0;
+    int major = 0;
+    bool simt_attr_set = false;
+};
+
+std::mutex g_dev_mu;
+DevInfo g_dev[kMaxDevices];
+
+// Current device's properties (cached).  Returns a status.
+int current_device(int *dev_out, DevInfo *info_out) {
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDevices) {
+        cudaGetLastError();
+        return MLA_B200_ERR_NO_DEVICE;
+    }
+    std::lock_guard<std::mutex> lk(g_dev_mu);
+    DevInfo &d = g_dev[dev];
+    if (d.sms == 0) {
+        int sms = 0, major = 0;
+        if (cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev) != cudaSuccess) {
+            cudaGetLastError();
+            return MLA_B200_ERR_NO_DEVICE;
+        }
+        d.sms = sms;
+        d.major = major;
+    }
+    if (d.major != 10) return MLA_B200_ERR_NO_DEVICE;  // kernels are built for sm_100a only
+    if (!d.simt_attr_set) {
+        if (cudaFuncSetAttribute(simt_partial_kernel<float>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSimtSmem) !=
+                cudaSuccess ||
+            cudaFuncSetAttribute(simt_partial_kernel<__half>,
+                                 cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSimtSmem) !=
+                cudaSuccess) {
+            cudaGetLastError();
+            return MLA_B200_ERR_CUDA;
+        }
+        d.simt_attr_set = true;
+    }
+    *dev_out = dev;
+    *info_out = d;
+    return MLA_B200_OK;
+}
+
+inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
+inline long long cdiv(long long a, long long b) { return (a + b - 1) / b; }
+
+// Split plan: rows per work item.  `units` is the number of workers one wave
+// of the decode kernel has; the chunk is the smallest multiple of kTile that
+// gives every worker at most one item, but never longer than a sequence.
+int plan_chunk(int batch, long long total_tokens, int max_seq_len, int num_sms) {
+    const long long units = num_sms > 1 ? num_sms / 2 : 1;
+    long long chunk = cdiv(cdiv(total_tokens > 0 ? total_tokens : 1, units), kTile) * kTile;
+    if (chunk < kTile) chunk = kTile;
+    if (max_seq_len > 0) {
+        const long long cap = cdiv(max_seq_len, kTile) * kTile;
+        if (chunk > cap) chunk = cap;
+    }
+    (void)batch;
+    if (chunk > (1 << 30)) chunk = 1 << 30;
+    return (int)chunk;
+}
+
+int chunk_for(int batch, long long total_tokens, int max_seq_len, int num_splits, int num_sms) {
+    if (num_splits > 0) {
+        const long long n = max_seq_len > 0 ? max_seq_len : 1;
+        long long c = cdiv(n, num_splits);
+        return (int)(c < 1 ? 1 : c);
+    }
+    return plan_chunk(batch, total_tokens, max_seq_len, num_sms);
+}
+
+long long max_items_for(int batch, long long total_tokens, int chunk) {
+    return cdiv(total_tokens, chunk) + batch;
+}
+
+struct WsLayout {
+    float *part_o = nullptr;
+    float *part_lse = nullptr;
+    int *item_off = nullptr;
+    int4 *items = nullptr;
+    size_t bytes = 0;
+};
+
+WsLayout ws_layout(void *base, long long max_items, int num_heads, int batch) {
+    WsLayout L;
+    size_t off = 0;
+    const size_t o_bytes = (size_t)max_items * num_heads * kDV * sizeof(float);
+    const size_t l_bytes = (size_t)max_items * num_heads * sizeof(float);
+    const size_t off_bytes = (size_t)(batch + 1) * sizeof(int);
+    const size_t it_bytes = (size_t)max_items * sizeof(int4);
+    char *p = static_cast<char *>(base);
+    L.part_o = reinterpret_cast<float *>(p + off);
+    off = align_up(off + o_bytes, 256);
+    L.part_lse = reinterpret_cast<float *>(p + off);
+    off = align_up(off + l_bytes, 256);
+    L.item_off = reinterpret_cast<int *>(p + off);
+    off = align_up(off + off_bytes, 256);
+    L.items = reinterpret_cast<int4 *>(p + off);
+    off = align_up(off + it_bytes, 256);
+    L.bytes = off;
+    return L;
+}
+
+inline bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int launch_status() {
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? MLA_B200_OK : MLA_B200_ERR_CUDA;
+}
+
+// Shared driver of the split-KV paths: plan -> partial kernel -> combine.
+template <typename T>
+int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int batch,
+                     int num_heads, long long total_tokens, int max_seq_len, float scale,
+                     int num_splits, void *out, int out_dtype, float *out_lse, void *workspace,
+                     size_t workspace_bytes, cudaStream_t stream) {
+    int dev;
+    DevInfo info;
+    int st = current_device(&dev, &info);
+    if (st != MLA_B200_OK) return st;
+    if (batch == 0) return MLA_B200_OK;
+
+    const int chunk = chunk_for(batch, total_tokens, max_seq_len, num_splits, info.sms);
+    const long long max_items = max_items_for(batch, total_tokens, chunk);
+    if (max_items > (1LL << 30)) return MLA_B200_ERR_UNSUPPORTED;
+    WsLayout L = ws_layout(workspace, max_items, num_heads, batch);
+    if (workspace == nullptr || workspace_bytes < L.bytes) return MLA_B200_ERR_WORKSPACE;
+
+    WorkList wl;
+    wl.batch = batch;
+    wl.chunk = chunk;
+    if (cu_seqlens == nullptr) {
+        wl.items = nullptr;
+        wl.item_off = nullptr;
+        wl.seq_len = max_seq_len;
+        wl.cps = max_seq_len > 0 ? (int)cdiv(max_seq_len, chunk) : 0;
+        wl.max_items = batch * wl.cps;
+    } else {
+        wl.items = L.items;
+        wl.item_off = L.item_off;
+        wl.seq_len = 0;
+        wl.cps = 0;
+        wl.max_items = (int)max_items;
+        plan_varlen_kernel<<<1, 1024, 0, stream>>>(cu_seqlens, batch, chunk, L.item_off, L.items,
+                                                   (int)max_items);
+    }
+    if (wl.max_items > 0) {
+        dim3 grid(wl.max_items, (unsigned)cdiv(num_heads, kSimtHeads));
+        simt_partial_kernel<T><<<grid, 256, kSimtSmem, stream>>>(
+            q, cache, wl, num_heads, scale * kLog2e, L.part_o, L.part_lse);
+    }
+    const long long rows = (long long)batch * num_heads;
+    const unsigned cgrid = (unsigned)cdiv(rows, kCombineWarps);
+    if (out_dtype == MLA_B200_OUT_F16) {
+        combine_kernel<__half><<<cgrid, kCombineWarps * 32, 0, stream>>>(
+            L.part_o, L.part_lse, wl, num_heads, rows, static_cast<__half *>(out), out_lse);
+    } else {
+        combine_kernel<float><<<cgrid, kCombineWarps * 32, 0, stream>>>(
+            L.part_o, L.part_lse, wl, num_heads, rows, static_cast<float *>(out), out_lse);
+    }
+    return launch_status();
+}
+
+}  // namespace
+
+extern "C" {
+
+const char *mla_b200_status_string(int status) {
+    switch (status) {
+        case MLA_B200_OK: return "ok";
+        case MLA_B200_ERR_INVALID_ARG: return "invalid argument";
+        case MLA_B200_ERR_UNSUPPORTED: return "unsupported shape";
+        case MLA_B200_ERR_WORKSPACE: return "workspace missing or too small";
+        case MLA_B200_ERR_CUDA: return "CUDA runtime error";
+        case MLA_B200_ERR_DEVICE_TIMEOUT: return "a kernel's bounded wait expired";
+        case MLA_B200_ERR_NO_DEVICE: return "no sm_100 device is current";
+        default: return "unknown status";
+    }
+}
+
+const char *mla_b200_version(void) { return "0.1.0"; }
+
+int mla_b200_constant(const char *name) {
+    if (name == nullptr) return -1;
+    if (!strcmp(name, "NUM_HEADS")) return MLA_B200_NUM_HEADS;
+    if (!strcmp(name, "HEAD_DIM")) return MLA_B200_HEAD_DIM;
+    if (!strcmp(name, "HEAD_DIM_C")) return MLA_B200_HEAD_DIM_C;
+    if (!strcmp(name, "HEAD_DIM_ROPE")) return MLA_B200_HEAD_DIM_ROPE;
+    if (!strcmp(name, "HEAD_DIM_K")) return MLA_B200_HEAD_DIM_K;
+    if (!strcmp(name, "HEAD_DIM_V")) return MLA_B200_HEAD_DIM_V;
+    return -1;
+}
+
+int mla_b200_plan(int batch, int num_heads, long long total_tokens, int max_seq_len, int num_sms,
+                  int *chunk_tokens, int *num_splits) {
+    if (batch < 0 || num_heads <= 0 || total_tokens < 0 || max_seq_len < 0)
+        return MLA_B200_ERR_INVALID_ARG;
+    if (num_sms <= 0) {
+        int dev = 0;
+        if (cudaGetDevice(&dev) != cudaSuccess ||
+            cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+            cudaGetLastError();
+            num_sms = 148;
+        }
+    }
+    const int chunk = plan_chunk(batch, total_tokens, max_seq_len, num_sms);
+    if (chunk_tokens) *chunk_tokens = chunk;
+    if (num_splits) *num_splits = max_seq_len > 0 ? (int)cdiv(max_seq_len, chunk) : 0;
+    return MLA_B200_OK;
+}
+
+size_t mla_b200_workspace_size(int batch, int num_heads, long long total_tokens, int max_seq_len,
+                               int num_splits) {
+    if (batch < 0 || num_heads <= 0 || total_tokens < 0) return 0;
+    int num_sms = 0, dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess ||
+        cudaDeviceGetAttribute(&num_sms, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) {
+        cudaGetLastError();
+        num_sms = 148;
+    }
+    if (max_seq_len <= 0 && batch > 0) max_seq_len = (int)cdiv(total_tokens, batch);
+    const int chunk = chunk_for(batch, total_tokens, max_seq_len, num_splits, num_sms);
+    const long long max_items = max_items_for(batch, total_tokens, chunk);
+    return ws_layout(nullptr, max_items, num_heads, batch).bytes;
+}
+
+int mla_b200_decode_split_f16(const void *query, const void *cache, void *out, int num_heads,
+                              int seq_length, int num_splits, void *workspace,
+                              size_t workspace_bytes, void *stream) {
+    if (query == nullptr || out == nullptr || num_heads <= 0 || seq_length < 0 ||
+        (seq_length > 0 && cache == nullptr))
+        return MLA_B200_ERR_INVALID_ARG;
+    if (!aligned(query, 16) || !aligned(cache, 16) || !aligned(out, 16))
+        return MLA_B200_ERR_INVALID_ARG;
+    return run_split_decode<__half>(static_cast<const __half *>(query),
+                                    static_cast<const __half *>(cache), nullptr, 1, num_heads,
+                                    seq_length, seq_length, kRefScale, num_splits, out,
+                                    MLA_B200_OUT_F16, nullptr, workspace, workspace_bytes,
+                                    static_cast<cudaStream_t>(stream));
+}
+
+int mla_b200_decode_batched_f16(const void *query, const void *cache, const int32_t *cu_seqlens,
+                                int batch, int num_heads, long long total_tokens, int max_seq_len,
+                                float softmax_scale, int num_splits, void *out, int out_dtype,
+                                float *out_lse, void *workspace, size_t workspace_bytes,
+                                void *stream) {
+    if (batch < 0 || num_heads <= 0 || total_tokens < 0 || max_seq_len < 0)
+        return MLA_B200_ERR_INVALID_ARG;
+    if (batch > 0 && (query == nullptr || out == nullptr)) return MLA_B200_ERR_INVALID_ARG;
+    if (total_tokens > 0 && cache == nullptr) return MLA_B200_ERR_INVALID_ARG;
+    if (out_dtype != MLA_B200_OUT_F16 && out_dtype != MLA_B200_OUT_F32)
+        return MLA_B200_ERR_INVALID_ARG;
+    if (!(softmax_scale > 0.f) || !isfinite(softmax_scale)) return MLA_B200_ERR_INVALID_ARG;
+    if (!aligned(query, 16) || !aligned(cache, 16) || !aligned(out, 16) || !aligned(out_lse, 4))
+        return MLA_B200_ERR_INVALID_ARG;
+    if (cu_seqlens == nullptr && (long long)batch * max_seq_len != total_tokens)
+        return MLA_B200_ERR_INVALID_ARG;
+    if (cu_seqlens != nullptr && max_seq_len == 0 && total_tokens > 0)
+        return MLA_B200_ERR_INVALID_ARG;
+    if (total_tokens >= (1LL << 31)) return MLA_B200_ERR_UNSUPPORTED;
+    return run_split_decode<__half>(static_cast<const __half *>(query),
+                                    static_cast<const __half *>(cache), cu_seqlens, batch,
+                                    num_heads, total_tokens, max_seq_len, softmax_scale,
+                                    num_splits, out, out_dtype, out_lse, workspace,
+                                    workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int mla_b200_decode_fused_f32(const float *query, const float *cache, float *out, int num_heads,
+                              int head_dim_c, int seq_length, void *workspace,
+                              size_t workspace_bytes, void *stream) {
+    if (query == nullptr || out == nullptr || num_heads <= 0 || seq_length < 0 ||
+        (seq_length > 0 && cache == nullptr))
+        return MLA_B200_ERR_INVALID_ARG;
+    if (head_dim_c != kDK) return MLA_B200_ERR_UNSUPPORTED;
+    if (!aligned(query, 16) || !aligned(cache, 16) || !aligned(out, 16))
+        return MLA_B200_ERR_INVALID_ARG;
+    return run_split_decode<float>(query, cache, nullptr, 1, num_heads, seq_length, seq_length,
+                                   kRefScale, 0, out, MLA_B200_OUT_F32, nullptr, workspace,
+                                   workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int mla_b200_decode_naive_f32(const float *query, const float *cache, float *attn, float *out,
+                              int num_heads, int head_dim_c, int seq_length, void *stream) {
+    if (query == nullptr || cache == nullptr || attn == nullptr || out == nullptr ||
+        num_heads <= 0 || head_dim_c <= 0 || seq_length <= 0)
+        return MLA_B200_ERR_INVALID_ARG;
+    if ((long long)num_heads * seq_length >= (1LL << 31) ||
+        (long long)seq_length * head_dim_c >= (1LL << 31))
+        return MLA_B200_ERR_UNSUPPORTED;
+    int dev;
+    DevInfo info;
+    int st = current_device(&dev, &info);
+    if (st != MLA_B200_OK) return st;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const float scale = (float)(1.0 / sqrt((double)head_dim_c));
+    // attn = scale * Q . C^T   [num_heads x seq_length]
+    naive_gemm_kernel<true><<<dim3((unsigned)cdiv(seq_length, 16), (unsigned)cdiv(num_heads, 16)),
+                              256, 0, s>>>(query, cache, attn, num_heads, seq_length, head_dim_c,
+                                           seq_length, scale);
+    naive_softmax_kernel<<<num_heads, 256, 0, s>>>(attn, seq_length);
+    // out = attn . C           [num_heads x head_dim_c]
+    naive_gemm_kernel<false><<<dim3((unsigned)cdiv(head_dim_c, 16), (unsigned)cdiv(num_heads, 16)),
+                               256, 0, s>>>(attn, cache, out, num_heads, head_dim_c, seq_length,
+                                            head_dim_c, 1.0f);
+    return launch_status();
+}
+
+int mla_b200_combine_f32(const float *part_o, const float *part_lse, int num_parts,
+                         long long rows, void *out, int out_dtype, float *out_lse, void *stream) {
+    if (num_parts < 0 || rows < 0 || rows >= (1LL << 31)) return MLA_B200_ERR_INVALID_ARG;
+    if (rows == 0) return MLA_B200_OK;
+    if (out == nullptr || (num_parts > 0 && (part_o == nullptr || part_lse == nullptr)))
+        return MLA_B200_ERR_INVALID_ARG;
+    if (out_dtype != MLA_B200_OUT_F16 && out_dtype != MLA_B200_OUT_F32)
+        return MLA_B200_ERR_INVALID_ARG;
+    if (!aligned(part_o, 16) || !aligned(out, 16)) return MLA_B200_ERR_INVALID_ARG;
+    int dev;
+    DevInfo info;
+    int st = current_device(&dev, &info);
+    if (st != MLA_B200_OK) return st;
+    WorkList wl;
+    wl.items = nullptr;
+    wl.item_off = nullptr;
+    wl.batch = 1;
+    wl.seq_len = num_parts;  // one "row" per part: item_range(0) = [0, num_parts)
+    wl.chunk = 1;
+    wl.cps = num_parts;
+    wl.max_items = num_parts;
+    const unsigned cgrid = (unsigned)cdiv(rows, kCombineWarps);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (out_dtype == MLA_B200_OUT_F16)
+        combine_kernel<__half><<<cgrid, kCombineWarps * 32, 0, s>>>(
+            part_o, part_lse, wl, (int)rows, rows, static_cast<__half *>(out), out_lse);
+    else
+        combine_kernel<float><<<cgrid, kCombineWarps * 32, 0, s>>>(
+            part_o, part_lse, wl, (int)rows, rows, static_cast<float *>(out), out_lse);
+    return launch_status();
+}
+
+int mla_b200_get_device_error(int *code, void *stream) {
+    int v = 0;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (cudaMemcpyFromSymbolAsync(&v, g_mla_error, sizeof(int), 0, cudaMemcpyDeviceToHost, s) !=
+            cudaSuccess ||
+        cudaStreamSynchronize(s) != cudaSuccess) {
+        cudaGetLastError();
+        return MLA_B200_ERR_CUDA;
+    }
+    if (code) *code = v;
+    if (v != 0) {
+        const int zero = 0;
+        if (cudaMemcpyToSymbolAsync(g_mla_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s) !=
+                cudaSuccess ||
+            cudaStreamSynchronize(s) != cudaSuccess) {
+            cudaGetLastError();
+            return MLA_B200_ERR_CUDA;
+        }
+        return MLA_B200_ERR_DEVICE_TIMEOUT;
+    }
+    return MLA_B200_OK;
+}
+
+}  // extern "C"

@@ -1,0 +1,423 @@
+"""Benchmark of the MLA decode step (the one hot path of lechebs/ada-mla).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config C] [--impl ours|reference]
+
+One step = one weight-absorbed decode O* = softmax(Q* C^T) C[:, :512] of the
+configured batch with inputs already resident in HBM.  Default workload is
+BASELINE config 1 (B=1, n_h=128, N=4096, fp16) on every rank: with N GPUs each
+rank decodes its own sequence (sequence sharding, no data-path collective), so
+per-GPU work is fixed ("scaling": "weak").
+
+Metric: latent-KV HBM GB/s = algorithmic cache bytes of all ranks / step time
+(max over ranks), plus us/step.  L2: every step reads a different copy of the
+inputs from a ring whose total size is >= 3x the L2, so each step streams its
+cache from HBM.  The timed region is a CUDA graph of exactly K steps launched
+through the C ABI (mla_b200_decode_batched_f16) with preallocated buffers.
+
+`--impl reference` times the reference's own FP32 CPU kernel
+(run_mla_decode_cpu, compiled from the reference sources into oracle/_ref, or
+our C restatement when that build is absent) on all host cores, rank 0 only.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import sys
+import threading
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "ada-mla_b200"))
+sys.path.insert(0, ROOT)
+
+HEAD_DIM_K = 576
+METRIC = "MLA decode latent-KV HBM GB/s (us/step alongside)"
+UNIT = "GB/s"
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
+    except Exception:
+        return 6650.0, 1590.0, "fallback"
+
+
+# ---------------------------------------------------------------------------
+# clocks during the timed region (NVML reads only; no setting is changed)
+# ---------------------------------------------------------------------------
+class ClockSampler:
+    REASONS = {
+        0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap",
+        0x8: "hw_slowdown", 0x10: "sync_boost", 0x20: "sw_thermal_slowdown",
+        0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
+    }
+
+    def __init__(self, device_index: int):
+        self.samples: list[tuple[int, int]] = []
+        self.max_mhz = None
+        self._stop = threading.Event()
+        self._t = None
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            self._nvml = pynvml
+            self._h = pynvml.nvmlDeviceGetHandleByIndex(device_index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self._h, pynvml.NVML_CLOCK_SM)
+        except Exception:
+            self._nvml = None
+
+    def _sample(self):
+        n = self._nvml
+        mhz = n.nvmlDeviceGetClockInfo(self._h, n.NVML_CLOCK_SM)
+        try:
+            reasons = n.nvmlDeviceGetCurrentClocksEventReasons(self._h)
+        except Exception:
+            reasons = n.nvmlDeviceGetCurrentClocksThrottleReasons(self._h)
+        self.samples.append((mhz, reasons))
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self._sample()
+            except Exception:
+                return
+            time.sleep(0.002)
+
+    def __enter__(self):
+        if self._nvml is not None:
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        return self
+
+    def __exit__(self, *a):
+        self._stop.set()
+        if self._t is not None:
+            self._t.join()
+            try:
+                self._sample()
+            except Exception:
+                pass
+
+    def summary(self):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"]}
+        mask = 0
+        for _, r in self.samples:
+            mask |= r
+        reasons = [name for bit, name in self.REASONS.items() if mask & bit and name != "gpu_idle"]
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples)}
+
+
+# ---------------------------------------------------------------------------
+# distributed plumbing
+# ---------------------------------------------------------------------------
+def dist_init(n_gpus: int):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        if torch.cuda.is_available():
+            torch.cuda.set_device(local)
+        dist.init_process_group("nccl" if torch.cuda.is_available() else "gloo",
+                                timeout=datetime.timedelta(seconds=120))
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda" if torch.cuda.is_available() else "cpu")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------------------
+# CPU baseline / reference arm
+# ---------------------------------------------------------------------------
+def cpu_decode_sample(wl_cpu, impl: str, threads: int, min_seconds: float):
+    """Runs the reference CPU kernel on the whole (small) workload until
+    min_seconds of wall time have passed.  Returns (GB/s, sample description)."""
+    import numpy as np
+
+    import oracle
+
+    q = wl_cpu.query.float().numpy()
+    bytes_done = 0
+    t0 = time.perf_counter()
+    reps = 0
+    while True:
+        for b in range(wl_cpu.batch):
+            c = wl_cpu.cache_rows(b).float().numpy()
+            qs = (q[b].astype(np.float64) * np.sqrt(HEAD_DIM_K)).astype(np.float32)
+            oracle.run_mla_decode_cpu(qs, c, impl=impl, threads=threads)
+            bytes_done += c.shape[0] * HEAD_DIM_K * 2
+        reps += 1
+        el = time.perf_counter() - t0
+        if el >= min_seconds:
+            break
+    return bytes_done / el / 1e9, el, reps
+
+
+def cpu_kind():
+    import oracle
+
+    return "reference" if oracle.have_ref() else "port"
+
+
+def run_reference_arm(args):
+    """--impl reference: the reference's FP32 CPU kernel on all host cores."""
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    from ada_mla.workloads import make_workload
+
+    wl = make_workload(args.config, seed=0, device="cpu")
+    kind = cpu_kind()
+    impl = "reference" if kind == "reference" else "oracle"
+    threads = os.cpu_count() or 1
+    import numpy as np
+
+    import oracle
+
+    q = wl.query.float().numpy()
+    cbytes = wl.cache_bytes
+
+    def one_step():
+        for b in range(wl.batch):
+            c = wl.cache_rows(b).float().numpy()
+            qs = (q[b].astype(np.float64) * np.sqrt(HEAD_DIM_K)).astype(np.float32)
+            oracle.run_mla_decode_cpu(qs, c, impl=impl, threads=threads)
+
+    for _ in range(args.warmup):
+        one_step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        one_step()
+    el = time.perf_counter() - t0
+    ms = el / args.steps * 1e3
+    gbs = cbytes * args.steps / el / 1e9
+    line = {
+        "impl": "reference", "metric": METRIC, "value": gbs, "unit": UNIT,
+        "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": ms, "us_per_step": ms * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": f"cfg{args.config}: B={wl.batch} n_h={wl.num_heads} "
+                               f"N={wl.max_seq_len} (full decode per step)", "cfg": args.config},
+        "cpu_baseline": {"value": gbs, "unit": UNIT, "cores": threads, "kind": kind,
+                         "sample": f"whole cfg{args.config} decode per step, {args.steps} steps"},
+        "e2e": {"value": gbs, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------------------
+# our arm
+# ---------------------------------------------------------------------------
+def run_ours(args):
+    import torch
+
+    rank, world, local = dist_init(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    import ada_mla
+    from ada_mla import capi
+    from ada_mla.workloads import make_workload
+
+    hbm_peak, _, peak_kind = _peaks()
+    L2 = torch.cuda.get_device_properties(dev).L2_cache_size or (126 << 20)
+
+    wl = make_workload(args.config, seed=1000 * rank, device=dev)
+    step_bytes = wl.cache_bytes + wl.query.numel() * wl.query.element_size()
+    ring = max(2, -(-3 * L2 // step_bytes)) if not args.no_rotate else 1
+    ring = min(ring, max(1, int(40e9 // step_bytes)))
+    qs = [wl.query] + [wl.query.clone() for _ in range(ring - 1)]
+    cs = [wl.cache] + [wl.cache.clone() for _ in range(ring - 1)]
+    cu = wl.cu_seqlens
+    total = wl.total_tokens
+    b, nh, maxlen = wl.batch, wl.num_heads, wl.max_seq_len
+    ws_bytes = capi.workspace_size(b, nh, total, maxlen, args.splits)
+    ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+    out = torch.empty((b, nh, 512), dtype=torch.float16, device=dev)
+    lib = capi.lib()
+    cache_2d = [c.view(-1, HEAD_DIM_K) for c in cs]
+
+    def step(i, stream):
+        st = lib.mla_b200_decode_batched_f16(
+            qs[i % ring].data_ptr(), cache_2d[i % ring].data_ptr(),
+            None if cu is None else cu.data_ptr(), b, nh, total, maxlen, 1.0, args.splits,
+            out.data_ptr(), capi.OUT_F16, None, ws.data_ptr(), ws_bytes, stream)
+        if st != 0:
+            raise RuntimeError(f"decode failed: {capi.status_string(st)}")
+
+    # warm-up (eager), then capture exactly K steps into one graph
+    s = torch.cuda.current_stream().cuda_stream
+    for i in range(args.warmup):
+        step(i, s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream()
+    with torch.cuda.stream(cap):
+        step(0, cap.cuda_stream)  # one eager call on the capture stream
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=cap):
+            for i in range(args.steps):
+                step(i, cap.cuda_stream)
+    graph.replay()  # warm the graph itself
+    torch.cuda.synchronize()
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    barrier(world)
+    torch.cuda.synchronize()
+    with sampler:
+        ev0.record()
+        graph.replay()
+        ev1.record()
+        torch.cuda.synchronize()
+    barrier(world)
+    ms_total = max_over_ranks(ev0.elapsed_time(ev1), world)
+    ms_step = ms_total / args.steps
+    value = world * wl.cache_bytes / (ms_step * 1e-3) / 1e9
+
+    # per-launch duration of the step's kernels, events on the launching stream
+    # (eager launches, same rotating inputs): used for the roofline
+    n_launch = max(args.steps, 50)
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(n_launch)]
+    torch.cuda.synchronize()
+    for i in range(n_launch):
+        evs[i][0].record()
+        step(i, s)
+        evs[i][1].record()
+    torch.cuda.synchronize()
+    launch_ms = statistics.mean(a.elapsed_time(e) for a, e in evs)
+    achieved = wl.cache_bytes / (launch_ms * 1e-3) / 1e9
+
+    # end-to-end through the public API: pinned host inputs -> device, decode,
+    # result -> host, every step
+    qh = [wl.query.cpu().pin_memory() for _ in range(2)]
+    ch = [wl.cache.cpu().pin_memory() for _ in range(2)]
+    qd, cd = torch.empty_like(wl.query), torch.empty_like(wl.cache)
+    oh = torch.empty((b, nh, 512), dtype=torch.float16).pin_memory()
+
+    def e2e_step(i):
+        qd.copy_(qh[i % 2], non_blocking=True)
+        cd.copy_(ch[i % 2], non_blocking=True)
+        o = ada_mla.mla_decode_batched(qd, cd, cu, max_seq_len=maxlen, softmax_scale=1.0,
+                                       num_splits=args.splits)
+        oh.copy_(o, non_blocking=True)
+
+    e2e_steps = max(3, min(args.steps, 200))
+    for i in range(3):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for i in range(e2e_steps):
+        e2e_step(i)
+    e1.record()
+    torch.cuda.synchronize()
+    barrier(world)
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / e2e_steps
+    e2e_value = world * wl.cache_bytes / (e2e_ms * 1e-3) / 1e9
+    h2d = qh[0].numel() * qh[0].element_size() + ch[0].numel() * ch[0].element_size()
+    d2h = oh.numel() * oh.element_size()
+
+    err = ada_mla.mla_get_device_error()
+    if err != 0:
+        raise RuntimeError(f"device error word set: {err}")
+
+    chunk, splits = capi.plan(b, nh, total, maxlen, torch.cuda.get_device_properties(dev).multi_processor_count)
+    kernels_per_step = 2 + (1 if cu is not None else 0)
+    if rank == 0:
+        line = {
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
+            "us_per_step": ms_step * 1e3, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "config": {"workload": f"cfg{args.config}: B={b} n_h={nh} N={maxlen} per rank "
+                                   f"({'packed varlen' if cu is not None else 'dense'}), "
+                                   "softmax scale folded into Q*",
+                       "cfg": args.config, "batch_per_rank": b, "num_heads": nh,
+                       "seq_len": maxlen, "total_tokens_per_rank": total,
+                       "num_splits": splits if args.splits <= 0 else args.splits,
+                       "chunk_tokens": chunk,
+                       "parallelism": f"sequence-sharded x{world}" if world > 1 else "single GPU",
+                       "l2": f"rotating ring of {ring} input copies ({ring * step_bytes / 2**20:.0f} MiB "
+                             f">= 3x L2)" if ring > 1 else "no rotation"},
+            "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
+                         "frac": achieved / hbm_peak, "peak_source": peak_kind,
+                         "traffic": None, "kernel": "decode step (partial + combine)",
+                         "launch_us": launch_ms * 1e3,
+                         "algorithmic_bytes_per_launch": wl.cache_bytes},
+            "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "us_per_step": e2e_ms * 1e3,
+                    "api": "ada_mla.mla_decode_batched"},
+            "gpu_launches": args.steps * kernels_per_step,
+            "clocks": sampler.summary(),
+        }
+        if not args.no_cpu_baseline and world == 1:
+            from ada_mla.workloads import make_workload as mk
+
+            wl_cpu = mk(args.config, seed=0, device="cpu") if args.config in (0, 1) else None
+            if wl_cpu is not None:
+                threads = os.cpu_count() or 1
+                kind = cpu_kind()
+                gbs, el, reps = cpu_decode_sample(wl_cpu, "reference" if kind == "reference" else "oracle",
+                                                  threads, args.cpu_seconds)
+                line["cpu_baseline"] = {"value": gbs, "unit": UNIT, "cores": threads, "kind": kind,
+                                        "sample": f"{reps} full cfg{args.config} decodes "
+                                                  f"({el:.1f} s wall)"}
+        print(json.dumps(line), flush=True)
+    del graph
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--config", type=int, default=1, choices=[1, 2, 3, 4])
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--splits", type=int, default=-1)
+    ap.add_argument("--cpu-seconds", type=float, default=10.0)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-rotate", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    if args.impl == "reference":
+        run_reference_arm(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,174 @@
+/*
+ * mla_b200.h -- C ABI of the B200 (sm_100a) MLA decode engine.
+ *
+ * Computes the weight-absorbed DeepSeek-V2 decode step
+ *
+ *     O*[b, h, :] = softmax(scale * Q*[b, h, :] . C_b^T) . C_b[:, :512]
+ *
+ * over a 576-wide latent cache C_b ([N_b, 576]: 512 latent + 64 rope columns).
+ *
+ * Conventions (all entry points):
+ *   - Every pointer is a DEVICE pointer unless its comment says "host".
+ *   - All tensors are dense row-major; the caller owns every buffer, including
+ *     the workspace (query its size with mla_b200_workspace_size()).
+ *   - `stream` is a cudaStream_t (NULL = legacy default stream).  Launches are
+ *     asynchronous on that stream; nothing synchronizes the device.
+ *   - Return value: MLA_B200_OK or an mla_b200_status code.  Nothing prints,
+ *     aborts or traps.  Argument errors are detected before any launch.
+ *   - Thread safety: calls may come from several host threads; concurrent
+ *     calls must use distinct workspaces.
+ *
+ * Each entry point names the reference interface it replaces (lechebs/ada-mla,
+ * path:line).  The reference's launchers return void, print CUDA errors and use
+ * the legacy default stream; these return a status and take a stream.
+ */
+#ifndef MLA_B200_H
+#define MLA_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Model constants the reference hard-codes in Python (mla.py:29-34, with the
+ * TODO "should be exported by the C++ module") and in KernelTraits
+ * (csrc/mla_decode_splitk_fwd.cuh:37-59). */
+#define MLA_B200_NUM_HEADS 128 /* reference default head count */
+#define MLA_B200_HEAD_DIM 128  /* nope head dim of the un-absorbed model */
+#define MLA_B200_HEAD_DIM_C 512 /* latent (value) width = HEAD_DIM_V */
+#define MLA_B200_HEAD_DIM_ROPE 64
+#define MLA_B200_HEAD_DIM_K 576 /* HEAD_DIM_C + HEAD_DIM_ROPE */
+#define MLA_B200_HEAD_DIM_V 512
+
+typedef enum {
+    MLA_B200_OK = 0,
+    MLA_B200_ERR_INVALID_ARG = 1,   /* bad pointer / shape / alignment */
+    MLA_B200_ERR_UNSUPPORTED = 2,   /* shape valid but not implemented */
+    MLA_B200_ERR_WORKSPACE = 3,     /* workspace missing or too small */
+    MLA_B200_ERR_CUDA = 4,          /* a CUDA runtime call failed */
+    MLA_B200_ERR_DEVICE_TIMEOUT = 5, /* a kernel's bounded wait expired */
+    MLA_B200_ERR_NO_DEVICE = 6      /* no sm_100 device current */
+} mla_b200_status;
+
+/* Output element type for entry points that can emit either. */
+typedef enum { MLA_B200_OUT_F16 = 0, MLA_B200_OUT_F32 = 1 } mla_b200_out_dtype;
+
+/* Human-readable name of a status code (static string). */
+const char *mla_b200_status_string(int status);
+
+/* Library version, e.g. "0.1.0". */
+const char *mla_b200_version(void);
+
+/* Value of a model constant by name ("NUM_HEADS", "HEAD_DIM", "HEAD_DIM_C",
+ * "HEAD_DIM_ROPE", "HEAD_DIM_K", "HEAD_DIM_V"); -1 for an unknown name.
+ * Retires the reference TODO at mla.py:29. */
+int mla_b200_constant(const char *name);
+
+/* ------------------------------------------------------------------------ */
+/* Planning                                                                  */
+/* ------------------------------------------------------------------------ */
+
+/* Split-count heuristic.  Replaces the constant `num_splits = 4`
+ * (csrc/mla_api.cpp:97).  Given `batch` sequences holding `total_tokens`
+ * cache rows in all and `num_heads` heads, chooses how many tokens one split
+ * (one work item) covers so that the items fill `num_sms` SMs (0 = the current
+ * device's count) while keeping the split-partial traffic small.  Writes the
+ * chunk length (a multiple of 64 tokens) to *chunk_tokens and, for a single
+ * sequence, the resulting split count to *num_splits (either may be NULL). */
+int mla_b200_plan(int batch, int num_heads, long long total_tokens, int max_seq_len,
+                  int num_sms, int *chunk_tokens, int *num_splits);
+
+/* Bytes of workspace the f16/f32 decode entry points need for this problem
+ * (split partials, the work table and the varlen schedule).  `num_splits` <= 0
+ * means "as chosen by mla_b200_plan".  For a single sequence pass batch = 1
+ * and total_tokens = seq_length. */
+size_t mla_b200_workspace_size(int batch, int num_heads, long long total_tokens,
+                               int max_seq_len, int num_splits);
+
+/* ------------------------------------------------------------------------ */
+/* Decode entry points                                                       */
+/* ------------------------------------------------------------------------ */
+
+/* fp16 split-KV decode of ONE sequence, reference semantics.
+ * Replaces run_mla_decode_splitk<at::Half> (csrc/mla_decode.hpp:25-34,
+ * csrc/mla_decode_splitk_fwd_sm89.cu:26-47 -> mla_decode_splitk_fwd.cuh:941-985).
+ *   query [num_heads, 576] fp16, cache [seq_length, 576] fp16,
+ *   out   [num_heads, 512] fp16.
+ * Softmax scale is the reference's 1/sqrt(HEAD_DIM + HEAD_DIM_ROPE) = 1/sqrt(192)
+ * (csrc/mla_decode_splitk_fwd.cuh:446-450).  num_splits <= 0 selects the
+ * heuristic; otherwise the sequence is cut into that many splits (tail masked,
+ * no multiple-of-64 requirement).  seq_length == 0 yields zeros.  Softmax
+ * state is fp32 (the reference keeps it in fp16). */
+int mla_b200_decode_split_f16(const void *query, const void *cache, void *out,
+                              int num_heads, int seq_length, int num_splits,
+                              void *workspace, size_t workspace_bytes, void *stream);
+
+/* Batched / variable-length fp16 decode (no reference counterpart: the
+ * reference has no batch dimension).
+ *   query [batch, num_heads, 576] fp16
+ *   cache packed [total_tokens, 576] fp16; sequence b owns rows
+ *         cu_seqlens[b] .. cu_seqlens[b+1]-1 (cu_seqlens: DEVICE int32 [batch+1],
+ *         cu_seqlens[0] = 0, cu_seqlens[batch] = total_tokens), or
+ *         cu_seqlens == NULL for a dense [batch, max_seq_len, 576] cache
+ *         (then total_tokens must equal batch * max_seq_len).
+ *   max_seq_len >= every N_b (used for planning only).
+ *   out [batch, num_heads, 512], fp16 or fp32 per out_dtype.
+ *   out_lse: optional [batch, num_heads] fp32 natural-log log-sum-exp of the
+ *         scaled logits (-inf for an empty sequence); NULL to skip.
+ * softmax_scale multiplies Q.C^T (pass 1.0 when the scale is folded into Q). */
+int mla_b200_decode_batched_f16(const void *query, const void *cache,
+                                const int32_t *cu_seqlens, int batch, int num_heads,
+                                long long total_tokens, int max_seq_len,
+                                float softmax_scale, int num_splits,
+                                void *out, int out_dtype, float *out_lse,
+                                void *workspace, size_t workspace_bytes, void *stream);
+
+/* fp32 fused decode of ONE sequence, reference semantics (scale 1/sqrt(192),
+ * 512 output columns).  Replaces run_mla_decode_fused (csrc/mla_decode.hpp:18-23,
+ * csrc/mla_decode_fused_fwd_sm89.cu:6-60).  head_dim_c must be 576. */
+int mla_b200_decode_fused_f32(const float *query, const float *cache, float *out,
+                              int num_heads, int head_dim_c, int seq_length,
+                              void *workspace, size_t workspace_bytes, void *stream);
+
+/* fp32 naive 3-kernel decode, reference semantics: scale 1/sqrt(head_dim_c),
+ * ALL head_dim_c output columns, attention matrix materialized in `attn`
+ * ([num_heads, seq_length] fp32, caller-owned scratch).  Replaces
+ * run_mla_decode_naive (csrc/mla_decode.hpp:10-16, csrc/mla_decode_naive_fwd.cu:4-31).
+ * Any head_dim_c >= 1; seq_length >= 1. */
+int mla_b200_decode_naive_f32(const float *query, const float *cache, float *attn,
+                              float *out, int num_heads, int head_dim_c,
+                              int seq_length, void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* Log-sum-exp merge of partial results                                      */
+/* ------------------------------------------------------------------------ */
+
+/* Merges `num_parts` partial decodes of the same queries over disjoint KV
+ * slices (e.g. one per GPU after an all-gather):
+ *   part_o   [num_parts, rows, 512] fp32, each normalized by its own sum
+ *   part_lse [num_parts, rows] fp32 natural-log LSE (-inf = empty slice)
+ *   out      [rows, 512] fp16 or fp32 (out_dtype); out_lse [rows] or NULL.
+ * rows = batch * num_heads.  Rows whose slices are all empty yield zeros.
+ * Generalises the reference's mla_decode_combine
+ * (csrc/mla_decode_splitk_fwd.cuh:894-939) to any part count and layout. */
+int mla_b200_combine_f32(const float *part_o, const float *part_lse, int num_parts,
+                         long long rows, void *out, int out_dtype, float *out_lse,
+                         void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* Device error word                                                         */
+/* ------------------------------------------------------------------------ */
+
+/* Every wait inside the kernels is bounded; a wait that expires records a
+ * code in a device-side error word and the kernel returns early.  This reads
+ * the word (synchronizing `stream`), writes it to *code (0 = none; may be NULL)
+ * and clears it.  Returns MLA_B200_ERR_DEVICE_TIMEOUT when it was set. */
+int mla_b200_get_device_error(int *code, void *stream);
+
+#ifdef __cplusplus
+} /* extern "C" */
+#endif
+
+#endif /* MLA_B200_H */

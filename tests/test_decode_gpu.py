@@ -1,0 +1,188 @@
+"""GPU parity of the decode entry points against the CPU oracle.
+
+Inputs are seeded; fp16 kernels are compared with the oracle run on the same
+fp16-rounded inputs upcast to fp32, on the north-star bar
+(max-abs <= 1e-2, mean-abs <= 1e-3 on O*)."""
+import os
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from conftest import assert_close_parity
+
+pytestmark = pytest.mark.gpu
+
+REF_SCALE = 1.0 / np.sqrt(192.0)
+GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden", "mla_ref_golden.npz")
+
+
+@pytest.fixture(scope="module")
+def mla():
+    import ada_mla
+
+    return ada_mla
+
+
+@pytest.fixture(scope="module")
+def capi():
+    from ada_mla import capi
+
+    return capi
+
+
+def _inputs(nh, n, seed, dtype=torch.float16, qscale=1.0):
+    g = torch.Generator().manual_seed(seed)
+    q = (torch.randn(nh, 576, generator=g) * qscale).to(dtype)
+    c = torch.randn(n, 576, generator=g).to(dtype)
+    return q, c
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy()
+
+
+def _no_device_error(mla):
+    assert mla.mla_get_device_error() == 0
+
+
+@pytest.mark.parametrize("n", [1, 15, 16, 17, 63, 64, 65, 1000, 4096, 4097])
+@pytest.mark.parametrize("nh", [16, 128])
+def test_split_f16_parity(mla, nh, n):
+    q, c = _inputs(nh, n, seed=nh * 7 + n)
+    out = mla.mla_decode_split(q.cuda(), c.cuda())
+    assert out.shape == (nh, 512) and out.dtype == torch.float16
+    ref = oracle.mla_decode_oracle(_np(q), _np(c), REF_SCALE, threads=8)
+    assert_close_parity(_np(out), ref, what=f"split nh={nh} n={n}")
+    _no_device_error(mla)
+
+
+@pytest.mark.parametrize("splits", [1, 2, 3, 4, 7, 64, 148, 5000])
+def test_split_f16_explicit_splits(mla, splits):
+    q, c = _inputs(128, 4100, seed=splits)
+    out = mla.mla_decode_split(q.cuda(), c.cuda(), splits)
+    ref = oracle.mla_decode_oracle(_np(q), _np(c), REF_SCALE, threads=8)
+    assert_close_parity(_np(out), ref, what=f"splits={splits}")
+
+
+def test_split_f16_through_capi(capi):
+    q, c = _inputs(128, 777, seed=3)
+    out = capi.decode_split_f16(q.cuda(), c.cuda())
+    torch.cuda.synchronize()
+    ref = oracle.mla_decode_oracle(_np(q), _np(c), REF_SCALE, threads=8)
+    assert_close_parity(_np(out), ref, what="capi split")
+    assert capi.get_device_error() == 0
+
+
+def test_split_empty_sequence_gives_zeros(capi):
+    q, _ = _inputs(128, 1, seed=4)
+    c = torch.empty(0, 576, dtype=torch.float16, device="cuda")
+    out = capi.decode_split_f16(q.cuda(), c)
+    torch.cuda.synchronize()
+    assert torch.count_nonzero(out).item() == 0
+
+
+def test_golden_fixtures_on_gpu(mla):
+    """The reference's own outputs (folded-scale fp16 cases) reproduced on the GPU."""
+    z = np.load(GOLDEN)
+    names = sorted({k.split("__")[0] for k in z.files if k.startswith("folded")})
+    assert names
+    for name in names:
+        q = torch.from_numpy(z[f"{name}__q"]).cuda()
+        c = torch.from_numpy(z[f"{name}__c"]).cuda()
+        ref = z[f"{name}__out"][:, :512]
+        out = mla.mla_decode_batched(q[None], c[None], softmax_scale=1.0, out_dtype=torch.float32)
+        assert_close_parity(_np(out[0]), ref, what=name)
+
+
+def test_fused_f32_parity(mla):
+    q, c = _inputs(128, 1000, seed=5, dtype=torch.float32)
+    out = mla.mla_decode_fused(q.cuda(), c.cuda())
+    assert out.shape == (128, 512) and out.dtype == torch.float32
+    ref = oracle.mla_decode_oracle(_np(q), _np(c), REF_SCALE, threads=8)
+    assert_close_parity(_np(out), ref, max_tol=1e-4, mean_tol=1e-5, what="fused f32")
+    # mla_decode_split with fp32 inputs works (the reference's fp32 branch is a stub)
+    out2 = mla.mla_decode_split(q.cuda(), c.cuda())
+    assert_close_parity(_np(out2), ref, max_tol=1e-4, mean_tol=1e-5, what="split f32")
+
+
+@pytest.mark.parametrize("nh,n,d", [(128, 1000, 576), (5, 33, 576), (7, 19, 100)])
+def test_naive_f32_reference_semantics(mla, capi, nh, n, d):
+    g = torch.Generator().manual_seed(nh + n)
+    q = torch.randn(nh, d, generator=g)
+    c = torch.randn(n, d, generator=g)
+    ref = oracle.run_mla_decode_cpu(_np(q), _np(c), threads=8)  # all d columns, 1/sqrt(d)
+    out = mla.mla_decode_naive(q.cuda(), c.cuda())
+    assert out.shape == (nh, d)
+    assert_close_parity(_np(out), ref, max_tol=1e-4, mean_tol=1e-5, what="naive")
+    out2 = capi.decode_naive_f32(q.cuda(), c.cuda())
+    torch.cuda.synchronize()
+    assert_close_parity(_np(out2), ref, max_tol=1e-4, mean_tol=1e-5, what="naive capi")
+
+
+def test_batched_dense(mla):
+    b, nh, n = 3, 16, 300
+    g = torch.Generator().manual_seed(11)
+    q = (torch.randn(b, nh, 576, generator=g) / np.sqrt(192)).half()
+    c = torch.randn(b, n, 576, generator=g).half()
+    out, lse = mla.mla_decode_batched(q.cuda(), c.cuda(), softmax_scale=1.0, return_lse=True)
+    for i in range(b):
+        ref = oracle.mla_decode_oracle(_np(q[i]), _np(c[i]), 1.0, threads=8)
+        assert_close_parity(_np(out[i]), ref, what=f"dense b={i}")
+        _, ref_lse = oracle.lse_partial_oracle(_np(q[i]), _np(c[i]), 1.0)
+        np.testing.assert_allclose(_np(lse[i]), ref_lse, atol=2e-3, rtol=0)
+
+
+def test_batched_varlen_with_empty(mla, capi):
+    lens = [5, 0, 64, 129, 1, 700]
+    nh = 128
+    g = torch.Generator().manual_seed(12)
+    q = (torch.randn(len(lens), nh, 576, generator=g) / np.sqrt(192)).half()
+    c = torch.randn(sum(lens), 576, generator=g).half()
+    cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32)
+    for num_splits in (-1, 1, 3):
+        out = mla.mla_decode_batched(q.cuda(), c.cuda(), cu.cuda(), max_seq_len=max(lens),
+                                     softmax_scale=1.0, num_splits=num_splits)
+        out_c = capi.decode_batched_f16(q.cuda(), c.cuda(), cu.cuda(), max(lens), 1.0,
+                                        num_splits=num_splits)
+        torch.cuda.synchronize()
+        lo = 0
+        for i, n in enumerate(lens):
+            if n == 0:
+                assert torch.count_nonzero(out[i]).item() == 0
+            else:
+                ref = oracle.mla_decode_oracle(_np(q[i]), _np(c[lo:lo + n]), 1.0, threads=8)
+                assert_close_parity(_np(out[i]), ref, what=f"varlen b={i} s={num_splits}")
+                assert_close_parity(_np(out_c[i]), ref, what=f"varlen capi b={i}")
+            lo += n
+
+
+def test_combine_matches_numpy_merge(capi):
+    rng = np.random.default_rng(4)
+    p, rows = 5, 37
+    po = rng.standard_normal((p, rows, 512)).astype(np.float32)
+    pl = rng.standard_normal((p, rows)).astype(np.float32) * 3
+    pl[1, :5] = -np.inf   # empty slices
+    pl[:, 7] = -np.inf    # a row with no data at all
+    out, lse = capi.combine_f32(torch.from_numpy(po).cuda(), torch.from_numpy(pl).cuda())
+    torch.cuda.synchronize()
+    m = pl.max(axis=0)
+    mm = np.where(np.isfinite(m), m, 0)
+    w = np.where(np.isfinite(pl), np.exp(pl - mm), 0)
+    s = w.sum(axis=0)
+    ref = np.einsum("pr,prd->rd", w, po) / np.where(s > 0, s, 1)[:, None]
+    np.testing.assert_allclose(_np(out), ref, atol=1e-5, rtol=1e-5)
+    assert np.all(_np(out)[7] == 0) and np.isneginf(_np(lse)[7])
+    fin = np.isfinite(m)
+    np.testing.assert_allclose(_np(lse)[fin], (m + np.log(np.where(s > 0, s, 1)))[fin], atol=1e-5)
+
+
+def test_errors_raise(mla):
+    q, c = _inputs(128, 64, seed=1)
+    with pytest.raises(RuntimeError):
+        mla.mla_decode_split(q.cuda(), c.cuda()[:, :512].contiguous())
+    with pytest.raises(RuntimeError):
+        mla.mla_decode_split(q.cuda(), c)  # cache on the host
+    with pytest.raises(RuntimeError):
+        mla.mla_decode_fused(q.cuda(), c.cuda())  # fp16 into the fp32 kernel name
