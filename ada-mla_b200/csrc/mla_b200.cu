@@ -5,13 +5,18 @@
 #include <math.h>
 #include <string.h>
 
+#include <algorithm>
 #include <atomic>
 #include <mutex>
+#include <type_traits>
+
+#include <cudaTypedefs.h>
 
 #include "mla_b200.h"
 #include "mla_combine.cuh"
 #include "mla_common.cuh"
 #include "mla_simt.cuh"
+#include "mla_tc.cuh"
 
 using namespace mla;
 
@@ -24,6 +29,7 @@ struct DevInfo {
     int sms = 0;
     int major = 0;
     bool simt_attr_set = false;
+    int tc_clusters = 0;  // co-resident 2-CTA clusters of the tcgen05 decode kernel
 };
 
 std::mutex g_dev_mu;
@@ -61,9 +67,64 @@ int current_device(int *dev_out, DevInfo *info_out) {
         }
         d.simt_attr_set = true;
     }
+    if (d.tc_clusters == 0) {
+        if (cudaFuncSetAttribute(tc::tc_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 tc::kSmemBytes) != cudaSuccess) {
+            cudaGetLastError();
+            return MLA_B200_ERR_CUDA;
+        }
+        cudaLaunchConfig_t cfg = {};
+        cfg.gridDim = dim3(2 * (d.sms / 2), 1, 1);
+        cfg.blockDim = dim3(tc::kThreads, 1, 1);
+        cfg.dynamicSmemBytes = tc::kSmemBytes;
+        cudaLaunchAttribute attr;
+        attr.id = cudaLaunchAttributeClusterDimension;
+        attr.val.clusterDim.x = 2;
+        attr.val.clusterDim.y = 1;
+        attr.val.clusterDim.z = 1;
+        cfg.attrs = &attr;
+        cfg.numAttrs = 1;
+        int n = 0;
+        if (cudaOccupancyMaxActiveClusters(&n, tc::tc_decode_kernel, &cfg) != cudaSuccess || n <= 0) {
+            cudaGetLastError();
+            n = d.sms / 2;
+        }
+        d.tc_clusters = n;
+    }
     *dev_out = dev;
     *info_out = d;
     return MLA_B200_OK;
+}
+
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no -lcuda).
+PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+    static std::once_flag once;
+    std::call_once(once, [] {
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+        cudaGetLastError();
+    });
+    return fn;
+}
+
+// 2-D view [rows, 576] fp16 of the cache; 64 x 64 boxes, 128-byte swizzle
+// (the UMMA K-major / MN-major SW128 operand layout).
+int make_cache_tmap(CUtensorMap *map, const void *cache, long long rows) {
+    auto enc = tmap_encoder();
+    if (enc == nullptr) return MLA_B200_ERR_CUDA;
+    cuuint64_t dims[2] = {(cuuint64_t)kDK, (cuuint64_t)rows};
+    cuuint64_t strides[1] = {(cuuint64_t)kDK * 2};
+    cuuint32_t box[2] = {64, (cuuint32_t)tc::kBN};
+    cuuint32_t estr[2] = {1, 1};
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(cache), dims,
+                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? MLA_B200_OK : MLA_B200_ERR_CUDA;
 }
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -73,7 +134,7 @@ inline long long cdiv(long long a, long long b) { return (a + b - 1) / b; }
 // of the decode kernel has; the chunk is the smallest multiple of kTile that
 // gives every worker at most one item, but never longer than a sequence.
 int plan_chunk(int batch, long long total_tokens, int max_seq_len, int num_sms) {
-    const long long units = num_sms > 1 ? num_sms / 2 : 1;
+    const long long units = num_sms > 1 ? num_sms / 2 : 1;  // 2-CTA clusters per wave
     long long chunk = cdiv(cdiv(total_tokens > 0 ? total_tokens : 1, units), kTile) * kTile;
     if (chunk < kTile) chunk = kTile;
     if (max_seq_len > 0) {
@@ -170,9 +231,24 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
                                                    (int)max_items);
     }
     if (wl.max_items > 0) {
-        dim3 grid(wl.max_items, (unsigned)cdiv(num_heads, kSimtHeads));
-        simt_partial_kernel<T><<<grid, 256, kSimtSmem, stream>>>(
-            q, cache, wl, num_heads, scale * kLog2e, L.part_o, L.part_lse);
+        if (std::is_same<T, __half>::value && num_heads <= 128) {
+            CUtensorMap map;
+            st = make_cache_tmap(&map, cache, total_tokens);
+            if (st != MLA_B200_OK) return st;
+            tc::TcParams tp;
+            tp.q = reinterpret_cast<const __half *>(q);
+            tp.wl = wl;
+            tp.num_heads = num_heads;
+            tp.scale_log2 = scale * kLog2e;
+            tp.part_o = L.part_o;
+            tp.part_lse = L.part_lse;
+            const int clusters = std::min(info.tc_clusters, wl.max_items);
+            tc::tc_decode_kernel<<<2 * clusters, tc::kThreads, tc::kSmemBytes, stream>>>(map, tp);
+        } else {
+            dim3 grid(wl.max_items, (unsigned)cdiv(num_heads, kSimtHeads));
+            simt_partial_kernel<T><<<grid, 256, kSimtSmem, stream>>>(
+                q, cache, wl, num_heads, scale * kLog2e, L.part_o, L.part_lse);
+        }
     }
     const long long rows = (long long)batch * num_heads;
     const unsigned cgrid = (unsigned)cdiv(rows, kCombineWarps);

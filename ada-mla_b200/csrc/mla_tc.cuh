@@ -1,0 +1,422 @@
+// mla_tc.cuh -- tcgen05 split-KV MLA decode for sm_100a (fp16 in, fp32 accumulate).
+//
+// Replaces the reference's mma.sync split kernel mla_decode_splitk_mma_fp16
+// (csrc/mla_decode_splitk_fwd.cuh:559-892).  One work item = up to `chunk`
+// cache rows of one sequence (mla_common.cuh WorkList); the item's partial
+// (O normalized by its own sum, natural-log LSE) goes to the workspace and
+// combine_kernel merges the items of each sequence.
+//
+// Why two CTAs per item.  For 128 heads the O accumulator is 128 x 512 fp32 =
+// all 512 TMEM columns of an SM, leaving no room for S = Q.C^T.  So each item
+// runs on a 2-CTA cluster (two SMs):
+//
+//   S-CTA (cluster rank 0)              O-CTA (cluster rank 1)
+//   Q* [128 x 576] fp16 in TMEM (288 col)  O [128 x 512] fp32 in TMEM (512 col)
+//   TMA: C tile [64 x 576] -> smem       TMA: C tile [64 x 512] -> smem
+//   GEMM1 S = Q.C^T  (TS, N=64)          GEMM2 O += P.C_N (SS, 2 x N=256,
+//   online softmax (fp32 m, l; lazy        C_N read MN-major from the tile)
+//     rescale, threshold 2^8)            rescale O rows when the S-CTA
+//   P fp16 + per-row alpha -----DSMEM--->  raised the running max; final
+//     bulk copy (17.5 KB / tile)           O / l and LSE to the workspace
+//
+// GEMM1 (576 MACs/token/head) and GEMM2 (512) are balanced across the pair,
+// no tensor work is duplicated, and each CTA streams its tile through a
+// 2-stage TMA/mbarrier ring.  The pair reads the same rows, so HBM sees each
+// cache byte about once (the second read hits L2).
+//
+// Warp roles (256 threads): warp 0 TMA producer, warp 1 MMA issuer (one
+// thread), warp 2 TMEM allocator, warps 4-7 the math warpgroup (softmax in
+// the S-CTA, correction + epilogue in the O-CTA); thread h of the warpgroup
+// owns TMEM lane h = head h.
+//
+// Heads: num_heads <= 128; rows >= num_heads are zero Q rows (their results
+// are dropped), so fewer heads cost the same tensor work as 128.
+#pragma once
+
+#include "mla_tc_ptx.cuh"
+
+namespace mla {
+namespace tc {
+
+constexpr int kBN = 64;                         // tokens per tile
+constexpr int kKBlocks = kDK / 64;              // 9 column blocks of 64 (TMA boxes)
+constexpr int kVBlocks = kDV / 64;              // 8
+constexpr int kBoxBytes = kBN * 128;            // 64 rows x 64 fp16
+constexpr int kCStageBytes = kKBlocks * kBoxBytes;   // 73728
+constexpr int kCNStageBytes = kVBlocks * kBoxBytes;  // 65536
+constexpr int kStages = 2;
+constexpr int kMsgP = 128 * kBN * 2;            // P tile, 128 rows x 128 B, SW128 K-major
+constexpr int kMsgAlpha = kMsgP;                // f32[128] rescale factors
+constexpr int kMsgL = kMsgP + 512;              // f32[128] row sums   (last tile of an item)
+constexpr int kMsgM = kMsgP + 1024;             // f32[128] row maxima (last tile of an item)
+constexpr int kMsgBytes = kMsgP + 1536;         // 17920
+constexpr int kMsgStride = 18 * 1024;           // keeps every P tile 1024-aligned
+constexpr int kMsgStages = 2;
+
+enum BarId {
+    kBarFull = 0,       // [2] TMA tile landed                 (count 1 + tx)
+    kBarEmpty = 2,      // [2] stage consumed by the MMAs      (count 1, commit)
+    kBarSFull = 4,      // [2] S-CTA: S tile in TMEM           (count 1, commit)
+    kBarSEmpty = 6,     // [2] S-CTA: S tile read by softmax   (count 128)
+    kBarQReady = 8,     //     S-CTA: Q rows stored in TMEM    (count 128)
+    kBarPFree = 9,      // [2] GEMM2 done with message stage   (count 1, multicast commit)
+    kBarPFull = 11,     // [2] O-CTA: message landed           (count 1 + tx, from the S-CTA)
+    kBarCorr = 13,      // [2] O-CTA: O ready for next GEMM2   (count 128)
+    kBarMmaDone = 15,   //     O-CTA: GEMM2 of a tile done     (count 1, commit)
+    kBarDrain = 16,     //     MMA issuer's own tcgen05 ops retired (teardown)
+    kNumBars = 17
+};
+
+constexpr int kOffStage = 0;
+constexpr int kOffMsg = kStages * kCStageBytes;                  // 147456
+constexpr int kOffBar = kOffMsg + kMsgStages * kMsgStride;       // 184320
+constexpr int kOffSlot = kOffBar + kNumBars * 8;
+constexpr int kOffAbort = kOffSlot + 4;
+constexpr int kSmemBytes = kOffAbort + 12 + 1024;                // + 1024 alignment slack
+
+constexpr int kThreads = 256;
+constexpr uint32_t kTmemCols = 512;
+constexpr uint32_t kTmemQ = 0;     // S-CTA: Q, 288 columns (2 fp16 per column)
+constexpr uint32_t kTmemS = 288;   // S-CTA: two S buffers of 64 columns
+constexpr float kRescaleLog2 = 8.0f;
+
+constexpr uint32_t kIdescS = ptx::idesc_f16_f32(128, kBN, 0, 0);   // M=128 heads, N=64 tokens
+constexpr uint32_t kIdescO = ptx::idesc_f16_f32(128, 256, 0, 1);   // M=128 heads, N=256 dims, B MN-major
+
+struct TcParams {
+    const __half *q;   // [batch, num_heads, 576]
+    WorkList wl;
+    int num_heads;
+    float scale_log2;  // softmax scale * log2(e)
+    float *part_o;     // [max_items, num_heads, 512]
+    float *part_lse;   // [max_items, num_heads]
+};
+
+__device__ __forceinline__ uint32_t u32_of(float f) { return __float_as_uint(f); }
+__device__ __forceinline__ float f32_of(uint32_t u) { return __uint_as_float(u); }
+
+__device__ __forceinline__ uint32_t pack_half2(float a, float b) {
+    __half2 h = __floats2half2_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+
+__global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
+    tc_decode_kernel(const __grid_constant__ CUtensorMap tmap, const TcParams p) {
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const uint32_t sbase = ptx::smem_u32(smem);
+    const uint32_t bar0 = sbase + kOffBar;
+    auto bar = [&](int id) -> uint32_t { return bar0 + 8u * id; };
+    volatile int *abort_flag = reinterpret_cast<volatile int *>(smem + kOffAbort);
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5, lane = tid & 31;
+    const uint32_t role = ptx::cluster_ctarank();  // 0 = S-CTA, 1 = O-CTA
+    const int cid = (int)ptx::cluster_id_x();
+    const int ncl = (int)ptx::nclusters_x();
+
+    if (tid == 0) {
+        for (int i = 0; i < 2; ++i) {
+            ptx::mbar_init(bar(kBarFull + i), 1);
+            ptx::mbar_init(bar(kBarEmpty + i), 1);
+            ptx::mbar_init(bar(kBarSFull + i), 1);
+            ptx::mbar_init(bar(kBarSEmpty + i), 128);
+            ptx::mbar_init(bar(kBarPFree + i), 1);
+            ptx::mbar_init(bar(kBarPFull + i), 1);
+            ptx::mbar_init(bar(kBarCorr + i), 128);
+        }
+        ptx::mbar_init(bar(kBarQReady), 128);
+        ptx::mbar_init(bar(kBarMmaDone), 1);
+        ptx::mbar_init(bar(kBarDrain), 1);
+        *abort_flag = 0;
+        ptx::fence_mbarrier_init_cluster();
+    }
+    if (warp == 0 && lane == 0) ptx::tma_prefetch_desc(&tmap);
+    if (warp == 2) {
+        ptx::tmem_alloc(sbase + kOffSlot, kTmemCols);
+        ptx::tmem_relinquish();
+    }
+    ptx::tc_fence_before();
+    ptx::cluster_sync();
+    ptx::tc_fence_after();
+    const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(smem + kOffSlot);
+
+    const WorkList &wl = p.wl;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ TMA producer
+        if (lane == 0) {
+            const int nblk = role == 0 ? kKBlocks : kVBlocks;
+            const uint32_t bytes = role == 0 ? kCStageBytes : kCNStageBytes;
+            const uint32_t stage_bytes = role == 0 ? kCStageBytes : kCNStageBytes;
+            uint32_t stage = 0, phase = 0;
+            bool ok = true;
+            for (int i = cid; ok && i < wl.max_items; i += ncl) {
+                const Item it = get_item(wl, i);
+                for (int t0 = 0; ok && t0 < it.len; t0 += kBN) {
+                    if (*abort_flag || !ptx::mbar_wait(bar(kBarEmpty + stage), phase ^ 1, kErrWaitEmpty)) {
+                        ok = false;
+                        break;
+                    }
+                    const uint32_t dst = sbase + kOffStage + stage * stage_bytes;
+                    ptx::mbar_arrive_expect_tx(bar(kBarFull + stage), bytes);
+                    const int row = (int)(it.row0 + t0);
+                    for (int kb = 0; kb < nblk; ++kb)
+                        ptx::tma_load_2d(dst + kb * kBoxBytes, &tmap, kb * 64, row, bar(kBarFull + stage));
+                    if (++stage == kStages) { stage = 0; phase ^= 1; }
+                }
+            }
+            if (!ok) *abort_flag = 1;
+            // drain: every issued tile has been consumed (or the wait expires)
+            for (int k = 0; k < kStages; ++k) {
+                ptx::mbar_wait(bar(kBarEmpty + stage), phase ^ 1, kErrWaitEmpty);
+                if (++stage == kStages) { stage = 0; phase ^= 1; }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA issuer
+        if (lane == 0) {
+            uint32_t stage = 0, phase = 0, jt = 0, qphase = 0;
+            int prev_b = -1;
+            bool ok = true;
+            for (int i = cid; ok && i < wl.max_items; i += ncl) {
+                const Item it = get_item(wl, i);
+                if (it.len <= 0) continue;
+                if (role == 0 && it.b != prev_b) {
+                    if (!ptx::mbar_wait(bar(kBarQReady), qphase, kErrWaitPeer)) { ok = false; break; }
+                    qphase ^= 1;
+                    prev_b = it.b;
+                }
+                for (int t0 = 0; t0 < it.len; t0 += kBN, ++jt) {
+                    const uint32_t sb = jt & 1;
+                    const uint32_t use = jt >> 1;
+                    if (*abort_flag || !ptx::mbar_wait(bar(kBarFull + stage), phase, kErrWaitFull)) { ok = false; break; }
+                    if (role == 0) {
+                        if (!ptx::mbar_wait(bar(kBarSEmpty + sb), (use & 1) ^ 1, kErrWaitMma)) { ok = false; break; }
+                        ptx::tc_fence_after();
+                        const uint32_t cst = sbase + kOffStage + stage * kCStageBytes;
+                        const uint32_t d = tmem + kTmemS + sb * kBN;
+#pragma unroll 4
+                        for (int kk = 0; kk < kDK / 16; ++kk) {
+                            const uint64_t bdesc = ptx::sdesc_sw128(cst + (kk >> 2) * kBoxBytes + (kk & 3) * 32, 16, 1024);
+                            ptx::mma_ts(d, tmem + kTmemQ + kk * 8, bdesc, kIdescS, kk > 0);
+                        }
+                        ptx::mma_commit(bar(kBarSFull + sb));
+                        ptx::mma_commit(bar(kBarEmpty + stage));
+                    } else {
+                        if (!ptx::mbar_wait(bar(kBarPFull + sb), use & 1, kErrWaitPeer) ||
+                            !ptx::mbar_wait(bar(kBarCorr + sb), use & 1, kErrWaitMma)) { ok = false; break; }
+                        ptx::tc_fence_after();
+                        const uint32_t cst = sbase + kOffStage + stage * kCNStageBytes;
+                        const uint32_t msg = sbase + kOffMsg + sb * kMsgStride;
+#pragma unroll
+                        for (int nh = 0; nh < 2; ++nh) {
+#pragma unroll
+                            for (int kk = 0; kk < kBN / 16; ++kk) {
+                                const uint64_t adesc = ptx::sdesc_sw128(msg + kk * 32, 16, 1024);
+                                const uint64_t bdesc = ptx::sdesc_sw128(cst + nh * 4 * kBoxBytes + kk * 16 * 128, kBoxBytes, 1024);
+                                ptx::mma_ss(tmem + nh * 256, adesc, bdesc, kIdescO, (t0 > 0 || kk > 0) ? 1u : 0u);
+                            }
+                        }
+                        ptx::mma_commit_mc(bar(kBarPFree + sb), 0x3);
+                        ptx::mma_commit(bar(kBarEmpty + stage));
+                        ptx::mma_commit(bar(kBarMmaDone));
+                    }
+                    if (++stage == kStages) { stage = 0; phase ^= 1; }
+                }
+            }
+            if (!ok) *abort_flag = 1;
+            // every MMA this thread issued has retired before TMEM is freed
+            ptx::mma_commit(bar(kBarDrain));
+            ptx::mbar_wait(bar(kBarDrain), 0, kErrWaitMma);
+        }
+    } else if (warp >= 4) {
+        // ------------------------------------------------------------ math warpgroup
+        const int h = tid - 128;                              // head row = TMEM lane
+        const uint32_t lane_addr = (uint32_t)((warp & 3) * 32) << 16;
+        const uint32_t trow = tmem + lane_addr;
+        uint32_t jt = 0;
+        bool ok = true;
+        if (role == 0) {
+            // ------------------------------------------------ S-CTA: softmax
+            int prev_b = -1;
+            const uint32_t peer_pfull0 = ptx::mapa(bar(kBarPFull), 1);
+            const uint32_t peer_msg0 = ptx::mapa(sbase + kOffMsg, 1);
+            for (int i = cid; ok && i < wl.max_items; i += ncl) {
+                const Item it = get_item(wl, i);
+                if (it.len <= 0) continue;
+                if (it.b != prev_b) {
+                    // Q row h of sequence b -> TMEM columns [0, 288) (zeros past num_heads).
+                    // Every GEMM1 of the previous item has completed: its S tiles were waited on.
+                    const uint4 *src = reinterpret_cast<const uint4 *>(p.q + ((size_t)it.b * p.num_heads + h) * kDK);
+                    const bool live = h < p.num_heads;
+#pragma unroll 1
+                    for (int c = 0; c < kKBlocks; ++c) {
+                        uint32_t r[32];
+#pragma unroll
+                        for (int v = 0; v < 8; ++v) {
+                            uint4 x = live ? __ldg(src + c * 8 + v) : make_uint4(0, 0, 0, 0);
+                            r[4 * v] = x.x; r[4 * v + 1] = x.y; r[4 * v + 2] = x.z; r[4 * v + 3] = x.w;
+                        }
+                        ptx::tmem_st_x32(trow + kTmemQ + c * 32, r);
+                    }
+                    ptx::tmem_wait_st();
+                    ptx::tc_fence_before();
+                    ptx::mbar_arrive(bar(kBarQReady));
+                    prev_b = it.b;
+                }
+                float m_used = -INFINITY, l_run = 0.f;
+                for (int t0 = 0; t0 < it.len; t0 += kBN, ++jt) {
+                    const uint32_t sb = jt & 1, use = jt >> 1;
+                    // Every decision below is made uniform across the warpgroup by the
+                    // bar.red at the end of the tile, so an expired wait can never split
+                    // a warp at a .sync.aligned tcgen05 op or strand a named barrier.
+                    bool w = !*abort_flag && ptx::mbar_wait(bar(kBarSFull + sb), use & 1, kErrWaitMma);
+                    w = __all_sync(0xffffffffu, w);
+                    float alpha = 1.f;
+                    const bool last = t0 + kBN >= it.len;
+                    uint32_t pk[32];
+                    if (w) {
+                        ptx::tc_fence_after();
+                        uint32_t r[64];
+                        {
+                            uint32_t a[32], b[32];
+                            ptx::tmem_ld_x32(trow + kTmemS + sb * kBN, a);
+                            ptx::tmem_ld_x32(trow + kTmemS + sb * kBN + 32, b);
+                            ptx::tmem_wait_ld();
+#pragma unroll
+                            for (int c = 0; c < 32; ++c) { r[c] = a[c]; r[32 + c] = b[c]; }
+                        }
+                        ptx::tc_fence_before();
+                        ptx::mbar_arrive(bar(kBarSEmpty + sb));
+
+                        const int valid = min(kBN, it.len - t0);
+                        float mx = -INFINITY;
+#pragma unroll
+                        for (int c = 0; c < kBN; ++c) {
+                            const float x = c < valid ? f32_of(r[c]) * p.scale_log2 : -INFINITY;
+                            r[c] = u32_of(x);
+                            mx = fmaxf(mx, x);
+                        }
+                        if (mx > m_used + kRescaleLog2) {
+                            alpha = (m_used == -INFINITY) ? 0.f : ptx::ex2(m_used - mx);
+                            m_used = mx;
+                        }
+                        float sum = 0.f;
+#pragma unroll
+                        for (int c = 0; c < kBN; c += 2) {
+                            const float p0 = ptx::ex2(f32_of(r[c]) - m_used);
+                            const float p1 = ptx::ex2(f32_of(r[c + 1]) - m_used);
+                            sum += p0 + p1;
+                            pk[c >> 1] = pack_half2(p0, p1);
+                        }
+                        l_run = l_run * alpha + sum;
+                        // message stage sb is free once GEMM2 of tile jt-2 finished
+                        w = ptx::mbar_wait(bar(kBarPFree + sb), (use & 1) ^ 1, kErrWaitPeer);
+                    }
+                    if (w) {
+                        uint8_t *msg = smem + kOffMsg + sb * kMsgStride;
+                        uint4 *prow = reinterpret_cast<uint4 *>(msg + h * 128);
+#pragma unroll
+                        for (int c8 = 0; c8 < 8; ++c8)
+                            prow[c8 ^ (h & 7)] = make_uint4(pk[4 * c8], pk[4 * c8 + 1], pk[4 * c8 + 2], pk[4 * c8 + 3]);
+                        reinterpret_cast<float *>(msg + kMsgAlpha)[h] = alpha;
+                        if (last) {
+                            reinterpret_cast<float *>(msg + kMsgL)[h] = l_run;
+                            reinterpret_cast<float *>(msg + kMsgM)[h] = m_used;
+                        }
+                        ptx::fence_proxy_async_smem();
+                    }
+                    if (!ptx::named_barrier_and(1, 128, w)) { ok = false; break; }
+                    if (h == 0) {
+                        const uint32_t rbar = peer_pfull0 + 8u * sb;
+                        ptx::mbar_remote_arrive_expect_tx(rbar, kMsgBytes);
+                        ptx::bulk_copy_s2cluster(peer_msg0 + sb * kMsgStride, sbase + kOffMsg + sb * kMsgStride,
+                                                 kMsgBytes, rbar);
+                        ptx::bulk_commit_group();
+                    }
+                }
+            }
+            if (!ok) *abort_flag = 1;
+            // The last two messages were consumed by the peer's GEMM2 (so no
+            // remote arrival is still in flight towards this CTA).
+            for (uint32_t k = (jt >= 2 ? jt - 2 : 0); k < jt; ++k)
+                ptx::mbar_wait(bar(kBarPFree + (k & 1)), (k >> 1) & 1, kErrWaitPeer);
+            if (h == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
+        } else {
+            // ------------------------------------------------ O-CTA: correction + epilogue
+            for (int i = cid; ok && i < wl.max_items; i += ncl) {
+                const Item it = get_item(wl, i);
+                if (it.len <= 0) continue;
+                for (int t0 = 0; t0 < it.len; t0 += kBN, ++jt) {
+                    const uint32_t sb = jt & 1, use = jt >> 1;
+                    // As in the S-CTA, every branch is warpgroup-uniform (bar.red).
+                    bool w = !*abort_flag && ptx::mbar_wait(bar(kBarPFull + sb), use & 1, kErrWaitPeer);
+                    if (!ptx::named_barrier_and(2, 128, w)) { ok = false; break; }
+                    const uint8_t *msg = smem + kOffMsg + sb * kMsgStride;
+                    const float alpha = reinterpret_cast<const float *>(msg + kMsgAlpha)[h];
+                    const bool last = t0 + kBN >= it.len;
+                    float l_fin = 0.f, m_fin = 0.f;
+                    if (last) {
+                        l_fin = reinterpret_cast<const float *>(msg + kMsgL)[h];
+                        m_fin = reinterpret_cast<const float *>(msg + kMsgM)[h];
+                    }
+                    if (t0 > 0 && ptx::named_barrier_or(2, 128, alpha != 1.f)) {
+                        w = ptx::mbar_wait(bar(kBarMmaDone), (jt - 1) & 1, kErrWaitMma);
+                        if (!ptx::named_barrier_and(2, 128, w)) { ok = false; break; }
+                        ptx::tc_fence_after();
+#pragma unroll 1
+                        for (int c = 0; c < kDV / 32; ++c) {
+                            uint32_t r[32];
+                            ptx::tmem_ld_x32(trow + c * 32, r);
+                            ptx::tmem_wait_ld();
+#pragma unroll
+                            for (int k = 0; k < 32; ++k) r[k] = u32_of(f32_of(r[k]) * alpha);
+                            ptx::tmem_st_x32(trow + c * 32, r);
+                        }
+                        ptx::tmem_wait_st();
+                    }
+                    ptx::tc_fence_before();
+                    ptx::mbar_arrive(bar(kBarCorr + sb));
+                    if (last) {
+                        w = ptx::mbar_wait(bar(kBarMmaDone), jt & 1, kErrWaitMma);
+                        if (!ptx::named_barrier_and(2, 128, w)) { ok = false; break; }
+                        ptx::tc_fence_after();
+                        const bool live = h < p.num_heads;
+                        const float inv_l = l_fin > 0.f ? 1.f / l_fin : 0.f;
+                        const size_t prow = (size_t)i * p.num_heads + h;
+                        float4 *dst = reinterpret_cast<float4 *>(p.part_o + prow * kDV);
+#pragma unroll 1
+                        for (int c = 0; c < kDV / 32; ++c) {
+                            uint32_t r[32];
+                            ptx::tmem_ld_x32(trow + c * 32, r);
+                            ptx::tmem_wait_ld();
+                            if (live) {
+#pragma unroll
+                                for (int k = 0; k < 8; ++k)
+                                    dst[c * 8 + k] = make_float4(f32_of(r[4 * k]) * inv_l, f32_of(r[4 * k + 1]) * inv_l,
+                                                                 f32_of(r[4 * k + 2]) * inv_l, f32_of(r[4 * k + 3]) * inv_l);
+                            }
+                        }
+                        if (live) p.part_lse[prow] = l_fin > 0.f ? (m_fin + __log2f(l_fin)) * kLn2 : -INFINITY;
+                        ptx::tc_fence_before();
+                    }
+                }
+            }
+            if (!ok) *abort_flag = 1;
+        }
+    }
+
+    // ---------------------------------------------------------------- teardown
+    ptx::tc_fence_before();
+    __syncthreads();
+    __syncwarp();
+    ptx::cluster_sync();  // neither CTA leaves while its partner may still target it
+    if (warp == 2) {
+        ptx::tc_fence_after();
+        ptx::tmem_dealloc(tmem, kTmemCols);
+    }
+}
+
+}  // namespace tc
+}  // namespace mla
