@@ -33,6 +33,7 @@ SIGNATURES = {
     "mla_b200_status_string": (ctypes.c_char_p, [_c_int]),
     "mla_b200_version": (ctypes.c_char_p, []),
     "mla_b200_constant": (_c_int, [ctypes.c_char_p]),
+    "mla_b200_device_info": (_c_int, [ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
     "mla_b200_plan": (_c_int, [_c_int, _c_int, _c_ll, _c_int, _c_int,
                                ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
     "mla_b200_workspace_size": (_c_size, [_c_int, _c_int, _c_ll, _c_int, _c_int]),
@@ -87,6 +88,13 @@ def _ptr(t: torch.Tensor | None) -> int | None:
 
 def constant(name: str) -> int:
     return lib().mla_b200_constant(name.encode())
+
+
+def device_info():
+    """(num_sms, resident 2-CTA decode clusters) of the current device."""
+    sms, cl = _c_int(0), _c_int(0)
+    _check("mla_b200_device_info", lib().mla_b200_device_info(ctypes.byref(sms), ctypes.byref(cl)))
+    return sms.value, cl.value
 
 
 def plan(batch: int, num_heads: int, total_tokens: int, max_seq_len: int, num_sms: int = 0):

@@ -111,16 +111,16 @@ PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
     return fn;
 }
 
-// 2-D view [rows, 576] fp16 of the cache; 64 x 64 boxes, 128-byte swizzle
+// 2-D view [rows, 576] fp16 with (64 x box_rows) boxes and 128-byte swizzle
 // (the UMMA K-major / MN-major SW128 operand layout).
-int make_cache_tmap(CUtensorMap *map, const void *cache, long long rows) {
+int make_tmap_576(CUtensorMap *map, const void *base, long long rows, int box_rows) {
     auto enc = tmap_encoder();
     if (enc == nullptr) return MLA_B200_ERR_CUDA;
     cuuint64_t dims[2] = {(cuuint64_t)kDK, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)kDK * 2};
-    cuuint32_t box[2] = {64, (cuuint32_t)tc::kBN};
+    cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
-    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(cache), dims,
+    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims,
                            strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -232,18 +232,18 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     }
     if (wl.max_items > 0) {
         if (std::is_same<T, __half>::value && num_heads <= 128) {
-            CUtensorMap map;
-            st = make_cache_tmap(&map, cache, total_tokens);
+            CUtensorMap cmap, qmap;
+            st = make_tmap_576(&cmap, cache, total_tokens, tc::kBN);
+            if (st == MLA_B200_OK) st = make_tmap_576(&qmap, q, (long long)batch * num_heads, 128);
             if (st != MLA_B200_OK) return st;
             tc::TcParams tp;
-            tp.q = reinterpret_cast<const __half *>(q);
             tp.wl = wl;
             tp.num_heads = num_heads;
             tp.scale_log2 = scale * kLog2e;
             tp.part_o = L.part_o;
             tp.part_lse = L.part_lse;
             const int clusters = std::min(info.tc_clusters, wl.max_items);
-            tc::tc_decode_kernel<<<2 * clusters, tc::kThreads, tc::kSmemBytes, stream>>>(map, tp);
+            tc::tc_decode_kernel<<<2 * clusters, tc::kThreads, tc::kSmemBytes, stream>>>(cmap, qmap, tp);
         } else {
             dim3 grid(wl.max_items, (unsigned)cdiv(num_heads, kSimtHeads));
             simt_partial_kernel<T><<<grid, 256, kSimtSmem, stream>>>(
@@ -290,6 +290,16 @@ int mla_b200_constant(const char *name) {
     if (!strcmp(name, "HEAD_DIM_K")) return MLA_B200_HEAD_DIM_K;
     if (!strcmp(name, "HEAD_DIM_V")) return MLA_B200_HEAD_DIM_V;
     return -1;
+}
+
+int mla_b200_device_info(int *num_sms, int *decode_clusters) {
+    int dev;
+    DevInfo info;
+    const int st = current_device(&dev, &info);
+    if (st != MLA_B200_OK) return st;
+    if (num_sms) *num_sms = info.sms;
+    if (decode_clusters) *decode_clusters = info.tc_clusters;
+    return MLA_B200_OK;
 }
 
 int mla_b200_plan(int batch, int num_heads, long long total_tokens, int max_seq_len, int num_sms,

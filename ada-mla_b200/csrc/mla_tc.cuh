@@ -10,27 +10,32 @@
 // all 512 TMEM columns of an SM, leaving no room for S = Q.C^T.  So each item
 // runs on a 2-CTA cluster (two SMs):
 //
-//   S-CTA (cluster rank 0)              O-CTA (cluster rank 1)
-//   Q* [128 x 576] fp16 in TMEM (288 col)  O [128 x 512] fp32 in TMEM (512 col)
-//   TMA: C tile [64 x 576] -> smem       TMA: C tile [64 x 512] -> smem
-//   GEMM1 S = Q.C^T  (TS, N=64)          GEMM2 O += P.C_N (SS, 2 x N=256,
-//   online softmax (fp32 m, l; lazy        C_N read MN-major from the tile)
-//     rescale, threshold 2^8)            rescale O rows when the S-CTA
-//   P fp16 + per-row alpha -----DSMEM--->  raised the running max; final
-//     bulk copy (17.5 KB / tile)           O / l and LSE to the workspace
+//   S-CTA (cluster rank 0)                O-CTA (cluster rank 1)
+//   Q* [128 x 576] fp16 in TMEM (288 col)   O [128 x 512] fp32 in TMEM (512 col)
+//   TMA: C tile [32 x 576] -> 5-stage ring TMA: C tile [32 x 512] -> 6-stage ring
+//   GEMM1 S = Q.C^T  (TS MMA, N=32)         GEMM2 O += P.C_N (SS MMA, 2 x N=256,
+//   online softmax (fp32 m, l; lazy           C_N read MN-major from the tile)
+//     rescale, threshold 2^8)               rescale O rows when the S-CTA
+//   P fp16 + per-row alpha -----DSMEM----->   raised the running max; final
+//     bulk copy (9.5 KB / tile)               O / l and LSE to the workspace
 //
-// GEMM1 (576 MACs/token/head) and GEMM2 (512) are balanced across the pair,
-// no tensor work is duplicated, and each CTA streams its tile through a
-// 2-stage TMA/mbarrier ring.  The pair reads the same rows, so HBM sees each
-// cache byte about once (the second read hits L2).
+// GEMM1 (576 MACs/token/head) and GEMM2 (512) are balanced across the pair
+// and no tensor work is duplicated.  Tiles are 32 tokens so that each SM keeps
+// four tiles (~140 KB) of cache reads in flight, which HBM latency needs.  The
+// pair reads the same rows; the second read of each byte hits L2.
+//
+// Q reaches TMEM through shared memory: at the first item of a sequence the
+// S-CTA's producer waits for its ring to drain, TMA-loads the 144 KB Q block
+// into the ring's space, and the softmax warpgroup moves each row into TMEM.
 //
 // Warp roles (256 threads): warp 0 TMA producer, warp 1 MMA issuer (one
 // thread), warp 2 TMEM allocator, warps 4-7 the math warpgroup (softmax in
 // the S-CTA, correction + epilogue in the O-CTA); thread h of the warpgroup
 // owns TMEM lane h = head h.
 //
-// Heads: num_heads <= 128; rows >= num_heads are zero Q rows (their results
-// are dropped), so fewer heads cost the same tensor work as 128.
+// Heads: num_heads <= 128; rows >= num_heads carry the next rows of Q (or the
+// TMA's zero fill) and their results are dropped, so fewer heads cost the same
+// tensor work as 128.
 #pragma once
 
 #include "mla_tc_ptx.cuh"
@@ -38,38 +43,47 @@
 namespace mla {
 namespace tc {
 
-constexpr int kBN = 64;                         // tokens per tile
-constexpr int kKBlocks = kDK / 64;              // 9 column blocks of 64 (TMA boxes)
-constexpr int kVBlocks = kDV / 64;              // 8
-constexpr int kBoxBytes = kBN * 128;            // 64 rows x 64 fp16
-constexpr int kCStageBytes = kKBlocks * kBoxBytes;   // 73728
-constexpr int kCNStageBytes = kVBlocks * kBoxBytes;  // 65536
-constexpr int kStages = 2;
-constexpr int kMsgP = 128 * kBN * 2;            // P tile, 128 rows x 128 B, SW128 K-major
-constexpr int kMsgAlpha = kMsgP;                // f32[128] rescale factors
-constexpr int kMsgL = kMsgP + 512;              // f32[128] row sums   (last tile of an item)
-constexpr int kMsgM = kMsgP + 1024;             // f32[128] row maxima (last tile of an item)
-constexpr int kMsgBytes = kMsgP + 1536;         // 17920
-constexpr int kMsgStride = 18 * 1024;           // keeps every P tile 1024-aligned
+constexpr int kBN = 32;                          // tokens per tile
+constexpr int kKBlocks = kDK / 64;               // 9 column blocks of 64 (TMA boxes)
+constexpr int kVBlocks = kDV / 64;               // 8
+constexpr int kBoxBytes = kBN * 128;             // one box: 32 rows x 64 fp16 (4 KB)
+constexpr int kStageS = kKBlocks * kBoxBytes;    // 36864: C tile [32 x 576]
+constexpr int kStageO = kVBlocks * kBoxBytes;    // 32768: C tile [32 x 512]
+constexpr int kStagesS = 5;
+constexpr int kStagesO = 6;
+constexpr int kQBoxBytes = 128 * 128;            // Q box: 128 rows x 64 fp16
+constexpr int kQBytes = kKBlocks * kQBoxBytes;   // 147456
+static_assert(kQBytes <= kStagesS * kStageS, "Q must fit in the S-CTA ring");
+
+constexpr int kMsgP = 128 * kBN * 2;             // P tile, 128 rows x 64 B, SW64 K-major
+constexpr int kMsgAlpha = kMsgP;                 // f32[128] rescale factors
+constexpr int kMsgL = kMsgP + 512;               // f32[128] row sums   (last tile of an item)
+constexpr int kMsgM = kMsgP + 1024;              // f32[128] row maxima (last tile of an item)
+constexpr int kMsgBytes = kMsgP + 1536;          // 9728
+constexpr int kMsgStride = 10 * 1024;
 constexpr int kMsgStages = 2;
 
 enum BarId {
-    kBarFull = 0,       // [2] TMA tile landed                 (count 1 + tx)
-    kBarEmpty = 2,      // [2] stage consumed by the MMAs      (count 1, commit)
-    kBarSFull = 4,      // [2] S-CTA: S tile in TMEM           (count 1, commit)
-    kBarSEmpty = 6,     // [2] S-CTA: S tile read by softmax   (count 128)
-    kBarQReady = 8,     //     S-CTA: Q rows stored in TMEM    (count 128)
-    kBarPFree = 9,      // [2] GEMM2 done with message stage   (count 1, multicast commit)
-    kBarPFull = 11,     // [2] O-CTA: message landed           (count 1 + tx, from the S-CTA)
-    kBarCorr = 13,      // [2] O-CTA: O ready for next GEMM2   (count 128)
-    kBarMmaDone = 15,   //     O-CTA: GEMM2 of a tile done     (count 1, commit)
-    kBarDrain = 16,     //     MMA issuer's own tcgen05 ops retired (teardown)
-    kNumBars = 17
+    kBarFull = 0,        // [6] TMA tile landed                  (count 1 + tx)
+    kBarEmpty = 6,       // [6] slot consumed by the MMAs        (count 1, commit)
+    kBarSFull = 12,      // [2] S-CTA: S tile in TMEM            (count 1, commit)
+    kBarSEmpty = 14,     // [2] S-CTA: S tile read by softmax    (count 128)
+    kBarQFull = 16,      //     S-CTA: Q block landed in smem    (count 1 + tx)
+    kBarQFree = 17,      //     S-CTA: Q moved to TMEM, smem free (count 128)
+    kBarQReady = 18,     //     S-CTA: Q rows in TMEM            (count 128)
+    kBarPFree = 19,      // [2] GEMM2 done with message stage    (count 1, multicast commit)
+    kBarPFull = 21,      // [2] O-CTA: message landed            (count 1 + tx, from the S-CTA)
+    kBarCorr = 23,       // [2] O-CTA: O ready for next GEMM2    (count 128)
+    kBarMmaDone = 25,    //     O-CTA: GEMM2 of a tile done      (count 1, commit)
+    kBarDrain = 26,      //     MMA issuer's tcgen05 ops retired (teardown)
+    kNumBars = 27
 };
 
 constexpr int kOffStage = 0;
-constexpr int kOffMsg = kStages * kCStageBytes;                  // 147456
-constexpr int kOffBar = kOffMsg + kMsgStages * kMsgStride;       // 184320
+constexpr int kRingBytes = kStagesO * kStageO;                   // 196608 (>= S ring)
+static_assert(kStagesS * kStageS <= kRingBytes, "ring");
+constexpr int kOffMsg = kRingBytes;
+constexpr int kOffBar = kOffMsg + kMsgStages * kMsgStride;       // 217088
 constexpr int kOffSlot = kOffBar + kNumBars * 8;
 constexpr int kOffAbort = kOffSlot + 4;
 constexpr int kSmemBytes = kOffAbort + 12 + 1024;                // + 1024 alignment slack
@@ -77,14 +91,13 @@ constexpr int kSmemBytes = kOffAbort + 12 + 1024;                // + 1024 align
 constexpr int kThreads = 256;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemQ = 0;     // S-CTA: Q, 288 columns (2 fp16 per column)
-constexpr uint32_t kTmemS = 288;   // S-CTA: two S buffers of 64 columns
+constexpr uint32_t kTmemS = 288;   // S-CTA: two S buffers of kBN columns
 constexpr float kRescaleLog2 = 8.0f;
 
-constexpr uint32_t kIdescS = ptx::idesc_f16_f32(128, kBN, 0, 0);   // M=128 heads, N=64 tokens
+constexpr uint32_t kIdescS = ptx::idesc_f16_f32(128, kBN, 0, 0);   // M=128 heads, N=32 tokens
 constexpr uint32_t kIdescO = ptx::idesc_f16_f32(128, 256, 0, 1);   // M=128 heads, N=256 dims, B MN-major
 
 struct TcParams {
-    const __half *q;   // [batch, num_heads, 576]
     WorkList wl;
     int num_heads;
     float scale_log2;  // softmax scale * log2(e)
@@ -100,8 +113,10 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
     return *reinterpret_cast<uint32_t *>(&h);
 }
 
+// cmap: cache [rows, 576] fp16, box 64 x kBN.   qmap: query [B * n_h, 576], box 64 x 128.
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-    tc_decode_kernel(const __grid_constant__ CUtensorMap tmap, const TcParams p) {
+    tc_decode_kernel(const __grid_constant__ CUtensorMap cmap,
+                     const __grid_constant__ CUtensorMap qmap, const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const uint32_t sbase = ptx::smem_u32(smem);
@@ -114,24 +129,33 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t role = ptx::cluster_ctarank();  // 0 = S-CTA, 1 = O-CTA
     const int cid = (int)ptx::cluster_id_x();
     const int ncl = (int)ptx::nclusters_x();
+    const int nstages = role == 0 ? kStagesS : kStagesO;
+    const uint32_t stage_bytes = role == 0 ? kStageS : kStageO;
 
     if (tid == 0) {
-        for (int i = 0; i < 2; ++i) {
+        for (int i = 0; i < kStagesO; ++i) {
             ptx::mbar_init(bar(kBarFull + i), 1);
             ptx::mbar_init(bar(kBarEmpty + i), 1);
+        }
+        for (int i = 0; i < 2; ++i) {
             ptx::mbar_init(bar(kBarSFull + i), 1);
             ptx::mbar_init(bar(kBarSEmpty + i), 128);
             ptx::mbar_init(bar(kBarPFree + i), 1);
             ptx::mbar_init(bar(kBarPFull + i), 1);
             ptx::mbar_init(bar(kBarCorr + i), 128);
         }
+        ptx::mbar_init(bar(kBarQFull), 1);
+        ptx::mbar_init(bar(kBarQFree), 128);
         ptx::mbar_init(bar(kBarQReady), 128);
         ptx::mbar_init(bar(kBarMmaDone), 1);
         ptx::mbar_init(bar(kBarDrain), 1);
         *abort_flag = 0;
         ptx::fence_mbarrier_init_cluster();
     }
-    if (warp == 0 && lane == 0) ptx::tma_prefetch_desc(&tmap);
+    if (warp == 0 && lane == 0) {
+        ptx::tma_prefetch_desc(&cmap);
+        ptx::tma_prefetch_desc(&qmap);
+    }
     if (warp == 2) {
         ptx::tmem_alloc(sbase + kOffSlot, kTmemCols);
         ptx::tmem_relinquish();
@@ -147,30 +171,51 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
             const int nblk = role == 0 ? kKBlocks : kVBlocks;
-            const uint32_t bytes = role == 0 ? kCStageBytes : kCNStageBytes;
-            const uint32_t stage_bytes = role == 0 ? kCStageBytes : kCNStageBytes;
-            uint32_t stage = 0, phase = 0;
+            uint32_t stage = 0, phase = 0, qround = 0;
+            int pre = 0;  // upcoming ring slots already known to be free
+            int prev_b = -1;
             bool ok = true;
             for (int i = cid; ok && i < wl.max_items; i += ncl) {
                 const Item it = get_item(wl, i);
-                for (int t0 = 0; ok && t0 < it.len; t0 += kBN) {
-                    if (*abort_flag || !ptx::mbar_wait(bar(kBarEmpty + stage), phase ^ 1, kErrWaitEmpty)) {
+                if (it.len <= 0) continue;
+                if (role == 0 && it.b != prev_b) {
+                    // Drain the ring (every slot consumed), then borrow it for Q.
+                    for (int k = pre; k < nstages; ++k) {
+                        const int s2 = (int)stage + k;
+                        const uint32_t slot = s2 % nstages;
+                        const uint32_t ph = s2 >= nstages ? phase ^ 1 : phase;
+                        if (*abort_flag || !ptx::mbar_wait(bar(kBarEmpty + slot), ph ^ 1, kErrWaitEmpty)) { ok = false; break; }
+                    }
+                    if (!ok) break;
+                    pre = nstages;
+                    ptx::mbar_arrive_expect_tx(bar(kBarQFull), kQBytes);
+                    const int qrow = it.b * p.num_heads;
+                    for (int kb = 0; kb < kKBlocks; ++kb)
+                        ptx::tma_load_2d(sbase + kOffStage + kb * kQBoxBytes, &qmap, kb * 64, qrow, bar(kBarQFull));
+                    if (!ptx::mbar_wait(bar(kBarQFree), qround & 1, kErrWaitPeer)) { ok = false; break; }
+                    ++qround;
+                    prev_b = it.b;
+                }
+                for (int t0 = 0; t0 < it.len; t0 += kBN) {
+                    if (pre > 0) {
+                        --pre;
+                    } else if (*abort_flag || !ptx::mbar_wait(bar(kBarEmpty + stage), phase ^ 1, kErrWaitEmpty)) {
                         ok = false;
                         break;
                     }
                     const uint32_t dst = sbase + kOffStage + stage * stage_bytes;
-                    ptx::mbar_arrive_expect_tx(bar(kBarFull + stage), bytes);
+                    ptx::mbar_arrive_expect_tx(bar(kBarFull + stage), stage_bytes);
                     const int row = (int)(it.row0 + t0);
                     for (int kb = 0; kb < nblk; ++kb)
-                        ptx::tma_load_2d(dst + kb * kBoxBytes, &tmap, kb * 64, row, bar(kBarFull + stage));
-                    if (++stage == kStages) { stage = 0; phase ^= 1; }
+                        ptx::tma_load_2d(dst + kb * kBoxBytes, &cmap, kb * 64, row, bar(kBarFull + stage));
+                    if (++stage == (uint32_t)nstages) { stage = 0; phase ^= 1; }
                 }
             }
             if (!ok) *abort_flag = 1;
             // drain: every issued tile has been consumed (or the wait expires)
-            for (int k = 0; k < kStages; ++k) {
-                ptx::mbar_wait(bar(kBarEmpty + stage), phase ^ 1, kErrWaitEmpty);
-                if (++stage == kStages) { stage = 0; phase ^= 1; }
+            for (int k = pre; k < nstages; ++k) {
+                const int s2 = (int)stage + k;
+                ptx::mbar_wait(bar(kBarEmpty + (s2 % nstages)), (s2 >= nstages ? phase ^ 1 : phase) ^ 1, kErrWaitEmpty);
             }
         }
     } else if (warp == 1) {
@@ -191,10 +236,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     const uint32_t sb = jt & 1;
                     const uint32_t use = jt >> 1;
                     if (*abort_flag || !ptx::mbar_wait(bar(kBarFull + stage), phase, kErrWaitFull)) { ok = false; break; }
+                    const uint32_t cst = sbase + kOffStage + stage * stage_bytes;
                     if (role == 0) {
                         if (!ptx::mbar_wait(bar(kBarSEmpty + sb), (use & 1) ^ 1, kErrWaitMma)) { ok = false; break; }
                         ptx::tc_fence_after();
-                        const uint32_t cst = sbase + kOffStage + stage * kCStageBytes;
                         const uint32_t d = tmem + kTmemS + sb * kBN;
 #pragma unroll 4
                         for (int kk = 0; kk < kDK / 16; ++kk) {
@@ -207,13 +252,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         if (!ptx::mbar_wait(bar(kBarPFull + sb), use & 1, kErrWaitPeer) ||
                             !ptx::mbar_wait(bar(kBarCorr + sb), use & 1, kErrWaitMma)) { ok = false; break; }
                         ptx::tc_fence_after();
-                        const uint32_t cst = sbase + kOffStage + stage * kCNStageBytes;
                         const uint32_t msg = sbase + kOffMsg + sb * kMsgStride;
 #pragma unroll
                         for (int nh = 0; nh < 2; ++nh) {
 #pragma unroll
                             for (int kk = 0; kk < kBN / 16; ++kk) {
-                                const uint64_t adesc = ptx::sdesc_sw128(msg + kk * 32, 16, 1024);
+                                const uint64_t adesc = ptx::sdesc_sw64(msg + kk * 32, 16, 512);
                                 const uint64_t bdesc = ptx::sdesc_sw128(cst + nh * 4 * kBoxBytes + kk * 16 * 128, kBoxBytes, 1024);
                                 ptx::mma_ss(tmem + nh * 256, adesc, bdesc, kIdescO, (t0 > 0 || kk > 0) ? 1u : 0u);
                             }
@@ -222,7 +266,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         ptx::mma_commit(bar(kBarEmpty + stage));
                         ptx::mma_commit(bar(kBarMmaDone));
                     }
-                    if (++stage == kStages) { stage = 0; phase ^= 1; }
+                    if (++stage == (uint32_t)nstages) { stage = 0; phase ^= 1; }
                 }
             }
             if (!ok) *abort_flag = 1;
@@ -240,28 +284,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (role == 0) {
             // ------------------------------------------------ S-CTA: softmax
             int prev_b = -1;
+            uint32_t qround = 0;
             const uint32_t peer_pfull0 = ptx::mapa(bar(kBarPFull), 1);
             const uint32_t peer_msg0 = ptx::mapa(sbase + kOffMsg, 1);
             for (int i = cid; ok && i < wl.max_items; i += ncl) {
                 const Item it = get_item(wl, i);
                 if (it.len <= 0) continue;
                 if (it.b != prev_b) {
-                    // Q row h of sequence b -> TMEM columns [0, 288) (zeros past num_heads).
+                    // Q row h (smem, 128-byte swizzled boxes) -> TMEM columns [0, 288).
                     // Every GEMM1 of the previous item has completed: its S tiles were waited on.
-                    const uint4 *src = reinterpret_cast<const uint4 *>(p.q + ((size_t)it.b * p.num_heads + h) * kDK);
-                    const bool live = h < p.num_heads;
+                    bool w = !*abort_flag && ptx::mbar_wait(bar(kBarQFull), qround & 1, kErrWaitFull);
+                    if (!ptx::named_barrier_and(1, 128, w)) { ok = false; break; }
+                    ++qround;
 #pragma unroll 1
                     for (int c = 0; c < kKBlocks; ++c) {
+                        const uint4 *row = reinterpret_cast<const uint4 *>(smem + kOffStage + c * kQBoxBytes + h * 128);
                         uint32_t r[32];
 #pragma unroll
                         for (int v = 0; v < 8; ++v) {
-                            uint4 x = live ? __ldg(src + c * 8 + v) : make_uint4(0, 0, 0, 0);
+                            const uint4 x = row[v ^ (h & 7)];
                             r[4 * v] = x.x; r[4 * v + 1] = x.y; r[4 * v + 2] = x.z; r[4 * v + 3] = x.w;
                         }
                         ptx::tmem_st_x32(trow + kTmemQ + c * 32, r);
                     }
                     ptx::tmem_wait_st();
                     ptx::tc_fence_before();
+                    ptx::mbar_arrive(bar(kBarQFree));
                     ptx::mbar_arrive(bar(kBarQReady));
                     prev_b = it.b;
                 }
@@ -275,18 +323,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     w = __all_sync(0xffffffffu, w);
                     float alpha = 1.f;
                     const bool last = t0 + kBN >= it.len;
-                    uint32_t pk[32];
+                    uint32_t pk[kBN / 2];
                     if (w) {
                         ptx::tc_fence_after();
-                        uint32_t r[64];
-                        {
-                            uint32_t a[32], b[32];
-                            ptx::tmem_ld_x32(trow + kTmemS + sb * kBN, a);
-                            ptx::tmem_ld_x32(trow + kTmemS + sb * kBN + 32, b);
-                            ptx::tmem_wait_ld();
-#pragma unroll
-                            for (int c = 0; c < 32; ++c) { r[c] = a[c]; r[32 + c] = b[c]; }
-                        }
+                        uint32_t r[32];
+                        ptx::tmem_ld_x32(trow + kTmemS + sb * kBN, r);
+                        ptx::tmem_wait_ld();
                         ptx::tc_fence_before();
                         ptx::mbar_arrive(bar(kBarSEmpty + sb));
 
@@ -316,10 +358,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     }
                     if (w) {
                         uint8_t *msg = smem + kOffMsg + sb * kMsgStride;
-                        uint4 *prow = reinterpret_cast<uint4 *>(msg + h * 128);
+                        uint4 *prow = reinterpret_cast<uint4 *>(msg + h * 64);  // SW64: chunk ^= (row >> 1) & 3
 #pragma unroll
-                        for (int c8 = 0; c8 < 8; ++c8)
-                            prow[c8 ^ (h & 7)] = make_uint4(pk[4 * c8], pk[4 * c8 + 1], pk[4 * c8 + 2], pk[4 * c8 + 3]);
+                        for (int c4 = 0; c4 < 4; ++c4)
+                            prow[c4 ^ ((h >> 1) & 3)] = make_uint4(pk[4 * c4], pk[4 * c4 + 1], pk[4 * c4 + 2], pk[4 * c4 + 3]);
                         reinterpret_cast<float *>(msg + kMsgAlpha)[h] = alpha;
                         if (last) {
                             reinterpret_cast<float *>(msg + kMsgL)[h] = l_run;

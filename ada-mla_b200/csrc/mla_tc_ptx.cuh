@@ -303,6 +303,17 @@ __device__ __forceinline__ uint64_t sdesc_sw128(uint32_t addr, uint32_t lbo, uin
     return d;
 }
 
+// Same with 64-byte swizzle (rows of 64 B, 8-row atoms of 512 B).
+__device__ __forceinline__ uint64_t sdesc_sw64(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr >> 4) & 0x3FFF);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)4 << 61;                        // layout: SWIZZLE_64B
+    return d;
+}
+
 // Instruction descriptor: f16 x f16 -> f32, dense, no negate.
 //   a_mn / b_mn: operand is MN-major (1) instead of K-major (0).
 __host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n, int a_mn, int b_mn) {

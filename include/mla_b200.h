@@ -66,6 +66,11 @@ const char *mla_b200_version(void);
  * Retires the reference TODO at mla.py:29. */
 int mla_b200_constant(const char *name);
 
+/* Properties of the current device as the library sees them: SM count and
+ * how many 2-CTA clusters of the tensor-core decode kernel can be resident at
+ * once (one wave of work items).  Either pointer may be NULL. */
+int mla_b200_device_info(int *num_sms, int *decode_clusters);
+
 /* ------------------------------------------------------------------------ */
 /* Planning                                                                  */
 /* ------------------------------------------------------------------------ */
