@@ -12,12 +12,13 @@
 //
 //   S-CTA (cluster rank 0)                O-CTA (cluster rank 1)
 //   Q* [128 x 576] fp16 in TMEM (288 col)   O [128 x 512] fp32 in TMEM (512 col)
-//   TMA: C tile [32 x 576] -> 5-stage ring TMA: C tile [32 x 512] -> 6-stage ring
+//   TMA: C tile [32 x 576] -> 5-stage ring TMA: C tile [32 x 512] -> 5-stage ring
 //   GEMM1 S = Q.C^T  (TS MMA, N=32)         GEMM2 O += P.C_N (SS MMA, 2 x N=256,
 //   online softmax (fp32 m, l; lazy           C_N read MN-major from the tile)
 //     rescale, threshold 2^8)               rescale O rows when the S-CTA
 //   P fp16 + per-row alpha -----DSMEM----->   raised the running max; final
-//     bulk copy (9.5 KB / tile)               O / l and LSE to the workspace
+//     bulk copy (9.5 KB / tile) into a        O / l and LSE to the workspace
+//     6-slot receive ring
 //
 // GEMM1 (576 MACs/token/head) and GEMM2 (512) are balanced across the pair
 // and no tensor work is duplicated.  Tiles are 32 tokens so that each SM keeps
@@ -50,40 +51,46 @@ constexpr int kBoxBytes = kBN * 128;             // one box: 32 rows x 64 fp16 (
 constexpr int kStageS = kKBlocks * kBoxBytes;    // 36864: C tile [32 x 576]
 constexpr int kStageO = kVBlocks * kBoxBytes;    // 32768: C tile [32 x 512]
 constexpr int kStagesS = 5;
-constexpr int kStagesO = 6;
+constexpr int kStagesO = 5;
 constexpr int kQBoxBytes = 128 * 128;            // Q box: 128 rows x 64 fp16
 constexpr int kQBytes = kKBlocks * kQBoxBytes;   // 147456
 static_assert(kQBytes <= kStagesS * kStageS, "Q must fit in the S-CTA ring");
 
+// Message S-CTA -> O-CTA, one per tile.
 constexpr int kMsgP = 128 * kBN * 2;             // P tile, 128 rows x 64 B, SW64 K-major
 constexpr int kMsgAlpha = kMsgP;                 // f32[128] rescale factors
 constexpr int kMsgL = kMsgP + 512;               // f32[128] row sums   (last tile of an item)
 constexpr int kMsgM = kMsgP + 1024;              // f32[128] row maxima (last tile of an item)
 constexpr int kMsgBytes = kMsgP + 1536;          // 9728
 constexpr int kMsgStride = 10 * 1024;
-constexpr int kMsgStages = 2;
+constexpr int kMsgSlots = 6;                     // O-CTA receive ring: the S-CTA runs up to 6 tiles ahead
+constexpr int kStgSlots = 3;                     // S-CTA staging buffers for the outgoing bulk copies
 
 enum BarId {
-    kBarFull = 0,        // [6] TMA tile landed                  (count 1 + tx)
-    kBarEmpty = 6,       // [6] slot consumed by the MMAs        (count 1, commit)
-    kBarSFull = 12,      // [2] S-CTA: S tile in TMEM            (count 1, commit)
-    kBarSEmpty = 14,     // [2] S-CTA: S tile read by softmax    (count 128)
-    kBarQFull = 16,      //     S-CTA: Q block landed in smem    (count 1 + tx)
-    kBarQFree = 17,      //     S-CTA: Q moved to TMEM, smem free (count 128)
-    kBarQReady = 18,     //     S-CTA: Q rows in TMEM            (count 128)
-    kBarPFree = 19,      // [2] GEMM2 done with message stage    (count 1, multicast commit)
-    kBarPFull = 21,      // [2] O-CTA: message landed            (count 1 + tx, from the S-CTA)
-    kBarCorr = 23,       // [2] O-CTA: O ready for next GEMM2    (count 128)
-    kBarMmaDone = 25,    //     O-CTA: GEMM2 of a tile done      (count 1, commit)
-    kBarDrain = 26,      //     MMA issuer's tcgen05 ops retired (teardown)
-    kNumBars = 27
+    kBarFull = 0,        // [5] TMA tile landed                  (count 1 + tx)
+    kBarEmpty = 5,       // [5] slot consumed by the MMAs        (count 1, commit)
+    kBarSFull = 10,      // [2] S-CTA: S tile in TMEM            (count 1, commit)
+    kBarSEmpty = 12,     // [2] S-CTA: S tile read by softmax    (count 128)
+    kBarQFull = 14,      //     S-CTA: Q block landed in smem    (count 1 + tx)
+    kBarQFree = 15,      //     S-CTA: Q moved to TMEM, smem free (count 128)
+    kBarQReady = 16,     //     S-CTA: Q rows in TMEM            (count 128)
+    kBarPFree = 17,      // [6] GEMM2 done with message slot     (count 1, multicast commit)
+    kBarPFull = 23,      // [6] O-CTA: message landed            (count 1 + tx, from the S-CTA)
+    kBarCorr = 29,       // [6] O-CTA: O ready for next GEMM2    (count 128)
+    kBarMmaDone = 35,    //     O-CTA: GEMM2 of a tile done      (count 1, commit)
+    kBarDrain = 36,      //     MMA issuer's tcgen05 ops retired (teardown)
+    kNumBars = 37
 };
 
+// Shared-memory layout (offsets from a 1024-aligned base).  The rings start at
+// 0; each role puts its message buffers behind its own ring; the barriers sit
+// at the same offset in both CTAs (remote arrivals and multicast commits
+// address them by offset).
 constexpr int kOffStage = 0;
-constexpr int kRingBytes = kStagesO * kStageO;                   // 196608 (>= S ring)
-static_assert(kStagesS * kStageS <= kRingBytes, "ring");
-constexpr int kOffMsg = kRingBytes;
-constexpr int kOffBar = kOffMsg + kMsgStages * kMsgStride;       // 217088
+constexpr int kOffStgS = kStagesS * kStageS;                     // 184320: S staging [3]
+constexpr int kOffMsgO = kStagesO * kStageO;                     // 163840: O receive ring [6]
+constexpr int kOffBar = kOffMsgO + kMsgSlots * kMsgStride;       // 225280
+static_assert(kOffStgS + kStgSlots * kMsgStride <= kOffBar, "S-CTA layout");
 constexpr int kOffSlot = kOffBar + kNumBars * 8;
 constexpr int kOffAbort = kOffSlot + 4;
 constexpr int kSmemBytes = kOffAbort + 12 + 1024;                // + 1024 alignment slack
@@ -133,13 +140,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t stage_bytes = role == 0 ? kStageS : kStageO;
 
     if (tid == 0) {
-        for (int i = 0; i < kStagesO; ++i) {
+        for (int i = 0; i < kStagesS; ++i) {
             ptx::mbar_init(bar(kBarFull + i), 1);
             ptx::mbar_init(bar(kBarEmpty + i), 1);
         }
         for (int i = 0; i < 2; ++i) {
             ptx::mbar_init(bar(kBarSFull + i), 1);
             ptx::mbar_init(bar(kBarSEmpty + i), 128);
+        }
+        for (int i = 0; i < kMsgSlots; ++i) {
             ptx::mbar_init(bar(kBarPFree + i), 1);
             ptx::mbar_init(bar(kBarPFull + i), 1);
             ptx::mbar_init(bar(kBarCorr + i), 128);
@@ -249,10 +258,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         ptx::mma_commit(bar(kBarSFull + sb));
                         ptx::mma_commit(bar(kBarEmpty + stage));
                     } else {
-                        if (!ptx::mbar_wait(bar(kBarPFull + sb), use & 1, kErrWaitPeer) ||
-                            !ptx::mbar_wait(bar(kBarCorr + sb), use & 1, kErrWaitMma)) { ok = false; break; }
+                        const uint32_t ms = jt % kMsgSlots, mu = jt / kMsgSlots;
+                        if (!ptx::mbar_wait(bar(kBarPFull + ms), mu & 1, kErrWaitPeer) ||
+                            !ptx::mbar_wait(bar(kBarCorr + ms), mu & 1, kErrWaitMma)) { ok = false; break; }
                         ptx::tc_fence_after();
-                        const uint32_t msg = sbase + kOffMsg + sb * kMsgStride;
+                        const uint32_t msg = sbase + kOffMsgO + ms * kMsgStride;
 #pragma unroll
                         for (int nh = 0; nh < 2; ++nh) {
 #pragma unroll
@@ -262,7 +272,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                 ptx::mma_ss(tmem + nh * 256, adesc, bdesc, kIdescO, (t0 > 0 || kk > 0) ? 1u : 0u);
                             }
                         }
-                        ptx::mma_commit_mc(bar(kBarPFree + sb), 0x3);
+                        ptx::mma_commit_mc(bar(kBarPFree + ms), 0x3);
                         ptx::mma_commit(bar(kBarEmpty + stage));
                         ptx::mma_commit(bar(kBarMmaDone));
                     }
@@ -286,7 +296,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             int prev_b = -1;
             uint32_t qround = 0;
             const uint32_t peer_pfull0 = ptx::mapa(bar(kBarPFull), 1);
-            const uint32_t peer_msg0 = ptx::mapa(sbase + kOffMsg, 1);
+            const uint32_t peer_msg0 = ptx::mapa(sbase + kOffMsgO, 1);
             for (int i = cid; ok && i < wl.max_items; i += ncl) {
                 const Item it = get_item(wl, i);
                 if (it.len <= 0) continue;
@@ -316,6 +326,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 float m_used = -INFINITY, l_run = 0.f;
                 for (int t0 = 0; t0 < it.len; t0 += kBN, ++jt) {
                     const uint32_t sb = jt & 1, use = jt >> 1;
+                    const uint32_t ms = jt % kMsgSlots, mu = jt / kMsgSlots, sg = jt % kStgSlots;
                     // Every decision below is made uniform across the warpgroup by the
                     // bar.red at the end of the tile, so an expired wait can never split
                     // a warp at a .sync.aligned tcgen05 op or strand a named barrier.
@@ -353,11 +364,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                             pk[c >> 1] = pack_half2(p0, p1);
                         }
                         l_run = l_run * alpha + sum;
-                        // message stage sb is free once GEMM2 of tile jt-2 finished
-                        w = ptx::mbar_wait(bar(kBarPFree + sb), (use & 1) ^ 1, kErrWaitPeer);
+                        // the peer's message slot is free once GEMM2 of tile jt-6 finished
+                        w = ptx::mbar_wait(bar(kBarPFree + ms), (mu & 1) ^ 1, kErrWaitPeer);
                     }
                     if (w) {
-                        uint8_t *msg = smem + kOffMsg + sb * kMsgStride;
+                        // staging slot jt%3: its previous bulk copy (tile jt-3) finished
+                        // reading before the previous tile's bar.red (wait_group.read below)
+                        uint8_t *msg = smem + kOffStgS + sg * kMsgStride;
                         uint4 *prow = reinterpret_cast<uint4 *>(msg + h * 64);  // SW64: chunk ^= (row >> 1) & 3
 #pragma unroll
                         for (int c4 = 0; c4 < 4; ++c4)
@@ -369,21 +382,22 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         }
                         ptx::fence_proxy_async_smem();
                     }
+                    if (h == 0) ptx::bulk_wait_group_read<1>();  // copy of tile jt-2 has read its staging
                     if (!ptx::named_barrier_and(1, 128, w)) { ok = false; break; }
                     if (h == 0) {
-                        const uint32_t rbar = peer_pfull0 + 8u * sb;
+                        const uint32_t rbar = peer_pfull0 + 8u * ms;
                         ptx::mbar_remote_arrive_expect_tx(rbar, kMsgBytes);
-                        ptx::bulk_copy_s2cluster(peer_msg0 + sb * kMsgStride, sbase + kOffMsg + sb * kMsgStride,
+                        ptx::bulk_copy_s2cluster(peer_msg0 + ms * kMsgStride, sbase + kOffStgS + sg * kMsgStride,
                                                  kMsgBytes, rbar);
                         ptx::bulk_commit_group();
                     }
                 }
             }
             if (!ok) *abort_flag = 1;
-            // The last two messages were consumed by the peer's GEMM2 (so no
-            // remote arrival is still in flight towards this CTA).
-            for (uint32_t k = (jt >= 2 ? jt - 2 : 0); k < jt; ++k)
-                ptx::mbar_wait(bar(kBarPFree + (k & 1)), (k >> 1) & 1, kErrWaitPeer);
+            // The last messages were consumed by the peer's GEMM2 (so no remote
+            // arrival is still in flight towards this CTA).
+            for (uint32_t k = (jt >= (uint32_t)kMsgSlots ? jt - kMsgSlots : 0); k < jt; ++k)
+                ptx::mbar_wait(bar(kBarPFree + (k % kMsgSlots)), (k / kMsgSlots) & 1, kErrWaitPeer);
             if (h == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
         } else {
             // ------------------------------------------------ O-CTA: correction + epilogue
@@ -391,11 +405,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const Item it = get_item(wl, i);
                 if (it.len <= 0) continue;
                 for (int t0 = 0; t0 < it.len; t0 += kBN, ++jt) {
-                    const uint32_t sb = jt & 1, use = jt >> 1;
+                    const uint32_t ms = jt % kMsgSlots, mu = jt / kMsgSlots;
                     // As in the S-CTA, every branch is warpgroup-uniform (bar.red).
-                    bool w = !*abort_flag && ptx::mbar_wait(bar(kBarPFull + sb), use & 1, kErrWaitPeer);
+                    bool w = !*abort_flag && ptx::mbar_wait(bar(kBarPFull + ms), mu & 1, kErrWaitPeer);
                     if (!ptx::named_barrier_and(2, 128, w)) { ok = false; break; }
-                    const uint8_t *msg = smem + kOffMsg + sb * kMsgStride;
+                    const uint8_t *msg = smem + kOffMsgO + ms * kMsgStride;
                     const float alpha = reinterpret_cast<const float *>(msg + kMsgAlpha)[h];
                     const bool last = t0 + kBN >= it.len;
                     float l_fin = 0.f, m_fin = 0.f;
@@ -419,7 +433,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         ptx::tmem_wait_st();
                     }
                     ptx::tc_fence_before();
-                    ptx::mbar_arrive(bar(kBarCorr + sb));
+                    ptx::mbar_arrive(bar(kBarCorr + ms));
                     if (last) {
                         w = ptx::mbar_wait(bar(kBarMmaDone), jt & 1, kErrWaitMma);
                         if (!ptx::named_barrier_and(2, 128, w)) { ok = false; break; }
