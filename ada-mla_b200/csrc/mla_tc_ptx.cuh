@@ -127,15 +127,21 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 }
 
 // Waits for the phase of `bar` with the given parity to complete.  Bounded:
-// after kWaitLimitNs records `err` and returns false.
+// after kWaitLimitNs records `err` and returns false.  The spin itself is just
+// try_wait; the (slow) global timer is read only every 256 misses.
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int err) {
     if (mbar_try_wait(bar, parity)) return true;
-    const uint64_t t0 = globaltimer_ns();
-    while (true) {
+    uint64_t t0 = 0;
+    for (uint32_t n = 1;; ++n) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (globaltimer_ns() - t0 > kWaitLimitNs) {
-            set_device_error(err);
-            return false;
+        if ((n & 255) == 0) {
+            const uint64_t t = globaltimer_ns();
+            if (t0 == 0) {
+                t0 = t;
+            } else if (t - t0 > kWaitLimitNs) {
+                set_device_error(err);
+                return false;
+            }
         }
     }
 }
