@@ -232,8 +232,9 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     }
     if (wl.max_items > 0) {
         if (std::is_same<T, __half>::value && num_heads <= 128) {
-            CUtensorMap cmap, qmap;
-            st = make_tmap_576(&cmap, cache, total_tokens, tc::kBN);
+            CUtensorMap cmap_s, cmap_o, qmap;
+            st = make_tmap_576(&cmap_s, cache, total_tokens, tc::kTS);
+            if (st == MLA_B200_OK) st = make_tmap_576(&cmap_o, cache, total_tokens, tc::kTO);
             if (st == MLA_B200_OK) st = make_tmap_576(&qmap, q, (long long)batch * num_heads, 128);
             if (st != MLA_B200_OK) return st;
             tc::TcParams tp;
@@ -243,7 +244,7 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
             tp.part_o = L.part_o;
             tp.part_lse = L.part_lse;
             const int clusters = std::min(info.tc_clusters, wl.max_items);
-            tc::tc_decode_kernel<<<2 * clusters, tc::kThreads, tc::kSmemBytes, stream>>>(cmap, qmap, tp);
+            tc::tc_decode_kernel<<<2 * clusters, tc::kThreads, tc::kSmemBytes, stream>>>(cmap_s, cmap_o, qmap, tp);
         } else {
             dim3 grid(wl.max_items, (unsigned)cdiv(num_heads, kSimtHeads));
             simt_partial_kernel<T><<<grid, 256, kSimtSmem, stream>>>(

@@ -12,7 +12,7 @@ namespace mla {
 
 constexpr int kDK = MLA_B200_HEAD_DIM_K;  // 576: latent + rope
 constexpr int kDV = MLA_B200_HEAD_DIM_V;  // 512: latent (value) columns
-constexpr int kTile = 64;                 // tokens per pipeline tile; chunks are multiples
+constexpr int kTile = 96;                 // tokens per tensor-core S tile; planned chunks are multiples
 constexpr float kLog2e = 1.4426950408889634f;
 constexpr float kLn2 = 0.6931471805599453f;
 
@@ -35,7 +35,7 @@ struct WorkList {
     const int *item_off;
     int batch;
     int seq_len;   // dense only
-    int chunk;     // rows per item (multiple of kTile)
+    int chunk;     // rows per item (a multiple of kTile when planned)
     int cps;       // dense: chunks per sequence
     int max_items; // launch bound
 };

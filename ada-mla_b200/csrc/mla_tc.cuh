@@ -10,20 +10,23 @@
 // all 512 TMEM columns of an SM, leaving no room for S = Q.C^T.  So each item
 // runs on a 2-CTA cluster (two SMs):
 //
-//   S-CTA (cluster rank 0)                O-CTA (cluster rank 1)
-//   Q* [128 x 576] fp16 in TMEM (288 col)   O [128 x 512] fp32 in TMEM (512 col)
-//   TMA: C tile [32 x 576] -> 5-stage ring TMA: C tile [32 x 512] -> 5-stage ring
-//   GEMM1 S = Q.C^T  (TS MMA, N=32)         GEMM2 O += P.C_N (SS MMA, 2 x N=256,
-//   online softmax (fp32 m, l; lazy           C_N read MN-major from the tile)
-//     rescale, threshold 2^8)               rescale O rows when the S-CTA
-//   P fp16 + per-row alpha -----DSMEM----->   raised the running max; final
-//     bulk copy (9.5 KB / tile) into a        O / l and LSE to the workspace
-//     6-slot receive ring
+//   S-CTA (cluster rank 0)                 O-CTA (cluster rank 1)
+//   Q* [128 x 576] fp16 in TMEM (288 col)    O [128 x 512] fp32 in TMEM (512 col)
+//   TMA: C in K-blocks [96 tok x 64 col]     TMA: C tile [32 tok x 512] -> 4-slot ring
+//     -> 13-slot ring (12 KB slots)          GEMM2 O += P.C_N (SS MMA, N=256,
+//   GEMM1 S = Q.C^T (TS MMA, N=96)             C_N read MN-major from the tile)
+//     into one of two S buffers (2 x 96 col)  rescale O rows when the S-CTA
+//   online softmax (fp32 m, l; lazy             raised the running max; final
+//     rescale, threshold 2^8)                   O / l and LSE to the workspace
+//   P fp16 + per-row alpha ---DSMEM bulk copy (26 KB / 96 tokens)---> 3-slot ring
 //
+// Tile sizes come from the tcgen05 MMA cost: an M=128 kind::f16 MMA takes at
+// least ~45 cycles, so N=32 runs at a third of peak while N >= 96 runs at the
+// full 4096 MAC/clk.  GEMM1 therefore uses 96-token tiles (its 576-deep K is
+// streamed through the ring one 64-column block at a time), GEMM2 uses N=256.
 // GEMM1 (576 MACs/token/head) and GEMM2 (512) are balanced across the pair
-// and no tensor work is duplicated.  Tiles are 32 tokens so that each SM keeps
-// four tiles (~140 KB) of cache reads in flight, which HBM latency needs.  The
-// pair reads the same rows; the second read of each byte hits L2.
+// and no tensor work is duplicated.  The pair reads the same rows; the second
+// read of each byte hits L2.
 //
 // Q reaches TMEM through shared memory: at the first item of a sequence the
 // S-CTA's producer waits for its ring to drain, TMA-loads the 144 KB Q block
@@ -44,53 +47,58 @@
 namespace mla {
 namespace tc {
 
-constexpr int kBN = 32;                          // tokens per tile
-constexpr int kKBlocks = kDK / 64;               // 9 column blocks of 64 (TMA boxes)
+constexpr int kTS = 96;                          // tokens per S tile (GEMM1 N)
+constexpr int kTO = 32;                          // tokens per O tile (C_N ring granularity)
+constexpr int kOPerS = kTS / kTO;                // 3
+constexpr int kKBlocks = kDK / 64;               // 9 column blocks of 64
 constexpr int kVBlocks = kDV / 64;               // 8
-constexpr int kBoxBytes = kBN * 128;             // one box: 32 rows x 64 fp16 (4 KB)
-constexpr int kStageS = kKBlocks * kBoxBytes;    // 36864: C tile [32 x 576]
-constexpr int kStageO = kVBlocks * kBoxBytes;    // 32768: C tile [32 x 512]
-constexpr int kStagesS = 5;
-constexpr int kStagesO = 5;
+constexpr int kSlotS = kTS * 128;                // 12288: one K-block [96 tok x 64 col]
+constexpr int kSlotsS = 13;
+constexpr int kBoxO = kTO * 128;                 // 4096: [32 tok x 64 col]
+constexpr int kSlotO = kVBlocks * kBoxO;         // 32768: C tile [32 x 512]
+constexpr int kSlotsO = 4;
 constexpr int kQBoxBytes = 128 * 128;            // Q box: 128 rows x 64 fp16
 constexpr int kQBytes = kKBlocks * kQBoxBytes;   // 147456
-static_assert(kQBytes <= kStagesS * kStageS, "Q must fit in the S-CTA ring");
+static_assert(kQBytes <= kSlotsS * kSlotS, "Q must fit in the S-CTA ring");
 
-// Message S-CTA -> O-CTA, one per tile.
-constexpr int kMsgP = 128 * kBN * 2;             // P tile, 128 rows x 64 B, SW64 K-major
-constexpr int kMsgAlpha = kMsgP;                 // f32[128] rescale factors
-constexpr int kMsgL = kMsgP + 512;               // f32[128] row sums   (last tile of an item)
-constexpr int kMsgM = kMsgP + 1024;              // f32[128] row maxima (last tile of an item)
-constexpr int kMsgBytes = kMsgP + 1536;          // 9728
-constexpr int kMsgStride = 10 * 1024;
-constexpr int kMsgSlots = 6;                     // O-CTA receive ring: the S-CTA runs up to 6 tiles ahead
-constexpr int kStgSlots = 3;                     // S-CTA staging buffers for the outgoing bulk copies
+// Message S-CTA -> O-CTA, one per S tile: P as three SW64 K-major sub-tiles of
+// [128 rows x 32 tokens] (8 KB each), then per-row alpha, l, m.
+constexpr int kSubP = 128 * kTO * 2;             // 8192
+constexpr int kMsgP = kOPerS * kSubP;            // 24576
+constexpr int kMsgAlpha = kMsgP;
+constexpr int kMsgL = kMsgP + 512;
+constexpr int kMsgM = kMsgP + 1024;
+constexpr int kMsgBytes = kMsgP + 1536;          // 26112
+constexpr int kMsgStride = 26 * 1024;
+constexpr int kMsgSlots = 3;                     // O-CTA receive ring
+constexpr int kStgSlots = 2;                     // S-CTA staging for outgoing copies
 
+constexpr int kRingSlots = kSlotsS > kSlotsO ? kSlotsS : kSlotsO;
 enum BarId {
-    kBarFull = 0,        // [5] TMA tile landed                  (count 1 + tx)
-    kBarEmpty = 5,       // [5] slot consumed by the MMAs        (count 1, commit)
-    kBarSFull = 10,      // [2] S-CTA: S tile in TMEM            (count 1, commit)
-    kBarSEmpty = 12,     // [2] S-CTA: S tile read by softmax    (count 128)
-    kBarQFull = 14,      //     S-CTA: Q block landed in smem    (count 1 + tx)
-    kBarQFree = 15,      //     S-CTA: Q moved to TMEM, smem free (count 128)
-    kBarQReady = 16,     //     S-CTA: Q rows in TMEM            (count 128)
-    kBarPFree = 17,      // [6] GEMM2 done with message slot     (count 1, multicast commit)
-    kBarPFull = 23,      // [6] O-CTA: message landed            (count 1 + tx, from the S-CTA)
-    kBarCorr = 29,       // [6] O-CTA: O ready for next GEMM2    (count 128)
-    kBarMmaDone = 35,    //     O-CTA: GEMM2 of a tile done      (count 1, commit)
-    kBarDrain = 36,      //     MMA issuer's tcgen05 ops retired (teardown)
-    kNumBars = 37
+    kBarFull = 0,                      // [13] ring slot landed            (count 1 + tx)
+    kBarEmpty = kRingSlots,            // [13] ring slot consumed          (count 1, commit)
+    kBarSFull = 2 * kRingSlots,        // [2] S-CTA: S tile in TMEM        (count 1, commit)
+    kBarSEmpty = kBarSFull + 2,        // [2] S-CTA: S tile read           (count 128)
+    kBarQFull = kBarSEmpty + 2,        //     S-CTA: Q block in smem       (count 1 + tx)
+    kBarQFree = kBarQFull + 1,         //     S-CTA: Q moved to TMEM       (count 128)
+    kBarQReady = kBarQFree + 1,        //     S-CTA: Q rows in TMEM        (count 128)
+    kBarPFree = kBarQReady + 1,        // [3] GEMM2 done with message slot (count 1, multicast commit)
+    kBarPFull = kBarPFree + kMsgSlots, // [3] O-CTA: message landed        (count 1 + tx, from the S-CTA)
+    kBarCorr = kBarPFull + kMsgSlots,  // [3] O-CTA: O ready for GEMM2     (count 128)
+    kBarMmaDone = kBarCorr + kMsgSlots,//     O-CTA: GEMM2 of an S tile done (count 1, commit)
+    kBarDrain = kBarMmaDone + 1,       //     MMA issuer's ops retired (teardown)
+    kNumBars = kBarDrain + 1
 };
 
-// Shared-memory layout (offsets from a 1024-aligned base).  The rings start at
-// 0; each role puts its message buffers behind its own ring; the barriers sit
-// at the same offset in both CTAs (remote arrivals and multicast commits
-// address them by offset).
-constexpr int kOffStage = 0;
-constexpr int kOffStgS = kStagesS * kStageS;                     // 184320: S staging [3]
-constexpr int kOffMsgO = kStagesO * kStageO;                     // 163840: O receive ring [6]
-constexpr int kOffBar = kOffMsgO + kMsgSlots * kMsgStride;       // 225280
-static_assert(kOffStgS + kStgSlots * kMsgStride <= kOffBar, "S-CTA layout");
+// Shared-memory layout (offsets from a 1024-aligned base).  Each role has its
+// own ring and message buffers; the barriers sit at the same offset in both
+// CTAs (remote arrivals and multicast commits address them by offset).
+constexpr int kOffRing = 0;
+constexpr int kOffStgS = kSlotsS * kSlotS;                       // 159744: S staging [2]
+constexpr int kOffMsgO = kSlotsO * kSlotO;                       // 131072: O receive ring [3]
+constexpr int kEndS = kOffStgS + kStgSlots * kMsgStride;         // 212992
+constexpr int kEndO = kOffMsgO + kMsgSlots * kMsgStride;         // 210944
+constexpr int kOffBar = kEndS > kEndO ? kEndS : kEndO;
 constexpr int kOffSlot = kOffBar + kNumBars * 8;
 constexpr int kOffAbort = kOffSlot + 4;
 constexpr int kSmemBytes = kOffAbort + 12 + 1024;                // + 1024 alignment slack
@@ -98,10 +106,11 @@ constexpr int kSmemBytes = kOffAbort + 12 + 1024;                // + 1024 align
 constexpr int kThreads = 256;
 constexpr uint32_t kTmemCols = 512;
 constexpr uint32_t kTmemQ = 0;     // S-CTA: Q, 288 columns (2 fp16 per column)
-constexpr uint32_t kTmemS = 288;   // S-CTA: two S buffers of kBN columns
+constexpr uint32_t kTmemS = 288;   // S-CTA: two S buffers of kTS columns
+static_assert(kTmemS + 2 * kTS <= kTmemCols, "TMEM budget");
 constexpr float kRescaleLog2 = 8.0f;
 
-constexpr uint32_t kIdescS = ptx::idesc_f16_f32(128, kBN, 0, 0);   // M=128 heads, N=32 tokens
+constexpr uint32_t kIdescS = ptx::idesc_f16_f32(128, kTS, 0, 0);   // M=128 heads, N=96 tokens
 constexpr uint32_t kIdescO = ptx::idesc_f16_f32(128, 256, 0, 1);   // M=128 heads, N=256 dims, B MN-major
 
 struct TcParams {
@@ -120,9 +129,19 @@ __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
     return *reinterpret_cast<uint32_t *>(&h);
 }
 
-// cmap: cache [rows, 576] fp16, box 64 x kBN.   qmap: query [B * n_h, 576], box 64 x 128.
+// Ring position: slot index and phase bit of a producer/consumer cursor.
+struct Ring {
+    uint32_t slot = 0, phase = 0;
+    __device__ __forceinline__ void next(int n) {
+        if (++slot == (uint32_t)n) { slot = 0; phase ^= 1; }
+    }
+};
+
+// cmap_s: cache [rows, 576], box 64 x 96.  cmap_o: same cache, box 64 x 32.
+// qmap: query [B * n_h, 576], box 64 x 128.  All 128-byte swizzled.
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
-    tc_decode_kernel(const __grid_constant__ CUtensorMap cmap,
+    tc_decode_kernel(const __grid_constant__ CUtensorMap cmap_s,
+                     const __grid_constant__ CUtensorMap cmap_o,
                      const __grid_constant__ CUtensorMap qmap, const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -136,11 +155,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t role = ptx::cluster_ctarank();  // 0 = S-CTA, 1 = O-CTA
     const int cid = (int)ptx::cluster_id_x();
     const int ncl = (int)ptx::nclusters_x();
-    const int nstages = role == 0 ? kStagesS : kStagesO;
-    const uint32_t stage_bytes = role == 0 ? kStageS : kStageO;
 
     if (tid == 0) {
-        for (int i = 0; i < kStagesS; ++i) {
+        for (int i = 0; i < kRingSlots; ++i) {
             ptx::mbar_init(bar(kBarFull + i), 1);
             ptx::mbar_init(bar(kBarEmpty + i), 1);
         }
@@ -162,8 +179,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         ptx::fence_mbarrier_init_cluster();
     }
     if (warp == 0 && lane == 0) {
-        ptx::tma_prefetch_desc(&cmap);
-        ptx::tma_prefetch_desc(&qmap);
+        ptx::tma_prefetch_desc(role == 0 ? &cmap_s : &cmap_o);
+        if (role == 0) ptx::tma_prefetch_desc(&qmap);
     }
     if (warp == 2) {
         ptx::tmem_alloc(sbase + kOffSlot, kTmemCols);
@@ -179,58 +196,71 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
-            const int nblk = role == 0 ? kKBlocks : kVBlocks;
-            uint32_t stage = 0, phase = 0, qround = 0;
+            const int nslots = role == 0 ? kSlotsS : kSlotsO;
+            Ring rg;
             int pre = 0;  // upcoming ring slots already known to be free
+            uint32_t qround = 0;
             int prev_b = -1;
             bool ok = true;
+            auto acquire = [&]() -> bool {
+                if (pre > 0) { --pre; return true; }
+                return !*abort_flag && ptx::mbar_wait(bar(kBarEmpty + rg.slot), rg.phase ^ 1, kErrWaitEmpty);
+            };
             for (int i = cid; ok && i < wl.max_items; i += ncl) {
                 const Item it = get_item(wl, i);
                 if (it.len <= 0) continue;
                 if (role == 0 && it.b != prev_b) {
                     // Drain the ring (every slot consumed), then borrow it for Q.
-                    for (int k = pre; k < nstages; ++k) {
-                        const int s2 = (int)stage + k;
-                        const uint32_t slot = s2 % nstages;
-                        const uint32_t ph = s2 >= nstages ? phase ^ 1 : phase;
-                        if (*abort_flag || !ptx::mbar_wait(bar(kBarEmpty + slot), ph ^ 1, kErrWaitEmpty)) { ok = false; break; }
+                    Ring r2 = rg;
+                    for (int k = 0; k < nslots; ++k, r2.next(nslots)) {
+                        if (k < pre) continue;
+                        if (*abort_flag || !ptx::mbar_wait(bar(kBarEmpty + r2.slot), r2.phase ^ 1, kErrWaitEmpty)) { ok = false; break; }
                     }
                     if (!ok) break;
-                    pre = nstages;
+                    pre = nslots;
                     ptx::mbar_arrive_expect_tx(bar(kBarQFull), kQBytes);
                     const int qrow = it.b * p.num_heads;
                     for (int kb = 0; kb < kKBlocks; ++kb)
-                        ptx::tma_load_2d(sbase + kOffStage + kb * kQBoxBytes, &qmap, kb * 64, qrow, bar(kBarQFull));
+                        ptx::tma_load_2d(sbase + kOffRing + kb * kQBoxBytes, &qmap, kb * 64, qrow, bar(kBarQFull));
                     if (!ptx::mbar_wait(bar(kBarQFree), qround & 1, kErrWaitPeer)) { ok = false; break; }
                     ++qround;
                     prev_b = it.b;
                 }
-                for (int t0 = 0; t0 < it.len; t0 += kBN) {
-                    if (pre > 0) {
-                        --pre;
-                    } else if (*abort_flag || !ptx::mbar_wait(bar(kBarEmpty + stage), phase ^ 1, kErrWaitEmpty)) {
-                        ok = false;
-                        break;
-                    }
-                    const uint32_t dst = sbase + kOffStage + stage * stage_bytes;
-                    ptx::mbar_arrive_expect_tx(bar(kBarFull + stage), stage_bytes);
+                for (int t0 = 0; ok && t0 < it.len; t0 += kTS) {
                     const int row = (int)(it.row0 + t0);
-                    for (int kb = 0; kb < nblk; ++kb)
-                        ptx::tma_load_2d(dst + kb * kBoxBytes, &cmap, kb * 64, row, bar(kBarFull + stage));
-                    if (++stage == (uint32_t)nstages) { stage = 0; phase ^= 1; }
+                    if (role == 0) {
+                        for (int kb = 0; kb < kKBlocks; ++kb) {
+                            if (!acquire()) { ok = false; break; }
+                            ptx::mbar_arrive_expect_tx(bar(kBarFull + rg.slot), kSlotS);
+                            ptx::tma_load_2d(sbase + kOffRing + rg.slot * kSlotS, &cmap_s, kb * 64, row, bar(kBarFull + rg.slot));
+                            rg.next(nslots);
+                        }
+                    } else {
+                        const int nct = (min(kTS, it.len - t0) + kTO - 1) / kTO;
+                        for (int ct = 0; ct < nct; ++ct) {
+                            if (!acquire()) { ok = false; break; }
+                            const uint32_t dst = sbase + kOffRing + rg.slot * kSlotO;
+                            ptx::mbar_arrive_expect_tx(bar(kBarFull + rg.slot), kSlotO);
+                            for (int kb = 0; kb < kVBlocks; ++kb)
+                                ptx::tma_load_2d(dst + kb * kBoxO, &cmap_o, kb * 64, row + ct * kTO, bar(kBarFull + rg.slot));
+                            rg.next(nslots);
+                        }
+                    }
                 }
             }
             if (!ok) *abort_flag = 1;
-            // drain: every issued tile has been consumed (or the wait expires)
-            for (int k = pre; k < nstages; ++k) {
-                const int s2 = (int)stage + k;
-                ptx::mbar_wait(bar(kBarEmpty + (s2 % nstages)), (s2 >= nstages ? phase ^ 1 : phase) ^ 1, kErrWaitEmpty);
+            // drain: every issued load has been consumed (or the wait expires)
+            for (int k = 0; k < nslots; ++k, rg.next(nslots)) {
+                if (k < pre) continue;
+                ptx::mbar_wait(bar(kBarEmpty + rg.slot), rg.phase ^ 1, kErrWaitEmpty);
             }
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
         if (lane == 0) {
-            uint32_t stage = 0, phase = 0, jt = 0, qphase = 0;
+            const int nslots = role == 0 ? kSlotsS : kSlotsO;
+            Ring rg;
+            uint32_t jt = 0, qphase = 0;
             int prev_b = -1;
             bool ok = true;
             for (int i = cid; ok && i < wl.max_items; i += ncl) {
@@ -241,42 +271,52 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     qphase ^= 1;
                     prev_b = it.b;
                 }
-                for (int t0 = 0; t0 < it.len; t0 += kBN, ++jt) {
-                    const uint32_t sb = jt & 1;
-                    const uint32_t use = jt >> 1;
-                    if (*abort_flag || !ptx::mbar_wait(bar(kBarFull + stage), phase, kErrWaitFull)) { ok = false; break; }
-                    const uint32_t cst = sbase + kOffStage + stage * stage_bytes;
+                for (int t0 = 0; ok && t0 < it.len; t0 += kTS, ++jt) {
                     if (role == 0) {
-                        if (!ptx::mbar_wait(bar(kBarSEmpty + sb), (use & 1) ^ 1, kErrWaitMma)) { ok = false; break; }
-                        ptx::tc_fence_after();
-                        const uint32_t d = tmem + kTmemS + sb * kBN;
-#pragma unroll 4
-                        for (int kk = 0; kk < kDK / 16; ++kk) {
-                            const uint64_t bdesc = ptx::sdesc_sw128(cst + (kk >> 2) * kBoxBytes + (kk & 3) * 32, 16, 1024);
-                            ptx::mma_ts(d, tmem + kTmemQ + kk * 8, bdesc, kIdescS, kk > 0);
+                        const uint32_t sb = jt & 1, use = jt >> 1;
+                        if (*abort_flag || !ptx::mbar_wait(bar(kBarSEmpty + sb), (use & 1) ^ 1, kErrWaitMma)) { ok = false; break; }
+                        const uint32_t d = tmem + kTmemS + sb * kTS;
+                        for (int kb = 0; kb < kKBlocks; ++kb) {
+                            if (!ptx::mbar_wait(bar(kBarFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
+                            ptx::tc_fence_after();
+                            const uint32_t slot = sbase + kOffRing + rg.slot * kSlotS;
+#pragma unroll
+                            for (int k4 = 0; k4 < 4; ++k4) {
+                                const int kk = kb * 4 + k4;
+                                ptx::mma_ts(d, tmem + kTmemQ + kk * 8, ptx::sdesc_sw128(slot + k4 * 32, 16, 1024),
+                                            kIdescS, kk > 0);
+                            }
+                            ptx::mma_commit(bar(kBarEmpty + rg.slot));
+                            rg.next(nslots);
                         }
+                        if (!ok) break;
                         ptx::mma_commit(bar(kBarSFull + sb));
-                        ptx::mma_commit(bar(kBarEmpty + stage));
                     } else {
                         const uint32_t ms = jt % kMsgSlots, mu = jt / kMsgSlots;
-                        if (!ptx::mbar_wait(bar(kBarPFull + ms), mu & 1, kErrWaitPeer) ||
+                        if (*abort_flag || !ptx::mbar_wait(bar(kBarPFull + ms), mu & 1, kErrWaitPeer) ||
                             !ptx::mbar_wait(bar(kBarCorr + ms), mu & 1, kErrWaitMma)) { ok = false; break; }
-                        ptx::tc_fence_after();
                         const uint32_t msg = sbase + kOffMsgO + ms * kMsgStride;
+                        const int nct = (min(kTS, it.len - t0) + kTO - 1) / kTO;
+                        for (int ct = 0; ct < nct; ++ct) {
+                            if (!ptx::mbar_wait(bar(kBarFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
+                            ptx::tc_fence_after();
+                            const uint32_t cst = sbase + kOffRing + rg.slot * kSlotO;
 #pragma unroll
-                        for (int nh = 0; nh < 2; ++nh) {
+                            for (int kk = 0; kk < kTO / 16; ++kk) {
+                                const uint64_t adesc = ptx::sdesc_sw64(msg + ct * kSubP + kk * 32, 16, 512);
 #pragma unroll
-                            for (int kk = 0; kk < kBN / 16; ++kk) {
-                                const uint64_t adesc = ptx::sdesc_sw64(msg + kk * 32, 16, 512);
-                                const uint64_t bdesc = ptx::sdesc_sw128(cst + nh * 4 * kBoxBytes + kk * 16 * 128, kBoxBytes, 1024);
-                                ptx::mma_ss(tmem + nh * 256, adesc, bdesc, kIdescO, (t0 > 0 || kk > 0) ? 1u : 0u);
+                                for (int nh = 0; nh < 2; ++nh) {
+                                    const uint64_t bdesc = ptx::sdesc_sw128(cst + nh * 4 * kBoxO + kk * 16 * 128, kBoxO, 1024);
+                                    ptx::mma_ss(tmem + nh * 256, adesc, bdesc, kIdescO, (t0 > 0 || ct > 0 || kk > 0) ? 1u : 0u);
+                                }
                             }
+                            ptx::mma_commit(bar(kBarEmpty + rg.slot));
+                            rg.next(nslots);
                         }
+                        if (!ok) break;
                         ptx::mma_commit_mc(bar(kBarPFree + ms), 0x3);
-                        ptx::mma_commit(bar(kBarEmpty + stage));
                         ptx::mma_commit(bar(kBarMmaDone));
                     }
-                    if (++stage == (uint32_t)nstages) { stage = 0; phase ^= 1; }
                 }
             }
             if (!ok) *abort_flag = 1;
@@ -308,7 +348,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     ++qround;
 #pragma unroll 1
                     for (int c = 0; c < kKBlocks; ++c) {
-                        const uint4 *row = reinterpret_cast<const uint4 *>(smem + kOffStage + c * kQBoxBytes + h * 128);
+                        const uint4 *row = reinterpret_cast<const uint4 *>(smem + kOffRing + c * kQBoxBytes + h * 128);
                         uint32_t r[32];
 #pragma unroll
                         for (int v = 0; v < 8; ++v) {
@@ -324,7 +364,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     prev_b = it.b;
                 }
                 float m_used = -INFINITY, l_run = 0.f;
-                for (int t0 = 0; t0 < it.len; t0 += kBN, ++jt) {
+                for (int t0 = 0; t0 < it.len; t0 += kTS, ++jt) {
                     const uint32_t sb = jt & 1, use = jt >> 1;
                     const uint32_t ms = jt % kMsgSlots, mu = jt / kMsgSlots, sg = jt % kStgSlots;
                     // Every decision below is made uniform across the warpgroup by the
@@ -333,20 +373,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     bool w = !*abort_flag && ptx::mbar_wait(bar(kBarSFull + sb), use & 1, kErrWaitMma);
                     w = __all_sync(0xffffffffu, w);
                     float alpha = 1.f;
-                    const bool last = t0 + kBN >= it.len;
-                    uint32_t pk[kBN / 2];
+                    const bool last = t0 + kTS >= it.len;
+                    uint32_t pk[kTS / 2];
                     if (w) {
                         ptx::tc_fence_after();
-                        uint32_t r[32];
-                        ptx::tmem_ld_x32(trow + kTmemS + sb * kBN, r);
-                        ptx::tmem_wait_ld();
+                        uint32_t r[kTS];
+                        {
+                            uint32_t a[32];
+#pragma unroll
+                            for (int q = 0; q < kTS / 32; ++q) {
+                                ptx::tmem_ld_x32(trow + kTmemS + sb * kTS + q * 32, a);
+                                ptx::tmem_wait_ld();
+#pragma unroll
+                                for (int c = 0; c < 32; ++c) r[q * 32 + c] = a[c];
+                            }
+                        }
                         ptx::tc_fence_before();
                         ptx::mbar_arrive(bar(kBarSEmpty + sb));
 
-                        const int valid = min(kBN, it.len - t0);
+                        const int valid = min(kTS, it.len - t0);
                         float mx = -INFINITY;
 #pragma unroll
-                        for (int c = 0; c < kBN; ++c) {
+                        for (int c = 0; c < kTS; ++c) {
                             const float x = c < valid ? f32_of(r[c]) * p.scale_log2 : -INFINITY;
                             r[c] = u32_of(x);
                             mx = fmaxf(mx, x);
@@ -357,24 +405,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         }
                         float sum = 0.f;
 #pragma unroll
-                        for (int c = 0; c < kBN; c += 2) {
+                        for (int c = 0; c < kTS; c += 2) {
                             const float p0 = ptx::ex2(f32_of(r[c]) - m_used);
                             const float p1 = ptx::ex2(f32_of(r[c + 1]) - m_used);
                             sum += p0 + p1;
                             pk[c >> 1] = pack_half2(p0, p1);
                         }
                         l_run = l_run * alpha + sum;
-                        // the peer's message slot is free once GEMM2 of tile jt-6 finished
+                        // the peer's message slot is free once GEMM2 of S tile jt-3 finished
                         w = ptx::mbar_wait(bar(kBarPFree + ms), (mu & 1) ^ 1, kErrWaitPeer);
                     }
                     if (w) {
-                        // staging slot jt%3: its previous bulk copy (tile jt-3) finished
-                        // reading before the previous tile's bar.red (wait_group.read below)
+                        // staging slot sg: its previous copy (tile jt-2) finished reading
+                        // before the previous tile's bar.red (wait_group.read below)
                         uint8_t *msg = smem + kOffStgS + sg * kMsgStride;
-                        uint4 *prow = reinterpret_cast<uint4 *>(msg + h * 64);  // SW64: chunk ^= (row >> 1) & 3
 #pragma unroll
-                        for (int c4 = 0; c4 < 4; ++c4)
-                            prow[c4 ^ ((h >> 1) & 3)] = make_uint4(pk[4 * c4], pk[4 * c4 + 1], pk[4 * c4 + 2], pk[4 * c4 + 3]);
+                        for (int st = 0; st < kOPerS; ++st) {
+                            uint4 *prow = reinterpret_cast<uint4 *>(msg + st * kSubP + h * 64);  // SW64
+#pragma unroll
+                            for (int c4 = 0; c4 < 4; ++c4) {
+                                const int q = st * 16 + c4 * 4;
+                                prow[c4 ^ ((h >> 1) & 3)] = make_uint4(pk[q], pk[q + 1], pk[q + 2], pk[q + 3]);
+                            }
+                        }
                         reinterpret_cast<float *>(msg + kMsgAlpha)[h] = alpha;
                         if (last) {
                             reinterpret_cast<float *>(msg + kMsgL)[h] = l_run;
@@ -382,7 +435,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         }
                         ptx::fence_proxy_async_smem();
                     }
-                    if (h == 0) ptx::bulk_wait_group_read<1>();  // copy of tile jt-2 has read its staging
+                    if (h == 0) ptx::bulk_wait_group_read<0>();  // previous copy has read its staging
                     if (!ptx::named_barrier_and(1, 128, w)) { ok = false; break; }
                     if (h == 0) {
                         const uint32_t rbar = peer_pfull0 + 8u * ms;
@@ -404,14 +457,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             for (int i = cid; ok && i < wl.max_items; i += ncl) {
                 const Item it = get_item(wl, i);
                 if (it.len <= 0) continue;
-                for (int t0 = 0; t0 < it.len; t0 += kBN, ++jt) {
+                for (int t0 = 0; t0 < it.len; t0 += kTS, ++jt) {
                     const uint32_t ms = jt % kMsgSlots, mu = jt / kMsgSlots;
                     // As in the S-CTA, every branch is warpgroup-uniform (bar.red).
                     bool w = !*abort_flag && ptx::mbar_wait(bar(kBarPFull + ms), mu & 1, kErrWaitPeer);
                     if (!ptx::named_barrier_and(2, 128, w)) { ok = false; break; }
                     const uint8_t *msg = smem + kOffMsgO + ms * kMsgStride;
                     const float alpha = reinterpret_cast<const float *>(msg + kMsgAlpha)[h];
-                    const bool last = t0 + kBN >= it.len;
+                    const bool last = t0 + kTS >= it.len;
                     float l_fin = 0.f, m_fin = 0.f;
                     if (last) {
                         l_fin = reinterpret_cast<const float *>(msg + kMsgL)[h];

@@ -80,7 +80,7 @@ int mla_b200_device_info(int *num_sms, int *decode_clusters);
  * cache rows in all and `num_heads` heads, chooses how many tokens one split
  * (one work item) covers so that the items fill `num_sms` SMs (0 = the current
  * device's count) while keeping the split-partial traffic small.  Writes the
- * chunk length (a multiple of 64 tokens) to *chunk_tokens and, for a single
+ * chunk length (a multiple of 96 tokens, the kernel's tile) to *chunk_tokens and, for a single
  * sequence, the resulting split count to *num_splits (either may be NULL). */
 int mla_b200_plan(int batch, int num_heads, long long total_tokens, int max_seq_len,
                   int num_sms, int *chunk_tokens, int *num_splits);

@@ -94,13 +94,13 @@ def test_plan_properties(batch, total, maxlen):
     chunk, splits = capi.plan(batch, 128, total, maxlen, 148)
     assert chunk >= 1
     if maxlen > 0:
-        assert chunk % 64 == 0 or chunk >= maxlen
-        assert chunk <= -(-maxlen // 64) * 64
+        assert chunk % 96 == 0 or chunk >= maxlen
+        assert chunk <= -(-maxlen // 96) * 96
         assert splits == -(-maxlen // chunk)
     if total:
         # a chunk is never shorter than an even share of the tokens over the 74 SM pairs
         # (unless the chunk is already a whole sequence)
-        assert -(-total // chunk) <= 74 or chunk == -(-maxlen // 64) * 64
+        assert -(-total // chunk) <= 74 or chunk == -(-maxlen // 96) * 96
     if maxlen and total == batch * maxlen:
         items = batch * -(-maxlen // chunk)
         assert items <= max(74, batch)
