@@ -293,7 +293,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         ptx::mma_commit(bar(kBarSFull + sb));
                     } else {
                         const uint32_t ms = jt % kMsgSlots, mu = jt / kMsgSlots;
-                        if (*abort_flag || !ptx::mbar_wait(bar(kBarPFull + ms), mu & 1, kErrWaitPeer) ||
+                        if (*abort_flag || !ptx::mbar_wait<true>(bar(kBarPFull + ms), mu & 1, kErrWaitPeer) ||
                             !ptx::mbar_wait(bar(kBarCorr + ms), mu & 1, kErrWaitMma)) { ok = false; break; }
                         const uint32_t msg = sbase + kOffMsgO + ms * kMsgStride;
                         const int nct = (min(kTS, it.len - t0) + kTO - 1) / kTO;
@@ -413,7 +413,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         }
                         l_run = l_run * alpha + sum;
                         // the peer's message slot is free once GEMM2 of S tile jt-3 finished
-                        w = ptx::mbar_wait(bar(kBarPFree + ms), (mu & 1) ^ 1, kErrWaitPeer);
+                        w = ptx::mbar_wait<true>(bar(kBarPFree + ms), (mu & 1) ^ 1, kErrWaitPeer);
                     }
                     if (w) {
                         // staging slot sg: its previous copy (tile jt-2) finished reading
@@ -450,7 +450,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             // The last messages were consumed by the peer's GEMM2 (so no remote
             // arrival is still in flight towards this CTA).
             for (uint32_t k = (jt >= (uint32_t)kMsgSlots ? jt - kMsgSlots : 0); k < jt; ++k)
-                ptx::mbar_wait(bar(kBarPFree + (k % kMsgSlots)), (k / kMsgSlots) & 1, kErrWaitPeer);
+                ptx::mbar_wait<true>(bar(kBarPFree + (k % kMsgSlots)), (k / kMsgSlots) & 1, kErrWaitPeer);
             if (h == 0) asm volatile("cp.async.bulk.wait_group 0;" ::: "memory");
         } else {
             // ------------------------------------------------ O-CTA: correction + epilogue
@@ -460,7 +460,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 for (int t0 = 0; t0 < it.len; t0 += kTS, ++jt) {
                     const uint32_t ms = jt % kMsgSlots, mu = jt / kMsgSlots;
                     // As in the S-CTA, every branch is warpgroup-uniform (bar.red).
-                    bool w = !*abort_flag && ptx::mbar_wait(bar(kBarPFull + ms), mu & 1, kErrWaitPeer);
+                    bool w = !*abort_flag && ptx::mbar_wait<true>(bar(kBarPFull + ms), mu & 1, kErrWaitPeer);
                     if (!ptx::named_barrier_and(2, 128, w)) { ok = false; break; }
                     const uint8_t *msg = smem + kOffMsgO + ms * kMsgStride;
                     const float alpha = reinterpret_cast<const float *>(msg + kMsgAlpha)[h];

@@ -114,26 +114,43 @@ __device__ __forceinline__ void mbar_remote_arrive_expect_tx(uint32_t remote_bar
         : "memory");
 }
 
+// try_wait with acquire semantics at CTA scope (barriers completed by this
+// CTA's own TMA loads, tcgen05 commits and threads) or at cluster scope
+// (barriers the partner CTA arrives on).  The cluster-scope acquire costs
+// about 200 cycles even on a completed barrier, so it is used only where a
+// remote arrival has to be ordered.
+template <bool kCluster = false>
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
     uint32_t ok;
-    asm volatile(
-        "{\n\t.reg .pred p;\n\t"
-        "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
-        "selp.u32 %0, 1, 0, p;\n\t}"
-        : "=r"(ok)
-        : "r"(bar), "r"(parity)
-        : "memory");
+    if constexpr (kCluster) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity)
+            : "memory");
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\t"
+            "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+            "selp.u32 %0, 1, 0, p;\n\t}"
+            : "=r"(ok)
+            : "r"(bar), "r"(parity)
+            : "memory");
+    }
     return ok != 0;
 }
 
 // Waits for the phase of `bar` with the given parity to complete.  Bounded:
 // after kWaitLimitNs records `err` and returns false.  The spin itself is just
-// try_wait; the (slow) global timer is read only every 256 misses.
+// try_wait; the global timer is read only every 256 misses.
+template <bool kCluster = false>
 __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int err) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait<kCluster>(bar, parity)) return true;
     uint64_t t0 = 0;
     for (uint32_t n = 1;; ++n) {
-        if (mbar_try_wait(bar, parity)) return true;
+        if (mbar_try_wait<kCluster>(bar, parity)) return true;
         if ((n & 255) == 0) {
             const uint64_t t = globaltimer_ns();
             if (t0 == 0) {
