@@ -12,8 +12,8 @@
 //
 //   S-CTA (cluster rank 0)                 O-CTA (cluster rank 1)
 //   Q* [128 x 576] fp16 in TMEM (288 col)    O [128 x 512] fp32 in TMEM (512 col)
-//   TMA: C in K-blocks [96 tok x 64 col]     TMA: C tile [32 tok x 512] -> 4-slot ring
-//     -> 13-slot ring (12 KB slots)          GEMM2 O += P.C_N (SS MMA, N=256,
+//   TMA: C in K-blocks [96 tok x 64 col],    TMA: C tile [32 tok x 512] -> 4-slot ring
+//     three per slot -> 4-slot ring          GEMM2 O += P.C_N (SS MMA, N=256,
 //   GEMM1 S = Q.C^T (TS MMA, N=96)             C_N read MN-major from the tile)
 //     into one of two S buffers (2 x 96 col)  rescale O rows when the S-CTA
 //   online softmax (fp32 m, l; lazy             raised the running max; final
@@ -23,7 +23,9 @@
 // Tile sizes come from the tcgen05 MMA cost: an M=128 kind::f16 MMA takes at
 // least ~45 cycles, so N=32 runs at a third of peak while N >= 96 runs at the
 // full 4096 MAC/clk.  GEMM1 therefore uses 96-token tiles (its 576-deep K is
-// streamed through the ring one 64-column block at a time), GEMM2 uses N=256.
+// streamed through the ring three 64-column blocks at a time), GEMM2 uses
+// N=256.  A ring wait in the MMA-issuing thread costs ~200 cycles, so every
+// wait is followed by at least 12 MMAs (~600 cycles of queued tensor work).
 // GEMM1 (576 MACs/token/head) and GEMM2 (512) are balanced across the pair
 // and no tensor work is duplicated.  The pair reads the same rows; the second
 // read of each byte hits L2.
@@ -52,8 +54,11 @@ constexpr int kTO = 32;                          // tokens per O tile (C_N ring 
 constexpr int kOPerS = kTS / kTO;                // 3
 constexpr int kKBlocks = kDK / 64;               // 9 column blocks of 64
 constexpr int kVBlocks = kDV / 64;               // 8
-constexpr int kSlotS = kTS * 128;                // 12288: one K-block [96 tok x 64 col]
-constexpr int kSlotsS = 13;
+constexpr int kBoxS = kTS * 128;                 // 12288: one K-block box [96 tok x 64 col]
+constexpr int kKbPerSlot = 3;                    // K-blocks per S ring slot (12 MMAs per wait)
+constexpr int kSlotS = kKbPerSlot * kBoxS;       // 36864
+constexpr int kSlotsPerTile = kKBlocks / kKbPerSlot;  // 3
+constexpr int kSlotsS = 4;
 constexpr int kBoxO = kTO * 128;                 // 4096: [32 tok x 64 col]
 constexpr int kSlotO = kVBlocks * kBoxO;         // 32768: C tile [32 x 512]
 constexpr int kSlotsO = 4;
@@ -94,9 +99,9 @@ enum BarId {
 // own ring and message buffers; the barriers sit at the same offset in both
 // CTAs (remote arrivals and multicast commits address them by offset).
 constexpr int kOffRing = 0;
-constexpr int kOffStgS = kSlotsS * kSlotS;                       // 159744: S staging [2]
+constexpr int kOffStgS = kSlotsS * kSlotS;                       // 147456: S staging [2]
 constexpr int kOffMsgO = kSlotsO * kSlotO;                       // 131072: O receive ring [3]
-constexpr int kEndS = kOffStgS + kStgSlots * kMsgStride;         // 212992
+constexpr int kEndS = kOffStgS + kStgSlots * kMsgStride;         // 200704
 constexpr int kEndO = kOffMsgO + kMsgSlots * kMsgStride;         // 210944
 constexpr int kOffBar = kEndS > kEndO ? kEndS : kEndO;
 constexpr int kOffSlot = kOffBar + kNumBars * 8;
@@ -229,10 +234,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 for (int t0 = 0; ok && t0 < it.len; t0 += kTS) {
                     const int row = (int)(it.row0 + t0);
                     if (role == 0) {
-                        for (int kb = 0; kb < kKBlocks; ++kb) {
+                        for (int sl = 0; sl < kSlotsPerTile; ++sl) {
                             if (!acquire()) { ok = false; break; }
+                            const uint32_t dst = sbase + kOffRing + rg.slot * kSlotS;
                             ptx::mbar_arrive_expect_tx(bar(kBarFull + rg.slot), kSlotS);
-                            ptx::tma_load_2d(sbase + kOffRing + rg.slot * kSlotS, &cmap_s, kb * 64, row, bar(kBarFull + rg.slot));
+                            for (int j = 0; j < kKbPerSlot; ++j)
+                                ptx::tma_load_2d(dst + j * kBoxS, &cmap_s, (sl * kKbPerSlot + j) * 64, row, bar(kBarFull + rg.slot));
                             rg.next(nslots);
                         }
                     } else {
@@ -276,14 +283,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         const uint32_t sb = jt & 1, use = jt >> 1;
                         if (*abort_flag || !ptx::mbar_wait(bar(kBarSEmpty + sb), (use & 1) ^ 1, kErrWaitMma)) { ok = false; break; }
                         const uint32_t d = tmem + kTmemS + sb * kTS;
-                        for (int kb = 0; kb < kKBlocks; ++kb) {
+                        for (int sl = 0; sl < kSlotsPerTile; ++sl) {
                             if (!ptx::mbar_wait(bar(kBarFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
                             ptx::tc_fence_after();
                             const uint32_t slot = sbase + kOffRing + rg.slot * kSlotS;
 #pragma unroll
-                            for (int k4 = 0; k4 < 4; ++k4) {
-                                const int kk = kb * 4 + k4;
-                                ptx::mma_ts(d, tmem + kTmemQ + kk * 8, ptx::sdesc_sw128(slot + k4 * 32, 16, 1024),
+                            for (int k = 0; k < kKbPerSlot * 4; ++k) {
+                                const int kk = sl * kKbPerSlot * 4 + k;
+                                ptx::mma_ts(d, tmem + kTmemQ + kk * 8,
+                                            ptx::sdesc_sw128(slot + (k >> 2) * kBoxS + (k & 3) * 32, 16, 1024),
                                             kIdescS, kk > 0);
                             }
                             ptx::mma_commit(bar(kBarEmpty + rg.slot));
@@ -379,39 +387,47 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         ptx::tc_fence_after();
                         uint32_t r[kTS];
                         {
-                            uint32_t a[32];
+                            uint32_t a[32], b[32], c[32];
+                            ptx::tmem_ld_x32(trow + kTmemS + sb * kTS, a);
+                            ptx::tmem_ld_x32(trow + kTmemS + sb * kTS + 32, b);
+                            ptx::tmem_ld_x32(trow + kTmemS + sb * kTS + 64, c);
+                            ptx::tmem_wait_ld();
 #pragma unroll
-                            for (int q = 0; q < kTS / 32; ++q) {
-                                ptx::tmem_ld_x32(trow + kTmemS + sb * kTS + q * 32, a);
-                                ptx::tmem_wait_ld();
-#pragma unroll
-                                for (int c = 0; c < 32; ++c) r[q * 32 + c] = a[c];
-                            }
+                            for (int k = 0; k < 32; ++k) { r[k] = a[k]; r[32 + k] = b[k]; r[64 + k] = c[k]; }
                         }
                         ptx::tc_fence_before();
                         ptx::mbar_arrive(bar(kBarSEmpty + sb));
 
+                        // Row max of the raw logits (scale > 0 commutes with max), with
+                        // masked tail columns at -inf; 8 independent chains.
                         const int valid = min(kTS, it.len - t0);
-                        float mx = -INFINITY;
+                        if (valid < kTS) {
 #pragma unroll
-                        for (int c = 0; c < kTS; ++c) {
-                            const float x = c < valid ? f32_of(r[c]) * p.scale_log2 : -INFINITY;
-                            r[c] = u32_of(x);
-                            mx = fmaxf(mx, x);
+                            for (int k = 0; k < kTS; ++k)
+                                if (k >= valid) r[k] = u32_of(-INFINITY);
                         }
+                        float m8[8];
+#pragma unroll
+                        for (int j = 0; j < 8; ++j) m8[j] = f32_of(r[j]);
+#pragma unroll
+                        for (int k = 8; k < kTS; ++k) m8[k & 7] = fmaxf(m8[k & 7], f32_of(r[k]));
+                        const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                                               fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * p.scale_log2;
                         if (mx > m_used + kRescaleLog2) {
                             alpha = (m_used == -INFINITY) ? 0.f : ptx::ex2(m_used - mx);
                             m_used = mx;
                         }
-                        float sum = 0.f;
+                        // p = 2^(s * scale_log2 - m_used): one FFMA + one EX2 per logit.
+                        const float neg_m = -m_used;
+                        float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
-                        for (int c = 0; c < kTS; c += 2) {
-                            const float p0 = ptx::ex2(f32_of(r[c]) - m_used);
-                            const float p1 = ptx::ex2(f32_of(r[c + 1]) - m_used);
-                            sum += p0 + p1;
-                            pk[c >> 1] = pack_half2(p0, p1);
+                        for (int k = 0; k < kTS; k += 2) {
+                            const float p0 = ptx::ex2(fmaf(f32_of(r[k]), p.scale_log2, neg_m));
+                            const float p1 = ptx::ex2(fmaf(f32_of(r[k + 1]), p.scale_log2, neg_m));
+                            s4[(k >> 1) & 3] += p0 + p1;
+                            pk[k >> 1] = pack_half2(p0, p1);
                         }
-                        l_run = l_run * alpha + sum;
+                        l_run = l_run * alpha + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
                         // the peer's message slot is free once GEMM2 of S tile jt-3 finished
                         w = ptx::mbar_wait<true>(bar(kBarPFree + ms), (mu & 1) ^ 1, kErrWaitPeer);
                     }
