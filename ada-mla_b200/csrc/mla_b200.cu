@@ -252,12 +252,12 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
         }
     }
     const long long rows = (long long)batch * num_heads;
-    const unsigned cgrid = (unsigned)cdiv(rows, kCombineWarps);
+    const unsigned cgrid = (unsigned)rows;
     if (out_dtype == MLA_B200_OUT_F16) {
-        combine_kernel<__half><<<cgrid, kCombineWarps * 32, 0, stream>>>(
+        combine_kernel<__half><<<cgrid, kCombineThreads, 0, stream>>>(
             L.part_o, L.part_lse, wl, num_heads, rows, static_cast<__half *>(out), out_lse);
     } else {
-        combine_kernel<float><<<cgrid, kCombineWarps * 32, 0, stream>>>(
+        combine_kernel<float><<<cgrid, kCombineThreads, 0, stream>>>(
             L.part_o, L.part_lse, wl, num_heads, rows, static_cast<float *>(out), out_lse);
     }
     return launch_status();
@@ -438,13 +438,13 @@ int mla_b200_combine_f32(const float *part_o, const float *part_lse, int num_par
     wl.chunk = 1;
     wl.cps = num_parts;
     wl.max_items = num_parts;
-    const unsigned cgrid = (unsigned)cdiv(rows, kCombineWarps);
+    const unsigned cgrid = (unsigned)rows;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (out_dtype == MLA_B200_OUT_F16)
-        combine_kernel<__half><<<cgrid, kCombineWarps * 32, 0, s>>>(
+        combine_kernel<__half><<<cgrid, kCombineThreads, 0, s>>>(
             part_o, part_lse, wl, (int)rows, rows, static_cast<__half *>(out), out_lse);
     else
-        combine_kernel<float><<<cgrid, kCombineWarps * 32, 0, s>>>(
+        combine_kernel<float><<<cgrid, kCombineThreads, 0, s>>>(
             part_o, part_lse, wl, (int)rows, rows, static_cast<float *>(out), out_lse);
     return launch_status();
 }

@@ -4,78 +4,94 @@
 // The reference merges its fp16 split partials in mla_decode_combine
 // (csrc/mla_decode_splitk_fwd.cuh:894-939): one 128-thread block per head,
 // each thread looping serially over the splits and recomputing expf for every
-// element.  Here one WARP owns one (sequence, head) row: the split weights
-// w_i = exp(lse_i - max_i lse_i) are computed once per split, every lane
-// accumulates 16 of the 512 columns with float4 loads, and the same kernel
-// serves the intra-GPU split merge and the cross-GPU merge after an
-// all-gather (any number of parts, fp16 or fp32 output, optional merged LSE).
+// element.  Here a block still owns one (sequence, head) row, but the split
+// weights w_i = exp(lse_i - max_i lse_i) are computed once per split into
+// shared memory and each thread streams one float4 column of every split with
+// several loads in flight.  The same kernel serves the intra-GPU split merge
+// and the cross-GPU merge after an all-gather (any number of parts, fp16 or
+// fp32 output, optional merged LSE).
 #pragma once
 
 #include "mla_common.cuh"
 
 namespace mla {
 
-constexpr int kCombineWarps = 8;
+constexpr int kCombineThreads = 128;     // one (row, float4 column) per thread
+constexpr int kCombineChunk = 1024;      // split weights staged per pass
 
-// rows = batch * num_heads; row r = (b, h).  Partial i of row (b, h) lives at
-// part_o[(i * num_heads + h) * 512] and part_lse[i * num_heads + h], for i in
-// item_range(b).  Normalized partials: O_i = sum_j p_j C_j / l_i and
-// lse_i = ln(l_i) + max logit.  Merged: O = sum_i e^{lse_i - M} O_i / sum_i e^{lse_i - M}.
+// rows = batch * num_heads; one block per row r = (b, h).  Partial i of row
+// (b, h) lives at part_o[(i * num_heads + h) * 512] and part_lse[i * num_heads
+// + h], for i in item_range(b).  Normalized partials: O_i = sum_j p_j C_j / l_i
+// and lse_i = ln(l_i) + max logit.  Merged:
+//   O = sum_i e^{lse_i - M} O_i / sum_i e^{lse_i - M},  M = max_i lse_i.
+// The weights are computed once per split into shared memory; every thread
+// then streams its float4 column of all splits with 4 loads in flight.
 template <typename OutT>
-__global__ void __launch_bounds__(kCombineWarps * 32) combine_kernel(
+__global__ void __launch_bounds__(kCombineThreads) combine_kernel(
     const float *__restrict__ part_o, const float *__restrict__ part_lse, WorkList wl,
     int num_heads, long long rows, OutT *__restrict__ out, float *__restrict__ out_lse) {
-    const int lane = threadIdx.x & 31;
-    const long long row = (long long)blockIdx.x * kCombineWarps + (threadIdx.x >> 5);
+    __shared__ float w_s[kCombineChunk];
+    __shared__ float red[kCombineThreads / 32];
+    const long long row = blockIdx.x;
     if (row >= rows) return;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int b = (int)(row / num_heads);
     const int h = (int)(row - (long long)b * num_heads);
     int i0, i1;
     item_range(wl, b, i0, i1);
 
     float mx = -INFINITY;
-    for (int i = i0 + lane; i < i1; i += 32) mx = fmaxf(mx, part_lse[(size_t)i * num_heads + h]);
+    for (int i = i0 + tid; i < i1; i += kCombineThreads) mx = fmaxf(mx, part_lse[(size_t)i * num_heads + h]);
     mx = warp_max(mx);
+    if (lane == 0) red[warp] = mx;
+    __syncthreads();
+    mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
 
-    float4 acc[4];
-#pragma unroll
-    for (int k = 0; k < 4; ++k) acc[k] = make_float4(0.f, 0.f, 0.f, 0.f);
-    float wsum = 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float wsum = 0.f;  // identical in every thread (same weights, same order)
     if (mx != -INFINITY) {
-        for (int i = i0; i < i1; ++i) {
-            const size_t pr = (size_t)i * num_heads + h;
-            const float lse = part_lse[pr];
-            if (lse == -INFINITY) continue;
-            const float w = __expf(lse - mx);
-            wsum += w;
-            const float4 *src = reinterpret_cast<const float4 *>(part_o + pr * kDV);
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {
-                const float4 v = src[lane + 32 * k];
-                acc[k].x = fmaf(w, v.x, acc[k].x);
-                acc[k].y = fmaf(w, v.y, acc[k].y);
-                acc[k].z = fmaf(w, v.z, acc[k].z);
-                acc[k].w = fmaf(w, v.w, acc[k].w);
+        for (int c0 = i0; c0 < i1; c0 += kCombineChunk) {
+            const int n = min(kCombineChunk, i1 - c0);
+            __syncthreads();
+            for (int k = tid; k < n; k += kCombineThreads) {
+                const float lse = part_lse[(size_t)(c0 + k) * num_heads + h];
+                w_s[k] = lse == -INFINITY ? 0.f : __expf(lse - mx);
+            }
+            __syncthreads();
+            const float4 *src = reinterpret_cast<const float4 *>(part_o) + ((size_t)c0 * num_heads + h) * (kDV / 4) + tid;
+            const size_t step = (size_t)num_heads * (kDV / 4);
+            int k = 0;
+            for (; k + 4 <= n; k += 4) {
+                const float4 v0 = src[(size_t)k * step], v1 = src[(size_t)(k + 1) * step];
+                const float4 v2 = src[(size_t)(k + 2) * step], v3 = src[(size_t)(k + 3) * step];
+                const float w0 = w_s[k], w1 = w_s[k + 1], w2 = w_s[k + 2], w3 = w_s[k + 3];
+                acc.x += w0 * v0.x + w1 * v1.x + w2 * v2.x + w3 * v3.x;
+                acc.y += w0 * v0.y + w1 * v1.y + w2 * v2.y + w3 * v3.y;
+                acc.z += w0 * v0.z + w1 * v1.z + w2 * v2.z + w3 * v3.z;
+                acc.w += w0 * v0.w + w1 * v1.w + w2 * v2.w + w3 * v3.w;
+                wsum += (w0 + w1) + (w2 + w3);
+            }
+            for (; k < n; ++k) {
+                const float4 v = src[(size_t)k * step];
+                const float w = w_s[k];
+                acc.x += w * v.x; acc.y += w * v.y; acc.z += w * v.z; acc.w += w * v.w;
+                wsum += w;
             }
         }
     }
     const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
-    OutT *dst = out + (size_t)row * kDV;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) {
-        const int col = 4 * (lane + 32 * k);
-        const float4 v = make_float4(acc[k].x * inv, acc[k].y * inv, acc[k].z * inv, acc[k].w * inv);
-        if constexpr (sizeof(OutT) == 4) {
-            *reinterpret_cast<float4 *>(dst + col) = v;
-        } else {
-            __half2 a = __floats2half2_rn(v.x, v.y), c = __floats2half2_rn(v.z, v.w);
-            uint2 u;
-            u.x = *reinterpret_cast<uint32_t *>(&a);
-            u.y = *reinterpret_cast<uint32_t *>(&c);
-            *reinterpret_cast<uint2 *>(dst + col) = u;
-        }
+    const float4 v = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+    OutT *dst = out + (size_t)row * kDV + 4 * tid;
+    if constexpr (sizeof(OutT) == 4) {
+        *reinterpret_cast<float4 *>(dst) = v;
+    } else {
+        __half2 a = __floats2half2_rn(v.x, v.y), c = __floats2half2_rn(v.z, v.w);
+        uint2 u;
+        u.x = *reinterpret_cast<uint32_t *>(&a);
+        u.y = *reinterpret_cast<uint32_t *>(&c);
+        *reinterpret_cast<uint2 *>(dst) = u;
     }
-    if (out_lse != nullptr && lane == 0) out_lse[row] = wsum > 0.f ? mx + __logf(wsum) : -INFINITY;
+    if (out_lse != nullptr && tid == 0) out_lse[row] = wsum > 0.f ? mx + __logf(wsum) : -INFINITY;
 }
 
 // Expands cu_seqlens[B+1] into item_off[B+1] (exclusive prefix of per-sequence
