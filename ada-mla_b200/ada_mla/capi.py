@@ -38,6 +38,7 @@ SIGNATURES = {
                                ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
     "mla_b200_workspace_size": (_c_size, [_c_int, _c_int, _c_ll, _c_int, _c_int]),
     "mla_b200_decode_split_f16": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _vp, _c_size, _vp]),
+    "mla_b200_decode_split_f16_noalloc": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _vp]),
     "mla_b200_decode_batched_f16": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_ll, _c_int, _c_float,
                                              _c_int, _vp, _c_int, _vp, _vp, _c_size, _vp]),
     "mla_b200_decode_fused_f32": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _vp, _c_size, _vp]),
@@ -123,6 +124,18 @@ def decode_split_f16(query: torch.Tensor, cache: torch.Tensor, num_splits: int =
     _check("mla_b200_decode_split_f16", lib().mla_b200_decode_split_f16(
         _ptr(query), _ptr(cache), _ptr(out), nh, n, num_splits, _ptr(workspace),
         workspace.numel(), _stream()))
+    return out
+
+
+def decode_split_f16_noalloc(query: torch.Tensor, cache: torch.Tensor, num_splits: int = -1,
+                             out: torch.Tensor | None = None):
+    """The allocation-free split decode: scratch comes from the library's static
+    device array, so only the output is passed (and allocated here if absent)."""
+    nh, n = query.shape[0], cache.shape[0]
+    if out is None:
+        out = torch.empty((nh, 512), dtype=torch.float16, device=query.device)
+    _check("mla_b200_decode_split_f16_noalloc", lib().mla_b200_decode_split_f16_noalloc(
+        _ptr(query), _ptr(cache), _ptr(out), nh, n, num_splits, _stream()))
     return out
 
 

@@ -449,6 +449,74 @@ int mla_b200_combine_f32(const float *part_o, const float *part_lse, int num_par
     return launch_status();
 }
 
+// ---------------------------------------------------------------------------
+// Allocation-free split decode.  Its scratch is this file-scope device array;
+// host code may not use the array's name as a device address, so each device
+// resolves the address once with cudaGetSymbolAddress (with that device current).
+// ---------------------------------------------------------------------------
+}  // extern "C"
+
+static __device__ __align__(256) unsigned char g_noalloc_scratch[MLA_B200_NOALLOC_SCRATCH_BYTES];
+
+namespace {
+std::mutex g_noalloc_mu;
+void *g_noalloc_ptr[kMaxDevices] = {};
+
+int noalloc_scratch(int dev, void **ptr) {
+    std::lock_guard<std::mutex> lk(g_noalloc_mu);
+    if (g_noalloc_ptr[dev] == nullptr) {
+        void *p = nullptr;
+        if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) {
+            cudaGetLastError();
+            return MLA_B200_ERR_CUDA;
+        }
+        g_noalloc_ptr[dev] = p;
+    }
+    *ptr = g_noalloc_ptr[dev];
+    return MLA_B200_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int mla_b200_decode_split_f16_noalloc(const void *query, const void *cache, void *out,
+                                      int num_heads, int seq_length, int num_splits,
+                                      void *stream) {
+    if (query == nullptr || out == nullptr || num_heads <= 0 || seq_length < 0 ||
+        (seq_length > 0 && cache == nullptr))
+        return MLA_B200_ERR_INVALID_ARG;
+    if (!aligned(query, 16) || !aligned(cache, 16) || !aligned(out, 16))
+        return MLA_B200_ERR_INVALID_ARG;
+    const size_t cap = MLA_B200_NOALLOC_SCRATCH_BYTES;
+    int splits = num_splits;
+    if (splits > 0) {
+        if (mla_b200_workspace_size(1, num_heads, seq_length, seq_length, splits) > cap)
+            return MLA_B200_ERR_WORKSPACE;
+    } else {
+        int chunk = 0;
+        int st = mla_b200_plan(1, num_heads, seq_length, seq_length, 0, &chunk, &splits);
+        if (st != MLA_B200_OK) return st;
+        if (splits < 1) splits = 1;
+        while (splits > 1 &&
+               mla_b200_workspace_size(1, num_heads, seq_length, seq_length, splits) > cap)
+            --splits;
+        if (mla_b200_workspace_size(1, num_heads, seq_length, seq_length, splits) > cap)
+            return MLA_B200_ERR_WORKSPACE;
+    }
+    int dev;
+    DevInfo info;
+    int st = current_device(&dev, &info);
+    if (st != MLA_B200_OK) return st;
+    void *scratch = nullptr;
+    st = noalloc_scratch(dev, &scratch);
+    if (st != MLA_B200_OK) return st;
+    return run_split_decode<__half>(static_cast<const __half *>(query),
+                                    static_cast<const __half *>(cache), nullptr, 1, num_heads,
+                                    seq_length, seq_length, kRefScale, splits, out,
+                                    MLA_B200_OUT_F16, nullptr, scratch, cap,
+                                    static_cast<cudaStream_t>(stream));
+}
+
 int mla_b200_get_device_error(int *code, void *stream) {
     int v = 0;
     cudaStream_t s = static_cast<cudaStream_t>(stream);

@@ -146,6 +146,34 @@ int mla_b200_decode_naive_f32(const float *query, const float *cache, float *att
                               float *out, int num_heads, int head_dim_c,
                               int seq_length, void *stream);
 
+/* Allocation-free variant of mla_b200_decode_split_f16 (no counterpart in the
+ * reference, whose launcher always allocates its split buffers with at::empty).
+ *
+ * Some callers cannot allocate device memory at decode time: a host program
+ * that reaches the library through a thin FFI (ctypes, cgo, JNI) with no CUDA
+ * allocator of its own, or a serving process whose memory pool has already
+ * reserved the whole GPU for its KV cache, where a cudaMalloc would fail or
+ * stall.  This entry point takes only the query, the cache and the output; its
+ * split scratch lives in a static device array of MLA_B200_NOALLOC_SCRATCH_BYTES
+ * inside this library, which every GPU that loads the library keeps until the
+ * process exits.  It calls no cudaMalloc, cudaFree or allocating library routine.
+ *
+ *   - Same inputs, output and semantics as mla_b200_decode_split_f16.
+ *   - num_splits <= 0: the split heuristic, reduced until the partials fit the
+ *     scratch.  An explicit num_splits whose partials do not fit is rejected
+ *     with MLA_B200_ERR_WORKSPACE before anything is launched.
+ *   - The first call on each device looks up the scratch array's device
+ *     address (cudaGetSymbolAddress) with that device current; make that first
+ *     call before any stream capture.
+ *   - All calls share the one scratch array.  Nothing in it must start at
+ *     zero (each call writes every partial it reads), but calls that overlap on
+ *     the GPU -- on different streams, or from different host threads -- race
+ *     on it: serialize them. */
+#define MLA_B200_NOALLOC_SCRATCH_BYTES (8u << 20)
+int mla_b200_decode_split_f16_noalloc(const void *query, const void *cache, void *out,
+                                      int num_heads, int seq_length, int num_splits,
+                                      void *stream);
+
 /* ------------------------------------------------------------------------ */
 /* Log-sum-exp merge of partial results                                      */
 /* ------------------------------------------------------------------------ */
