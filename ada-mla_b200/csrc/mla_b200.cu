@@ -230,6 +230,7 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
         plan_varlen_kernel<<<1, 1024, 0, stream>>>(cu_seqlens, batch, chunk, L.item_off, L.items,
                                                    (int)max_items);
     }
+    bool tc_direct = false;  // the tcgen05 kernel wrote single-item sequences itself
     if (wl.max_items > 0) {
         if (std::is_same<T, __half>::value && num_heads <= 128) {
             CUtensorMap cmap_s, cmap_o, qmap;
@@ -243,6 +244,10 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
             tp.scale_log2 = scale * kLog2e;
             tp.part_o = L.part_o;
             tp.part_lse = L.part_lse;
+            tp.out = out;
+            tp.out_f16 = out_dtype == MLA_B200_OUT_F16 ? 1 : 0;
+            tp.out_lse = out_lse;
+            tc_direct = true;
             const int clusters = std::min(info.tc_clusters, wl.max_items);
             tc::tc_decode_kernel<<<2 * clusters, tc::kThreads, tc::kSmemBytes, stream>>>(cmap_s, cmap_o, qmap, tp);
         } else {
@@ -251,14 +256,17 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
                 q, cache, wl, num_heads, scale * kLog2e, L.part_o, L.part_lse);
         }
     }
+    // A dense batch split into one item per sequence is complete already.
+    if (tc_direct && cu_seqlens == nullptr && wl.cps == 1) return launch_status();
     const long long rows = (long long)batch * num_heads;
     const unsigned cgrid = (unsigned)rows;
+    const int skip = tc_direct ? 1 : 0;
     if (out_dtype == MLA_B200_OUT_F16) {
         combine_kernel<__half><<<cgrid, kCombineThreads, 0, stream>>>(
-            L.part_o, L.part_lse, wl, num_heads, rows, static_cast<__half *>(out), out_lse);
+            L.part_o, L.part_lse, wl, num_heads, rows, static_cast<__half *>(out), out_lse, skip);
     } else {
         combine_kernel<float><<<cgrid, kCombineThreads, 0, stream>>>(
-            L.part_o, L.part_lse, wl, num_heads, rows, static_cast<float *>(out), out_lse);
+            L.part_o, L.part_lse, wl, num_heads, rows, static_cast<float *>(out), out_lse, skip);
     }
     return launch_status();
 }
@@ -442,10 +450,10 @@ int mla_b200_combine_f32(const float *part_o, const float *part_lse, int num_par
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (out_dtype == MLA_B200_OUT_F16)
         combine_kernel<__half><<<cgrid, kCombineThreads, 0, s>>>(
-            part_o, part_lse, wl, (int)rows, rows, static_cast<__half *>(out), out_lse);
+            part_o, part_lse, wl, (int)rows, rows, static_cast<__half *>(out), out_lse, 0);
     else
         combine_kernel<float><<<cgrid, kCombineThreads, 0, s>>>(
-            part_o, part_lse, wl, (int)rows, rows, static_cast<float *>(out), out_lse);
+            part_o, part_lse, wl, (int)rows, rows, static_cast<float *>(out), out_lse, 0);
     return launch_status();
 }
 

@@ -26,10 +26,13 @@ constexpr int kCombineChunk = 1024;      // split weights staged per pass
 //   O = sum_i e^{lse_i - M} O_i / sum_i e^{lse_i - M},  M = max_i lse_i.
 // The weights are computed once per split into shared memory; every thread
 // then streams its float4 column of all splits with 4 loads in flight.
+// skip_single: rows of sequences with exactly one item were already written
+// by the decode kernel itself and are left alone.
 template <typename OutT>
 __global__ void __launch_bounds__(kCombineThreads) combine_kernel(
     const float *__restrict__ part_o, const float *__restrict__ part_lse, WorkList wl,
-    int num_heads, long long rows, OutT *__restrict__ out, float *__restrict__ out_lse) {
+    int num_heads, long long rows, OutT *__restrict__ out, float *__restrict__ out_lse,
+    int skip_single) {
     __shared__ float w_s[kCombineChunk];
     __shared__ float red[kCombineThreads / 32];
     const long long row = blockIdx.x;
@@ -39,6 +42,7 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(
     const int h = (int)(row - (long long)b * num_heads);
     int i0, i1;
     item_range(wl, b, i0, i1);
+    if (skip_single && i1 - i0 == 1) return;
 
     float mx = -INFINITY;
     for (int i = i0 + tid; i < i1; i += kCombineThreads) mx = fmaxf(mx, part_lse[(size_t)i * num_heads + h]);

@@ -106,7 +106,10 @@ constexpr int kEndO = kOffMsgO + kMsgSlots * kMsgStride;         // 210944
 constexpr int kOffBar = kEndS > kEndO ? kEndS : kEndO;
 constexpr int kOffSlot = kOffBar + kNumBars * 8;
 constexpr int kOffAbort = kOffSlot + 4;
-constexpr int kSmemBytes = kOffAbort + 12 + 1024;                // + 1024 alignment slack
+constexpr int kOffEpi = (kOffAbort + 4 + 1023) / 1024 * 1024;    // O-CTA epilogue staging
+constexpr int kEpiWarpBytes = 32 * 32 * 4;                       // one warp's 32 x 32 fp32 chunk
+constexpr int kSmemBytes = kOffEpi + 4 * kEpiWarpBytes + 1024;   // + 1024 alignment slack
+static_assert(kSmemBytes <= 232448, "dynamic shared memory limit");
 
 constexpr int kThreads = 256;
 constexpr uint32_t kTmemCols = 512;
@@ -124,6 +127,9 @@ struct TcParams {
     float scale_log2;  // softmax scale * log2(e)
     float *part_o;     // [max_items, num_heads, 512]
     float *part_lse;   // [max_items, num_heads]
+    void *out;         // [batch, num_heads, 512]: written directly for single-item sequences
+    int out_f16;       // out element type: 1 = fp16, 0 = fp32
+    float *out_lse;    // [batch, num_heads] or null
 };
 
 __device__ __forceinline__ uint32_t u32_of(float f) { return __float_as_uint(f); }
@@ -281,10 +287,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 for (int t0 = 0; ok && t0 < it.len; t0 += kTS, ++jt) {
                     if (role == 0) {
                         const uint32_t sb = jt & 1, use = jt >> 1;
-                        if (*abort_flag || !ptx::mbar_wait(bar(kBarSEmpty + sb), (use & 1) ^ 1, kErrWaitMma)) { ok = false; break; }
+                        if (*abort_flag || !ptx::mbar_spin(bar(kBarSEmpty + sb), (use & 1) ^ 1, kErrWaitMma)) { ok = false; break; }
                         const uint32_t d = tmem + kTmemS + sb * kTS;
                         for (int sl = 0; sl < kSlotsPerTile; ++sl) {
-                            if (!ptx::mbar_wait(bar(kBarFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
+                            if (!ptx::mbar_spin(bar(kBarFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
                             ptx::tc_fence_after();
                             const uint32_t slot = sbase + kOffRing + rg.slot * kSlotS;
 #pragma unroll
@@ -302,11 +308,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     } else {
                         const uint32_t ms = jt % kMsgSlots, mu = jt / kMsgSlots;
                         if (*abort_flag || !ptx::mbar_wait<true>(bar(kBarPFull + ms), mu & 1, kErrWaitPeer) ||
-                            !ptx::mbar_wait(bar(kBarCorr + ms), mu & 1, kErrWaitMma)) { ok = false; break; }
+                            !ptx::mbar_spin(bar(kBarCorr + ms), mu & 1, kErrWaitMma)) { ok = false; break; }
                         const uint32_t msg = sbase + kOffMsgO + ms * kMsgStride;
                         const int nct = (min(kTS, it.len - t0) + kTO - 1) / kTO;
                         for (int ct = 0; ct < nct; ++ct) {
-                            if (!ptx::mbar_wait(bar(kBarFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
+                            if (!ptx::mbar_spin(bar(kBarFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
                             ptx::tc_fence_after();
                             const uint32_t cst = sbase + kOffRing + rg.slot * kSlotO;
 #pragma unroll
@@ -507,23 +513,60 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         w = ptx::mbar_wait(bar(kBarMmaDone), jt & 1, kErrWaitMma);
                         if (!ptx::named_barrier_and(2, 128, w)) { ok = false; break; }
                         ptx::tc_fence_after();
-                        const bool live = h < p.num_heads;
+                        // A sequence covered by this one item gets its final output here;
+                        // otherwise the item's partial goes to the workspace for the combine.
+                        int ni0, ni1;
+                        item_range(wl, it.b, ni0, ni1);
+                        const bool single = ni1 - ni0 == 1;
                         const float inv_l = l_fin > 0.f ? 1.f / l_fin : 0.f;
-                        const size_t prow = (size_t)i * p.num_heads + h;
-                        float4 *dst = reinterpret_cast<float4 *>(p.part_o + prow * kDV);
+                        const float lse = l_fin > 0.f ? (m_fin + __log2f(l_fin)) * kLn2 : -INFINITY;
+                        // Rows go out through a per-warp swizzled 32 x 32 staging tile, so that
+                        // each store instruction covers 4 rows x 128 contiguous bytes.
+                        float *stg = reinterpret_cast<float *>(smem + kOffEpi + (warp & 3) * kEpiWarpBytes);
+                        const int row0 = (warp & 3) * 32;  // first head of this warp
+                        const int rr = lane >> 3, qq = lane & 7;
 #pragma unroll 1
                         for (int c = 0; c < kDV / 32; ++c) {
                             uint32_t r[32];
                             ptx::tmem_ld_x32(trow + c * 32, r);
                             ptx::tmem_wait_ld();
-                            if (live) {
+                            __syncwarp();
 #pragma unroll
-                                for (int k = 0; k < 8; ++k)
-                                    dst[c * 8 + k] = make_float4(f32_of(r[4 * k]) * inv_l, f32_of(r[4 * k + 1]) * inv_l,
-                                                                 f32_of(r[4 * k + 2]) * inv_l, f32_of(r[4 * k + 3]) * inv_l);
+                            for (int q = 0; q < 8; ++q)
+                                reinterpret_cast<float4 *>(stg + lane * 32)[q ^ (lane & 7)] =
+                                    make_float4(f32_of(r[4 * q]) * inv_l, f32_of(r[4 * q + 1]) * inv_l,
+                                                f32_of(r[4 * q + 2]) * inv_l, f32_of(r[4 * q + 3]) * inv_l);
+                            __syncwarp();
+#pragma unroll
+                            for (int k = 0; k < 8; ++k) {
+                                const int lr = 4 * k + rr;  // row within the warp
+                                const int head = row0 + lr;
+                                if (head >= p.num_heads) continue;
+                                const float4 v = reinterpret_cast<const float4 *>(stg + lr * 32)[qq ^ (lr & 7)];
+                                const int col = c * 32 + 4 * qq;
+                                if (single) {
+                                    const size_t o = ((size_t)it.b * p.num_heads + head) * kDV + col;
+                                    if (p.out_f16) {
+                                        __half2 a = __floats2half2_rn(v.x, v.y), bb = __floats2half2_rn(v.z, v.w);
+                                        uint2 u;
+                                        u.x = *reinterpret_cast<uint32_t *>(&a);
+                                        u.y = *reinterpret_cast<uint32_t *>(&bb);
+                                        *reinterpret_cast<uint2 *>(static_cast<__half *>(p.out) + o) = u;
+                                    } else {
+                                        *reinterpret_cast<float4 *>(static_cast<float *>(p.out) + o) = v;
+                                    }
+                                } else {
+                                    *reinterpret_cast<float4 *>(p.part_o + ((size_t)i * p.num_heads + head) * kDV + col) = v;
+                                }
                             }
                         }
-                        if (live) p.part_lse[prow] = l_fin > 0.f ? (m_fin + __log2f(l_fin)) * kLn2 : -INFINITY;
+                        if (h < p.num_heads) {
+                            if (single) {
+                                if (p.out_lse != nullptr) p.out_lse[(size_t)it.b * p.num_heads + h] = lse;
+                            } else {
+                                p.part_lse[(size_t)i * p.num_heads + h] = lse;
+                            }
+                        }
                         ptx::tc_fence_before();
                     }
                 }

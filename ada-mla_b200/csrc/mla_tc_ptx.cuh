@@ -163,6 +163,40 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int err
     }
 }
 
+// Non-blocking probe of a phase (CTA-scope acquire).  Cheaper than try_wait
+// (~80 vs ~180 cycles on an already completed phase), which matters in the
+// MMA-issuing thread: tcgen05.mma issue blocks on a shallow queue, so every
+// cycle that thread spends waiting is a cycle the tensor pipe runs dry.
+__device__ __forceinline__ bool mbar_test_wait(uint32_t bar, uint32_t parity) {
+    uint32_t ok;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.test_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(ok)
+        : "r"(bar), "r"(parity)
+        : "memory");
+    return ok != 0;
+}
+
+// Spin on test_wait; same bound and error reporting as mbar_wait.
+__device__ __forceinline__ bool mbar_spin(uint32_t bar, uint32_t parity, int err) {
+    if (mbar_test_wait(bar, parity)) return true;
+    uint64_t t0 = 0;
+    for (uint32_t n = 1;; ++n) {
+        if (mbar_test_wait(bar, parity)) return true;
+        if ((n & 1023) == 0) {
+            const uint64_t t = globaltimer_ns();
+            if (t0 == 0) {
+                t0 = t;
+            } else if (t - t0 > kWaitLimitNs) {
+                set_device_error(err);
+                return false;
+            }
+        }
+    }
+}
+
 // ---------------------------------------------------------------------------
 // TMA and bulk copies
 // ---------------------------------------------------------------------------
