@@ -399,6 +399,78 @@ def run_ours(args):
         dist.destroy_process_group()
 
 
+def run_kv(args):
+    """--mode kv: ONE workload (identical on every rank) whose KV length is split
+    across the ranks; each step = local decode of the rank's slice + NCCL
+    all-gather of the (O, LSE) partials + LSE merge, captured in one CUDA graph.
+    Total work is fixed as N grows ("scaling": "strong")."""
+    import torch
+
+    rank, world, local = dist_init(args.gpus)
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    import torch.distributed as dist
+
+    from ada_mla import multigpu
+    from ada_mla.workloads import make_workload
+
+    wl = make_workload(args.config, seed=0, device=dev)
+    assert wl.cu_seqlens is None, "kv mode takes a dense config (1 or 3)"
+    n = wl.max_seq_len
+    dec = multigpu.KvSplitDecoder() if world > 1 else None
+    lo, hi = dec.bounds(n) if dec else (0, n)
+    cache_slice = wl.cache[:, lo:hi].contiguous()
+
+    def step():
+        if dec is None:
+            import ada_mla
+
+            return ada_mla.mla_decode_batched(wl.query, cache_slice, softmax_scale=1.0)
+        return dec(wl.query, cache_slice, 1.0)
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    cap = torch.cuda.Stream()
+    cap.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(cap):
+        step()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph, stream=cap):
+            for _ in range(args.steps):
+                step()
+    graph.replay()
+    torch.cuda.synchronize()
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local)
+    barrier(world)
+    torch.cuda.synchronize()
+    with sampler:
+        ev0.record()
+        graph.replay()
+        ev1.record()
+        torch.cuda.synchronize()
+    barrier(world)
+    ms_step = max_over_ranks(ev0.elapsed_time(ev1), world) / args.steps
+    value = wl.cache_bytes / (ms_step * 1e-3) / 1e9
+    if rank == 0:
+        print(json.dumps({
+            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "us_per_step": ms_step * 1e3,
+            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
+            "data": "synthetic",
+            "config": {"workload": f"cfg{args.config}: B={wl.batch} n_h={wl.num_heads} N={n}, KV length "
+                                   f"split over {world} GPU(s), (O, LSE) all-gather + LSE merge",
+                       "cfg": args.config, "parallelism": f"kv-split x{world}",
+                       "l2": "single copy (no rotation)"},
+            "clocks": sampler.summary()}), flush=True)
+    del graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -410,11 +482,16 @@ def main():
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-rotate", action="store_true")
+    ap.add_argument("--mode", default="shard", choices=["shard", "kv"],
+                    help="shard: every rank decodes its own sequence(s), no collective (default); "
+                         "kv: one sequence's KV length split across the ranks")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     if args.impl == "reference":
         run_reference_arm(args)
+    elif args.mode == "kv":
+        run_kv(args)
     else:
         run_ours(args)
 
