@@ -87,7 +87,7 @@ enum BarId {
     kBarQFull = kBarSEmpty + 2,        //     S-CTA: Q block in smem       (count 1 + tx)
     kBarQFree = kBarQFull + 1,         //     S-CTA: Q moved to TMEM       (count 128)
     kBarQReady = kBarQFree + 1,        //     S-CTA: Q rows in TMEM        (count 128)
-    kBarPFree = kBarQReady + 1,        // [3] GEMM2 done with message slot (count 1, multicast commit)
+    kBarPFree = kBarQReady + 1,        // [3] GEMM2 done with message slot (count 1, commit arriving in both CTAs)
     kBarPFull = kBarPFree + kMsgSlots, // [3] O-CTA: message landed        (count 1 + tx, from the S-CTA)
     kBarCorr = kBarPFull + kMsgSlots,  // [3] O-CTA: O ready for GEMM2     (count 128)
     kBarMmaDone = kBarCorr + kMsgSlots,//     O-CTA: GEMM2 of an S tile done (count 1, commit)
@@ -97,7 +97,7 @@ enum BarId {
 
 // Shared-memory layout (offsets from a 1024-aligned base).  Each role has its
 // own ring and message buffers; the barriers sit at the same offset in both
-// CTAs (remote arrivals and multicast commits address them by offset).
+// CTAs (remote arrivals and the two-CTA commit address them by offset).
 constexpr int kOffRing = 0;
 constexpr int kOffStgS = kSlotsS * kSlotS;                       // 147456: S staging [2]
 constexpr int kOffMsgO = kSlotsO * kSlotO;                       // 131072: O receive ring [3]

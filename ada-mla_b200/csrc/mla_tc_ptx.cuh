@@ -216,7 +216,7 @@ __device__ __forceinline__ void tma_load_2d(uint32_t dst, const CUtensorMap *map
 
 // Bulk copy of `bytes` from this CTA's smem to another CTA's smem of the
 // cluster (dst and bar are shared::cluster addresses); completion is signalled
-// on the destination CTA's barrier.  No multicast.
+// on the destination CTA's barrier.  Point to point: exactly one destination CTA.
 __device__ __forceinline__ void bulk_copy_s2cluster(uint32_t dst, uint32_t src, uint32_t bytes,
                                                     uint32_t bar) {
     asm volatile(
