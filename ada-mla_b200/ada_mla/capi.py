@@ -33,6 +33,7 @@ SIGNATURES = {
     "mla_b200_status_string": (ctypes.c_char_p, [_c_int]),
     "mla_b200_version": (ctypes.c_char_p, []),
     "mla_b200_constant": (_c_int, [ctypes.c_char_p]),
+    "mla_b200_set_kernel_timing": (_c_int, [_vp, _vp]),
     "mla_b200_device_info": (_c_int, [ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
     "mla_b200_plan": (_c_int, [_c_int, _c_int, _c_ll, _c_int, _c_int,
                                ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
@@ -89,6 +90,14 @@ def _ptr(t: torch.Tensor | None) -> int | None:
 
 def constant(name: str) -> int:
     return lib().mla_b200_constant(name.encode())
+
+
+def set_kernel_timing(start: "torch.cuda.Event | None", stop: "torch.cuda.Event | None") -> None:
+    """Record `start`/`stop` around every later main decode-kernel launch of this
+    host thread (None, None turns it off)."""
+    a = None if start is None else start.cuda_event
+    b = None if stop is None else stop.cuda_event
+    _check("mla_b200_set_kernel_timing", lib().mla_b200_set_kernel_timing(a, b))
 
 
 def device_info():

@@ -187,6 +187,13 @@ WsLayout ws_layout(void *base, long long max_items, int num_heads, int batch) {
     return L;
 }
 
+thread_local cudaEvent_t t_ev_start = nullptr;  // mla_b200_set_kernel_timing
+thread_local cudaEvent_t t_ev_stop = nullptr;
+
+inline void timing_mark(cudaEvent_t ev, cudaStream_t stream) {
+    if (ev != nullptr) cudaEventRecord(ev, stream);
+}
+
 inline bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
 
 int launch_status() {
@@ -249,11 +256,15 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
             tp.out_lse = out_lse;
             tc_direct = true;
             const int clusters = std::min(info.tc_clusters, wl.max_items);
+            timing_mark(t_ev_start, stream);
             tc::tc_decode_kernel<<<2 * clusters, tc::kThreads, tc::kSmemBytes, stream>>>(cmap_s, cmap_o, qmap, tp);
+            timing_mark(t_ev_stop, stream);
         } else {
             dim3 grid(wl.max_items, (unsigned)cdiv(num_heads, kSimtHeads));
+            timing_mark(t_ev_start, stream);
             simt_partial_kernel<T><<<grid, 256, kSimtSmem, stream>>>(
                 q, cache, wl, num_heads, scale * kLog2e, L.part_o, L.part_lse);
+            timing_mark(t_ev_stop, stream);
         }
     }
     // A dense batch split into one item per sequence is complete already.
@@ -299,6 +310,13 @@ int mla_b200_constant(const char *name) {
     if (!strcmp(name, "HEAD_DIM_K")) return MLA_B200_HEAD_DIM_K;
     if (!strcmp(name, "HEAD_DIM_V")) return MLA_B200_HEAD_DIM_V;
     return -1;
+}
+
+int mla_b200_set_kernel_timing(void *ev_start, void *ev_stop) {
+    if ((ev_start == nullptr) != (ev_stop == nullptr)) return MLA_B200_ERR_INVALID_ARG;
+    t_ev_start = static_cast<cudaEvent_t>(ev_start);
+    t_ev_stop = static_cast<cudaEvent_t>(ev_stop);
+    return MLA_B200_OK;
 }
 
 int mla_b200_device_info(int *num_sms, int *decode_clusters) {

@@ -33,6 +33,10 @@ sys.path.insert(0, os.path.join(ROOT, "ada-mla_b200"))
 sys.path.insert(0, ROOT)
 
 HEAD_DIM_K = 576
+# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of the
+# main decode kernel per config, from an `ncu --set full` capture of this kernel
+# on this workload (cfg 1: 4.93 MB read, 0 written; cfg 3: 151.3 + 3.7 MB).
+NCU_TRAFFIC = {1: 4.934e6, 3: 155.03e6}
 METRIC = "MLA decode latent-KV HBM GB/s (us/step alongside)"
 UNIT = "GB/s"
 
@@ -301,18 +305,26 @@ def run_ours(args):
     ms_step = ms_total / args.steps
     value = world * wl.cache_bytes / (ms_step * 1e-3) / 1e9
 
-    # per-launch duration of the step's kernels, events on the launching stream
-    # (eager launches, same rotating inputs): used for the roofline
+    # per-launch duration of the dominant (main decode) kernel: the library
+    # records these events immediately around that launch on its stream
     n_launch = max(args.steps, 50)
     evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
            for _ in range(n_launch)]
+    steps_ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+                for _ in range(n_launch)]
+    for a, e in evs:  # torch creates its CUDA event on first record
+        a.record()
+        e.record()
     torch.cuda.synchronize()
     for i in range(n_launch):
-        evs[i][0].record()
+        capi.set_kernel_timing(*evs[i])
+        steps_ev[i][0].record()
         step(i, s)
-        evs[i][1].record()
+        steps_ev[i][1].record()
+    capi.set_kernel_timing(None, None)
     torch.cuda.synchronize()
     launch_ms = statistics.mean(a.elapsed_time(e) for a, e in evs)
+    step_launch_ms = statistics.mean(a.elapsed_time(e) for a, e in steps_ev)
     achieved = wl.cache_bytes / (launch_ms * 1e-3) / 1e9
 
     # end-to-end through the public API: pinned host inputs -> device, decode,
@@ -370,8 +382,8 @@ def run_ours(args):
                              f">= 3x L2)" if ring > 1 else "no rotation"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved / hbm_peak, "peak_source": peak_kind,
-                         "traffic": None, "kernel": "decode step (partial + combine)",
-                         "launch_us": launch_ms * 1e3,
+                         "traffic": NCU_TRAFFIC.get(args.config), "kernel": "mla::tc::tc_decode_kernel",
+                         "launch_us": launch_ms * 1e3, "step_us_eager": step_launch_ms * 1e3,
                          "algorithmic_bytes_per_launch": wl.cache_bytes},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "us_per_step": e2e_ms * 1e3,

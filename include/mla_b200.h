@@ -71,6 +71,15 @@ int mla_b200_constant(const char *name);
  * once (one wave of work items).  Either pointer may be NULL. */
 int mla_b200_device_info(int *num_sms, int *decode_clusters);
 
+/* Kernel timing hook for benchmarks (no reference counterpart; the reference
+ * is timed from Python with triton.testing.do_bench around the whole call).
+ * While set on the calling host thread, every decode entry point records
+ * `ev_start` immediately before and `ev_stop` immediately after the launch of
+ * its main decode kernel, on the stream it launches on (the split-merge and
+ * planning kernels fall outside).  Both are cudaEvent_t handles created by the
+ * caller; pass NULL, NULL to turn the hook off. */
+int mla_b200_set_kernel_timing(void *ev_start, void *ev_stop);
+
 /* ------------------------------------------------------------------------ */
 /* Planning                                                                  */
 /* ------------------------------------------------------------------------ */
