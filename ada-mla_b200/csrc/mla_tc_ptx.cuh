@@ -105,10 +105,13 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(uint32_t bar, uint32_t byt
 }
 
 // Arrive (with expected transaction bytes) on a barrier of another CTA of the
-// cluster; `remote_bar` is a shared::cluster address from mapa().
+// cluster; `remote_bar` is a shared::cluster address from mapa().  Relaxed:
+// the arrive only posts the byte count of a bulk copy that follows, whose own
+// complete_tx makes its data visible; a release here would make the thread
+// wait for its outstanding memory operations (~1 us per message measured).
 __device__ __forceinline__ void mbar_remote_arrive_expect_tx(uint32_t remote_bar, uint32_t bytes) {
     asm volatile(
-        "mbarrier.arrive.expect_tx.release.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(
+        "mbarrier.arrive.expect_tx.relaxed.cluster.shared::cluster.b64 _, [%0], %1;" ::"r"(
             remote_bar),
         "r"(bytes)
         : "memory");
@@ -150,6 +153,9 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int err
     if (mbar_try_wait<kCluster>(bar, parity)) return true;
     uint64_t t0 = 0;
     for (uint32_t n = 1;; ++n) {
+        // back off: a hot try_wait loop competes with the tensor core's
+        // shared-memory operand reads on the same SM
+        __nanosleep(32);
         if (mbar_try_wait<kCluster>(bar, parity)) return true;
         if ((n & 255) == 0) {
             const uint64_t t = globaltimer_ns();
