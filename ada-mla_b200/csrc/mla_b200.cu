@@ -251,6 +251,7 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
             tp.scale_log2 = scale * kLog2e;
             tp.part_o = L.part_o;
             tp.part_lse = L.part_lse;
+            tp.part_f16 = out_dtype == MLA_B200_OUT_F16 ? 1 : 0;
             tp.out = out;
             tp.out_f16 = out_dtype == MLA_B200_OUT_F16 ? 1 : 0;
             tp.out_lse = out_lse;
@@ -272,11 +273,16 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     const long long rows = (long long)batch * num_heads;
     const unsigned cgrid = (unsigned)rows;
     const int skip = tc_direct ? 1 : 0;
-    if (out_dtype == MLA_B200_OUT_F16) {
-        combine_kernel<__half><<<cgrid, kCombineThreads, 0, stream>>>(
+    // The tcgen05 kernel keeps fp16 partials for fp16 output; the SIMT kernel's are fp32.
+    if (out_dtype == MLA_B200_OUT_F16 && tc_direct) {
+        combine_kernel<__half, __half><<<cgrid, kCombineThreads, 0, stream>>>(
+            reinterpret_cast<const __half *>(L.part_o), L.part_lse, wl, num_heads, rows,
+            static_cast<__half *>(out), out_lse, skip);
+    } else if (out_dtype == MLA_B200_OUT_F16) {
+        combine_kernel<__half, float><<<cgrid, kCombineThreads, 0, stream>>>(
             L.part_o, L.part_lse, wl, num_heads, rows, static_cast<__half *>(out), out_lse, skip);
     } else {
-        combine_kernel<float><<<cgrid, kCombineThreads, 0, stream>>>(
+        combine_kernel<float, float><<<cgrid, kCombineThreads, 0, stream>>>(
             L.part_o, L.part_lse, wl, num_heads, rows, static_cast<float *>(out), out_lse, skip);
     }
     return launch_status();
@@ -467,10 +473,10 @@ int mla_b200_combine_f32(const float *part_o, const float *part_lse, int num_par
     const unsigned cgrid = (unsigned)rows;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (out_dtype == MLA_B200_OUT_F16)
-        combine_kernel<__half><<<cgrid, kCombineThreads, 0, s>>>(
+        combine_kernel<__half, float><<<cgrid, kCombineThreads, 0, s>>>(
             part_o, part_lse, wl, (int)rows, rows, static_cast<__half *>(out), out_lse, 0);
     else
-        combine_kernel<float><<<cgrid, kCombineThreads, 0, s>>>(
+        combine_kernel<float, float><<<cgrid, kCombineThreads, 0, s>>>(
             part_o, part_lse, wl, (int)rows, rows, static_cast<float *>(out), out_lse, 0);
     return launch_status();
 }

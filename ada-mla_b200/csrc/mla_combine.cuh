@@ -6,8 +6,9 @@
 // each thread looping serially over the splits and recomputing expf for every
 // element.  Here a block still owns one (sequence, head) row, but the split
 // weights w_i = exp(lse_i - max_i lse_i) are computed once per split into
-// shared memory and each thread streams one float4 column of every split with
-// several loads in flight.  The same kernel serves the intra-GPU split merge
+// shared memory and groups of threads stream disjoint splits of the row with
+// several 16-byte loads in flight.  Partials are fp16 (as in the reference)
+// when the output is fp16, fp32 otherwise.  The same kernel serves the intra-GPU split merge
 // and the cross-GPU merge after an all-gather (any number of parts, fp16 or
 // fp32 output, optional merged LSE).
 #pragma once
@@ -16,28 +17,50 @@
 
 namespace mla {
 
-constexpr int kCombineThreads = 128;     // one (row, float4 column) per thread
+constexpr int kCombineThreads = 256;
 constexpr int kCombineChunk = 1024;      // split weights staged per pass
+
+// Unpacks one 16-byte vector of partial elements to fp32.
+__device__ __forceinline__ void unpack16(const uint4 u, float (&v)[4]) {
+    v[0] = __uint_as_float(u.x); v[1] = __uint_as_float(u.y);
+    v[2] = __uint_as_float(u.z); v[3] = __uint_as_float(u.w);
+}
+__device__ __forceinline__ void unpack16(const uint4 u, float (&v)[8]) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float2 f = __half22float2(*reinterpret_cast<const __half2 *>(&w[j]));
+        v[2 * j] = f.x;
+        v[2 * j + 1] = f.y;
+    }
+}
 
 // rows = batch * num_heads; one block per row r = (b, h).  Partial i of row
 // (b, h) lives at part_o[(i * num_heads + h) * 512] and part_lse[i * num_heads
 // + h], for i in item_range(b).  Normalized partials: O_i = sum_j p_j C_j / l_i
 // and lse_i = ln(l_i) + max logit.  Merged:
 //   O = sum_i e^{lse_i - M} O_i / sum_i e^{lse_i - M},  M = max_i lse_i.
-// The weights are computed once per split into shared memory; every thread
-// then streams its float4 column of all splits with 4 loads in flight.
+// The weights are computed once per split into shared memory.  A thread owns
+// one 16-byte vector of the row (4 fp32 or 8 fp16 partial elements); the
+// block's 256 threads form 2 (fp32) or 4 (fp16) groups that stream disjoint
+// splits with 4 loads in flight each, and their sums meet in shared memory.
 // skip_single: rows of sequences with exactly one item were already written
 // by the decode kernel itself and are left alone.
-template <typename OutT>
+template <typename OutT, typename PartT>
 __global__ void __launch_bounds__(kCombineThreads) combine_kernel(
-    const float *__restrict__ part_o, const float *__restrict__ part_lse, WorkList wl,
+    const PartT *__restrict__ part_o, const float *__restrict__ part_lse, WorkList wl,
     int num_heads, long long rows, OutT *__restrict__ out, float *__restrict__ out_lse,
     int skip_single) {
+    constexpr int kVec = 16 / (int)sizeof(PartT);       // partial elements per thread
+    constexpr int kTpr = kDV / kVec;                    // threads covering one row
+    constexpr int kGroups = kCombineThreads / kTpr;     // split groups per block
     __shared__ float w_s[kCombineChunk];
     __shared__ float red[kCombineThreads / 32];
+    __shared__ __align__(16) float acc_s[kGroups - 1][kDV];
     const long long row = blockIdx.x;
     if (row >= rows) return;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int col = tid % kTpr, g = tid / kTpr;
     const int b = (int)(row / num_heads);
     const int h = (int)(row - (long long)b * num_heads);
     int i0, i1;
@@ -49,11 +72,15 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(
     mx = warp_max(mx);
     if (lane == 0) red[warp] = mx;
     __syncthreads();
-    mx = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+#pragma unroll
+    for (int w = 0; w < kCombineThreads / 32; ++w) mx = fmaxf(mx, red[w]);
 
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float acc[kVec];
+#pragma unroll
+    for (int j = 0; j < kVec; ++j) acc[j] = 0.f;
     float wsum = 0.f;  // identical in every thread (same weights, same order)
     if (mx != -INFINITY) {
+        const size_t step = (size_t)num_heads * (kDV / kVec);  // one split, in 16-byte vectors
         for (int c0 = i0; c0 < i1; c0 += kCombineChunk) {
             const int n = min(kCombineChunk, i1 - c0);
             __syncthreads();
@@ -62,38 +89,56 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(
                 w_s[k] = lse == -INFINITY ? 0.f : __expf(lse - mx);
             }
             __syncthreads();
-            const float4 *src = reinterpret_cast<const float4 *>(part_o) + ((size_t)c0 * num_heads + h) * (kDV / 4) + tid;
-            const size_t step = (size_t)num_heads * (kDV / 4);
-            int k = 0;
-            for (; k + 4 <= n; k += 4) {
-                const float4 v0 = src[(size_t)k * step], v1 = src[(size_t)(k + 1) * step];
-                const float4 v2 = src[(size_t)(k + 2) * step], v3 = src[(size_t)(k + 3) * step];
-                const float w0 = w_s[k], w1 = w_s[k + 1], w2 = w_s[k + 2], w3 = w_s[k + 3];
-                acc.x += w0 * v0.x + w1 * v1.x + w2 * v2.x + w3 * v3.x;
-                acc.y += w0 * v0.y + w1 * v1.y + w2 * v2.y + w3 * v3.y;
-                acc.z += w0 * v0.z + w1 * v1.z + w2 * v2.z + w3 * v3.z;
-                acc.w += w0 * v0.w + w1 * v1.w + w2 * v2.w + w3 * v3.w;
-                wsum += (w0 + w1) + (w2 + w3);
+            for (int k = 0; k < n; ++k) wsum += w_s[k];
+            const uint4 *src = reinterpret_cast<const uint4 *>(part_o + ((size_t)c0 * num_heads + h) * kDV) + col;
+            int k = g;
+            for (; k + 3 * kGroups < n; k += 4 * kGroups) {
+                uint4 u[4];
+#pragma unroll
+                for (int j = 0; j < 4; ++j) u[j] = __ldg(src + (size_t)(k + j * kGroups) * step);
+#pragma unroll
+                for (int j = 0; j < 4; ++j) {
+                    float v[kVec];
+                    unpack16(u[j], v);
+                    const float w = w_s[k + j * kGroups];
+#pragma unroll
+                    for (int e = 0; e < kVec; ++e) acc[e] = fmaf(w, v[e], acc[e]);
+                }
             }
-            for (; k < n; ++k) {
-                const float4 v = src[(size_t)k * step];
+            for (; k < n; k += kGroups) {
+                float v[kVec];
+                unpack16(__ldg(src + (size_t)k * step), v);
                 const float w = w_s[k];
-                acc.x += w * v.x; acc.y += w * v.y; acc.z += w * v.z; acc.w += w * v.w;
-                wsum += w;
+#pragma unroll
+                for (int e = 0; e < kVec; ++e) acc[e] = fmaf(w, v[e], acc[e]);
             }
         }
     }
+    if (g > 0) {
+#pragma unroll
+        for (int e = 0; e < kVec; ++e) acc_s[g - 1][col * kVec + e] = acc[e];
+    }
+    __syncthreads();
+    if (g != 0) return;
+#pragma unroll
+    for (int o = 0; o < kGroups - 1; ++o) {
+#pragma unroll
+        for (int e = 0; e < kVec; ++e) acc[e] += acc_s[o][col * kVec + e];
+    }
     const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
-    const float4 v = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-    OutT *dst = out + (size_t)row * kDV + 4 * tid;
-    if constexpr (sizeof(OutT) == 4) {
-        *reinterpret_cast<float4 *>(dst) = v;
-    } else {
-        __half2 a = __floats2half2_rn(v.x, v.y), c = __floats2half2_rn(v.z, v.w);
-        uint2 u;
-        u.x = *reinterpret_cast<uint32_t *>(&a);
-        u.y = *reinterpret_cast<uint32_t *>(&c);
-        *reinterpret_cast<uint2 *>(dst) = u;
+    OutT *dst = out + (size_t)row * kDV + col * kVec;
+#pragma unroll
+    for (int e0 = 0; e0 < kVec; e0 += 4) {
+        const float4 v = make_float4(acc[e0] * inv, acc[e0 + 1] * inv, acc[e0 + 2] * inv, acc[e0 + 3] * inv);
+        if constexpr (sizeof(OutT) == 4) {
+            *reinterpret_cast<float4 *>(dst + e0) = v;
+        } else {
+            __half2 a = __floats2half2_rn(v.x, v.y), c = __floats2half2_rn(v.z, v.w);
+            uint2 u;
+            u.x = *reinterpret_cast<uint32_t *>(&a);
+            u.y = *reinterpret_cast<uint32_t *>(&c);
+            *reinterpret_cast<uint2 *>(dst + e0) = u;
+        }
     }
     if (out_lse != nullptr && tid == 0) out_lse[row] = wsum > 0.f ? mx + __logf(wsum) : -INFINITY;
 }

@@ -107,7 +107,7 @@ constexpr int kOffBar = kEndS > kEndO ? kEndS : kEndO;
 constexpr int kOffSlot = kOffBar + kNumBars * 8;
 constexpr int kOffAbort = kOffSlot + 4;
 constexpr int kOffEpi = (kOffAbort + 4 + 1023) / 1024 * 1024;    // O-CTA epilogue staging
-constexpr int kEpiWarpBytes = 32 * 32 * 4;                       // one warp's 32 x 32 fp32 chunk
+constexpr int kEpiWarpBytes = 32 * 128;                          // one warp's 32 rows x 128 bytes
 constexpr int kSmemBytes = kOffEpi + 4 * kEpiWarpBytes + 1024;   // + 1024 alignment slack
 static_assert(kSmemBytes <= 232448, "dynamic shared memory limit");
 
@@ -125,8 +125,9 @@ struct TcParams {
     WorkList wl;
     int num_heads;
     float scale_log2;  // softmax scale * log2(e)
-    float *part_o;     // [max_items, num_heads, 512]
+    void *part_o;      // [max_items, num_heads, 512] fp16 or fp32 (part_f16)
     float *part_lse;   // [max_items, num_heads]
+    int part_f16;      // partial element type: 1 = fp16, 0 = fp32
     void *out;         // [batch, num_heads, 512]: written directly for single-item sequences
     int out_f16;       // out element type: 1 = fp16, 0 = fp32
     float *out_lse;    // [batch, num_heads] or null
@@ -520,44 +521,54 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         const bool single = ni1 - ni0 == 1;
                         const float inv_l = l_fin > 0.f ? 1.f / l_fin : 0.f;
                         const float lse = l_fin > 0.f ? (m_fin + __log2f(l_fin)) * kLn2 : -INFINITY;
-                        // Rows go out through a per-warp swizzled 32 x 32 staging tile, so that
+                        const bool f16 = single ? p.out_f16 != 0 : p.part_f16 != 0;
+                        const size_t row_bytes = (size_t)kDV * (f16 ? 2 : 4);
+                        uint8_t *dst = single ? static_cast<uint8_t *>(p.out) + (size_t)it.b * p.num_heads * row_bytes
+                                              : static_cast<uint8_t *>(p.part_o) + (size_t)i * p.num_heads * row_bytes;
+                        // Each pass moves a 128-byte segment of every row (64 fp16 or 32 fp32
+                        // columns) through a per-warp swizzled 32-row staging tile, so that
                         // each store instruction covers 4 rows x 128 contiguous bytes.
-                        float *stg = reinterpret_cast<float *>(smem + kOffEpi + (warp & 3) * kEpiWarpBytes);
+                        const uint32_t stg = sbase + kOffEpi + (warp & 3) * kEpiWarpBytes;
+                        const uint32_t srow = stg + lane * 128;
                         const int row0 = (warp & 3) * 32;  // first head of this warp
                         const int rr = lane >> 3, qq = lane & 7;
+                        const int passes = f16 ? kDV / 64 : kDV / 32;
 #pragma unroll 1
-                        for (int c = 0; c < kDV / 32; ++c) {
-                            uint32_t r[32];
-                            ptx::tmem_ld_x32(trow + c * 32, r);
-                            ptx::tmem_wait_ld();
-                            __syncwarp();
+                        for (int c = 0; c < passes; ++c) {
+                            uint32_t wv[32];
+                            if (f16) {
+                                uint32_t a[32], b[32];
+                                ptx::tmem_ld_x32(trow + c * 64, a);
+                                ptx::tmem_ld_x32(trow + c * 64 + 32, b);
+                                ptx::tmem_wait_ld();
+#pragma unroll
+                                for (int j = 0; j < 16; ++j) {
+                                    wv[j] = pack_half2(f32_of(a[2 * j]) * inv_l, f32_of(a[2 * j + 1]) * inv_l);
+                                    wv[16 + j] = pack_half2(f32_of(b[2 * j]) * inv_l, f32_of(b[2 * j + 1]) * inv_l);
+                                }
+                            } else {
+                                ptx::tmem_ld_x32(trow + c * 32, wv);
+                                ptx::tmem_wait_ld();
+#pragma unroll
+                                for (int j = 0; j < 32; ++j) wv[j] = u32_of(f32_of(wv[j]) * inv_l);
+                            }
+                            __syncwarp();  // the previous pass has read the staging tile
 #pragma unroll
                             for (int q = 0; q < 8; ++q)
-                                reinterpret_cast<float4 *>(stg + lane * 32)[q ^ (lane & 7)] =
-                                    make_float4(f32_of(r[4 * q]) * inv_l, f32_of(r[4 * q + 1]) * inv_l,
-                                                f32_of(r[4 * q + 2]) * inv_l, f32_of(r[4 * q + 3]) * inv_l);
+                                ptx::st_shared_v4(srow + ((q ^ (lane & 7)) << 4), wv[4 * q], wv[4 * q + 1],
+                                                  wv[4 * q + 2], wv[4 * q + 3]);
                             __syncwarp();
+                            uint4 v[8];
 #pragma unroll
                             for (int k = 0; k < 8; ++k) {
                                 const int lr = 4 * k + rr;  // row within the warp
-                                const int head = row0 + lr;
-                                if (head >= p.num_heads) continue;
-                                const float4 v = reinterpret_cast<const float4 *>(stg + lr * 32)[qq ^ (lr & 7)];
-                                const int col = c * 32 + 4 * qq;
-                                if (single) {
-                                    const size_t o = ((size_t)it.b * p.num_heads + head) * kDV + col;
-                                    if (p.out_f16) {
-                                        __half2 a = __floats2half2_rn(v.x, v.y), bb = __floats2half2_rn(v.z, v.w);
-                                        uint2 u;
-                                        u.x = *reinterpret_cast<uint32_t *>(&a);
-                                        u.y = *reinterpret_cast<uint32_t *>(&bb);
-                                        *reinterpret_cast<uint2 *>(static_cast<__half *>(p.out) + o) = u;
-                                    } else {
-                                        *reinterpret_cast<float4 *>(static_cast<float *>(p.out) + o) = v;
-                                    }
-                                } else {
-                                    *reinterpret_cast<float4 *>(p.part_o + ((size_t)i * p.num_heads + head) * kDV + col) = v;
-                                }
+                                v[k] = ptx::ld_shared_v4(stg + lr * 128 + ((qq ^ (lr & 7)) << 4));
+                            }
+#pragma unroll
+                            for (int k = 0; k < 8; ++k) {
+                                const int head = row0 + 4 * k + rr;
+                                if (head < p.num_heads)
+                                    *reinterpret_cast<uint4 *>(dst + head * row_bytes + c * 128 + qq * 16) = v[k];
                             }
                         }
                         if (h < p.num_heads) {
