@@ -28,8 +28,10 @@ EXT_NAME = "_ada_mla_ext"
 EXT_PATH = os.path.join(EXT_DIR, EXT_NAME + ".so")
 
 ARCH_FLAGS = ["-gencode", "arch=compute_100a,code=sm_100a"]
+# Hidden visibility: only the MLA_B200_API entry points of include/mla_b200.h
+# are exported (not the kernels' host stubs nor the static CUDA runtime).
 NVCC_FLAGS = ARCH_FLAGS + ["-lineinfo", "-O3", "-std=c++17", "-Xcompiler", "-fPIC",
-                           "-Xcompiler", "-Wall"]
+                           "-Xcompiler", "-Wall", "-Xcompiler", "-fvisibility=hidden"]
 
 
 def _sources() -> list[str]:

@@ -46,6 +46,7 @@ SIGNATURES = {
     "mla_b200_decode_naive_f32": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _vp]),
     "mla_b200_combine_f32": (_c_int, [_vp, _vp, _c_int, _c_ll, _vp, _c_int, _vp, _vp]),
     "mla_b200_get_device_error": (_c_int, [ctypes.POINTER(_c_int), _vp]),
+    "mla_b200_last_cuda_error": (_c_int, []),
 }
 
 _lib: ctypes.CDLL | None = None
@@ -53,7 +54,10 @@ _lib: ctypes.CDLL | None = None
 
 class MlaError(RuntimeError):
     def __init__(self, fn: str, status: int):
-        super().__init__(f"{fn}: {status_string(status)} (status {status})")
+        detail = ""
+        if status == ERR_CUDA and _lib is not None:
+            detail = f", cudaError {_lib.mla_b200_last_cuda_error()}"
+        super().__init__(f"{fn}: {status_string(status)} (status {status}{detail})")
         self.status = status
 
 

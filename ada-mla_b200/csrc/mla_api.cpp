@@ -15,6 +15,11 @@
 namespace {
 
 void check_status(int st, const char *what) {
+    if (st == MLA_B200_ERR_CUDA) {
+        const auto e = static_cast<cudaError_t>(mla_b200_last_cuda_error());
+        TORCH_CHECK(false, what, " failed: ", mla_b200_status_string(st), " (status ", st, ", ",
+                    cudaGetErrorName(e), ")");
+    }
     TORCH_CHECK(st == MLA_B200_OK, what, " failed: ", mla_b200_status_string(st), " (status ", st,
                 ")");
 }

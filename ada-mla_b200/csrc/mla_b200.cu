@@ -35,6 +35,13 @@ struct DevInfo {
 std::mutex g_dev_mu;
 DevInfo g_dev[kMaxDevices];
 
+thread_local int t_last_cuda_error = 0;  // behind the last MLA_B200_ERR_CUDA of this thread
+
+int cuda_failure(cudaError_t e) {
+    t_last_cuda_error = (int)e;
+    return MLA_B200_ERR_CUDA;
+}
+
 // Current device's properties (cached).  Returns a status.
 int current_device(int *dev_out, DevInfo *info_out) {
     int dev = 0;
@@ -62,16 +69,14 @@ int current_device(int *dev_out, DevInfo *info_out) {
             cudaFuncSetAttribute(simt_partial_kernel<__half>,
                                  cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSimtSmem) !=
                 cudaSuccess) {
-            cudaGetLastError();
-            return MLA_B200_ERR_CUDA;
+            return cuda_failure(cudaGetLastError());
         }
         d.simt_attr_set = true;
     }
     if (d.tc_clusters == 0) {
         if (cudaFuncSetAttribute(tc::tc_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  tc::kSmemBytes) != cudaSuccess) {
-            cudaGetLastError();
-            return MLA_B200_ERR_CUDA;
+            return cuda_failure(cudaGetLastError());
         }
         cudaLaunchConfig_t cfg = {};
         cfg.gridDim = dim3(2 * (d.sms / 2), 1, 1);
@@ -115,7 +120,7 @@ PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
 // (the UMMA K-major / MN-major SW128 operand layout).
 int make_tmap_576(CUtensorMap *map, const void *base, long long rows, int box_rows) {
     auto enc = tmap_encoder();
-    if (enc == nullptr) return MLA_B200_ERR_CUDA;
+    if (enc == nullptr) return cuda_failure(cudaErrorSymbolNotFound);
     cuuint64_t dims[2] = {(cuuint64_t)kDK, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)kDK * 2};
     cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
@@ -124,7 +129,7 @@ int make_tmap_576(CUtensorMap *map, const void *base, long long rows, int box_ro
                            strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    return r == CUDA_SUCCESS ? MLA_B200_OK : MLA_B200_ERR_CUDA;
+    return r == CUDA_SUCCESS ? MLA_B200_OK : cuda_failure(cudaErrorInvalidValue);
 }
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -198,7 +203,7 @@ inline bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_
 
 int launch_status() {
     const cudaError_t e = cudaGetLastError();
-    return e == cudaSuccess ? MLA_B200_OK : MLA_B200_ERR_CUDA;
+    return e == cudaSuccess ? MLA_B200_OK : cuda_failure(e);
 }
 
 // Shared driver of the split-KV paths: plan -> partial kernel -> combine.
@@ -499,8 +504,7 @@ int noalloc_scratch(int dev, void **ptr) {
     if (g_noalloc_ptr[dev] == nullptr) {
         void *p = nullptr;
         if (cudaGetSymbolAddress(&p, g_noalloc_scratch) != cudaSuccess || p == nullptr) {
-            cudaGetLastError();
-            return MLA_B200_ERR_CUDA;
+            return cuda_failure(cudaGetLastError());
         }
         g_noalloc_ptr[dev] = p;
     }
@@ -555,8 +559,7 @@ int mla_b200_get_device_error(int *code, void *stream) {
     if (cudaMemcpyFromSymbolAsync(&v, g_mla_error, sizeof(int), 0, cudaMemcpyDeviceToHost, s) !=
             cudaSuccess ||
         cudaStreamSynchronize(s) != cudaSuccess) {
-        cudaGetLastError();
-        return MLA_B200_ERR_CUDA;
+        return cuda_failure(cudaGetLastError());
     }
     if (code) *code = v;
     if (v != 0) {
@@ -564,12 +567,13 @@ int mla_b200_get_device_error(int *code, void *stream) {
         if (cudaMemcpyToSymbolAsync(g_mla_error, &zero, sizeof(int), 0, cudaMemcpyHostToDevice, s) !=
                 cudaSuccess ||
             cudaStreamSynchronize(s) != cudaSuccess) {
-            cudaGetLastError();
-            return MLA_B200_ERR_CUDA;
+            return cuda_failure(cudaGetLastError());
         }
         return MLA_B200_ERR_DEVICE_TIMEOUT;
     }
     return MLA_B200_OK;
 }
+
+int mla_b200_last_cuda_error(void) { return t_last_cuda_error; }
 
 }  // extern "C"

@@ -28,6 +28,15 @@
 #include <stddef.h>
 #include <stdint.h>
 
+/* Only these entry points are exported: the library is built with hidden
+ * default visibility, so its kernels and its static CUDA runtime never clash
+ * with another library's in the same process. */
+#if defined(__GNUC__)
+#define MLA_B200_API __attribute__((visibility("default")))
+#else
+#define MLA_B200_API
+#endif
+
 #ifdef __cplusplus
 extern "C" {
 #endif
@@ -56,20 +65,20 @@ typedef enum {
 typedef enum { MLA_B200_OUT_F16 = 0, MLA_B200_OUT_F32 = 1 } mla_b200_out_dtype;
 
 /* Human-readable name of a status code (static string). */
-const char *mla_b200_status_string(int status);
+MLA_B200_API const char *mla_b200_status_string(int status);
 
 /* Library version, e.g. "0.1.0". */
-const char *mla_b200_version(void);
+MLA_B200_API const char *mla_b200_version(void);
 
 /* Value of a model constant by name ("NUM_HEADS", "HEAD_DIM", "HEAD_DIM_C",
  * "HEAD_DIM_ROPE", "HEAD_DIM_K", "HEAD_DIM_V"); -1 for an unknown name.
  * Retires the reference TODO at mla.py:29. */
-int mla_b200_constant(const char *name);
+MLA_B200_API int mla_b200_constant(const char *name);
 
 /* Properties of the current device as the library sees them: SM count and
  * how many 2-CTA clusters of the tensor-core decode kernel can be resident at
  * once (one wave of work items).  Either pointer may be NULL. */
-int mla_b200_device_info(int *num_sms, int *decode_clusters);
+MLA_B200_API int mla_b200_device_info(int *num_sms, int *decode_clusters);
 
 /* Kernel timing hook for benchmarks (no reference counterpart; the reference
  * is timed from Python with triton.testing.do_bench around the whole call).
@@ -78,7 +87,7 @@ int mla_b200_device_info(int *num_sms, int *decode_clusters);
  * its main decode kernel, on the stream it launches on (the split-merge and
  * planning kernels fall outside).  Both are cudaEvent_t handles created by the
  * caller; pass NULL, NULL to turn the hook off. */
-int mla_b200_set_kernel_timing(void *ev_start, void *ev_stop);
+MLA_B200_API int mla_b200_set_kernel_timing(void *ev_start, void *ev_stop);
 
 /* ------------------------------------------------------------------------ */
 /* Planning                                                                  */
@@ -91,15 +100,15 @@ int mla_b200_set_kernel_timing(void *ev_start, void *ev_stop);
  * device's count) while keeping the split-partial traffic small.  Writes the
  * chunk length (a multiple of 96 tokens, the kernel's tile) to *chunk_tokens and, for a single
  * sequence, the resulting split count to *num_splits (either may be NULL). */
-int mla_b200_plan(int batch, int num_heads, long long total_tokens, int max_seq_len,
-                  int num_sms, int *chunk_tokens, int *num_splits);
+MLA_B200_API int mla_b200_plan(int batch, int num_heads, long long total_tokens, int max_seq_len,
+                               int num_sms, int *chunk_tokens, int *num_splits);
 
 /* Bytes of workspace the f16/f32 decode entry points need for this problem
  * (split partials, the work table and the varlen schedule).  `num_splits` <= 0
  * means "as chosen by mla_b200_plan".  For a single sequence pass batch = 1
  * and total_tokens = seq_length. */
-size_t mla_b200_workspace_size(int batch, int num_heads, long long total_tokens,
-                               int max_seq_len, int num_splits);
+MLA_B200_API size_t mla_b200_workspace_size(int batch, int num_heads, long long total_tokens,
+                                            int max_seq_len, int num_splits);
 
 /* ------------------------------------------------------------------------ */
 /* Decode entry points                                                       */
@@ -115,9 +124,9 @@ size_t mla_b200_workspace_size(int batch, int num_heads, long long total_tokens,
  * heuristic; otherwise the sequence is cut into that many splits (tail masked,
  * no multiple-of-64 requirement).  seq_length == 0 yields zeros.  Softmax
  * state is fp32 (the reference keeps it in fp16). */
-int mla_b200_decode_split_f16(const void *query, const void *cache, void *out,
-                              int num_heads, int seq_length, int num_splits,
-                              void *workspace, size_t workspace_bytes, void *stream);
+MLA_B200_API int mla_b200_decode_split_f16(const void *query, const void *cache, void *out,
+                                           int num_heads, int seq_length, int num_splits,
+                                           void *workspace, size_t workspace_bytes, void *stream);
 
 /* Batched / variable-length fp16 decode (no reference counterpart: the
  * reference has no batch dimension).
@@ -132,28 +141,28 @@ int mla_b200_decode_split_f16(const void *query, const void *cache, void *out,
  *   out_lse: optional [batch, num_heads] fp32 natural-log log-sum-exp of the
  *         scaled logits (-inf for an empty sequence); NULL to skip.
  * softmax_scale multiplies Q.C^T (pass 1.0 when the scale is folded into Q). */
-int mla_b200_decode_batched_f16(const void *query, const void *cache,
-                                const int32_t *cu_seqlens, int batch, int num_heads,
-                                long long total_tokens, int max_seq_len,
-                                float softmax_scale, int num_splits,
-                                void *out, int out_dtype, float *out_lse,
-                                void *workspace, size_t workspace_bytes, void *stream);
+MLA_B200_API int mla_b200_decode_batched_f16(const void *query, const void *cache,
+                                             const int32_t *cu_seqlens, int batch, int num_heads,
+                                             long long total_tokens, int max_seq_len,
+                                             float softmax_scale, int num_splits,
+                                             void *out, int out_dtype, float *out_lse,
+                                             void *workspace, size_t workspace_bytes, void *stream);
 
 /* fp32 fused decode of ONE sequence, reference semantics (scale 1/sqrt(192),
  * 512 output columns).  Replaces run_mla_decode_fused (csrc/mla_decode.hpp:18-23,
  * csrc/mla_decode_fused_fwd_sm89.cu:6-60).  head_dim_c must be 576. */
-int mla_b200_decode_fused_f32(const float *query, const float *cache, float *out,
-                              int num_heads, int head_dim_c, int seq_length,
-                              void *workspace, size_t workspace_bytes, void *stream);
+MLA_B200_API int mla_b200_decode_fused_f32(const float *query, const float *cache, float *out,
+                                           int num_heads, int head_dim_c, int seq_length,
+                                           void *workspace, size_t workspace_bytes, void *stream);
 
 /* fp32 naive 3-kernel decode, reference semantics: scale 1/sqrt(head_dim_c),
  * ALL head_dim_c output columns, attention matrix materialized in `attn`
  * ([num_heads, seq_length] fp32, caller-owned scratch).  Replaces
  * run_mla_decode_naive (csrc/mla_decode.hpp:10-16, csrc/mla_decode_naive_fwd.cu:4-31).
  * Any head_dim_c >= 1; seq_length >= 1. */
-int mla_b200_decode_naive_f32(const float *query, const float *cache, float *attn,
-                              float *out, int num_heads, int head_dim_c,
-                              int seq_length, void *stream);
+MLA_B200_API int mla_b200_decode_naive_f32(const float *query, const float *cache, float *attn,
+                                           float *out, int num_heads, int head_dim_c,
+                                           int seq_length, void *stream);
 
 /* Allocation-free variant of mla_b200_decode_split_f16 (no counterpart in the
  * reference, whose launcher always allocates its split buffers with at::empty).
@@ -179,9 +188,9 @@ int mla_b200_decode_naive_f32(const float *query, const float *cache, float *att
  *     the GPU -- on different streams, or from different host threads -- race
  *     on it: serialize them. */
 #define MLA_B200_NOALLOC_SCRATCH_BYTES (8u << 20)
-int mla_b200_decode_split_f16_noalloc(const void *query, const void *cache, void *out,
-                                      int num_heads, int seq_length, int num_splits,
-                                      void *stream);
+MLA_B200_API int mla_b200_decode_split_f16_noalloc(const void *query, const void *cache, void *out,
+                                                   int num_heads, int seq_length, int num_splits,
+                                                   void *stream);
 
 /* ------------------------------------------------------------------------ */
 /* Log-sum-exp merge of partial results                                      */
@@ -195,9 +204,9 @@ int mla_b200_decode_split_f16_noalloc(const void *query, const void *cache, void
  * rows = batch * num_heads.  Rows whose slices are all empty yield zeros.
  * Generalises the reference's mla_decode_combine
  * (csrc/mla_decode_splitk_fwd.cuh:894-939) to any part count and layout. */
-int mla_b200_combine_f32(const float *part_o, const float *part_lse, int num_parts,
-                         long long rows, void *out, int out_dtype, float *out_lse,
-                         void *stream);
+MLA_B200_API int mla_b200_combine_f32(const float *part_o, const float *part_lse, int num_parts,
+                                      long long rows, void *out, int out_dtype, float *out_lse,
+                                      void *stream);
 
 /* ------------------------------------------------------------------------ */
 /* Device error word                                                         */
@@ -207,7 +216,14 @@ int mla_b200_combine_f32(const float *part_o, const float *part_lse, int num_par
  * code in a device-side error word and the kernel returns early.  This reads
  * the word (synchronizing `stream`), writes it to *code (0 = none; may be NULL)
  * and clears it.  Returns MLA_B200_ERR_DEVICE_TIMEOUT when it was set. */
-int mla_b200_get_device_error(int *code, void *stream);
+MLA_B200_API int mla_b200_get_device_error(int *code, void *stream);
+
+/* The cudaError_t value behind the most recent MLA_B200_ERR_CUDA status this
+ * library returned on the calling thread (0 when there was none).  Replaces
+ * the reference's printf of cudaGetErrorString after each launch
+ * (csrc/mla_decode_splitk_fwd.cuh:965-985, csrc/mla_decode_fused_fwd_sm89.cu:
+ * 43-60): a caller can name the failure without the library printing. */
+MLA_B200_API int mla_b200_last_cuda_error(void);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -85,6 +85,8 @@ def test_no_device_reported_without_gpu():
                                                 16, 1 << 30, None)
     assert st == capi.ERR_NO_DEVICE
     assert capi.lib().mla_b200_get_device_error(ctypes.byref(code), None) == capi.ERR_CUDA
+    # ... and names the CUDA error behind that status
+    assert capi.lib().mla_b200_last_cuda_error() != 0
 
 
 @pytest.mark.parametrize("batch,total,maxlen", [(1, 4096, 4096), (1, 131072, 131072),
