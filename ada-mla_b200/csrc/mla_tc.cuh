@@ -30,9 +30,11 @@
 // and no tensor work is duplicated.  The pair reads the same rows; the second
 // read of each byte hits L2.
 //
-// Q reaches TMEM through shared memory: at the first item of a sequence the
-// S-CTA's producer waits for its ring to drain, TMA-loads the 144 KB Q block
-// into the ring's space, and the softmax warpgroup moves each row into TMEM.
+// Q reaches TMEM through the same ring as the cache: at the first item of a
+// sequence the S-CTA's producer TMA-loads the nine 128 x 64 Q boxes into five
+// ring slots, and the MMA thread copies each landed slot into TMEM with
+// tcgen05.cp before the GEMM1 MMAs that read it (the copy and the MMAs are
+// ordered in the tensor pipe), releasing the slot with a commit.
 //
 // Warp roles (256 threads): warp 0 TMA producer, warp 1 MMA issuer (one
 // thread), warp 2 TMEM allocator, warps 4-7 the math warpgroup (softmax in
@@ -64,7 +66,7 @@ constexpr int kSlotO = kVBlocks * kBoxO;         // 32768: C tile [32 x 512]
 constexpr int kSlotsO = 4;
 constexpr int kQBoxBytes = 128 * 128;            // Q box: 128 rows x 64 fp16
 constexpr int kQBytes = kKBlocks * kQBoxBytes;   // 147456
-static_assert(kQBytes <= kSlotsS * kSlotS, "Q must fit in the S-CTA ring");
+static_assert(2 * kQBoxBytes <= kSlotS, "two Q boxes per ring slot");
 
 // Message S-CTA -> O-CTA, one per S tile: P as three SW64 K-major sub-tiles of
 // [128 rows x 32 tokens] (8 KB each), then per-row alpha, l, m.
@@ -84,10 +86,8 @@ enum BarId {
     kBarEmpty = kRingSlots,            // [13] ring slot consumed          (count 1, commit)
     kBarSFull = 2 * kRingSlots,        // [2] S-CTA: S tile in TMEM        (count 1, commit)
     kBarSEmpty = kBarSFull + 2,        // [2] S-CTA: S tile read           (count 128)
-    kBarQFull = kBarSEmpty + 2,        //     S-CTA: Q block in smem       (count 1 + tx)
-    kBarQFree = kBarQFull + 1,         //     S-CTA: Q moved to TMEM       (count 128)
-    kBarQReady = kBarQFree + 1,        //     S-CTA: Q rows in TMEM        (count 128)
-    kBarPFree = kBarQReady + 1,        // [3] GEMM2 done with message slot (count 1, commit arriving in both CTAs)
+    kBarQFree = kBarSEmpty + 2,        //     S-CTA: GEMM1s reading Q done (count 1, commit)
+    kBarPFree = kBarQFree + 1,        // [3] GEMM2 done with message slot (count 1, commit arriving in both CTAs)
     kBarPFull = kBarPFree + kMsgSlots, // [3] O-CTA: message landed        (count 1 + tx, from the S-CTA)
     kBarCorr = kBarPFull + kMsgSlots,  // [3] O-CTA: O ready for GEMM2     (count 128)
     kBarMmaDone = kBarCorr + kMsgSlots,//     O-CTA: GEMM2 of an S tile done (count 1, commit)
@@ -182,9 +182,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             ptx::mbar_init(bar(kBarPFull + i), 1);
             ptx::mbar_init(bar(kBarCorr + i), 128);
         }
-        ptx::mbar_init(bar(kBarQFull), 1);
-        ptx::mbar_init(bar(kBarQFree), 128);
-        ptx::mbar_init(bar(kBarQReady), 128);
+        ptx::mbar_init(bar(kBarQFree), 1);
         ptx::mbar_init(bar(kBarMmaDone), 1);
         ptx::mbar_init(bar(kBarDrain), 1);
         *abort_flag = 0;
@@ -210,32 +208,26 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             const int nslots = role == 0 ? kSlotsS : kSlotsO;
             Ring rg;
-            int pre = 0;  // upcoming ring slots already known to be free
-            uint32_t qround = 0;
             int prev_b = -1;
             bool ok = true;
             auto acquire = [&]() -> bool {
-                if (pre > 0) { --pre; return true; }
                 return !*abort_flag && ptx::mbar_wait(bar(kBarEmpty + rg.slot), rg.phase ^ 1, kErrWaitEmpty);
             };
             for (int i = cid; ok && i < wl.max_items; i += ncl) {
                 const Item it = get_item(wl, i);
                 if (it.len <= 0) continue;
                 if (role == 0 && it.b != prev_b) {
-                    // Drain the ring (every slot consumed), then borrow it for Q.
-                    Ring r2 = rg;
-                    for (int k = 0; k < nslots; ++k, r2.next(nslots)) {
-                        if (k < pre) continue;
-                        if (*abort_flag || !ptx::mbar_wait(bar(kBarEmpty + r2.slot), r2.phase ^ 1, kErrWaitEmpty)) { ok = false; break; }
-                    }
-                    if (!ok) break;
-                    pre = nslots;
-                    ptx::mbar_arrive_expect_tx(bar(kBarQFull), kQBytes);
+                    // Q of the new sequence: two 128 x 64 boxes per ring slot
                     const int qrow = it.b * p.num_heads;
-                    for (int kb = 0; kb < kKBlocks; ++kb)
-                        ptx::tma_load_2d(sbase + kOffRing + kb * kQBoxBytes, &qmap, kb * 64, qrow, bar(kBarQFull));
-                    if (!ptx::mbar_wait(bar(kBarQFree), qround & 1, kErrWaitPeer)) { ok = false; break; }
-                    ++qround;
+                    for (int kb = 0; kb < kKBlocks; kb += 2) {
+                        if (!acquire()) { ok = false; break; }
+                        const int nb = min(2, kKBlocks - kb);
+                        const uint32_t dst = sbase + kOffRing + rg.slot * kSlotS;
+                        ptx::mbar_arrive_expect_tx(bar(kBarFull + rg.slot), nb * kQBoxBytes);
+                        for (int j = 0; j < nb; ++j)
+                            ptx::tma_load_2d(dst + j * kQBoxBytes, &qmap, (kb + j) * 64, qrow, bar(kBarFull + rg.slot));
+                        rg.next(nslots);
+                    }
                     prev_b = it.b;
                 }
                 for (int t0 = 0; ok && t0 < it.len; t0 += kTS) {
@@ -264,10 +256,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
             if (!ok) *abort_flag = 1;
             // drain: every issued load has been consumed (or the wait expires)
-            for (int k = 0; k < nslots; ++k, rg.next(nslots)) {
-                if (k < pre) continue;
+            for (int k = 0; k < nslots; ++k, rg.next(nslots))
                 ptx::mbar_wait(bar(kBarEmpty + rg.slot), rg.phase ^ 1, kErrWaitEmpty);
-            }
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
@@ -281,8 +271,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 const Item it = get_item(wl, i);
                 if (it.len <= 0) continue;
                 if (role == 0 && it.b != prev_b) {
-                    if (!ptx::mbar_wait(bar(kBarQReady), qphase, kErrWaitPeer)) { ok = false; break; }
-                    qphase ^= 1;
+                    // The previous sequence's GEMM1s read Q from TMEM: they complete
+                    // before the copy overwrites it (an MMA is not ordered before a
+                    // later tcgen05.cp).
+                    if (prev_b >= 0) {
+                        ptx::mma_commit(bar(kBarQFree));
+                        if (!ptx::mbar_spin(bar(kBarQFree), qphase, kErrWaitMma)) { ok = false; break; }
+                        qphase ^= 1;
+                    }
+                    for (int kb = 0; ok && kb < kKBlocks; kb += 2) {
+                        if (*abort_flag || !ptx::mbar_spin(bar(kBarFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
+                        ptx::tc_fence_after();
+                        const uint32_t slot = sbase + kOffRing + rg.slot * kSlotS;
+                        const int nb = min(2, kKBlocks - kb);
+                        for (int j = 0; j < nb; ++j) {
+#pragma unroll
+                            for (int c = 0; c < 4; ++c)
+                                ptx::tmem_cp_128x256b(tmem + kTmemQ + ((kb + j) * 4 + c) * 8,
+                                                      ptx::sdesc_sw128(slot + j * kQBoxBytes + c * 32, 16, 1024));
+                        }
+                        ptx::mma_commit(bar(kBarEmpty + rg.slot));
+                        rg.next(nslots);
+                    }
+                    if (!ok) break;
                     prev_b = it.b;
                 }
                 for (int t0 = 0; ok && t0 < it.len; t0 += kTS, ++jt) {
@@ -348,36 +359,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         bool ok = true;
         if (role == 0) {
             // ------------------------------------------------ S-CTA: softmax
-            int prev_b = -1;
-            uint32_t qround = 0;
             const uint32_t peer_pfull0 = ptx::mapa(bar(kBarPFull), 1);
             const uint32_t peer_msg0 = ptx::mapa(sbase + kOffMsgO, 1);
             for (int i = cid; ok && i < wl.max_items; i += ncl) {
                 const Item it = get_item(wl, i);
                 if (it.len <= 0) continue;
-                if (it.b != prev_b) {
-                    // Q row h (smem, 128-byte swizzled boxes) -> TMEM columns [0, 288).
-                    // Every GEMM1 of the previous item has completed: its S tiles were waited on.
-                    bool w = !*abort_flag && ptx::mbar_wait(bar(kBarQFull), qround & 1, kErrWaitFull);
-                    if (!ptx::named_barrier_and(1, 128, w)) { ok = false; break; }
-                    ++qround;
-#pragma unroll 1
-                    for (int c = 0; c < kKBlocks; ++c) {
-                        const uint4 *row = reinterpret_cast<const uint4 *>(smem + kOffRing + c * kQBoxBytes + h * 128);
-                        uint32_t r[32];
-#pragma unroll
-                        for (int v = 0; v < 8; ++v) {
-                            const uint4 x = row[v ^ (h & 7)];
-                            r[4 * v] = x.x; r[4 * v + 1] = x.y; r[4 * v + 2] = x.z; r[4 * v + 3] = x.w;
-                        }
-                        ptx::tmem_st_x32(trow + kTmemQ + c * 32, r);
-                    }
-                    ptx::tmem_wait_st();
-                    ptx::tc_fence_before();
-                    ptx::mbar_arrive(bar(kBarQFree));
-                    ptx::mbar_arrive(bar(kBarQReady));
-                    prev_b = it.b;
-                }
                 float m_used = -INFINITY, l_run = 0.f;
                 for (int t0 = 0; t0 < it.len; t0 += kTS, ++jt) {
                     const uint32_t sb = jt & 1, use = jt >> 1;

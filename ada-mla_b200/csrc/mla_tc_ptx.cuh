@@ -297,6 +297,13 @@ __device__ __forceinline__ void mma_ss(uint32_t d_tmem, uint64_t a_desc, uint64_
 }
 
 // D[tmem] (+)= A[tmem] * B[smem desc]^T, kind::f16, fp32 accumulate.
+// Shared memory -> TMEM copy of a 128-row x 32-byte matrix (row r to lane r,
+// the 32 bytes to 8 consecutive columns), read through a matrix descriptor
+// like an MMA operand.  A later tcgen05.mma of this thread is ordered after it.
+__device__ __forceinline__ void tmem_cp_128x256b(uint32_t d_tmem, uint64_t s_desc) {
+    asm volatile("tcgen05.cp.cta_group::1.128x256b [%0], %1;" ::"r"(d_tmem), "l"(s_desc) : "memory");
+}
+
 __device__ __forceinline__ void mma_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc,
                                        uint32_t idesc, uint32_t accumulate) {
     asm volatile(
