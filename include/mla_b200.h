@@ -85,8 +85,10 @@ MLA_B200_API int mla_b200_device_info(int *num_sms, int *decode_clusters);
  * While set on the calling host thread, every decode entry point records
  * `ev_start` immediately before and `ev_stop` immediately after the launch of
  * its main decode kernel, on the stream it launches on (the split-merge and
- * planning kernels fall outside).  Both are cudaEvent_t handles created by the
- * caller; pass NULL, NULL to turn the hook off. */
+ * planning kernels fall outside).  During stream capture the records become
+ * event-record nodes of the graph, so the kernel can be timed at replay.
+ * Both are cudaEvent_t handles created by the caller; pass NULL, NULL to turn
+ * the hook off. */
 MLA_B200_API int mla_b200_set_kernel_timing(void *ev_start, void *ev_stop);
 
 /* ------------------------------------------------------------------------ */
