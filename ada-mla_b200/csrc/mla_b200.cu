@@ -253,9 +253,8 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     bool tc_direct = false;  // the tcgen05 kernel wrote single-item sequences itself
     if (wl.max_items > 0) {
         if (std::is_same<T, __half>::value && num_heads <= 128) {
-            CUtensorMap cmap_s, cmap_s96, cmap_o, qmap;
-            st = make_tmap_576(&cmap_s, cache, total_tokens, tc::kTG);
-            if (st == MLA_B200_OK) st = make_tmap_576(&cmap_s96, cache, total_tokens, tc::kTS);
+            CUtensorMap cmap_s, cmap_o, qmap;
+            st = make_tmap_576(&cmap_s, cache, total_tokens, tc::kTS);
             if (st == MLA_B200_OK) st = make_tmap_576(&cmap_o, cache, total_tokens, tc::kTO);
             if (st == MLA_B200_OK) st = make_tmap_576(&qmap, q, (long long)batch * num_heads, 128);
             if (st != MLA_B200_OK) return st;
@@ -272,8 +271,7 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
             tc_direct = true;
             const int clusters = std::min(info.tc_clusters, wl.max_items);
             timing_mark(t_ev_start, stream);
-            tc::tc_decode_kernel<<<2 * clusters, tc::kThreads, tc::kSmemBytes, stream>>>(cmap_s, cmap_s96, cmap_o,
-                                                                                      qmap, tp);
+            tc::tc_decode_kernel<<<2 * clusters, tc::kThreads, tc::kSmemBytes, stream>>>(cmap_s, cmap_o, qmap, tp);
             timing_mark(t_ev_stop, stream);
         } else {
             dim3 grid(wl.max_items, (unsigned)cdiv(num_heads, kSimtHeads));

@@ -10,33 +10,31 @@
 // all 512 TMEM columns of an SM, leaving no room for S = Q.C^T.  So each item
 // runs on a 2-CTA cluster (two SMs):
 //
-//   S-CTA (cluster rank 0)                   O-CTA (cluster rank 1)
-//   Q* K-blocks 0-3 in TMEM (128 col),         O [128 x 512] fp32 in TMEM (512 col)
-//     K-blocks 4-8 in smem (80 KB)             TMA: C tile [32 tok x 512] -> 4-slot ring
-//   TMA: C K-blocks [192 tok x 64 col]         GEMM2 O += P.C_N (SS MMA, N=256,
-//     -> 4-slot ring                             C_N read MN-major from the tile)
-//   GEMM1 S = Q.C^T (N=192; TS MMAs for        rescale O rows when the S-CTA
-//     K-blocks 0-3, SS for 4-8) into one         raised the running max; final
-//     of two S buffers (2 x 192 col)             O / l and LSE to the workspace
-//   online softmax per 96-token half (fp32
-//     m, l; lazy rescale, threshold 2^8)
+//   S-CTA (cluster rank 0)                 O-CTA (cluster rank 1)
+//   Q* [128 x 576] fp16 in TMEM (288 col)    O [128 x 512] fp32 in TMEM (512 col)
+//   TMA: C in K-blocks [96 tok x 64 col],    TMA: C tile [32 tok x 512] -> 4-slot ring
+//     three per slot -> 4-slot ring          GEMM2 O += P.C_N (SS MMA, N=256,
+//   GEMM1 S = Q.C^T (TS MMA, N=96)             C_N read MN-major from the tile)
+//     into one of two S buffers (2 x 96 col)  rescale O rows when the S-CTA
+//   online softmax (fp32 m, l; lazy             raised the running max; final
+//     rescale, threshold 2^8)                   O / l and LSE to the workspace
 //   P fp16 + per-row alpha ---DSMEM bulk copy (26 KB / 96 tokens)---> 3-slot ring
 //
-// Tile sizes come from the tcgen05 MMA cost measured on B200: with TMA writes
-// landing in the ring, an M=128 kind::f16 MMA carries a fixed ~45-cycle
-// overhead on top of its N/2 cycles, so N=96 runs at ~45% of the tensor rate
-// while N=192 reaches ~85-90% and N=256 the full rate.  GEMM1 therefore issues
-// N=192 MMAs; its TMEM budget (2 x 192 S columns) leaves 128 columns for Q, so
-// the rest of Q is an SS operand in shared memory.  GEMM2 uses N=256.  GEMM1
-// (576 MACs/token/head) and GEMM2 (512) are balanced across the pair and no
-// tensor work is duplicated.  The pair reads the same rows; the second read of
-// each byte hits L2.
+// Tile sizes come from tcgen05 costs measured on B200.  One thread issues an
+// M=128 kind::f16 MMA at most every ~46 cycles and the tensor pipe queues ~8,
+// so N=96 (48 cycles of work) is the smallest tile that keeps the pipe busy;
+// Q (288 TMEM columns) leaves room for two N=96 S buffers, and TS MMAs (A in
+// TMEM) issue faster than SS ones.  GEMM1's 576-deep K is streamed through the
+// ring three 64-column blocks at a time, so every ring wait is followed by 12
+// MMAs.  GEMM2 uses N=256.  GEMM1 (576 MACs/token/head) and GEMM2 (512) are
+// balanced across the pair and no tensor work is duplicated.  The pair reads
+// the same rows; the second read of each byte hits L2.
 //
-// Q reaches the S-CTA at the first item of a sequence: K-blocks 0-3 through
-// the ring (one 128 x 64 box per slot), copied into TMEM by the MMA thread
-// with tcgen05.cp ahead of the GEMM1 MMAs that read them (the copy and the
-// MMAs are ordered in the tensor pipe); K-blocks 4-8 by TMA into their own
-// region once the previous sequence's GEMM1s have completed.
+// Q reaches TMEM through the same ring as the cache: at the first item of a
+// sequence the S-CTA's producer TMA-loads the nine 128 x 64 Q boxes into five
+// ring slots, and the MMA thread copies each landed slot into TMEM with
+// tcgen05.cp before the GEMM1 MMAs that read it (the copy and the MMAs are
+// ordered in the tensor pipe), releasing the slot with a commit.
 //
 // Warp roles (256 threads): warp 0 TMA producer, warp 1 MMA issuer (one
 // thread), warp 2 TMEM allocator, warps 4-7 the math warpgroup (softmax in
@@ -53,26 +51,24 @@
 namespace mla {
 namespace tc {
 
-constexpr int kTS = 96;                          // tokens per message tile (softmax, GEMM2)
-constexpr int kTG = 192;                         // tokens per S tile (GEMM1 N)
-constexpr int kMsgPerS = kTG / kTS;              // 2 message tiles per S tile
+constexpr int kTS = 96;                          // tokens per S tile (GEMM1 N)
 constexpr int kTO = 32;                          // tokens per O tile (C_N ring granularity)
-constexpr int kOPerS = kTS / kTO;                // 3 O tiles per message tile
+constexpr int kOPerS = kTS / kTO;                // 3
 constexpr int kKBlocks = kDK / 64;               // 9 column blocks of 64
 constexpr int kVBlocks = kDV / 64;               // 8
-constexpr int kKbTmem = 4;                       // Q K-blocks in TMEM (TS MMAs)
-constexpr int kKbSmem = kKBlocks - kKbTmem;      // 5 Q K-blocks in shared memory (SS MMAs)
-constexpr int kSlotS = kTG * 128;                // 24576: one K-block box [192 tok x 64 col]
+constexpr int kBoxS = kTS * 128;                 // 12288: one K-block box [96 tok x 64 col]
+constexpr int kKbPerSlot = 3;                    // K-blocks per S ring slot (12 MMAs per wait)
+constexpr int kSlotS = kKbPerSlot * kBoxS;       // 36864
+constexpr int kSlotsPerTile = kKBlocks / kKbPerSlot;  // 3
 constexpr int kSlotsS = 4;
 constexpr int kBoxO = kTO * 128;                 // 4096: [32 tok x 64 col]
 constexpr int kSlotO = kVBlocks * kBoxO;         // 32768: C tile [32 x 512]
 constexpr int kSlotsO = 4;
 constexpr int kQBoxBytes = 128 * 128;            // Q box: 128 rows x 64 fp16
-static_assert(kQBoxBytes <= kSlotS, "a Q box fits a ring slot");
+static_assert(2 * kQBoxBytes <= kSlotS, "two Q boxes per ring slot");
 
-// Message S-CTA -> O-CTA, one per 96-token half of an S tile: P as three SW64
-// K-major sub-tiles of [128 rows x 32 tokens] (8 KB each), then per-row alpha,
-// l, m.
+// Message S-CTA -> O-CTA, one per S tile: P as three SW64 K-major sub-tiles of
+// [128 rows x 32 tokens] (8 KB each), then per-row alpha, l, m.
 constexpr int kSubP = 128 * kTO * 2;             // 8192
 constexpr int kMsgP = kOPerS * kSubP;            // 24576
 constexpr int kMsgAlpha = kMsgP;
@@ -81,16 +77,16 @@ constexpr int kMsgM = kMsgP + 1024;
 constexpr int kMsgBytes = kMsgP + 1536;          // 26112
 constexpr int kMsgStride = 26 * 1024;
 constexpr int kMsgSlots = 3;                     // O-CTA receive ring
+constexpr int kStgSlots = 2;                     // S-CTA staging for outgoing copies
 
 constexpr int kRingSlots = kSlotsS > kSlotsO ? kSlotsS : kSlotsO;
 enum BarId {
-    kBarFull = 0,                      // [13] ring slot landed            (count 1 + tx)
-    kBarEmpty = kRingSlots,            // [13] ring slot consumed          (count 1, commit)
+    kBarFull = 0,                      // [4] ring slot landed            (count 1 + tx)
+    kBarEmpty = kRingSlots,            // [4] ring slot consumed          (count 1, commit)
     kBarSFull = 2 * kRingSlots,        // [2] S-CTA: S tile in TMEM        (count 1, commit)
     kBarSEmpty = kBarSFull + 2,        // [2] S-CTA: S tile read           (count 128)
     kBarQFree = kBarSEmpty + 2,        //     S-CTA: GEMM1s reading Q done (count 1, commit)
-    kBarQHi = kBarQFree + 1,           //     S-CTA: Q K-blocks 4-8 in smem (count 1 + tx)
-    kBarPFree = kBarQHi + 1,        // [3] GEMM2 done with message slot (count 1, commit arriving in both CTAs)
+    kBarPFree = kBarQFree + 1,        // [3] GEMM2 done with message slot (count 1, commit arriving in both CTAs)
     kBarPFull = kBarPFree + kMsgSlots, // [3] O-CTA: message landed        (count 1 + tx, from the S-CTA)
     kBarCorr = kBarPFull + kMsgSlots,  // [3] O-CTA: O ready for GEMM2     (count 128)
     kBarMmaDone = kBarCorr + kMsgSlots,// [3] O-CTA: GEMM2 of a message done (count 1, commit)
@@ -102,10 +98,9 @@ enum BarId {
 // own ring and message buffers; the barriers sit at the same offset in both
 // CTAs (remote arrivals and the two-CTA commit address them by offset).
 constexpr int kOffRing = 0;
-constexpr int kOffQS = kSlotsS * kSlotS;                         // 98304: Q K-blocks 4-8
-constexpr int kOffStgS = kOffQS + kKbSmem * kQBoxBytes;          // 180224: S staging
+constexpr int kOffStgS = kSlotsS * kSlotS;                       // 147456: S staging [2]
 constexpr int kOffMsgO = kSlotsO * kSlotO;                       // 131072: O receive ring [3]
-constexpr int kEndS = kOffStgS + kMsgStride;                     // 206848
+constexpr int kEndS = kOffStgS + kStgSlots * kMsgStride;         // 200704
 constexpr int kEndO = kOffMsgO + kMsgSlots * kMsgStride;         // 210944
 constexpr int kOffBar = kEndS > kEndO ? kEndS : kEndO;
 constexpr int kOffSlot = kOffBar + kNumBars * 8;
@@ -117,13 +112,12 @@ static_assert(kSmemBytes <= 232448, "dynamic shared memory limit");
 
 constexpr int kThreads = 256;
 constexpr uint32_t kTmemCols = 512;
-constexpr uint32_t kTmemQ = 0;     // S-CTA: Q K-blocks 0-3, 128 columns (2 fp16 per column)
-constexpr uint32_t kTmemS = kKbTmem * 32;  // S-CTA: two S buffers of kTG columns
-static_assert(kTmemS + 2 * kTG <= kTmemCols, "TMEM budget");
+constexpr uint32_t kTmemQ = 0;     // S-CTA: Q, 288 columns (2 fp16 per column)
+constexpr uint32_t kTmemS = 288;   // S-CTA: two S buffers of kTS columns
+static_assert(kTmemS + 2 * kTS <= kTmemCols, "TMEM budget");
 constexpr float kRescaleLog2 = 8.0f;
 
-constexpr uint32_t kIdescS = ptx::idesc_f16_f32(128, kTG, 0, 0);   // M=128 heads, N=192 tokens
-constexpr uint32_t kIdescS96 = ptx::idesc_f16_f32(128, kTS, 0, 0); // an item's last <= 96 tokens
+constexpr uint32_t kIdescS = ptx::idesc_f16_f32(128, kTS, 0, 0);   // M=128 heads, N=96 tokens
 constexpr uint32_t kIdescO = ptx::idesc_f16_f32(128, 256, 0, 1);   // M=128 heads, N=256 dims, B MN-major
 
 struct TcParams {
@@ -154,12 +148,10 @@ struct Ring {
     }
 };
 
-// cmap_s: cache [rows, 576], box 64 x 192 (cmap_s96: 64 x 96, for an item's
-// last S tile when at most 96 tokens remain).  cmap_o: same cache, box 64 x 32.
+// cmap_s: cache [rows, 576], box 64 x 96.  cmap_o: same cache, box 64 x 32.
 // qmap: query [B * n_h, 576], box 64 x 128.  All 128-byte swizzled.
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tc_decode_kernel(const __grid_constant__ CUtensorMap cmap_s,
-                     const __grid_constant__ CUtensorMap cmap_s96,
                      const __grid_constant__ CUtensorMap cmap_o,
                      const __grid_constant__ CUtensorMap qmap, const TcParams p) {
     extern __shared__ uint8_t smem_raw[];
@@ -191,17 +183,13 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             ptx::mbar_init(bar(kBarMmaDone + i), 1);
         }
         ptx::mbar_init(bar(kBarQFree), 1);
-        ptx::mbar_init(bar(kBarQHi), 1);
         ptx::mbar_init(bar(kBarDrain), 1);
         *abort_flag = 0;
         ptx::fence_mbarrier_init_cluster();
     }
     if (warp == 0 && lane == 0) {
         ptx::tma_prefetch_desc(role == 0 ? &cmap_s : &cmap_o);
-        if (role == 0) {
-            ptx::tma_prefetch_desc(&cmap_s96);
-            ptx::tma_prefetch_desc(&qmap);
-        }
+        if (role == 0) ptx::tma_prefetch_desc(&qmap);
     }
     if (warp == 2) {
         ptx::tmem_alloc(sbase + kOffSlot, kTmemCols);
@@ -220,7 +208,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int nslots = role == 0 ? kSlotsS : kSlotsO;
             Ring rg;
             int prev_b = -1;
-            uint32_t qphase = 0;
             bool ok = true;
             auto acquire = [&]() -> bool {
                 return !*abort_flag && ptx::mbar_wait(bar(kBarEmpty + rg.slot), rg.phase ^ 1, kErrWaitEmpty);
@@ -228,44 +215,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             for (int i = cid; ok && i < wl.max_items; i += ncl) {
                 const Item it = get_item(wl, i);
                 if (it.len <= 0) continue;
-                if (role == 0) {
-                    if (it.b != prev_b) {
-                        // Q of the new sequence: K-blocks 0-3 through the ring (one box
-                        // per slot), K-blocks 4-8 into their region once the previous
-                        // sequence's GEMM1s have read it.
-                        const int qrow = it.b * p.num_heads;
-                        for (int kb = 0; kb < kKbTmem; ++kb) {
+                if (role == 0 && it.b != prev_b) {
+                    // Q of the new sequence: two 128 x 64 boxes per ring slot
+                    const int qrow = it.b * p.num_heads;
+                    for (int kb = 0; kb < kKBlocks; kb += 2) {
+                        if (!acquire()) { ok = false; break; }
+                        const int nb = min(2, kKBlocks - kb);
+                        const uint32_t dst = sbase + kOffRing + rg.slot * kSlotS;
+                        ptx::mbar_arrive_expect_tx(bar(kBarFull + rg.slot), nb * kQBoxBytes);
+                        for (int j = 0; j < nb; ++j)
+                            ptx::tma_load_2d(dst + j * kQBoxBytes, &qmap, (kb + j) * 64, qrow, bar(kBarFull + rg.slot));
+                        rg.next(nslots);
+                    }
+                    prev_b = it.b;
+                }
+                for (int t0 = 0; ok && t0 < it.len; t0 += kTS) {
+                    const int row = (int)(it.row0 + t0);
+                    if (role == 0) {
+                        for (int sl = 0; sl < kSlotsPerTile; ++sl) {
                             if (!acquire()) { ok = false; break; }
-                            ptx::mbar_arrive_expect_tx(bar(kBarFull + rg.slot), kQBoxBytes);
-                            ptx::tma_load_2d(sbase + kOffRing + rg.slot * kSlotS, &qmap, kb * 64, qrow,
-                                             bar(kBarFull + rg.slot));
+                            const uint32_t dst = sbase + kOffRing + rg.slot * kSlotS;
+                            ptx::mbar_arrive_expect_tx(bar(kBarFull + rg.slot), kSlotS);
+                            for (int j = 0; j < kKbPerSlot; ++j)
+                                ptx::tma_load_2d(dst + j * kBoxS, &cmap_s, (sl * kKbPerSlot + j) * 64, row, bar(kBarFull + rg.slot));
                             rg.next(nslots);
                         }
-                        if (!ok) break;
-                        if (prev_b >= 0) {
-                            if (*abort_flag || !ptx::mbar_wait(bar(kBarQFree), qphase, kErrWaitMma)) { ok = false; break; }
-                            qphase ^= 1;
-                        }
-                        ptx::mbar_arrive_expect_tx(bar(kBarQHi), kKbSmem * kQBoxBytes);
-                        for (int j = 0; j < kKbSmem; ++j)
-                            ptx::tma_load_2d(sbase + kOffQS + j * kQBoxBytes, &qmap, (kKbTmem + j) * 64, qrow,
-                                             bar(kBarQHi));
-                        prev_b = it.b;
-                    }
-                    for (int t0 = 0; ok && t0 < it.len; t0 += kTG) {
-                        const int row = (int)(it.row0 + t0);
-                        const bool narrow = it.len - t0 <= kTS;  // a 96-row tile ends the item
-                        for (int kb = 0; kb < kKBlocks; ++kb) {
-                            if (!acquire()) { ok = false; break; }
-                            ptx::mbar_arrive_expect_tx(bar(kBarFull + rg.slot), narrow ? kSlotS / 2 : kSlotS);
-                            ptx::tma_load_2d(sbase + kOffRing + rg.slot * kSlotS, narrow ? &cmap_s96 : &cmap_s, kb * 64,
-                                             row, bar(kBarFull + rg.slot));
-                            rg.next(nslots);
-                        }
-                    }
-                } else {
-                    for (int t0 = 0; ok && t0 < it.len; t0 += kTS) {
-                        const int row = (int)(it.row0 + t0);
+                    } else {
                         const int nct = (min(kTS, it.len - t0) + kTO - 1) / kTO;
                         for (int ct = 0; ct < nct; ++ct) {
                             if (!acquire()) { ok = false; break; }
@@ -288,68 +263,60 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         if (lane == 0) {
             const int nslots = role == 0 ? kSlotsS : kSlotsO;
             Ring rg;
-            uint32_t jt = 0, st = 0, qphase = 0;
+            uint32_t jt = 0, qphase = 0;
             int prev_b = -1;
             bool ok = true;
             for (int i = cid; ok && i < wl.max_items; i += ncl) {
                 const Item it = get_item(wl, i);
                 if (it.len <= 0) continue;
-                if (role == 0) {
-                    if (it.b != prev_b) {
-                        // The previous sequence's GEMM1s read Q: they complete before the
-                        // copy overwrites its TMEM part (an MMA is not ordered before a later
-                        // tcgen05.cp) and before the producer reloads its shared part.
-                        if (prev_b >= 0) {
-                            ptx::mma_commit(bar(kBarQFree));
-                            if (!ptx::mbar_spin(bar(kBarQFree), (qphase - 1) & 1, kErrWaitMma)) { ok = false; break; }
-                        }
-                        for (int kb = 0; ok && kb < kKbTmem; ++kb) {
-                            if (*abort_flag || !ptx::mbar_spin(bar(kBarFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
-                            ptx::tc_fence_after();
-                            const uint32_t slot = sbase + kOffRing + rg.slot * kSlotS;
+                if (role == 0 && it.b != prev_b) {
+                    // The previous sequence's GEMM1s read Q from TMEM: they complete
+                    // before the copy overwrites it (an MMA is not ordered before a
+                    // later tcgen05.cp).
+                    if (prev_b >= 0) {
+                        ptx::mma_commit(bar(kBarQFree));
+                        if (!ptx::mbar_spin(bar(kBarQFree), qphase, kErrWaitMma)) { ok = false; break; }
+                        qphase ^= 1;
+                    }
+                    for (int kb = 0; ok && kb < kKBlocks; kb += 2) {
+                        if (*abort_flag || !ptx::mbar_spin(bar(kBarFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
+                        ptx::tc_fence_after();
+                        const uint32_t slot = sbase + kOffRing + rg.slot * kSlotS;
+                        const int nb = min(2, kKBlocks - kb);
+                        for (int j = 0; j < nb; ++j) {
 #pragma unroll
                             for (int c = 0; c < 4; ++c)
-                                ptx::tmem_cp_128x256b(tmem + kTmemQ + (kb * 4 + c) * 8,
-                                                      ptx::sdesc_sw128(slot + c * 32, 16, 1024));
-                            ptx::mma_commit(bar(kBarEmpty + rg.slot));
-                            rg.next(nslots);
+                                ptx::tmem_cp_128x256b(tmem + kTmemQ + ((kb + j) * 4 + c) * 8,
+                                                      ptx::sdesc_sw128(slot + j * kQBoxBytes + c * 32, 16, 1024));
                         }
-                        if (!ok) break;
-                        // Q K-blocks 4-8 in shared memory (qphase = sequences started so far)
-                        if (!ptx::mbar_spin(bar(kBarQHi), qphase & 1, kErrWaitFull)) { ok = false; break; }
-                        ptx::tc_fence_after();
-                        ++qphase;
-                        prev_b = it.b;
+                        ptx::mma_commit(bar(kBarEmpty + rg.slot));
+                        rg.next(nslots);
                     }
-                    for (int t0 = 0; ok && t0 < it.len; t0 += kTG, ++st) {
-                        const uint32_t sb = st & 1, use = st >> 1;
+                    if (!ok) break;
+                    prev_b = it.b;
+                }
+                for (int t0 = 0; ok && t0 < it.len; t0 += kTS, ++jt) {
+                    if (role == 0) {
+                        const uint32_t sb = jt & 1, use = jt >> 1;
                         if (*abort_flag || !ptx::mbar_spin(bar(kBarSEmpty + sb), (use & 1) ^ 1, kErrWaitMma)) { ok = false; break; }
-                        const uint32_t d = tmem + kTmemS + sb * kTG;
-                        const uint32_t idesc = it.len - t0 <= kTS ? kIdescS96 : kIdescS;
-                        for (int kb = 0; kb < kKBlocks; ++kb) {
+                        const uint32_t d = tmem + kTmemS + sb * kTS;
+                        for (int sl = 0; sl < kSlotsPerTile; ++sl) {
                             if (!ptx::mbar_spin(bar(kBarFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
                             ptx::tc_fence_after();
                             const uint32_t slot = sbase + kOffRing + rg.slot * kSlotS;
-                            if (kb < kKbTmem) {
 #pragma unroll
-                                for (int k = 0; k < 4; ++k)
-                                    ptx::mma_ts(d, tmem + kTmemQ + (kb * 4 + k) * 8,
-                                                ptx::sdesc_sw128(slot + k * 32, 16, 1024), idesc, (kb | k) != 0);
-                            } else {
-                                const uint32_t qs = sbase + kOffQS + (kb - kKbTmem) * kQBoxBytes;
-#pragma unroll
-                                for (int k = 0; k < 4; ++k)
-                                    ptx::mma_ss(d, ptx::sdesc_sw128(qs + k * 32, 16, 1024),
-                                                ptx::sdesc_sw128(slot + k * 32, 16, 1024), idesc, 1u);
+                            for (int k = 0; k < kKbPerSlot * 4; ++k) {
+                                const int kk = sl * kKbPerSlot * 4 + k;
+                                ptx::mma_ts(d, tmem + kTmemQ + kk * 8,
+                                            ptx::sdesc_sw128(slot + (k >> 2) * kBoxS + (k & 3) * 32, 16, 1024),
+                                            kIdescS, kk > 0);
                             }
                             ptx::mma_commit(bar(kBarEmpty + rg.slot));
                             rg.next(nslots);
                         }
                         if (!ok) break;
                         ptx::mma_commit(bar(kBarSFull + sb));
-                    }
-                } else {
-                    for (int t0 = 0; ok && t0 < it.len; t0 += kTS, ++jt) {
+                    } else {
                         const uint32_t ms = jt % kMsgSlots, mu = jt / kMsgSlots;
                         if (*abort_flag || !ptx::mbar_wait<true>(bar(kBarPFull + ms), mu & 1, kErrWaitPeer) ||
                             !ptx::mbar_spin(bar(kBarCorr + ms), mu & 1, kErrWaitMma)) { ok = false; break; }
@@ -393,104 +360,97 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             // ------------------------------------------------ S-CTA: softmax
             const uint32_t peer_pfull0 = ptx::mapa(bar(kBarPFull), 1);
             const uint32_t peer_msg0 = ptx::mapa(sbase + kOffMsgO, 1);
-            uint32_t st = 0;
             for (int i = cid; ok && i < wl.max_items; i += ncl) {
                 const Item it = get_item(wl, i);
                 if (it.len <= 0) continue;
                 float m_used = -INFINITY, l_run = 0.f;
-                for (int t0 = 0; ok && t0 < it.len; t0 += kTG, ++st) {
-                    const uint32_t sb = st & 1, use = st >> 1;
-                    const int nmsg = min(kMsgPerS, (it.len - t0 + kTS - 1) / kTS);
+                for (int t0 = 0; t0 < it.len; t0 += kTS, ++jt) {
+                    const uint32_t sb = jt & 1, use = jt >> 1;
+                    const uint32_t ms = jt % kMsgSlots, mu = jt / kMsgSlots, sg = jt % kStgSlots;
                     // Every decision below is made uniform across the warpgroup by the
-                    // bar.red at the end of each message, so an expired wait can never
-                    // split a warp at a .sync.aligned tcgen05 op or strand a named barrier.
+                    // bar.red at the end of the tile, so an expired wait can never split
+                    // a warp at a .sync.aligned tcgen05 op or strand a named barrier.
                     bool w = !*abort_flag && ptx::mbar_wait(bar(kBarSFull + sb), use & 1, kErrWaitMma);
                     w = __all_sync(0xffffffffu, w);
-                    for (int hm = 0; hm < nmsg; ++hm, ++jt) {
-                        const int t1 = t0 + hm * kTS;  // first token of this message tile
-                        const uint32_t ms = jt % kMsgSlots, mu = jt / kMsgSlots;
-                        float alpha = 1.f;
-                        const bool last = t1 + kTS >= it.len;
-                        uint32_t pk[kTS / 2];
-                        if (w) {
-                            ptx::tc_fence_after();
-                            uint32_t r[kTS];
-                            {
-                                const uint32_t sc = trow + kTmemS + sb * kTG + hm * kTS;
-                                uint32_t a[32], b[32], c[32];
-                                ptx::tmem_ld_x32(sc, a);
-                                ptx::tmem_ld_x32(sc + 32, b);
-                                ptx::tmem_ld_x32(sc + 64, c);
-                                ptx::tmem_wait_ld();
+                    float alpha = 1.f;
+                    const bool last = t0 + kTS >= it.len;
+                    uint32_t pk[kTS / 2];
+                    if (w) {
+                        ptx::tc_fence_after();
+                        uint32_t r[kTS];
+                        {
+                            uint32_t a[32], b[32], c[32];
+                            ptx::tmem_ld_x32(trow + kTmemS + sb * kTS, a);
+                            ptx::tmem_ld_x32(trow + kTmemS + sb * kTS + 32, b);
+                            ptx::tmem_ld_x32(trow + kTmemS + sb * kTS + 64, c);
+                            ptx::tmem_wait_ld();
 #pragma unroll
-                                for (int k = 0; k < 32; ++k) { r[k] = a[k]; r[32 + k] = b[k]; r[64 + k] = c[k]; }
-                            }
-                            if (hm == nmsg - 1) {  // the S buffer is read
-                                ptx::tc_fence_before();
-                                ptx::mbar_arrive(bar(kBarSEmpty + sb));
-                            }
+                            for (int k = 0; k < 32; ++k) { r[k] = a[k]; r[32 + k] = b[k]; r[64 + k] = c[k]; }
+                        }
+                        ptx::tc_fence_before();
+                        ptx::mbar_arrive(bar(kBarSEmpty + sb));
 
-                            // Row max of the raw logits (scale > 0 commutes with max), with
-                            // masked tail columns at -inf; 8 independent chains.
-                            const int valid = min(kTS, it.len - t1);
-                            if (valid < kTS) {
+                        // Row max of the raw logits (scale > 0 commutes with max), with
+                        // masked tail columns at -inf; 8 independent chains.
+                        const int valid = min(kTS, it.len - t0);
+                        if (valid < kTS) {
 #pragma unroll
-                                for (int k = 0; k < kTS; ++k)
-                                    if (k >= valid) r[k] = u32_of(-INFINITY);
-                            }
-                            float m8[8];
-#pragma unroll
-                            for (int j = 0; j < 8; ++j) m8[j] = f32_of(r[j]);
-#pragma unroll
-                            for (int k = 8; k < kTS; ++k) m8[k & 7] = fmaxf(m8[k & 7], f32_of(r[k]));
-                            const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                                                   fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * p.scale_log2;
-                            if (mx > m_used + kRescaleLog2) {
-                                alpha = (m_used == -INFINITY) ? 0.f : ptx::ex2(m_used - mx);
-                                m_used = mx;
-                            }
-                            // p = 2^(s * scale_log2 - m_used): one FFMA + one EX2 per logit.
-                            const float neg_m = -m_used;
-                            float s4[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                            for (int k = 0; k < kTS; k += 2) {
-                                const float p0 = ptx::ex2(fmaf(f32_of(r[k]), p.scale_log2, neg_m));
-                                const float p1 = ptx::ex2(fmaf(f32_of(r[k + 1]), p.scale_log2, neg_m));
-                                s4[(k >> 1) & 3] += p0 + p1;
-                                pk[k >> 1] = pack_half2(p0, p1);
-                            }
-                            l_run = l_run * alpha + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
-                            // the peer's message slot is free once GEMM2 of message jt-3 finished
-                            w = ptx::mbar_wait<true>(bar(kBarPFree + ms), (mu & 1) ^ 1, kErrWaitPeer);
+                            for (int k = 0; k < kTS; ++k)
+                                if (k >= valid) r[k] = u32_of(-INFINITY);
                         }
-                        // one staging buffer: the previous message's copy has finished reading it
-                        if (h == 0) ptx::bulk_wait_group_read<0>();
-                        ptx::named_barrier(1, 128);
-                        if (w) {
-                            uint8_t *msg = smem + kOffStgS;
+                        float m8[8];
 #pragma unroll
-                            for (int sub = 0; sub < kOPerS; ++sub) {
-                                uint4 *prow = reinterpret_cast<uint4 *>(msg + sub * kSubP + h * 64);  // SW64
+                        for (int j = 0; j < 8; ++j) m8[j] = f32_of(r[j]);
 #pragma unroll
-                                for (int c4 = 0; c4 < 4; ++c4) {
-                                    const int q = sub * 16 + c4 * 4;
-                                    prow[c4 ^ ((h >> 1) & 3)] = make_uint4(pk[q], pk[q + 1], pk[q + 2], pk[q + 3]);
-                                }
-                            }
-                            reinterpret_cast<float *>(msg + kMsgAlpha)[h] = alpha;
-                            if (last) {
-                                reinterpret_cast<float *>(msg + kMsgL)[h] = l_run;
-                                reinterpret_cast<float *>(msg + kMsgM)[h] = m_used;
-                            }
-                            ptx::fence_proxy_async_smem();
+                        for (int k = 8; k < kTS; ++k) m8[k & 7] = fmaxf(m8[k & 7], f32_of(r[k]));
+                        const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
+                                               fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * p.scale_log2;
+                        if (mx > m_used + kRescaleLog2) {
+                            alpha = (m_used == -INFINITY) ? 0.f : ptx::ex2(m_used - mx);
+                            m_used = mx;
                         }
-                        if (!ptx::named_barrier_and(1, 128, w)) { ok = false; break; }
-                        if (h == 0) {
-                            const uint32_t rbar = peer_pfull0 + 8u * ms;
-                            ptx::mbar_remote_arrive_expect_tx(rbar, kMsgBytes);
-                            ptx::bulk_copy_s2cluster(peer_msg0 + ms * kMsgStride, sbase + kOffStgS, kMsgBytes, rbar);
-                            ptx::bulk_commit_group();
+                        // p = 2^(s * scale_log2 - m_used): one FFMA + one EX2 per logit.
+                        const float neg_m = -m_used;
+                        float s4[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                        for (int k = 0; k < kTS; k += 2) {
+                            const float p0 = ptx::ex2(fmaf(f32_of(r[k]), p.scale_log2, neg_m));
+                            const float p1 = ptx::ex2(fmaf(f32_of(r[k + 1]), p.scale_log2, neg_m));
+                            s4[(k >> 1) & 3] += p0 + p1;
+                            pk[k >> 1] = pack_half2(p0, p1);
                         }
+                        l_run = l_run * alpha + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
+                        // the peer's message slot is free once GEMM2 of S tile jt-3 finished
+                        w = ptx::mbar_wait<true>(bar(kBarPFree + ms), (mu & 1) ^ 1, kErrWaitPeer);
+                    }
+                    if (w) {
+                        // staging slot sg: its previous copy (tile jt-2) finished reading
+                        // before the previous tile's bar.red (wait_group.read below)
+                        uint8_t *msg = smem + kOffStgS + sg * kMsgStride;
+#pragma unroll
+                        for (int st = 0; st < kOPerS; ++st) {
+                            uint4 *prow = reinterpret_cast<uint4 *>(msg + st * kSubP + h * 64);  // SW64
+#pragma unroll
+                            for (int c4 = 0; c4 < 4; ++c4) {
+                                const int q = st * 16 + c4 * 4;
+                                prow[c4 ^ ((h >> 1) & 3)] = make_uint4(pk[q], pk[q + 1], pk[q + 2], pk[q + 3]);
+                            }
+                        }
+                        reinterpret_cast<float *>(msg + kMsgAlpha)[h] = alpha;
+                        if (last) {
+                            reinterpret_cast<float *>(msg + kMsgL)[h] = l_run;
+                            reinterpret_cast<float *>(msg + kMsgM)[h] = m_used;
+                        }
+                        ptx::fence_proxy_async_smem();
+                    }
+                    if (h == 0) ptx::bulk_wait_group_read<0>();  // previous copy has read its staging
+                    if (!ptx::named_barrier_and(1, 128, w)) { ok = false; break; }
+                    if (h == 0) {
+                        const uint32_t rbar = peer_pfull0 + 8u * ms;
+                        ptx::mbar_remote_arrive_expect_tx(rbar, kMsgBytes);
+                        ptx::bulk_copy_s2cluster(peer_msg0 + ms * kMsgStride, sbase + kOffStgS + sg * kMsgStride,
+                                                 kMsgBytes, rbar);
+                        ptx::bulk_commit_group();
                     }
                 }
             }
