@@ -74,7 +74,9 @@ int current_device(int *dev_out, DevInfo *info_out) {
         d.simt_attr_set = true;
     }
     if (d.tc_clusters == 0) {
-        if (cudaFuncSetAttribute(tc::tc_decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(tc::tc_decode_kernel<kSchedChunked>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 tc::kSmemBytes) != cudaSuccess ||
+            cudaFuncSetAttribute(tc::tc_decode_kernel<kSchedBalanced>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  tc::kSmemBytes) != cudaSuccess) {
             return cuda_failure(cudaGetLastError());
         }
@@ -90,7 +92,7 @@ int current_device(int *dev_out, DevInfo *info_out) {
         cfg.attrs = &attr;
         cfg.numAttrs = 1;
         int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, tc::tc_decode_kernel, &cfg) != cudaSuccess || n <= 0) {
+        if (cudaOccupancyMaxActiveClusters(&n, tc::tc_decode_kernel<kSchedChunked>, &cfg) != cudaSuccess || n <= 0) {
             cudaGetLastError();
             n = d.sms / 2;
         }
@@ -136,11 +138,13 @@ inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
 inline long long cdiv(long long a, long long b) { return (a + b - 1) / b; }
 
 // Split plan: rows per work item.  `units` is the number of workers one wave
-// of the decode kernel has; the chunk is the smallest multiple of kTile that
-// gives every worker at most one item, but never longer than a sequence.
+// of the decode kernel has; the chunk is an even share of the batch's tiles
+// plus the fixed per-item cost (the balanced schedule's quota, mla_common.cuh),
+// but never longer than a sequence.
 int plan_chunk(int batch, long long total_tokens, int max_seq_len, int num_sms) {
     const long long units = num_sms > 1 ? num_sms / 2 : 1;  // 2-CTA clusters per wave
-    long long chunk = cdiv(cdiv(total_tokens > 0 ? total_tokens : 1, units), kTile) * kTile;
+    const long long cost = cdiv(total_tokens > 0 ? total_tokens : 1, kTile) + (long long)kItemCost * (batch > 0 ? batch : 1);
+    long long chunk = cdiv(cost, units) * kTile;
     if (chunk < kTile) chunk = kTile;
     if (max_seq_len > 0) {
         const long long cap = cdiv(max_seq_len, kTile) * kTile;
@@ -226,16 +230,51 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     if (st != MLA_B200_OK) return st;
     if (batch == 0) return MLA_B200_OK;
 
+    // The tensor-core kernel with an automatic split runs the balanced schedule
+    // (every cluster gets an equal share of the batch's tiles); explicit split
+    // counts and the SIMT kernels use fixed-size chunks.
+    const bool tc_path = std::is_same<T, __half>::value && num_heads <= 128;
+    // (A single sequence splits evenly in the chunked schedule already.)
+    const bool balanced = tc_path && num_splits <= 0 && batch > 1;
     const int chunk = chunk_for(batch, total_tokens, max_seq_len, num_splits, info.sms);
-    const long long max_items = max_items_for(batch, total_tokens, chunk);
+    const long long max_items = balanced ? (long long)batch + info.tc_clusters
+                                         : max_items_for(batch, total_tokens, chunk);
     if (max_items > (1LL << 30)) return MLA_B200_ERR_UNSUPPORTED;
     WsLayout L = ws_layout(workspace, max_items, num_heads, batch);
     if (workspace == nullptr || workspace_bytes < L.bytes) return MLA_B200_ERR_WORKSPACE;
 
-    WorkList wl;
+    WorkList wl = {};
     wl.batch = batch;
-    wl.chunk = chunk;
-    if (cu_seqlens == nullptr) {
+    wl.chunk = balanced ? 0 : chunk;
+    int bal_clusters = 0;      // balanced: clusters to launch
+    bool bal_split = true;     // balanced: some sequence has more than one item
+    if (balanced) {
+        wl.max_items = (int)max_items;
+        if (cu_seqlens == nullptr) {
+            wl.seq_len = max_seq_len;
+            const long long tiles = cdiv(max_seq_len, kTile);
+            const long long cost = tiles > 0 ? tiles + kItemCost : 0;
+            const long long total = (long long)batch * cost;
+            if (total >= (1LL << 31)) return MLA_B200_ERR_UNSUPPORTED;
+            const long long q = std::max(1LL, cdiv(total, info.tc_clusters));
+            wl.quota = (int)q;
+            bal_clusters = total > 0 ? (int)cdiv(total, q) : 0;
+            bal_split = total == 0;  // empty sequences get their zeros from the combine
+            for (long long b = 0; b < batch && tiles > 0; ++b) {
+                const long long base = b * cost + kItemCost;
+                if (base / q != (base + tiles - 1) / q) {
+                    bal_split = true;
+                    break;
+                }
+            }
+        } else {
+            wl.cost_off = L.item_off;
+            wl.cu_seqlens = cu_seqlens;
+            wl.nworkers = info.tc_clusters;
+            bal_clusters = info.tc_clusters;
+            plan_balanced_kernel<<<1, 1024, 0, stream>>>(cu_seqlens, batch, L.item_off);
+        }
+    } else if (cu_seqlens == nullptr) {
         wl.items = nullptr;
         wl.item_off = nullptr;
         wl.seq_len = max_seq_len;
@@ -251,8 +290,8 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
                                                    (int)max_items);
     }
     bool tc_direct = false;  // the tcgen05 kernel wrote single-item sequences itself
-    if (wl.max_items > 0) {
-        if (std::is_same<T, __half>::value && num_heads <= 128) {
+    if (wl.max_items > 0 && (!balanced || bal_clusters > 0)) {
+        if (tc_path) {
             CUtensorMap cmap_s, cmap_o, qmap;
             st = make_tmap_576(&cmap_s, cache, total_tokens, tc::kTS);
             if (st == MLA_B200_OK) st = make_tmap_576(&cmap_o, cache, total_tokens, tc::kTO);
@@ -269,9 +308,12 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
             tp.out_f16 = out_dtype == MLA_B200_OUT_F16 ? 1 : 0;
             tp.out_lse = out_lse;
             tc_direct = true;
-            const int clusters = std::min(info.tc_clusters, wl.max_items);
+            const int clusters = balanced ? bal_clusters : std::min(info.tc_clusters, wl.max_items);
             timing_mark(t_ev_start, stream);
-            tc::tc_decode_kernel<<<2 * clusters, tc::kThreads, tc::kSmemBytes, stream>>>(cmap_s, cmap_o, qmap, tp);
+            if (balanced)
+                tc::tc_decode_kernel<kSchedBalanced><<<2 * clusters, tc::kThreads, tc::kSmemBytes, stream>>>(cmap_s, cmap_o, qmap, tp);
+            else
+                tc::tc_decode_kernel<kSchedChunked><<<2 * clusters, tc::kThreads, tc::kSmemBytes, stream>>>(cmap_s, cmap_o, qmap, tp);
             timing_mark(t_ev_stop, stream);
         } else {
             dim3 grid(wl.max_items, (unsigned)cdiv(num_heads, kSimtHeads));
@@ -281,8 +323,8 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
             timing_mark(t_ev_stop, stream);
         }
     }
-    // A dense batch split into one item per sequence is complete already.
-    if (tc_direct && cu_seqlens == nullptr && wl.cps == 1) return launch_status();
+    // A dense batch decoded as one item per sequence is complete already.
+    if (tc_direct && cu_seqlens == nullptr && (balanced ? !bal_split : wl.cps == 1)) return launch_status();
     const long long rows = (long long)batch * num_heads;
     const unsigned cgrid = (unsigned)rows;
     const int skip = tc_direct ? 1 : 0;
@@ -377,7 +419,9 @@ size_t mla_b200_workspace_size(int batch, int num_heads, long long total_tokens,
     }
     if (max_seq_len <= 0 && batch > 0) max_seq_len = (int)cdiv(total_tokens, batch);
     const int chunk = chunk_for(batch, total_tokens, max_seq_len, num_splits, num_sms);
-    const long long max_items = max_items_for(batch, total_tokens, chunk);
+    long long max_items = max_items_for(batch, total_tokens, chunk);
+    // an automatic split may run the balanced schedule: batch + one item per cluster
+    if (num_splits <= 0) max_items = std::max(max_items, (long long)batch + std::max(1, num_sms / 2));
     return ws_layout(nullptr, max_items, num_heads, batch).bytes;
 }
 

@@ -199,4 +199,48 @@ __global__ void __launch_bounds__(1024) plan_varlen_kernel(const int32_t *__rest
     if (tid == 0) item_off[batch] = min(carry_s, max_items);
 }
 
+// Balanced schedule, varlen: cost_off[b] = sum over b' < b of the cost of
+// sequence b' (kItemCost + its 96-row tiles, 0 for an empty sequence), and
+// cost_off[B] the total.  One block; a block-wide scan per 1024 sequences.
+__global__ void __launch_bounds__(1024) plan_balanced_kernel(const int32_t *__restrict__ cu_seqlens,
+                                                             int batch, int *__restrict__ cost_off) {
+    __shared__ int warp_tot[32];
+    __shared__ int carry_s;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) carry_s = 0;
+    __syncthreads();
+    for (int base = 0; base < batch; base += 1024) {
+        const int b = base + tid;
+        int cost = 0;
+        if (b < batch) {
+            const int len = cu_seqlens[b + 1] - cu_seqlens[b];
+            cost = len > 0 ? (len + kTile - 1) / kTile + kItemCost : 0;
+        }
+        int v = cost;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int n = __shfl_up_sync(0xffffffffu, v, o);
+            if (lane >= o) v += n;
+        }
+        if (lane == 31) warp_tot[warp] = v;
+        __syncthreads();
+        if (warp == 0) {
+            int w = warp_tot[lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int n = __shfl_up_sync(0xffffffffu, w, o);
+                if (lane >= o) w += n;
+            }
+            warp_tot[lane] = w;
+        }
+        __syncthreads();
+        const int excl = carry_s + (warp > 0 ? warp_tot[warp - 1] : 0) + v - cost;
+        if (b < batch) cost_off[b] = excl;
+        __syncthreads();
+        if (tid == 1023) carry_s = excl + cost;
+        __syncthreads();
+    }
+    if (tid == 0) cost_off[batch] = carry_s;
+}
+
 }  // namespace mla

@@ -19,25 +19,49 @@ constexpr float kLn2 = 0.6931471805599453f;
 // ---------------------------------------------------------------------------
 // Split work list.
 //
-// A work item is a contiguous run of at most `chunk` cache rows of ONE
-// sequence.  Items of sequence b are numbered consecutively; item i writes
-// partial i (normalized O and its log-sum-exp) and the combine kernel merges
-// the partials of each sequence.
+// A work item is a contiguous run of cache rows of ONE sequence, decoded by
+// one worker (a 2-CTA cluster of the tensor-core kernel, or one SIMT block);
+// item i writes partial i (normalized O and its log-sum-exp) and the combine
+// kernel merges the partials of each sequence.  Two schedules:
 //
-//  dense  (items == nullptr): every sequence has seq_len rows at stride
-//         seq_len; sequence b owns items [b*cps, (b+1)*cps).
-//  varlen (items != nullptr): a plan kernel expanded cu_seqlens into
-//         items[] = {b, row_begin, row_end, 0} and item_off[B+1]; launches are
-//         sized for max_items and items >= item_off[B] are empty.
+// Chunked (chunk > 0): items of at most `chunk` rows, numbered consecutively
+//   per sequence, dealt to the workers round-robin (explicit split counts and
+//   the SIMT kernels).
+//    dense  (items == nullptr): every sequence has seq_len rows at stride
+//           seq_len; sequence b owns items [b*cps, (b+1)*cps).
+//    varlen (items != nullptr): a plan kernel expanded cu_seqlens into
+//           items[] = {b, row_begin, row_end, 0} and item_off[B+1]; launches
+//           are sized for max_items and items >= item_off[B] are empty.
+//
+// Balanced (chunk == 0, tensor-core kernel with an automatic split): the
+//   batch is laid out on a cost line.  Sequence b occupies the interval
+//   [cost0_b, cost0_b + kItemCost + tiles_b): kItemCost units stand for the
+//   fixed cost of a work item (Q load, epilogue), then one unit per 96-row
+//   tile.  Worker c owns the units [c*quota, (c+1)*quota) and decodes, as one
+//   item, the tiles of each sequence that fall into its units.  So every
+//   worker gets the same work, whatever the lengths, and a sequence is split
+//   only where a worker's share ends.  The item of (sequence b, worker c) has
+//   id b + c: the ids of one sequence are consecutive and all ids are below
+//   batch + workers (some ids stay unused).
+//    dense : cost0_b = b * (kItemCost + tiles), quota given by the host.
+//    varlen: cost0_b = cost_off[b] (prefix computed by plan_balanced_kernel),
+//            quota = ceil(cost_off[B] / nworkers), derived on the device.
 // ---------------------------------------------------------------------------
+constexpr int kItemCost = 2;  // fixed cost of one work item, in 96-row tiles
+
 struct WorkList {
     const int4 *items;
     const int *item_off;
     int batch;
     int seq_len;   // dense only
-    int chunk;     // rows per item (a multiple of kTile when planned)
-    int cps;       // dense: chunks per sequence
-    int max_items; // launch bound
+    int chunk;     // chunked: rows per item (a multiple of kTile when planned); 0 = balanced
+    int cps;       // chunked dense: chunks per sequence
+    int max_items; // chunked: launch bound; balanced: batch + nworkers
+    // balanced schedule
+    const int *cost_off;        // varlen: [batch + 1] cost prefix (device)
+    const int32_t *cu_seqlens;  // varlen: row offsets [batch + 1]
+    int quota;                  // dense: cost units per worker
+    int nworkers;               // varlen: workers the cost line is divided among
 };
 
 struct Item {
@@ -72,8 +96,136 @@ __device__ __forceinline__ Item get_item(const WorkList &w, int i) {
     return it;
 }
 
+// Balanced schedule: one sequence's place on the cost line.
+struct SeqSpan {
+    int cost0;       // first cost unit
+    int tiles;       // 96-row tiles (its units after the kItemCost fixed ones)
+    long long row0;  // first cache row
+    int len;         // rows
+};
+
+__device__ __forceinline__ SeqSpan seq_span(const WorkList &w, int b) {
+    SeqSpan s;
+    if (w.cost_off == nullptr) {
+        s.len = w.seq_len;
+        s.tiles = (w.seq_len + kTile - 1) / kTile;
+        s.cost0 = b * (s.tiles > 0 ? s.tiles + kItemCost : 0);
+        s.row0 = (long long)b * w.seq_len;
+    } else {
+        s.cost0 = w.cost_off[b];
+        s.row0 = w.cu_seqlens[b];
+        s.len = w.cu_seqlens[b + 1] - w.cu_seqlens[b];
+        s.tiles = (s.len + kTile - 1) / kTile;
+    }
+    return s;
+}
+
+__device__ __forceinline__ int bal_total(const WorkList &w) {
+    if (w.cost_off == nullptr) {
+        const int t = (w.seq_len + kTile - 1) / kTile;
+        return w.batch * (t > 0 ? t + kItemCost : 0);
+    }
+    return w.cost_off[w.batch];
+}
+
+__device__ __forceinline__ int bal_quota(const WorkList &w) {
+    if (w.cost_off == nullptr) return w.quota;
+    const int n = max(w.nworkers, 1);
+    return max(1, (w.cost_off[w.batch] + n - 1) / n);
+}
+
+// The sequence whose cost interval contains unit x (x < total).
+__device__ __forceinline__ int bal_seq_at(const WorkList &w, int x) {
+    if (w.cost_off == nullptr) {
+        const int t = (w.seq_len + kTile - 1) / kTile;
+        return x / (t + kItemCost);
+    }
+    int lo = 0, hi = w.batch - 1;  // largest b with cost_off[b] <= x
+    while (lo < hi) {
+        const int mid = (lo + hi + 1) >> 1;
+        if (w.cost_off[mid] <= x) lo = mid; else hi = mid - 1;
+    }
+    return lo;
+}
+
+// Which schedule a kernel is compiled for: a kernel instantiated for one of
+// them carries no code (and no registers) for the other.
+enum SchedKind : int { kSchedAny = 0, kSchedChunked = 1, kSchedBalanced = 2 };
+
+// Walks the items of worker `wid` in order.
+struct ItemCursor {
+    int next;    // chunked: next item index; balanced: next sequence
+    int step;    // chunked: worker count
+    int wid;     // balanced: this worker
+    int x0, x1;  // balanced: this worker's cost units
+};
+
+template <int kSched = kSchedAny>
+__device__ __forceinline__ ItemCursor items_begin(const WorkList &w, int wid, int nworkers) {
+    ItemCursor c;
+    c.wid = wid;
+    c.step = nworkers;
+    if (kSched == kSchedChunked || (kSched == kSchedAny && w.chunk > 0)) {
+        c.next = wid;
+        c.x0 = c.x1 = 0;
+    } else {
+        const int q = bal_quota(w), total = bal_total(w);
+        c.x0 = min(wid * q, total);
+        c.x1 = min(c.x0 + q, total);
+        c.next = c.x0 < c.x1 ? bal_seq_at(w, c.x0) : w.batch;
+    }
+    return c;
+}
+
+// Next non-empty item of the cursor's worker: its id and rows.  False when done.
+template <int kSched = kSchedAny>
+__device__ __forceinline__ bool items_next(const WorkList &w, ItemCursor &c, Item &it, int &id) {
+    if constexpr (kSched != kSchedBalanced) {
+        if (kSched == kSchedChunked || w.chunk > 0) {
+            while (c.next < w.max_items) {
+                id = c.next;
+                it = get_item(w, id);
+                c.next += c.step;
+                if (it.len > 0) return true;
+            }
+            return false;
+        }
+    }
+    if constexpr (kSched != kSchedChunked) {
+        while (c.next < w.batch) {
+            const int b = c.next++;
+            const SeqSpan s = seq_span(w, b);
+            if (s.cost0 >= c.x1) {
+                c.next = w.batch;
+                return false;
+            }
+            const int base = s.cost0 + kItemCost;  // cost unit of tile 0
+            const int lo = max(c.x0 - base, 0), hi = min(c.x1 - base, s.tiles);
+            if (hi <= lo) continue;
+            id = b + c.wid;
+            it.b = b;
+            it.row0 = s.row0 + (long long)lo * kTile;
+            it.len = min(hi * kTile, s.len) - lo * kTile;
+            return true;
+        }
+    }
+    return false;
+}
+
+// Ids [i0, i1) of the items of sequence b (its partials, for the combine).
+template <int kSched = kSchedAny>
 __device__ __forceinline__ void item_range(const WorkList &w, int b, int &i0, int &i1) {
-    if (w.items == nullptr) {
+    if (kSched == kSchedBalanced || (kSched == kSchedAny && w.chunk == 0)) {
+        const SeqSpan s = seq_span(w, b);
+        if (s.tiles <= 0) {
+            i0 = i1 = 0;
+            return;
+        }
+        const int q = bal_quota(w);
+        const int base = s.cost0 + kItemCost;
+        i0 = b + base / q;
+        i1 = b + (base + s.tiles - 1) / q + 1;
+    } else if (w.items == nullptr) {
         i0 = b * w.cps;
         i1 = i0 + (w.seq_len > 0 ? w.cps : 0);
     } else {

@@ -150,6 +150,10 @@ struct Ring {
 
 // cmap_s: cache [rows, 576], box 64 x 96.  cmap_o: same cache, box 64 x 32.
 // qmap: query [B * n_h, 576], box 64 x 128.  All 128-byte swizzled.
+// kSched: the work-list schedule this instantiation serves (kSchedChunked or
+// kSchedBalanced); the other schedule's iteration code would cost registers in
+// every role.
+template <int kSched>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tc_decode_kernel(const __grid_constant__ CUtensorMap cmap_s,
                      const __grid_constant__ CUtensorMap cmap_o,
@@ -212,9 +216,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             auto acquire = [&]() -> bool {
                 return !*abort_flag && ptx::mbar_wait(bar(kBarEmpty + rg.slot), rg.phase ^ 1, kErrWaitEmpty);
             };
-            for (int i = cid; ok && i < wl.max_items; i += ncl) {
-                const Item it = get_item(wl, i);
-                if (it.len <= 0) continue;
+            ItemCursor cur = items_begin<kSched>(wl, cid, ncl);
+            Item it;
+            int i;
+            while (ok && items_next<kSched>(wl, cur, it, i)) {
                 if (role == 0 && it.b != prev_b) {
                     // Q of the new sequence: two 128 x 64 boxes per ring slot
                     const int qrow = it.b * p.num_heads;
@@ -266,9 +271,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             uint32_t jt = 0, qphase = 0;
             int prev_b = -1;
             bool ok = true;
-            for (int i = cid; ok && i < wl.max_items; i += ncl) {
-                const Item it = get_item(wl, i);
-                if (it.len <= 0) continue;
+            ItemCursor cur = items_begin<kSched>(wl, cid, ncl);
+            Item it;
+            int i;
+            while (ok && items_next<kSched>(wl, cur, it, i)) {
                 if (role == 0 && it.b != prev_b) {
                     // The previous sequence's GEMM1s read Q from TMEM: they complete
                     // before the copy overwrites it (an MMA is not ordered before a
@@ -360,9 +366,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             // ------------------------------------------------ S-CTA: softmax
             const uint32_t peer_pfull0 = ptx::mapa(bar(kBarPFull), 1);
             const uint32_t peer_msg0 = ptx::mapa(sbase + kOffMsgO, 1);
-            for (int i = cid; ok && i < wl.max_items; i += ncl) {
-                const Item it = get_item(wl, i);
-                if (it.len <= 0) continue;
+            ItemCursor cur = items_begin<kSched>(wl, cid, ncl);
+            Item it;
+            int i;
+            while (ok && items_next<kSched>(wl, cur, it, i)) {
                 float m_used = -INFINITY, l_run = 0.f;
                 for (int t0 = 0; t0 < it.len; t0 += kTS, ++jt) {
                     const uint32_t sb = jt & 1, use = jt >> 1;
@@ -470,9 +477,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             auto gemm2_done = [&](uint32_t x) -> bool {
                 return ptx::mbar_wait(bar(kBarMmaDone + x % kMsgSlots), (x / kMsgSlots) & 1, kErrWaitMma);
             };
-            for (int i = cid; ok && i < wl.max_items; i += ncl) {
-                const Item it = get_item(wl, i);
-                if (it.len <= 0) continue;
+            ItemCursor cur = items_begin<kSched>(wl, cid, ncl);
+            Item it;
+            int i;
+            while (ok && items_next<kSched>(wl, cur, it, i)) {
                 for (int t0 = 0; t0 < it.len; t0 += kTS, ++jt) {
                     const uint32_t ms = jt % kMsgSlots, mu = jt / kMsgSlots;
                     // As in the S-CTA, every branch is warpgroup-uniform (bar.red).
@@ -510,7 +518,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         // A sequence covered by this one item gets its final output here;
                         // otherwise the item's partial goes to the workspace for the combine.
                         int ni0, ni1;
-                        item_range(wl, it.b, ni0, ni1);
+                        item_range<kSched>(wl, it.b, ni0, ni1);
                         const bool single = ni1 - ni0 == 1;
                         const float inv_l = l_fin > 0.f ? 1.f / l_fin : 0.f;
                         const float lse = l_fin > 0.f ? (m_fin + __log2f(l_fin)) * kLn2 : -INFINITY;

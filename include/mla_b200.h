@@ -101,7 +101,14 @@ MLA_B200_API int mla_b200_set_kernel_timing(void *ev_start, void *ev_stop);
  * (one work item) covers so that the items fill `num_sms` SMs (0 = the current
  * device's count) while keeping the split-partial traffic small.  Writes the
  * chunk length (a multiple of 96 tokens, the kernel's tile) to *chunk_tokens and, for a single
- * sequence, the resulting split count to *num_splits (either may be NULL). */
+ * sequence, the resulting split count to *num_splits (either may be NULL).
+ *
+ * This is the schedule of an automatic split of one sequence.  For a batch
+ * of several sequences on the fp16 tensor-core path the decode entry points
+ * balance the work instead: the batch's 96-row tiles plus a fixed cost per
+ * work item are divided evenly among the resident clusters, a sequence being
+ * split only where a cluster's share ends; *chunk_tokens is then that share
+ * (in tokens, capped at the longest sequence). */
 MLA_B200_API int mla_b200_plan(int batch, int num_heads, long long total_tokens, int max_seq_len,
                                int num_sms, int *chunk_tokens, int *num_splits);
 

@@ -186,3 +186,48 @@ def test_errors_raise(mla):
         mla.mla_decode_split(q.cuda(), c)  # cache on the host
     with pytest.raises(RuntimeError):
         mla.mla_decode_fused(q.cuda(), c.cuda())  # fp16 into the fp32 kernel name
+
+
+@pytest.mark.parametrize("nh", [128, 16])
+def test_balanced_schedule_varlen(mla, nh):
+    """Automatic split of a mixed-length batch: the balanced schedule cuts sequences
+    wherever a cluster's share ends (and skips empty ones); every sequence must
+    still match the oracle."""
+    rng = np.random.default_rng(21 + nh)
+    lens = [int(x) for x in rng.integers(1, 1500, size=61)]
+    lens[5] = 0
+    lens[17] = 96
+    lens[40] = 97
+    g = torch.Generator().manual_seed(22)
+    q = (torch.randn(len(lens), nh, 576, generator=g) / np.sqrt(192)).half()
+    c = torch.randn(sum(lens), 576, generator=g).half()
+    cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32)
+    out, lse = mla.mla_decode_batched(q.cuda(), c.cuda(), cu.cuda(), max_seq_len=max(lens),
+                                      softmax_scale=1.0, return_lse=True)
+    torch.cuda.synchronize()
+    lo = 0
+    for i, n in enumerate(lens):
+        if n == 0:
+            assert torch.count_nonzero(out[i]).item() == 0
+        else:
+            ref = oracle.mla_decode_oracle(_np(q[i]), _np(c[lo:lo + n]), 1.0, threads=8)
+            assert_close_parity(_np(out[i]), ref, what=f"balanced varlen b={i} n={n}")
+            if i % 10 == 0:
+                _, ref_lse = oracle.lse_partial_oracle(_np(q[i]), _np(c[lo:lo + n]), 1.0)
+                np.testing.assert_allclose(_np(lse[i]), ref_lse, atol=2e-3, rtol=0)
+        lo += n
+    _no_device_error(mla)
+
+
+@pytest.mark.parametrize("b,n", [(37, 500), (3, 9000), (200, 96)])
+def test_balanced_schedule_dense(mla, b, n):
+    nh = 128
+    g = torch.Generator().manual_seed(b + n)
+    q = (torch.randn(b, nh, 576, generator=g) / np.sqrt(192)).half()
+    c = torch.randn(b, n, 576, generator=g).half()
+    out = mla.mla_decode_batched(q.cuda(), c.cuda(), softmax_scale=1.0)
+    torch.cuda.synchronize()
+    for i in range(0, b, max(1, b // 12)):
+        ref = oracle.mla_decode_oracle(_np(q[i]), _np(c[i]), 1.0, threads=8)
+        assert_close_parity(_np(out[i]), ref, what=f"balanced dense b={i}")
+    _no_device_error(mla)
