@@ -283,10 +283,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         ptx::mma_commit(bar(kBarQFree));
                         if (!ptx::mbar_spin(bar(kBarQFree), qphase, kErrWaitMma)) { ok = false; break; }
                         qphase ^= 1;
+                        ptx::tc_fence_after();
                     }
+                    // Ring slots filled by TMA need no tcgen05 fence: the full barrier's
+                    // complete_tx orders the loaded bytes before the copy / MMA reads
+                    // them.  (A fence stalls this thread until the tensor pipe drains,
+                    // ~230 cycles: per slot that cost a quarter of the N=96 MMA rate.)
                     for (int kb = 0; ok && kb < kKBlocks; kb += 2) {
                         if (*abort_flag || !ptx::mbar_spin(bar(kBarFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
-                        ptx::tc_fence_after();
                         const uint32_t slot = sbase + kOffRing + rg.slot * kSlotS;
                         const int nb = min(2, kKBlocks - kb);
                         for (int j = 0; j < nb; ++j) {
@@ -305,18 +309,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     if (role == 0) {
                         const uint32_t sb = jt & 1, use = jt >> 1;
                         if (*abort_flag || !ptx::mbar_spin(bar(kBarSEmpty + sb), (use & 1) ^ 1, kErrWaitMma)) { ok = false; break; }
+                        ptx::tc_fence_after();  // the softmax's loads of this S buffer come first
                         const uint32_t d = tmem + kTmemS + sb * kTS;
                         for (int sl = 0; sl < kSlotsPerTile; ++sl) {
                             if (!ptx::mbar_spin(bar(kBarFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
-                            ptx::tc_fence_after();
-                            const uint32_t slot = sbase + kOffRing + rg.slot * kSlotS;
+                            // descriptor of the slot, plus compile-time offsets per K-step: a
+                            // short issue sequence between MMAs keeps the N=96 tensor rate
+                            const uint64_t b0 = ptx::sdesc_sw128(sbase + kOffRing + rg.slot * kSlotS, 16, 1024);
+                            const uint32_t a0 = tmem + kTmemQ + sl * (kKbPerSlot * 32);
+                            const uint32_t acc0 = sl > 0 ? 1u : 0u;
 #pragma unroll
-                            for (int k = 0; k < kKbPerSlot * 4; ++k) {
-                                const int kk = sl * kKbPerSlot * 4 + k;
-                                ptx::mma_ts(d, tmem + kTmemQ + kk * 8,
-                                            ptx::sdesc_sw128(slot + (k >> 2) * kBoxS + (k & 3) * 32, 16, 1024),
-                                            kIdescS, kk > 0);
-                            }
+                            for (int k = 0; k < kKbPerSlot * 4; ++k)
+                                ptx::mma_ts(d, a0 + k * 8, b0 + (uint64_t)(((k >> 2) * kBoxS + (k & 3) * 32) >> 4),
+                                            kIdescS, k > 0 ? 1u : acc0);
                             ptx::mma_commit(bar(kBarEmpty + rg.slot));
                             rg.next(nslots);
                         }
@@ -326,20 +331,21 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         const uint32_t ms = jt % kMsgSlots, mu = jt / kMsgSlots;
                         if (*abort_flag || !ptx::mbar_wait<true>(bar(kBarPFull + ms), mu & 1, kErrWaitPeer) ||
                             !ptx::mbar_spin(bar(kBarCorr + ms), mu & 1, kErrWaitMma)) { ok = false; break; }
-                        const uint32_t msg = sbase + kOffMsgO + ms * kMsgStride;
+                        ptx::tc_fence_after();  // the correction's TMEM stores to O come first
+                        const uint64_t p0 = ptx::sdesc_sw64(sbase + kOffMsgO + ms * kMsgStride, 16, 512);
                         const int nct = (min(kTS, it.len - t0) + kTO - 1) / kTO;
                         for (int ct = 0; ct < nct; ++ct) {
                             if (!ptx::mbar_spin(bar(kBarFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
-                            ptx::tc_fence_after();
-                            const uint32_t cst = sbase + kOffRing + rg.slot * kSlotO;
+                            const uint64_t c0 = ptx::sdesc_sw128(sbase + kOffRing + rg.slot * kSlotO, kBoxO, 1024);
+                            const uint64_t pa = p0 + (uint64_t)(ct * (kSubP >> 4));
+                            const uint32_t acc0 = (t0 > 0 || ct > 0) ? 1u : 0u;
 #pragma unroll
                             for (int kk = 0; kk < kTO / 16; ++kk) {
-                                const uint64_t adesc = ptx::sdesc_sw64(msg + ct * kSubP + kk * 32, 16, 512);
 #pragma unroll
-                                for (int nh = 0; nh < 2; ++nh) {
-                                    const uint64_t bdesc = ptx::sdesc_sw128(cst + nh * 4 * kBoxO + kk * 16 * 128, kBoxO, 1024);
-                                    ptx::mma_ss(tmem + nh * 256, adesc, bdesc, kIdescO, (t0 > 0 || ct > 0 || kk > 0) ? 1u : 0u);
-                                }
+                                for (int nh = 0; nh < 2; ++nh)
+                                    ptx::mma_ss(tmem + nh * 256, pa + (uint64_t)((kk * 32) >> 4),
+                                                c0 + (uint64_t)((nh * 4 * kBoxO + kk * 16 * 128) >> 4), kIdescO,
+                                                kk > 0 ? 1u : acc0);
                             }
                             ptx::mma_commit(bar(kBarEmpty + rg.slot));
                             rg.next(nslots);
