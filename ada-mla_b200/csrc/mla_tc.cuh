@@ -65,6 +65,7 @@ constexpr int kBoxO = kTO * 128;                 // 4096: [32 tok x 64 col]
 constexpr int kSlotO = kVBlocks * kBoxO;         // 32768: C tile [32 x 512]
 constexpr int kSlotsO = 4;
 constexpr int kQBoxBytes = 128 * 128;            // Q box: 128 rows x 64 fp16
+constexpr int kQSlots = (kKBlocks + 1) / 2;      // 5 ring slots carry Q (two boxes each)
 static_assert(2 * kQBoxBytes <= kSlotS, "two Q boxes per ring slot");
 
 // Message S-CTA -> O-CTA, one per S tile: P as three SW64 K-major sub-tiles of
@@ -85,13 +86,14 @@ enum BarId {
     kBarEmpty = kRingSlots,            // [4] ring slot consumed          (count 1, commit)
     kBarSFull = 2 * kRingSlots,        // [2] S-CTA: S tile in TMEM        (count 1, commit)
     kBarSEmpty = kBarSFull + 2,        // [2] S-CTA: S tile read           (count 128)
-    kBarQFree = kBarSEmpty + 2,        //     S-CTA: GEMM1s reading Q done (count 1, commit)
-    kBarPFree = kBarQFree + 1,        // [3] GEMM2 done with message slot (count 1, commit arriving in both CTAs)
+    kBarQFree = kBarSEmpty + 2,        // [2] S-CTA: an issuer's GEMM1s reading Q done (count 1, commit)
+    kBarQReady = kBarQFree + 2,        //     S-CTA: a sequence's Q copied into TMEM (count 1, commit)
+    kBarPFree = kBarQReady + 1,        // [3] GEMM2 done with message slot (count 1, commit arriving in both CTAs)
     kBarPFull = kBarPFree + kMsgSlots, // [3] O-CTA: message landed        (count 1 + tx, from the S-CTA)
     kBarCorr = kBarPFull + kMsgSlots,  // [3] O-CTA: O ready for GEMM2     (count 128)
     kBarMmaDone = kBarCorr + kMsgSlots,// [3] O-CTA: GEMM2 of a message done (count 1, commit)
-    kBarDrain = kBarMmaDone + kMsgSlots,//    MMA issuer's ops retired (teardown)
-    kNumBars = kBarDrain + 1
+    kBarDrain = kBarMmaDone + kMsgSlots,// [2] an MMA issuer's ops retired (teardown)
+    kNumBars = kBarDrain + 2
 };
 
 // Shared-memory layout (offsets from a 1024-aligned base).  Each role has its
@@ -186,8 +188,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             ptx::mbar_init(bar(kBarCorr + i), 128);
             ptx::mbar_init(bar(kBarMmaDone + i), 1);
         }
-        ptx::mbar_init(bar(kBarQFree), 1);
-        ptx::mbar_init(bar(kBarDrain), 1);
+        for (int i = 0; i < 2; ++i) {
+            ptx::mbar_init(bar(kBarQFree + i), 1);
+            ptx::mbar_init(bar(kBarDrain + i), 1);
+        }
+        ptx::mbar_init(bar(kBarQReady), 1);
         *abort_flag = 0;
         ptx::fence_mbarrier_init_cluster();
     }
@@ -263,58 +268,86 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             for (int k = 0; k < nslots; ++k, rg.next(nslots))
                 ptx::mbar_wait(bar(kBarEmpty + rg.slot), rg.phase ^ 1, kErrWaitEmpty);
         }
-    } else if (warp == 1) {
-        // ------------------------------------------------------------ MMA issuer
+    } else if (warp == 1 || (warp == 3 && role == 0)) {
+        // ------------------------------------------------------------ MMA issuers
+        // S-CTA: GEMM1 is issued by two threads, lane 0 of warps 1 and 3, taking
+        // alternate S tiles (and so alternate S buffers).  One thread issues an
+        // N=96 MMA every ~90 cycles in this kernel, twice the MMA's tensor time;
+        // two issuers keep the tensor pipe busy.  At the first tile of a sequence
+        // the tile's issuer copies Q into TMEM once every GEMM1 of the previous
+        // sequence (its own and the other issuer's last tile) is done, and the
+        // other issuer waits for the copy before its next tile.  Both walk the
+        // same items and ring positions, skipping the other's slots.
+        // O-CTA: lane 0 of warp 1 issues GEMM2.
         if (lane == 0) {
             const int nslots = role == 0 ? kSlotsS : kSlotsO;
+            const uint32_t me = warp == 1 ? 0u : 1u;
             Ring rg;
-            uint32_t jt = 0, qphase = 0;
+            uint32_t jt = 0, qphase = 0, nseq = 0, qready_seq = 0;
             int prev_b = -1;
             bool ok = true;
             ItemCursor cur = items_begin<kSched>(wl, cid, ncl);
             Item it;
             int i;
             while (ok && items_next<kSched>(wl, cur, it, i)) {
-                if (role == 0 && it.b != prev_b) {
-                    // The previous sequence's GEMM1s read Q from TMEM: they complete
-                    // before the copy overwrites it (an MMA is not ordered before a
-                    // later tcgen05.cp).
-                    if (prev_b >= 0) {
-                        ptx::mma_commit(bar(kBarQFree));
-                        if (!ptx::mbar_spin(bar(kBarQFree), qphase, kErrWaitMma)) { ok = false; break; }
-                        qphase ^= 1;
-                        ptx::tc_fence_after();
-                    }
-                    // Ring slots filled by TMA need no tcgen05 fence: the full barrier's
-                    // complete_tx orders the loaded bytes before the copy / MMA reads
-                    // them.  (A fence stalls this thread until the tensor pipe drains,
-                    // ~230 cycles: per slot that cost a quarter of the N=96 MMA rate.)
-                    for (int kb = 0; ok && kb < kKBlocks; kb += 2) {
-                        if (*abort_flag || !ptx::mbar_spin(bar(kBarFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
-                        const uint32_t slot = sbase + kOffRing + rg.slot * kSlotS;
-                        const int nb = min(2, kKBlocks - kb);
-                        for (int j = 0; j < nb; ++j) {
-#pragma unroll
-                            for (int c = 0; c < 4; ++c)
-                                ptx::tmem_cp_128x256b(tmem + kTmemQ + ((kb + j) * 4 + c) * 8,
-                                                      ptx::sdesc_sw128(slot + j * kQBoxBytes + c * 32, 16, 1024));
-                        }
-                        ptx::mma_commit(bar(kBarEmpty + rg.slot));
-                        rg.next(nslots);
-                    }
-                    if (!ok) break;
-                    prev_b = it.b;
-                }
+                const bool new_seq = role == 0 && it.b != prev_b;
+                prev_b = it.b;
                 for (int t0 = 0; ok && t0 < it.len; t0 += kTS, ++jt) {
                     if (role == 0) {
+                        const bool mine = (jt & 1u) == me;
+                        if (new_seq && t0 == 0) {
+                            ++nseq;
+                            if (mine) {
+                                if (jt > 0) {
+                                    // An MMA is not ordered before a later tcgen05.cp: every
+                                    // GEMM1 reading the old Q completes first.
+                                    ptx::mma_commit(bar(kBarQFree + me));
+                                    if (!ptx::mbar_spin(bar(kBarQFree + me), qphase, kErrWaitMma)) { ok = false; break; }
+                                    qphase ^= 1;
+                                    const uint32_t pj = jt - 1;  // the other issuer's last tile
+                                    if (!ptx::mbar_spin(bar(kBarSFull + (pj & 1)), (pj >> 1) & 1, kErrWaitMma)) { ok = false; break; }
+                                    ptx::tc_fence_after();
+                                }
+                                // Ring slots filled by TMA need no tcgen05 fence: the full
+                                // barrier's complete_tx orders the loaded bytes before the
+                                // copy / MMA reads them.  (A fence stalls this thread until
+                                // the tensor pipe drains, ~230 cycles.)
+                                for (int kb = 0; ok && kb < kKBlocks; kb += 2) {
+                                    if (*abort_flag || !ptx::mbar_spin(bar(kBarFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
+                                    const uint32_t slot = sbase + kOffRing + rg.slot * kSlotS;
+                                    const int nb = min(2, kKBlocks - kb);
+                                    for (int j = 0; j < nb; ++j) {
+#pragma unroll
+                                        for (int c = 0; c < 4; ++c)
+                                            ptx::tmem_cp_128x256b(tmem + kTmemQ + ((kb + j) * 4 + c) * 8,
+                                                                  ptx::sdesc_sw128(slot + j * kQBoxBytes + c * 32, 16, 1024));
+                                    }
+                                    ptx::mma_commit(bar(kBarEmpty + rg.slot));
+                                    rg.next(nslots);
+                                }
+                                if (!ok) break;
+                                ptx::mma_commit(bar(kBarQReady));
+                                qready_seq = nseq;
+                            } else {
+                                for (int q = 0; q < kQSlots; ++q) rg.next(nslots);
+                            }
+                        }
+                        if (!mine) {
+                            for (int sl = 0; sl < kSlotsPerTile; ++sl) rg.next(nslots);
+                            continue;
+                        }
+                        if (qready_seq != nseq) {  // the other issuer copied this sequence's Q
+                            if (!ptx::mbar_spin(bar(kBarQReady), (nseq - 1) & 1, kErrWaitMma)) { ok = false; break; }
+                            qready_seq = nseq;
+                        }
                         const uint32_t sb = jt & 1, use = jt >> 1;
                         if (*abort_flag || !ptx::mbar_spin(bar(kBarSEmpty + sb), (use & 1) ^ 1, kErrWaitMma)) { ok = false; break; }
-                        ptx::tc_fence_after();  // the softmax's loads of this S buffer come first
+                        ptx::tc_fence_after();  // the softmax's loads of this S buffer (and Q's copy) come first
                         const uint32_t d = tmem + kTmemS + sb * kTS;
                         for (int sl = 0; sl < kSlotsPerTile; ++sl) {
                             if (!ptx::mbar_spin(bar(kBarFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
                             // descriptor of the slot, plus compile-time offsets per K-step: a
-                            // short issue sequence between MMAs keeps the N=96 tensor rate
+                            // short issue sequence between MMAs
                             const uint64_t b0 = ptx::sdesc_sw128(sbase + kOffRing + rg.slot * kSlotS, 16, 1024);
                             const uint32_t a0 = tmem + kTmemQ + sl * (kKbPerSlot * 32);
                             const uint32_t acc0 = sl > 0 ? 1u : 0u;
@@ -358,8 +391,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
             if (!ok) *abort_flag = 1;
             // every MMA this thread issued has retired before TMEM is freed
-            ptx::mma_commit(bar(kBarDrain));
-            ptx::mbar_wait(bar(kBarDrain), 0, kErrWaitMma);
+            ptx::mma_commit(bar(kBarDrain + me));
+            ptx::mbar_wait(bar(kBarDrain + me), 0, kErrWaitMma);
         }
     } else if (warp >= 4) {
         // ------------------------------------------------------------ math warpgroup
