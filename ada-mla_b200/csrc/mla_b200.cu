@@ -329,6 +329,23 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     const unsigned cgrid = (unsigned)rows;
     const int skip = tc_direct ? 1 : 0;
     // The tcgen05 kernel keeps fp16 partials for fp16 output; the SIMT kernel's are fp32.
+    // Batches merge row-parallel (a warp per row, few splits each); a few long
+    // sequences merge split-parallel (a block per row, many splits).
+    if (batch >= 8) {
+        const dim3 rgrid((unsigned)cdiv(num_heads, kRowsPerCombineBlock), (unsigned)batch);
+        const dim3 rblock(32 * kRowsPerCombineBlock);
+        if (out_dtype == MLA_B200_OUT_F16 && tc_direct)
+            combine_rows_kernel<__half, __half><<<rgrid, rblock, 0, stream>>>(
+                reinterpret_cast<const __half *>(L.part_o), L.part_lse, wl, num_heads, static_cast<__half *>(out),
+                out_lse, skip);
+        else if (out_dtype == MLA_B200_OUT_F16)
+            combine_rows_kernel<__half, float><<<rgrid, rblock, 0, stream>>>(
+                L.part_o, L.part_lse, wl, num_heads, static_cast<__half *>(out), out_lse, skip);
+        else
+            combine_rows_kernel<float, float><<<rgrid, rblock, 0, stream>>>(
+                L.part_o, L.part_lse, wl, num_heads, static_cast<float *>(out), out_lse, skip);
+        return launch_status();
+    }
     if (out_dtype == MLA_B200_OUT_F16 && tc_direct) {
         combine_kernel<__half, __half><<<cgrid, kCombineThreads, 0, stream>>>(
             reinterpret_cast<const __half *>(L.part_o), L.part_lse, wl, num_heads, rows,

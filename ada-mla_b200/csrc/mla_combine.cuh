@@ -17,7 +17,7 @@
 
 namespace mla {
 
-constexpr int kCombineThreads = 256;
+constexpr int kCombineThreads = 512;
 constexpr int kCombineChunk = 1024;      // split weights staged per pass
 
 // Unpacks one 16-byte vector of partial elements to fp32.
@@ -42,8 +42,8 @@ __device__ __forceinline__ void unpack16(const uint4 u, float (&v)[8]) {
 //   O = sum_i e^{lse_i - M} O_i / sum_i e^{lse_i - M},  M = max_i lse_i.
 // The weights are computed once per split into shared memory.  A thread owns
 // one 16-byte vector of the row (4 fp32 or 8 fp16 partial elements); the
-// block's 256 threads form 2 (fp32) or 4 (fp16) groups that stream disjoint
-// splits with 4 loads in flight each, and their sums meet in shared memory.
+// block's 512 threads form 4 (fp32) or 8 (fp16) groups that stream disjoint
+// splits with 8 loads in flight each, and their sums meet in shared memory.
 // skip_single: rows of sequences with exactly one item were already written
 // by the decode kernel itself and are left alone.
 template <typename OutT, typename PartT>
@@ -91,26 +91,22 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(
             __syncthreads();
             for (int k = 0; k < n; ++k) wsum += w_s[k];
             const uint4 *src = reinterpret_cast<const uint4 *>(part_o + ((size_t)c0 * num_heads + h) * kDV) + col;
-            int k = g;
-            for (; k + 3 * kGroups < n; k += 4 * kGroups) {
-                uint4 u[4];
+            // up to 8 splits' loads in flight per thread (predicated at the end)
+            for (int k = g; k < n; k += 8 * kGroups) {
+                uint4 u[8];
 #pragma unroll
-                for (int j = 0; j < 4; ++j) u[j] = __ldg(src + (size_t)(k + j * kGroups) * step);
+                for (int j = 0; j < 8; ++j)
+                    if (k + j * kGroups < n) u[j] = __ldg(src + (size_t)(k + j * kGroups) * step);
 #pragma unroll
-                for (int j = 0; j < 4; ++j) {
-                    float v[kVec];
-                    unpack16(u[j], v);
-                    const float w = w_s[k + j * kGroups];
+                for (int j = 0; j < 8; ++j) {
+                    if (k + j * kGroups < n) {
+                        float v[kVec];
+                        unpack16(u[j], v);
+                        const float w = w_s[k + j * kGroups];
 #pragma unroll
-                    for (int e = 0; e < kVec; ++e) acc[e] = fmaf(w, v[e], acc[e]);
+                        for (int e = 0; e < kVec; ++e) acc[e] = fmaf(w, v[e], acc[e]);
+                    }
                 }
-            }
-            for (; k < n; k += kGroups) {
-                float v[kVec];
-                unpack16(__ldg(src + (size_t)k * step), v);
-                const float w = w_s[k];
-#pragma unroll
-                for (int e = 0; e < kVec; ++e) acc[e] = fmaf(w, v[e], acc[e]);
             }
         }
     }
@@ -141,6 +137,92 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(
         }
     }
     if (out_lse != nullptr && tid == 0) out_lse[row] = wsum > 0.f ? mx + __logf(wsum) : -INFINITY;
+}
+
+// Row-parallel merge for batches: one warp per (sequence, head) row and one
+// block per 8 heads of one sequence, so a sequence's item range is read once
+// per block and a block of a sequence decoded as a single item (already final)
+// exits at once.  Lane l owns columns [16 l, 16 l + 16); the split weights
+// e^{lse_i - M} live in the lanes (lane j holds split s0 + j) and are
+// broadcast with shuffles while four splits' loads are in flight.
+constexpr int kRowsPerCombineBlock = 8;
+
+template <typename PartT>
+__device__ __forceinline__ void load16(const PartT *row, int lane, uint4 (&u)[16 / (16 / (int)sizeof(PartT))]) {
+    const uint4 *src = reinterpret_cast<const uint4 *>(row) + lane * (16 * (int)sizeof(PartT) / 16);
+#pragma unroll
+    for (int j = 0; j < 16 * (int)sizeof(PartT) / 16; ++j) u[j] = __ldg(src + j);
+}
+
+template <typename OutT, typename PartT>
+__global__ void __launch_bounds__(32 * kRowsPerCombineBlock) combine_rows_kernel(
+    const PartT *__restrict__ part_o, const float *__restrict__ part_lse, WorkList wl, int num_heads,
+    OutT *__restrict__ out, float *__restrict__ out_lse, int skip_single) {
+    constexpr int kU = 16 * (int)sizeof(PartT) / 16;  // 16-byte vectors per lane per split
+    const int lane = threadIdx.x & 31;
+    const int b = blockIdx.y;
+    const int h = blockIdx.x * kRowsPerCombineBlock + (threadIdx.x >> 5);
+    int i0, i1;
+    item_range(wl, b, i0, i1);
+    if ((skip_single && i1 - i0 == 1) || h >= num_heads) return;
+    const int n = i1 - i0;
+    float mx = -INFINITY;
+    for (int s = lane; s < n; s += 32) mx = fmaxf(mx, part_lse[(size_t)(i0 + s) * num_heads + h]);
+    mx = warp_max(mx);
+    float acc[16];
+#pragma unroll
+    for (int e = 0; e < 16; ++e) acc[e] = 0.f;
+    float wsum = 0.f;
+    if (mx != -INFINITY) {
+        for (int s0 = 0; s0 < n; s0 += 32) {
+            const int m = min(32, n - s0);
+            float w = 0.f;
+            if (lane < m) {
+                const float lse = part_lse[(size_t)(i0 + s0 + lane) * num_heads + h];
+                w = lse == -INFINITY ? 0.f : __expf(lse - mx);
+            }
+            wsum += warp_sum(w);
+            const PartT *base = part_o + ((size_t)(i0 + s0) * num_heads + h) * kDV;
+            const size_t step = (size_t)num_heads * kDV;
+            for (int j = 0; j < m; j += 4) {
+                uint4 u[4][kU];
+#pragma unroll
+                for (int k = 0; k < 4; ++k)
+                    if (j + k < m) load16<PartT>(base + (size_t)(j + k) * step, lane, u[k]);
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float wk = __shfl_sync(0xffffffffu, w, (j + k) & 31);
+                    if (j + k < m) {
+#pragma unroll
+                        for (int q = 0; q < kU; ++q) {
+                            float v[16 / kU];
+                            unpack16(u[k][q], v);
+#pragma unroll
+                            for (int e = 0; e < 16 / kU; ++e) acc[q * (16 / kU) + e] = fmaf(wk, v[e], acc[q * (16 / kU) + e]);
+                        }
+                    }
+                }
+            }
+        }
+    }
+    const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+    OutT *dst = out + ((size_t)b * num_heads + h) * kDV + lane * 16;
+    if constexpr (sizeof(OutT) == 4) {
+#pragma unroll
+        for (int e = 0; e < 16; e += 4)
+            *reinterpret_cast<float4 *>(dst + e) = make_float4(acc[e] * inv, acc[e + 1] * inv, acc[e + 2] * inv, acc[e + 3] * inv);
+    } else {
+        uint32_t pk[8];
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+            __half2 t = __floats2half2_rn(acc[2 * e] * inv, acc[2 * e + 1] * inv);
+            pk[e] = *reinterpret_cast<uint32_t *>(&t);
+        }
+        reinterpret_cast<uint4 *>(dst)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+        reinterpret_cast<uint4 *>(dst)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+    }
+    if (out_lse != nullptr && lane == 0)
+        out_lse[(size_t)b * num_heads + h] = wsum > 0.f ? mx + __logf(wsum) : -INFINITY;
 }
 
 // Expands cu_seqlens[B+1] into item_off[B+1] (exclusive prefix of per-sequence
