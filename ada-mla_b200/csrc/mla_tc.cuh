@@ -60,7 +60,7 @@ constexpr int kBoxS = kTS * 128;                 // 12288: one K-block box [96 t
 constexpr int kKbPerSlot = 3;                    // K-blocks per S ring slot (12 MMAs per wait)
 constexpr int kSlotS = kKbPerSlot * kBoxS;       // 36864
 constexpr int kSlotsPerTile = kKBlocks / kKbPerSlot;  // 3
-constexpr int kSlotsS = 4;
+constexpr int kSlotsS = 5;
 constexpr int kBoxO = kTO * 128;                 // 4096: [32 tok x 64 col]
 constexpr int kSlotO = kVBlocks * kBoxO;         // 32768: C tile [32 x 512]
 constexpr int kSlotsO = 4;
@@ -78,7 +78,6 @@ constexpr int kMsgM = kMsgP + 1024;
 constexpr int kMsgBytes = kMsgP + 1536;          // 26112
 constexpr int kMsgStride = 26 * 1024;
 constexpr int kMsgSlots = 3;                     // O-CTA receive ring
-constexpr int kStgSlots = 2;                     // S-CTA staging for outgoing copies
 
 constexpr int kRingSlots = kSlotsS > kSlotsO ? kSlotsS : kSlotsO;
 enum BarId {
@@ -100,9 +99,9 @@ enum BarId {
 // own ring and message buffers; the barriers sit at the same offset in both
 // CTAs (remote arrivals and the two-CTA commit address them by offset).
 constexpr int kOffRing = 0;
-constexpr int kOffStgS = kSlotsS * kSlotS;                       // 147456: S staging [2]
+constexpr int kOffStgS = kSlotsS * kSlotS;                       // 184320: S staging
 constexpr int kOffMsgO = kSlotsO * kSlotO;                       // 131072: O receive ring [3]
-constexpr int kEndS = kOffStgS + kStgSlots * kMsgStride;         // 200704
+constexpr int kEndS = kOffStgS + kMsgStride;                     // 210944
 constexpr int kEndO = kOffMsgO + kMsgSlots * kMsgStride;         // 210944
 constexpr int kOffBar = kEndS > kEndO ? kEndS : kEndO;
 constexpr int kOffSlot = kOffBar + kNumBars * 8;
@@ -412,7 +411,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 float m_used = -INFINITY, l_run = 0.f;
                 for (int t0 = 0; t0 < it.len; t0 += kTS, ++jt) {
                     const uint32_t sb = jt & 1, use = jt >> 1;
-                    const uint32_t ms = jt % kMsgSlots, mu = jt / kMsgSlots, sg = jt % kStgSlots;
+                    const uint32_t ms = jt % kMsgSlots, mu = jt / kMsgSlots;
                     // Every decision below is made uniform across the warpgroup by the
                     // bar.red at the end of the tile, so an expired wait can never split
                     // a warp at a .sync.aligned tcgen05 op or strand a named barrier.
@@ -469,10 +468,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         // the peer's message slot is free once GEMM2 of S tile jt-3 finished
                         w = ptx::mbar_wait<true>(bar(kBarPFree + ms), (mu & 1) ^ 1, kErrWaitPeer);
                     }
+                    // the previous tile's outgoing copy has finished reading the staging buffer
+                    if (h == 0) ptx::bulk_wait_group_read<0>();
+                    ptx::named_barrier(1, 128);
                     if (w) {
-                        // staging slot sg: its previous copy (tile jt-2) finished reading
-                        // before the previous tile's bar.red (wait_group.read below)
-                        uint8_t *msg = smem + kOffStgS + sg * kMsgStride;
+                        uint8_t *msg = smem + kOffStgS;
 #pragma unroll
                         for (int st = 0; st < kOPerS; ++st) {
                             uint4 *prow = reinterpret_cast<uint4 *>(msg + st * kSubP + h * 64);  // SW64
@@ -489,12 +489,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         }
                         ptx::fence_proxy_async_smem();
                     }
-                    if (h == 0) ptx::bulk_wait_group_read<0>();  // previous copy has read its staging
                     if (!ptx::named_barrier_and(1, 128, w)) { ok = false; break; }
                     if (h == 0) {
                         const uint32_t rbar = peer_pfull0 + 8u * ms;
                         ptx::mbar_remote_arrive_expect_tx(rbar, kMsgBytes);
-                        ptx::bulk_copy_s2cluster(peer_msg0 + ms * kMsgStride, sbase + kOffStgS + sg * kMsgStride,
+                        ptx::bulk_copy_s2cluster(peer_msg0 + ms * kMsgStride, sbase + kOffStgS,
                                                  kMsgBytes, rbar);
                         ptx::bulk_commit_group();
                     }
