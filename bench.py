@@ -35,8 +35,8 @@ sys.path.insert(0, ROOT)
 HEAD_DIM_K = 576
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of the
 # main decode kernel per config, from an `ncu --set full` capture of this kernel
-# on this workload (cfg 1: 4.93 MB read, 0 written; cfg 3: 151.3 + 3.7 MB).
-NCU_TRAFFIC = {1: 4.934e6, 3: 155.03e6}
+# on this workload (cfg 1: 4.95 MB read, 0 written; cfg 3: 151.9 + 4.7 MB).
+NCU_TRAFFIC = {1: 4.951e6, 3: 156.62e6}
 METRIC = "MLA decode latent-KV HBM GB/s (us/step alongside)"
 UNIT = "GB/s"
 
