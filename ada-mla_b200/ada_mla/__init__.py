@@ -77,16 +77,19 @@ ext_path = EXT_PATH
 def mla_decode_batched(query, cache, cu_seqlens=None, max_seq_len: int = -1,
                        softmax_scale: float = SOFTMAX_SCALE, num_splits: int = -1,
                        return_lse: bool = False, out_dtype=None):
-    """Batched / variable-length fp16 decode.
+    """Batched / variable-length fp16 or bf16 decode.
 
-    query  [B, n_h, 576] fp16.
-    cache  dense [B, N, 576] fp16, or packed [T, 576] fp16 with
-           ``cu_seqlens`` int32 [B+1] (sequence b owns rows
-           cu_seqlens[b]:cu_seqlens[b+1]).  Pass ``max_seq_len`` to avoid a
-           device->host read of the longest length.
-    Returns O* [B, n_h, 512] (fp16, or fp32 when ``out_dtype=torch.float32``)
-    and, with ``return_lse``, the natural-log LSE [B, n_h] fp32 as a tuple.
+    query  [B, n_h, 576] fp16 or bf16 (bf16: n_h <= 128).
+    cache  dense [B, N, 576], or packed [T, 576] with ``cu_seqlens`` int32
+           [B+1] (sequence b owns rows cu_seqlens[b]:cu_seqlens[b+1]), in the
+           query's dtype.  Pass ``max_seq_len`` to avoid a device->host read of
+           the longest length.
+    Returns O* [B, n_h, 512] (the input dtype, or fp32 when
+    ``out_dtype=torch.float32``) and, with ``return_lse``, the natural-log LSE
+    [B, n_h] fp32 as a tuple.
     """
+    if out_dtype not in (None, torch.float32, query.dtype):
+        raise ValueError(f"mla_decode_batched: out_dtype must be None, float32 or {query.dtype}")
     out_fp32 = out_dtype == torch.float32
     out, lse = _ext.mla_decode_batched(query, cache, cu_seqlens, int(max_seq_len),
                                        float(softmax_scale), int(num_splits),

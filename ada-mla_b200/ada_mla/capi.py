@@ -24,6 +24,7 @@ ERR_DEVICE_TIMEOUT = 5
 ERR_NO_DEVICE = 6
 OUT_F16 = 0
 OUT_F32 = 1
+OUT_BF16 = 2
 
 _c_int, _c_ll, _c_size, _c_float = ctypes.c_int, ctypes.c_longlong, ctypes.c_size_t, ctypes.c_float
 _vp = ctypes.c_void_p
@@ -42,6 +43,8 @@ SIGNATURES = {
     "mla_b200_decode_split_f16_noalloc": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _vp]),
     "mla_b200_decode_batched_f16": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_ll, _c_int, _c_float,
                                              _c_int, _vp, _c_int, _vp, _vp, _c_size, _vp]),
+    "mla_b200_decode_batched_bf16": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_ll, _c_int, _c_float,
+                                              _c_int, _vp, _c_int, _vp, _vp, _c_size, _vp]),
     "mla_b200_decode_fused_f32": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _vp, _c_size, _vp]),
     "mla_b200_decode_naive_f32": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _vp]),
     "mla_b200_combine_f32": (_c_int, [_vp, _vp, _c_int, _c_ll, _vp, _c_int, _vp, _vp]),
@@ -156,18 +159,27 @@ def decode_batched_f16(query: torch.Tensor, cache: torch.Tensor, cu_seqlens: tor
                        max_seq_len: int, softmax_scale: float, num_splits: int = -1,
                        out_fp32: bool = False, return_lse: bool = False,
                        workspace: torch.Tensor | None = None):
+    """Batched / varlen decode; the entry point follows query.dtype (fp16 ->
+    mla_b200_decode_batched_f16, bf16 -> mla_b200_decode_batched_bf16) and the
+    16-bit output takes the input dtype."""
     b, nh = query.shape[0], query.shape[1]
+    bf16 = query.dtype == torch.bfloat16
     total = cache.shape[0] if cu_seqlens is not None else b * max_seq_len
-    out = torch.empty((b, nh, 512), dtype=torch.float32 if out_fp32 else torch.float16,
+    out = torch.empty((b, nh, 512), dtype=torch.float32 if out_fp32 else query.dtype,
                       device=query.device)
     lse = torch.empty((b, nh), dtype=torch.float32, device=query.device) if return_lse else None
     if workspace is None:
         workspace = _workspace(workspace_size(b, nh, total, max_seq_len, num_splits), query.device)
-    _check("mla_b200_decode_batched_f16", lib().mla_b200_decode_batched_f16(
+    name = "mla_b200_decode_batched_bf16" if bf16 else "mla_b200_decode_batched_f16"
+    odt = OUT_F32 if out_fp32 else (OUT_BF16 if bf16 else OUT_F16)
+    _check(name, getattr(lib(), name)(
         _ptr(query), _ptr(cache), _ptr(cu_seqlens), b, nh, total, max_seq_len,
-        float(softmax_scale), num_splits, _ptr(out), OUT_F32 if out_fp32 else OUT_F16,
+        float(softmax_scale), num_splits, _ptr(out), odt,
         _ptr(lse), _ptr(workspace), workspace.numel(), _stream()))
     return (out, lse) if return_lse else out
+
+
+decode_batched = decode_batched_f16
 
 
 def decode_fused_f32(query: torch.Tensor, cache: torch.Tensor):

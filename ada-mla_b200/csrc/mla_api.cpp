@@ -116,9 +116,10 @@ at::Tensor mla_decode_split(const at::Tensor &query, const at::Tensor &cache, in
 }
 
 // Batched / varlen decode (no reference counterpart).
-//   query [B, n_h, 576] fp16; cache [B, N, 576] (dense) or [T, 576] with
-//   cu_seqlens int32 [B+1] on the same device (packed).
-// Returns (out [B, n_h, 512] in out_dtype, lse [B, n_h] fp32 or empty).
+//   query [B, n_h, 576] fp16 or bf16 (cache the same dtype); cache [B, N, 576]
+//   (dense) or [T, 576] with cu_seqlens int32 [B+1] on the same device (packed).
+// Returns (out [B, n_h, 512] in the input dtype, or fp32 when out_fp32,
+// lse [B, n_h] fp32 or empty).
 std::vector<at::Tensor> mla_decode_batched(const at::Tensor &query, const at::Tensor &cache,
                                            const c10::optional<at::Tensor> &cu_seqlens,
                                            int64_t max_seq_len, double softmax_scale,
@@ -127,8 +128,10 @@ std::vector<at::Tensor> mla_decode_batched(const at::Tensor &query, const at::Te
     check_cuda(query, "query");
     check_cuda(cache, "cache");
     TORCH_CHECK(query.device() == cache.device(), "query and cache on different devices");
-    TORCH_CHECK(query.scalar_type() == at::kHalf && cache.scalar_type() == at::kHalf,
-                "mla_decode_batched: float16 inputs expected");
+    const bool bf16 = query.scalar_type() == at::kBFloat16;
+    TORCH_CHECK((query.scalar_type() == at::kHalf || bf16) &&
+                    cache.scalar_type() == query.scalar_type(),
+                "mla_decode_batched: float16 or bfloat16 inputs (query and cache alike) expected");
     TORCH_CHECK(query.dim() == 3 && query.size(2) == MLA_B200_HEAD_DIM_K,
                 "mla_decode_batched: query must be [B, n_h, 576]");
     const int64_t b = query.size(0), nh = query.size(1);
@@ -155,18 +158,19 @@ std::vector<at::Tensor> mla_decode_batched(const at::Tensor &query, const at::Te
         total = b * max_seq_len;
     }
     at::Tensor out = at::empty({b, nh, MLA_B200_HEAD_DIM_V},
-                               query.options().dtype(out_fp32 ? at::kFloat : at::kHalf));
+                               query.options().dtype(out_fp32 ? at::kFloat
+                                                              : query.scalar_type()));
     at::Tensor lse = return_lse ? at::empty({b, nh}, query.options().dtype(at::kFloat))
                                 : at::Tensor();
     const size_t ws = mla_b200_workspace_size((int)b, (int)nh, total, (int)max_seq_len,
                                               (int)num_splits);
     at::Tensor w = workspace(query, ws);
-    check_status(mla_b200_decode_batched_f16(
-                     query.data_ptr(), cache.data_ptr(), cu_ptr, (int)b, (int)nh, total,
-                     (int)max_seq_len, (float)softmax_scale, (int)num_splits, out.data_ptr(),
-                     out_fp32 ? MLA_B200_OUT_F32 : MLA_B200_OUT_F16,
-                     return_lse ? lse.data_ptr<float>() : nullptr, w.data_ptr(), w.numel(),
-                     stream_ptr()),
+    auto *fn = bf16 ? mla_b200_decode_batched_bf16 : mla_b200_decode_batched_f16;
+    const int odt = out_fp32 ? MLA_B200_OUT_F32 : (bf16 ? MLA_B200_OUT_BF16 : MLA_B200_OUT_F16);
+    check_status(fn(query.data_ptr(), cache.data_ptr(), cu_ptr, (int)b, (int)nh, total,
+                    (int)max_seq_len, (float)softmax_scale, (int)num_splits, out.data_ptr(), odt,
+                    return_lse ? lse.data_ptr<float>() : nullptr, w.data_ptr(), w.numel(),
+                    stream_ptr()),
                  "mla_decode_batched");
     if (!return_lse) lse = at::empty({0}, query.options().dtype(at::kFloat));
     return {out, lse};

@@ -74,9 +74,13 @@ int current_device(int *dev_out, DevInfo *info_out) {
         d.simt_attr_set = true;
     }
     if (d.tc_clusters == 0) {
-        if (cudaFuncSetAttribute(tc::tc_decode_kernel<kSchedChunked>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+        if (cudaFuncSetAttribute(tc::tc_decode_kernel<kSchedChunked, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  tc::kSmemBytes) != cudaSuccess ||
-            cudaFuncSetAttribute(tc::tc_decode_kernel<kSchedBalanced>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+            cudaFuncSetAttribute(tc::tc_decode_kernel<kSchedBalanced, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 tc::kSmemBytes) != cudaSuccess ||
+            cudaFuncSetAttribute(tc::tc_decode_kernel<kSchedChunked, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 tc::kSmemBytes) != cudaSuccess ||
+            cudaFuncSetAttribute(tc::tc_decode_kernel<kSchedBalanced, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
                                  tc::kSmemBytes) != cudaSuccess) {
             return cuda_failure(cudaGetLastError());
         }
@@ -92,7 +96,7 @@ int current_device(int *dev_out, DevInfo *info_out) {
         cfg.attrs = &attr;
         cfg.numAttrs = 1;
         int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, tc::tc_decode_kernel<kSchedChunked>, &cfg) != cudaSuccess || n <= 0) {
+        if (cudaOccupancyMaxActiveClusters(&n, tc::tc_decode_kernel<kSchedChunked, false>, &cfg) != cudaSuccess || n <= 0) {
             cudaGetLastError();
             n = d.sms / 2;
         }
@@ -120,14 +124,15 @@ PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
 
 // 2-D view [rows, 576] fp16 with (64 x box_rows) boxes and 128-byte swizzle
 // (the UMMA K-major / MN-major SW128 operand layout).
-int make_tmap_576(CUtensorMap *map, const void *base, long long rows, int box_rows) {
+int make_tmap_576(CUtensorMap *map, const void *base, long long rows, int box_rows, bool bf16 = false) {
     auto enc = tmap_encoder();
     if (enc == nullptr) return cuda_failure(cudaErrorSymbolNotFound);
     cuuint64_t dims[2] = {(cuuint64_t)kDK, (cuuint64_t)rows};
     cuuint64_t strides[1] = {(cuuint64_t)kDK * 2};
     cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
     cuuint32_t estr[2] = {1, 1};
-    const CUresult r = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2, const_cast<void *>(base), dims,
+    const CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
+                           const_cast<void *>(base), dims,
                            strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
                            CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
@@ -233,7 +238,9 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     // The tensor-core kernel with an automatic split runs the balanced schedule
     // (every cluster gets an equal share of the batch's tiles); explicit split
     // counts and the SIMT kernels use fixed-size chunks.
-    const bool tc_path = std::is_same<T, __half>::value && num_heads <= 128;
+    constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+    const bool tc_path = !std::is_same<T, float>::value && num_heads <= 128;
+    if (kBf16 && !tc_path) return MLA_B200_ERR_UNSUPPORTED;  // bf16 has no SIMT kernel
     // (A single sequence splits evenly in the chunked schedule already.)
     const bool balanced = tc_path && num_splits <= 0 && batch > 1;
     const int chunk = chunk_for(batch, total_tokens, max_seq_len, num_splits, info.sms);
@@ -293,9 +300,9 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     if (wl.max_items > 0 && (!balanced || bal_clusters > 0)) {
         if (tc_path) {
             CUtensorMap cmap_s, cmap_o, qmap;
-            st = make_tmap_576(&cmap_s, cache, total_tokens, tc::kTS);
-            if (st == MLA_B200_OK) st = make_tmap_576(&cmap_o, cache, total_tokens, tc::kTO);
-            if (st == MLA_B200_OK) st = make_tmap_576(&qmap, q, (long long)batch * num_heads, 128);
+            st = make_tmap_576(&cmap_s, cache, total_tokens, tc::kTS, kBf16);
+            if (st == MLA_B200_OK) st = make_tmap_576(&cmap_o, cache, total_tokens, tc::kTO, kBf16);
+            if (st == MLA_B200_OK) st = make_tmap_576(&qmap, q, (long long)batch * num_heads, 128, kBf16);
             if (st != MLA_B200_OK) return st;
             tc::TcParams tp;
             tp.wl = wl;
@@ -303,19 +310,22 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
             tp.scale_log2 = scale * kLog2e;
             tp.part_o = L.part_o;
             tp.part_lse = L.part_lse;
-            tp.part_f16 = out_dtype == MLA_B200_OUT_F16 ? 1 : 0;
+            // fp16 partials for fp16 output; bf16 runs keep fp32 partials (bf16 data
+            // may exceed the fp16 range)
+            tp.part_kind = out_dtype == MLA_B200_OUT_F16 ? tc::kOutF16 : tc::kOutF32;
             tp.out = out;
-            tp.out_f16 = out_dtype == MLA_B200_OUT_F16 ? 1 : 0;
+            tp.out_kind = out_dtype == MLA_B200_OUT_F16 ? tc::kOutF16
+                          : out_dtype == MLA_B200_OUT_BF16 ? tc::kOutBF16 : tc::kOutF32;
             tp.out_lse = out_lse;
             tc_direct = true;
             const int clusters = balanced ? bal_clusters : std::min(info.tc_clusters, wl.max_items);
             timing_mark(t_ev_start, stream);
             if (balanced)
-                tc::tc_decode_kernel<kSchedBalanced><<<2 * clusters, tc::kThreads, tc::kSmemBytes, stream>>>(cmap_s, cmap_o, qmap, tp);
+                tc::tc_decode_kernel<kSchedBalanced, kBf16><<<2 * clusters, tc::kThreads, tc::kSmemBytes, stream>>>(cmap_s, cmap_o, qmap, tp);
             else
-                tc::tc_decode_kernel<kSchedChunked><<<2 * clusters, tc::kThreads, tc::kSmemBytes, stream>>>(cmap_s, cmap_o, qmap, tp);
+                tc::tc_decode_kernel<kSchedChunked, kBf16><<<2 * clusters, tc::kThreads, tc::kSmemBytes, stream>>>(cmap_s, cmap_o, qmap, tp);
             timing_mark(t_ev_stop, stream);
-        } else {
+        } else if constexpr (!kBf16) {
             dim3 grid(wl.max_items, (unsigned)cdiv(num_heads, kSimtHeads));
             timing_mark(t_ev_start, stream);
             simt_partial_kernel<T><<<grid, 256, kSimtSmem, stream>>>(
@@ -334,7 +344,10 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     if (batch >= 8) {
         const dim3 rgrid((unsigned)cdiv(num_heads, kRowsPerCombineBlock), (unsigned)batch);
         const dim3 rblock(32 * kRowsPerCombineBlock);
-        if (out_dtype == MLA_B200_OUT_F16 && tc_direct)
+        if (out_dtype == MLA_B200_OUT_BF16)
+            combine_rows_kernel<__nv_bfloat16, float><<<rgrid, rblock, 0, stream>>>(
+                L.part_o, L.part_lse, wl, num_heads, static_cast<__nv_bfloat16 *>(out), out_lse, skip);
+        else if (out_dtype == MLA_B200_OUT_F16 && tc_direct)
             combine_rows_kernel<__half, __half><<<rgrid, rblock, 0, stream>>>(
                 reinterpret_cast<const __half *>(L.part_o), L.part_lse, wl, num_heads, static_cast<__half *>(out),
                 out_lse, skip);
@@ -346,7 +359,10 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
                 L.part_o, L.part_lse, wl, num_heads, static_cast<float *>(out), out_lse, skip);
         return launch_status();
     }
-    if (out_dtype == MLA_B200_OUT_F16 && tc_direct) {
+    if (out_dtype == MLA_B200_OUT_BF16) {
+        combine_kernel<__nv_bfloat16, float><<<cgrid, kCombineThreads, 0, stream>>>(
+            L.part_o, L.part_lse, wl, num_heads, rows, static_cast<__nv_bfloat16 *>(out), out_lse, skip);
+    } else if (out_dtype == MLA_B200_OUT_F16 && tc_direct) {
         combine_kernel<__half, __half><<<cgrid, kCombineThreads, 0, stream>>>(
             reinterpret_cast<const __half *>(L.part_o), L.part_lse, wl, num_heads, rows,
             static_cast<__half *>(out), out_lse, skip);
@@ -481,6 +497,31 @@ int mla_b200_decode_batched_f16(const void *query, const void *cache, const int3
                                     num_heads, total_tokens, max_seq_len, softmax_scale,
                                     num_splits, out, out_dtype, out_lse, workspace,
                                     workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int mla_b200_decode_batched_bf16(const void *query, const void *cache, const int32_t *cu_seqlens,
+                                 int batch, int num_heads, long long total_tokens, int max_seq_len,
+                                 float softmax_scale, int num_splits, void *out, int out_dtype,
+                                 float *out_lse, void *workspace, size_t workspace_bytes, void *stream) {
+    if (batch < 0 || num_heads <= 0 || total_tokens < 0 || max_seq_len < 0)
+        return MLA_B200_ERR_INVALID_ARG;
+    if (batch > 0 && (query == nullptr || out == nullptr)) return MLA_B200_ERR_INVALID_ARG;
+    if (total_tokens > 0 && cache == nullptr) return MLA_B200_ERR_INVALID_ARG;
+    if (out_dtype != MLA_B200_OUT_BF16 && out_dtype != MLA_B200_OUT_F32) return MLA_B200_ERR_INVALID_ARG;
+    if (!(softmax_scale > 0.f) || !isfinite(softmax_scale)) return MLA_B200_ERR_INVALID_ARG;
+    if (!aligned(query, 16) || !aligned(cache, 16) || !aligned(out, 16) || !aligned(out_lse, 4))
+        return MLA_B200_ERR_INVALID_ARG;
+    if (cu_seqlens == nullptr && (long long)batch * max_seq_len != total_tokens)
+        return MLA_B200_ERR_INVALID_ARG;
+    if (cu_seqlens != nullptr && max_seq_len == 0 && total_tokens > 0)
+        return MLA_B200_ERR_INVALID_ARG;
+    if (total_tokens >= (1LL << 31)) return MLA_B200_ERR_UNSUPPORTED;
+    if (num_heads > 128) return MLA_B200_ERR_UNSUPPORTED;
+    return run_split_decode<__nv_bfloat16>(static_cast<const __nv_bfloat16 *>(query),
+                                           static_cast<const __nv_bfloat16 *>(cache), cu_seqlens, batch,
+                                           num_heads, total_tokens, max_seq_len, softmax_scale,
+                                           num_splits, out, out_dtype, out_lse, workspace,
+                                           workspace_bytes, static_cast<cudaStream_t>(stream));
 }
 
 int mla_b200_decode_fused_f32(const float *query, const float *cache, float *out, int num_heads,

@@ -13,11 +13,25 @@
 // fp32 output, optional merged LSE).
 #pragma once
 
+#include <type_traits>
+
 #include "mla_common.cuh"
 
 namespace mla {
 
 constexpr int kCombineThreads = 512;
+
+// Two output elements (fp16 or bf16) packed into 32 bits.
+template <typename OutT>
+__device__ __forceinline__ uint32_t pack_out2(float a, float b) {
+    if constexpr (std::is_same<OutT, __nv_bfloat16>::value) {
+        __nv_bfloat162 t = __floats2bfloat162_rn(a, b);
+        return *reinterpret_cast<uint32_t *>(&t);
+    } else {
+        __half2 t = __floats2half2_rn(a, b);
+        return *reinterpret_cast<uint32_t *>(&t);
+    }
+}
 constexpr int kCombineChunk = 1024;      // split weights staged per pass
 
 // Unpacks one 16-byte vector of partial elements to fp32.
@@ -129,10 +143,9 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(
         if constexpr (sizeof(OutT) == 4) {
             *reinterpret_cast<float4 *>(dst + e0) = v;
         } else {
-            __half2 a = __floats2half2_rn(v.x, v.y), c = __floats2half2_rn(v.z, v.w);
             uint2 u;
-            u.x = *reinterpret_cast<uint32_t *>(&a);
-            u.y = *reinterpret_cast<uint32_t *>(&c);
+            u.x = pack_out2<OutT>(v.x, v.y);
+            u.y = pack_out2<OutT>(v.z, v.w);
             *reinterpret_cast<uint2 *>(dst + e0) = u;
         }
     }
@@ -214,10 +227,7 @@ __global__ void __launch_bounds__(32 * kRowsPerCombineBlock) combine_rows_kernel
     } else {
         uint32_t pk[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) {
-            __half2 t = __floats2half2_rn(acc[2 * e] * inv, acc[2 * e + 1] * inv);
-            pk[e] = *reinterpret_cast<uint32_t *>(&t);
-        }
+        for (int e = 0; e < 8; ++e) pk[e] = pack_out2<OutT>(acc[2 * e] * inv, acc[2 * e + 1] * inv);
         reinterpret_cast<uint4 *>(dst)[0] = make_uint4(pk[0], pk[1], pk[2], pk[3]);
         reinterpret_cast<uint4 *>(dst)[1] = make_uint4(pk[4], pk[5], pk[6], pk[7]);
     }

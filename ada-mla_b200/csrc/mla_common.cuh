@@ -2,6 +2,7 @@
 // small device helpers shared by every MLA decode kernel.
 #pragma once
 
+#include <cuda_bf16.h>
 #include <cuda_fp16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>

@@ -118,27 +118,41 @@ constexpr uint32_t kTmemS = 288;   // S-CTA: two S buffers of kTS columns
 static_assert(kTmemS + 2 * kTS <= kTmemCols, "TMEM budget");
 constexpr float kRescaleLog2 = 8.0f;
 
-constexpr uint32_t kIdescS = ptx::idesc_f16_f32(128, kTS, 0, 0);   // M=128 heads, N=96 tokens
-constexpr uint32_t kIdescO = ptx::idesc_f16_f32(128, 256, 0, 1);   // M=128 heads, N=256 dims, B MN-major
+// GEMM1: M=128 heads, N=96 tokens; GEMM2: M=128 heads, N=256 dims, B MN-major.
+template <bool kBf16> __host__ __device__ constexpr uint32_t idesc_s() { return ptx::idesc_f16_f32(128, kTS, 0, 0, kBf16 ? 1 : 0); }
+template <bool kBf16> __host__ __device__ constexpr uint32_t idesc_o() { return ptx::idesc_f16_f32(128, 256, 0, 1, kBf16 ? 1 : 0); }
 
 struct TcParams {
     WorkList wl;
     int num_heads;
     float scale_log2;  // softmax scale * log2(e)
-    void *part_o;      // [max_items, num_heads, 512] fp16 or fp32 (part_f16)
+    void *part_o;      // [max_items, num_heads, 512], element type part_kind
     float *part_lse;   // [max_items, num_heads]
-    int part_f16;      // partial element type: 1 = fp16, 0 = fp32
+    int part_kind;     // partial element type: kOutF32 / kOutF16
     void *out;         // [batch, num_heads, 512]: written directly for single-item sequences
-    int out_f16;       // out element type: 1 = fp16, 0 = fp32
+    int out_kind;      // out element type: kOutF32 / kOutF16 / kOutBF16
     float *out_lse;    // [batch, num_heads] or null
 };
 
 __device__ __forceinline__ uint32_t u32_of(float f) { return __float_as_uint(f); }
 __device__ __forceinline__ float f32_of(uint32_t u) { return __uint_as_float(u); }
 
+enum OutKind : int { kOutF32 = 0, kOutF16 = 1, kOutBF16 = 2 };
+
 __device__ __forceinline__ uint32_t pack_half2(float a, float b) {
     __half2 h = __floats2half2_rn(a, b);
     return *reinterpret_cast<uint32_t *>(&h);
+}
+
+__device__ __forceinline__ uint32_t pack_bf162(float a, float b) {
+    __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+    return *reinterpret_cast<uint32_t *>(&h);
+}
+
+template <bool kBf16>
+__device__ __forceinline__ uint32_t pack2(float a, float b) {
+    if constexpr (kBf16) return pack_bf162(a, b);
+    else return pack_half2(a, b);
 }
 
 // Ring position: slot index and phase bit of a producer/consumer cursor.
@@ -153,8 +167,9 @@ struct Ring {
 // qmap: query [B * n_h, 576], box 64 x 128.  All 128-byte swizzled.
 // kSched: the work-list schedule this instantiation serves (kSchedChunked or
 // kSchedBalanced); the other schedule's iteration code would cost registers in
-// every role.
-template <int kSched>
+// every role.  kBf16: Q* and the cache are bf16 (P goes to GEMM2 as bf16 too:
+// the MMA takes A and B of one type); otherwise fp16.
+template <int kSched, bool kBf16>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tc_decode_kernel(const __grid_constant__ CUtensorMap cmap_s,
                      const __grid_constant__ CUtensorMap cmap_o,
@@ -353,7 +368,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                             for (int k = 0; k < kKbPerSlot * 4; ++k)
                                 ptx::mma_ts(d, a0 + k * 8, b0 + (uint64_t)(((k >> 2) * kBoxS + (k & 3) * 32) >> 4),
-                                            kIdescS, k > 0 ? 1u : acc0);
+                                            idesc_s<kBf16>(), k > 0 ? 1u : acc0);
                             ptx::mma_commit(bar(kBarEmpty + rg.slot));
                             rg.next(nslots);
                         }
@@ -376,7 +391,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                                 for (int nh = 0; nh < 2; ++nh)
                                     ptx::mma_ss(tmem + nh * 256, pa + (uint64_t)((kk * 32) >> 4),
-                                                c0 + (uint64_t)((nh * 4 * kBoxO + kk * 16 * 128) >> 4), kIdescO,
+                                                c0 + (uint64_t)((nh * 4 * kBoxO + kk * 16 * 128) >> 4), idesc_o<kBf16>(),
                                                 kk > 0 ? 1u : acc0);
                             }
                             ptx::mma_commit(bar(kBarEmpty + rg.slot));
@@ -462,7 +477,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                             const float p0 = ptx::ex2(fmaf(f32_of(r[k]), p.scale_log2, neg_m));
                             const float p1 = ptx::ex2(fmaf(f32_of(r[k + 1]), p.scale_log2, neg_m));
                             s4[(k >> 1) & 3] += p0 + p1;
-                            pk[k >> 1] = pack_half2(p0, p1);
+                            pk[k >> 1] = pack2<kBf16>(p0, p1);
                         }
                         l_run = l_run * alpha + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
                         // the peer's message slot is free once GEMM2 of S tile jt-3 finished
@@ -560,7 +575,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         const bool single = ni1 - ni0 == 1;
                         const float inv_l = l_fin > 0.f ? 1.f / l_fin : 0.f;
                         const float lse = l_fin > 0.f ? (m_fin + __log2f(l_fin)) * kLn2 : -INFINITY;
-                        const bool f16 = single ? p.out_f16 != 0 : p.part_f16 != 0;
+                        // 16-bit output: fp16 from fp16 inputs, bf16 from bf16 inputs
+                        const bool f16 = (single ? p.out_kind : p.part_kind) != kOutF32;
                         const size_t row_bytes = (size_t)kDV * (f16 ? 2 : 4);
                         uint8_t *dst = single ? static_cast<uint8_t *>(p.out) + (size_t)it.b * p.num_heads * row_bytes
                                               : static_cast<uint8_t *>(p.part_o) + (size_t)i * p.num_heads * row_bytes;
@@ -582,8 +598,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                 ptx::tmem_wait_ld();
 #pragma unroll
                                 for (int j = 0; j < 16; ++j) {
-                                    wv[j] = pack_half2(f32_of(a[2 * j]) * inv_l, f32_of(a[2 * j + 1]) * inv_l);
-                                    wv[16 + j] = pack_half2(f32_of(b[2 * j]) * inv_l, f32_of(b[2 * j + 1]) * inv_l);
+                                    wv[j] = pack2<kBf16>(f32_of(a[2 * j]) * inv_l, f32_of(a[2 * j + 1]) * inv_l);
+                                    wv[16 + j] = pack2<kBf16>(f32_of(b[2 * j]) * inv_l, f32_of(b[2 * j + 1]) * inv_l);
                                 }
                             } else {
                                 ptx::tmem_ld_x32(trow + c * 32, wv);

@@ -399,11 +399,13 @@ __device__ __forceinline__ uint64_t sdesc_sw64(uint32_t addr, uint32_t lbo, uint
     return d;
 }
 
-// Instruction descriptor: f16 x f16 -> f32, dense, no negate.
+// Instruction descriptor: f16 x f16 (or bf16 x bf16) -> f32, dense, no negate.
 //   a_mn / b_mn: operand is MN-major (1) instead of K-major (0).
-__host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n, int a_mn, int b_mn) {
+//   bf16: both operands bf16 (kind::f16 takes A and B of the same type).
+__host__ __device__ constexpr uint32_t idesc_f16_f32(int m, int n, int a_mn, int b_mn, int bf16 = 0) {
     return (1u << 4)                         // [4,6)   D format: f32
-           | (0u << 7) | (0u << 10)          // [7,10) [10,13) A/B format: f16
+           | ((uint32_t)bf16 << 7)           // [7,10)  A format: 0 f16, 1 bf16
+           | ((uint32_t)bf16 << 10)          // [10,13) B format
            | ((uint32_t)a_mn << 15)          // [15]    A major
            | ((uint32_t)b_mn << 16)          // [16]    B major
            | ((uint32_t)(n >> 3) << 17)      // [17,23) N >> 3

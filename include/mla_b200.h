@@ -62,7 +62,7 @@ typedef enum {
 } mla_b200_status;
 
 /* Output element type for entry points that can emit either. */
-typedef enum { MLA_B200_OUT_F16 = 0, MLA_B200_OUT_F32 = 1 } mla_b200_out_dtype;
+typedef enum { MLA_B200_OUT_F16 = 0, MLA_B200_OUT_F32 = 1, MLA_B200_OUT_BF16 = 2 } mla_b200_out_dtype;
 
 /* Human-readable name of a status code (static string). */
 MLA_B200_API const char *mla_b200_status_string(int status);
@@ -156,6 +156,18 @@ MLA_B200_API int mla_b200_decode_batched_f16(const void *query, const void *cach
                                              float softmax_scale, int num_splits,
                                              void *out, int out_dtype, float *out_lse,
                                              void *workspace, size_t workspace_bytes, void *stream);
+
+/* Batched / variable-length bf16 decode: the same contract as
+ * mla_b200_decode_batched_f16 with query and cache in bf16 (no reference
+ * counterpart; the reference lists bf16 as future work, README.md:407).  out is
+ * bf16 (MLA_B200_OUT_BF16) or fp32 (MLA_B200_OUT_F32); P enters the second
+ * GEMM as bf16, accumulation and softmax state are fp32.  num_heads <= 128. */
+MLA_B200_API int mla_b200_decode_batched_bf16(const void *query, const void *cache,
+                                              const int32_t *cu_seqlens, int batch, int num_heads,
+                                              long long total_tokens, int max_seq_len,
+                                              float softmax_scale, int num_splits,
+                                              void *out, int out_dtype, float *out_lse,
+                                              void *workspace, size_t workspace_bytes, void *stream);
 
 /* fp32 fused decode of ONE sequence, reference semantics (scale 1/sqrt(192),
  * 512 output columns).  Replaces run_mla_decode_fused (csrc/mla_decode.hpp:18-23,

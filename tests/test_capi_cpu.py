@@ -66,6 +66,11 @@ def test_invalid_arguments_rejected_before_launch():
                                            None) == capi.ERR_INVALID_ARG
     assert lib.mla_b200_decode_batched_f16(16, 16, None, 1, 128, 64, 64, float("nan"), 0, 16, 0, None,
                                            None, 0, None) == capi.ERR_INVALID_ARG
+    # bf16 entry: fp16 output is not a bf16 output dtype; more than 128 heads unsupported
+    assert lib.mla_b200_decode_batched_bf16(16, 16, None, 1, 128, 64, 64, 1.0, 0, 16, capi.OUT_F16,
+                                            None, None, 0, None) == capi.ERR_INVALID_ARG
+    assert lib.mla_b200_decode_batched_bf16(16, 16, None, 1, 256, 64, 64, 1.0, 0, 16, capi.OUT_BF16,
+                                            None, None, 0, None) == capi.ERR_UNSUPPORTED
     # fused fp32 requires head_dim_c = 576
     assert lib.mla_b200_decode_fused_f32(16, 16, 16, 128, 512, 64, None, 0, None) == capi.ERR_UNSUPPORTED
     # naive needs all buffers

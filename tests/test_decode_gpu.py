@@ -231,3 +231,88 @@ def test_balanced_schedule_dense(mla, b, n):
         ref = oracle.mla_decode_oracle(_np(q[i]), _np(c[i]), 1.0, threads=8)
         assert_close_parity(_np(out[i]), ref, what=f"balanced dense b={i}")
     _no_device_error(mla)
+
+
+# bf16 inputs: O* is checked at the north-star bar with fp32 output (P enters the
+# second GEMM as bf16, a 2^-9 relative rounding against fp16's 2^-11).  bf16
+# output adds its own rounding of up to half a bf16 ulp, 2^-9 * |O*|, so that
+# check is elementwise |got - ref| <= 1e-2 + 2^-8 * |ref| with mean-abs <= 2e-3.
+def _assert_bf16_out(got, ref, what):
+    g = np.asarray(got, dtype=np.float64)
+    r = np.asarray(ref, dtype=np.float64)
+    d = np.abs(g - r)
+    assert np.isfinite(g).all(), f"{what}: non-finite output"
+    assert np.all(d <= 1e-2 + 2.0 ** -8 * np.abs(r)), f"{what}: max-abs {d.max():.3g}"
+    assert d.mean() <= 2e-3, f"{what}: mean-abs {d.mean():.3g}"
+
+
+@pytest.mark.parametrize("b,nh,n", [(3, 128, 300), (2, 16, 1), (40, 128, 257)])
+def test_bf16_batched_dense(mla, b, nh, n):
+    g = torch.Generator().manual_seed(31 + n)
+    q = (torch.randn(b, nh, 576, generator=g) / np.sqrt(192)).bfloat16()
+    c = torch.randn(b, n, 576, generator=g).bfloat16()
+    out32, lse = mla.mla_decode_batched(q.cuda(), c.cuda(), softmax_scale=1.0, return_lse=True,
+                                        out_dtype=torch.float32)
+    out16 = mla.mla_decode_batched(q.cuda(), c.cuda(), softmax_scale=1.0)
+    assert out16.dtype == torch.bfloat16 and out32.dtype == torch.float32
+    torch.cuda.synchronize()
+    for i in range(0, b, max(1, b // 8)):
+        ref = oracle.mla_decode_oracle(_np(q[i]), _np(c[i]), 1.0, threads=8)
+        assert_close_parity(_np(out32[i]), ref, what=f"bf16 dense fp32-out b={i}")
+        _assert_bf16_out(_np(out16[i]), ref, what=f"bf16 dense bf16-out b={i}")
+        _, ref_lse = oracle.lse_partial_oracle(_np(q[i]), _np(c[i]), 1.0)
+        np.testing.assert_allclose(_np(lse[i]), ref_lse, atol=2e-3, rtol=0)
+    _no_device_error(mla)
+
+
+def test_bf16_batched_varlen(mla, capi):
+    lens = [5, 0, 64, 96, 97, 129, 1, 700, 2500]
+    nh = 128
+    g = torch.Generator().manual_seed(32)
+    q = (torch.randn(len(lens), nh, 576, generator=g) / np.sqrt(192)).bfloat16()
+    c = torch.randn(sum(lens), 576, generator=g).bfloat16()
+    cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32)
+    refs, lo = [], 0
+    for n in lens:
+        refs.append(oracle.mla_decode_oracle(_np(q[len(refs)]), _np(c[lo:lo + n]), 1.0, threads=8)
+                    if n else None)
+        lo += n
+    for num_splits in (-1, 1, 3):
+        out = mla.mla_decode_batched(q.cuda(), c.cuda(), cu.cuda(), max_seq_len=max(lens),
+                                     softmax_scale=1.0, num_splits=num_splits)
+        out_c = capi.decode_batched(q.cuda(), c.cuda(), cu.cuda(), max(lens), 1.0,
+                                    num_splits=num_splits, out_fp32=True)
+        torch.cuda.synchronize()
+        for i, n in enumerate(lens):
+            if n == 0:
+                assert torch.count_nonzero(out[i]).item() == 0
+                assert torch.count_nonzero(out_c[i]).item() == 0
+            else:
+                _assert_bf16_out(_np(out[i]), refs[i], what=f"bf16 varlen b={i} s={num_splits}")
+                assert_close_parity(_np(out_c[i]), refs[i], what=f"bf16 varlen capi b={i}")
+    _no_device_error(mla)
+
+
+def test_bf16_beyond_fp16_range(mla):
+    """bf16 carries magnitudes fp16 cannot (|x| > 65504): the cache is scaled by
+    1e5 and the query by 1e-5 so the scores stay moderate while O* ~ 1e5; the
+    partials stay fp32, so O* matches the oracle relative to that scale."""
+    b, nh, n, s = 4, 128, 1000, 1e5
+    g = torch.Generator().manual_seed(33)
+    q = (torch.randn(b, nh, 576, generator=g) / np.sqrt(192) / s).bfloat16()
+    c = (torch.randn(b, n, 576, generator=g) * s).bfloat16()
+    out = mla.mla_decode_batched(q.cuda(), c.cuda(), softmax_scale=1.0, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    for i in range(b):
+        ref = oracle.mla_decode_oracle(_np(q[i]), _np(c[i]), 1.0, threads=8)
+        assert_close_parity(_np(out[i]) / s, ref / s, what=f"bf16 large b={i}")
+    _no_device_error(mla)
+
+
+def test_bf16_rejects_mixed_dtypes(mla):
+    q = torch.randn(1, 16, 576).bfloat16().cuda()
+    c = torch.randn(1, 64, 576).half().cuda()
+    with pytest.raises(RuntimeError):
+        mla.mla_decode_batched(q, c)
+    with pytest.raises(ValueError):
+        mla.mla_decode_batched(q, c.bfloat16(), out_dtype=torch.float16)
