@@ -12,7 +12,8 @@ module (csrc/mla_api.cpp:115-120):
   the split-KV kernels + LSE combine; fp32 -> the fp32 kernel (reference
   csrc/mla_api.cpp:86-113, whose fp32 branch is an empty stub).
 
-plus ``mla_decode_batched`` (batch / varlen), ``mla_combine`` (the LSE merge the
+plus ``mla_decode_batched`` (batch / varlen), ``mla_decode_paged`` (a paged
+latent cache through a block table), ``mla_combine`` (the LSE merge the
 multi-GPU layer uses), ``mla_get_device_error`` and the model constants the
 reference left as a TODO in mla.py:29-34.
 
@@ -32,6 +33,7 @@ from ._build import EXT_NAME, EXT_PATH, LIB_PATH
 
 __all__ = [
     "mla_decode_naive", "mla_decode_fused", "mla_decode_split", "mla_decode_batched",
+    "mla_decode_paged",
     "mla_combine", "mla_get_device_error", "NUM_HEADS", "HEAD_DIM", "HEAD_DIM_C",
     "HEAD_DIM_ROPE", "HEAD_DIM_K", "HEAD_DIM_V", "SOFTMAX_SCALE", "lib_path", "ext_path",
 ]
@@ -94,4 +96,28 @@ def mla_decode_batched(query, cache, cu_seqlens=None, max_seq_len: int = -1,
     out, lse = _ext.mla_decode_batched(query, cache, cu_seqlens, int(max_seq_len),
                                        float(softmax_scale), int(num_splits),
                                        bool(return_lse), out_fp32)
+    return (out, lse) if return_lse else out
+
+
+def mla_decode_paged(query, kv_pages, block_table, seq_lens, max_seq_len: int = -1,
+                     softmax_scale: float = SOFTMAX_SCALE, num_splits: int = -1,
+                     return_lse: bool = False, out_dtype=None):
+    """Decode over a paged latent cache.
+
+    query        [B, n_h, 576] fp16 or bf16 (n_h <= 128).
+    kv_pages     [num_pages, page_size, 576] page pool in the query's dtype;
+                 page_size a multiple of 32.
+    block_table  int32 [B, max_blocks]: token t of sequence b is row
+                 t % page_size of page block_table[b, t // page_size].
+    seq_lens     int32 [B].  Pass ``max_seq_len`` (>= every length) to avoid a
+                 device->host read.
+    Rows of a page past its sequence's end may hold anything.  Returns O*
+    [B, n_h, 512] (input dtype, or fp32 with ``out_dtype=torch.float32``) and,
+    with ``return_lse``, the natural-log LSE [B, n_h] fp32.
+    """
+    if out_dtype not in (None, torch.float32, query.dtype):
+        raise ValueError(f"mla_decode_paged: out_dtype must be None, float32 or {query.dtype}")
+    out, lse = _ext.mla_decode_paged(query, kv_pages, block_table, seq_lens, int(max_seq_len),
+                                     float(softmax_scale), int(num_splits), bool(return_lse),
+                                     out_dtype == torch.float32)
     return (out, lse) if return_lse else out

@@ -45,6 +45,10 @@ SIGNATURES = {
                                              _c_int, _vp, _c_int, _vp, _vp, _c_size, _vp]),
     "mla_b200_decode_batched_bf16": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_ll, _c_int, _c_float,
                                               _c_int, _vp, _c_int, _vp, _vp, _c_size, _vp]),
+    "mla_b200_decode_paged_f16": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                           _c_int, _c_float, _c_int, _vp, _c_int, _vp, _vp, _c_size, _vp]),
+    "mla_b200_decode_paged_bf16": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int,
+                                            _c_int, _c_float, _c_int, _vp, _c_int, _vp, _vp, _c_size, _vp]),
     "mla_b200_decode_fused_f32": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _vp, _c_size, _vp]),
     "mla_b200_decode_naive_f32": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _vp]),
     "mla_b200_combine_f32": (_c_int, [_vp, _vp, _c_int, _c_ll, _vp, _c_int, _vp, _vp]),
@@ -180,6 +184,29 @@ def decode_batched_f16(query: torch.Tensor, cache: torch.Tensor, cu_seqlens: tor
 
 
 decode_batched = decode_batched_f16
+
+
+def decode_paged(query: torch.Tensor, kv_pages: torch.Tensor, block_table: torch.Tensor,
+                 seq_lens: torch.Tensor, max_seq_len: int, softmax_scale: float,
+                 num_splits: int = -1, out_fp32: bool = False, return_lse: bool = False,
+                 workspace: torch.Tensor | None = None):
+    """Paged decode through mla_b200_decode_paged_f16 / _bf16 (by query.dtype)."""
+    b, nh = query.shape[0], query.shape[1]
+    bf16 = query.dtype == torch.bfloat16
+    out = torch.empty((b, nh, 512), dtype=torch.float32 if out_fp32 else query.dtype,
+                      device=query.device)
+    lse = torch.empty((b, nh), dtype=torch.float32, device=query.device) if return_lse else None
+    if workspace is None:
+        workspace = _workspace(workspace_size(b, nh, b * max_seq_len, max_seq_len, num_splits),
+                               query.device)
+    name = "mla_b200_decode_paged_bf16" if bf16 else "mla_b200_decode_paged_f16"
+    odt = OUT_F32 if out_fp32 else (OUT_BF16 if bf16 else OUT_F16)
+    _check(name, getattr(lib(), name)(
+        _ptr(query), _ptr(kv_pages), _ptr(block_table), _ptr(seq_lens), b, nh,
+        kv_pages.shape[0], kv_pages.shape[1], block_table.shape[1], max_seq_len,
+        float(softmax_scale), num_splits, _ptr(out), odt, _ptr(lse), _ptr(workspace),
+        workspace.numel(), _stream()))
+    return (out, lse) if return_lse else out
 
 
 def decode_fused_f32(query: torch.Tensor, cache: torch.Tensor):

@@ -176,6 +176,60 @@ std::vector<at::Tensor> mla_decode_batched(const at::Tensor &query, const at::Te
     return {out, lse};
 }
 
+// Paged decode (no reference counterpart).
+//   query [B, n_h, 576] fp16 or bf16; kv_pages [num_pages, page_size, 576] in the
+//   same dtype; block_table int32 [B, max_blocks]; seq_lens int32 [B]; all on
+//   one device.  max_seq_len < 0 reads max(seq_lens) from the device.
+// Returns (out [B, n_h, 512] in the input dtype or fp32, lse [B, n_h] fp32 or empty).
+std::vector<at::Tensor> mla_decode_paged(const at::Tensor &query, const at::Tensor &kv_pages,
+                                         const at::Tensor &block_table, const at::Tensor &seq_lens,
+                                         int64_t max_seq_len, double softmax_scale,
+                                         int64_t num_splits, bool return_lse, bool out_fp32) {
+    check_cuda(query, "query");
+    check_cuda(kv_pages, "kv_pages");
+    check_cuda(block_table, "block_table");
+    check_cuda(seq_lens, "seq_lens");
+    TORCH_CHECK(query.device() == kv_pages.device() && query.device() == block_table.device() &&
+                    query.device() == seq_lens.device(),
+                "mla_decode_paged: all tensors on one device");
+    const bool bf16 = query.scalar_type() == at::kBFloat16;
+    TORCH_CHECK((query.scalar_type() == at::kHalf || bf16) &&
+                    kv_pages.scalar_type() == query.scalar_type(),
+                "mla_decode_paged: float16 or bfloat16 inputs (query and kv_pages alike) expected");
+    TORCH_CHECK(query.dim() == 3 && query.size(2) == MLA_B200_HEAD_DIM_K,
+                "mla_decode_paged: query must be [B, n_h, 576]");
+    TORCH_CHECK(kv_pages.dim() == 3 && kv_pages.size(2) == MLA_B200_HEAD_DIM_K,
+                "mla_decode_paged: kv_pages must be [num_pages, page_size, 576]");
+    const int64_t b = query.size(0), nh = query.size(1);
+    TORCH_CHECK(block_table.scalar_type() == at::kInt && block_table.dim() == 2 &&
+                    block_table.size(0) == b,
+                "mla_decode_paged: block_table must be int32 [B, max_blocks]");
+    TORCH_CHECK(seq_lens.scalar_type() == at::kInt && seq_lens.dim() == 1 && seq_lens.size(0) == b,
+                "mla_decode_paged: seq_lens must be int32 [B]");
+    c10::cuda::CUDAGuard g(query.device());
+    const int64_t num_pages = kv_pages.size(0), page_size = kv_pages.size(1);
+    const int64_t max_blocks = block_table.size(1);
+    if (max_seq_len < 0) max_seq_len = b > 0 ? seq_lens.max().item<int64_t>() : 0;
+    at::Tensor out = at::empty({b, nh, MLA_B200_HEAD_DIM_V},
+                               query.options().dtype(out_fp32 ? at::kFloat
+                                                              : query.scalar_type()));
+    at::Tensor lse = return_lse ? at::empty({b, nh}, query.options().dtype(at::kFloat))
+                                : at::Tensor();
+    const size_t ws = mla_b200_workspace_size((int)b, (int)nh, b * max_seq_len, (int)max_seq_len,
+                                              (int)num_splits);
+    at::Tensor w = workspace(query, ws);
+    auto *fn = bf16 ? mla_b200_decode_paged_bf16 : mla_b200_decode_paged_f16;
+    const int odt = out_fp32 ? MLA_B200_OUT_F32 : (bf16 ? MLA_B200_OUT_BF16 : MLA_B200_OUT_F16);
+    check_status(fn(query.data_ptr(), kv_pages.data_ptr(), block_table.data_ptr<int32_t>(),
+                    seq_lens.data_ptr<int32_t>(), (int)b, (int)nh, (int)num_pages, (int)page_size,
+                    (int)max_blocks, (int)max_seq_len, (float)softmax_scale, (int)num_splits,
+                    out.data_ptr(), odt, return_lse ? lse.data_ptr<float>() : nullptr,
+                    w.data_ptr(), w.numel(), stream_ptr()),
+                 "mla_decode_paged");
+    if (!return_lse) lse = at::empty({0}, query.options().dtype(at::kFloat));
+    return {out, lse};
+}
+
 // LSE merge of partials: part_o [P, rows, 512] fp32, part_lse [P, rows] fp32.
 std::vector<at::Tensor> mla_combine(const at::Tensor &part_o, const at::Tensor &part_lse,
                                     bool out_fp32) {
@@ -216,6 +270,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("query"), py::arg("cache"), py::arg("num_splits") = -1);
     m.def("mla_decode_batched", &mla_decode_batched, "batched / varlen fp16 decode",
           py::arg("query"), py::arg("cache"), py::arg("cu_seqlens") = py::none(),
+          py::arg("max_seq_len") = -1, py::arg("softmax_scale") = 0.07216878364870322,
+          py::arg("num_splits") = -1, py::arg("return_lse") = false, py::arg("out_fp32") = false);
+    m.def("mla_decode_paged", &mla_decode_paged, "decode over a paged latent cache",
+          py::arg("query"), py::arg("kv_pages"), py::arg("block_table"), py::arg("seq_lens"),
           py::arg("max_seq_len") = -1, py::arg("softmax_scale") = 0.07216878364870322,
           py::arg("num_splits") = -1, py::arg("return_lse") = false, py::arg("out_fp32") = false);
     m.def("mla_combine", &mla_combine, "log-sum-exp merge of partial decodes", py::arg("part_o"),

@@ -42,6 +42,16 @@ int cuda_failure(cudaError_t e) {
     return MLA_B200_ERR_CUDA;
 }
 
+// Opts a tensor-core kernel instantiation (both schedules) into its dynamic
+// shared memory.
+template <bool kBf16, bool kPaged>
+bool set_tc_smem() {
+    return cudaFuncSetAttribute(tc::tc_decode_kernel<kSchedChunked, kBf16, kPaged>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmemBytes) == cudaSuccess &&
+           cudaFuncSetAttribute(tc::tc_decode_kernel<kSchedBalanced, kBf16, kPaged>,
+                                cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmemBytes) == cudaSuccess;
+}
+
 // Current device's properties (cached).  Returns a status.
 int current_device(int *dev_out, DevInfo *info_out) {
     int dev = 0;
@@ -74,14 +84,8 @@ int current_device(int *dev_out, DevInfo *info_out) {
         d.simt_attr_set = true;
     }
     if (d.tc_clusters == 0) {
-        if (cudaFuncSetAttribute(tc::tc_decode_kernel<kSchedChunked, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 tc::kSmemBytes) != cudaSuccess ||
-            cudaFuncSetAttribute(tc::tc_decode_kernel<kSchedBalanced, false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 tc::kSmemBytes) != cudaSuccess ||
-            cudaFuncSetAttribute(tc::tc_decode_kernel<kSchedChunked, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 tc::kSmemBytes) != cudaSuccess ||
-            cudaFuncSetAttribute(tc::tc_decode_kernel<kSchedBalanced, true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                 tc::kSmemBytes) != cudaSuccess) {
+        if (!set_tc_smem<false, false>() || !set_tc_smem<true, false>() ||
+            !set_tc_smem<false, true>() || !set_tc_smem<true, true>()) {
             return cuda_failure(cudaGetLastError());
         }
         cudaLaunchConfig_t cfg = {};
@@ -96,7 +100,7 @@ int current_device(int *dev_out, DevInfo *info_out) {
         cfg.attrs = &attr;
         cfg.numAttrs = 1;
         int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, tc::tc_decode_kernel<kSchedChunked, false>, &cfg) != cudaSuccess || n <= 0) {
+        if (cudaOccupancyMaxActiveClusters(&n, tc::tc_decode_kernel<kSchedChunked, false, false>, &cfg) != cudaSuccess || n <= 0) {
             cudaGetLastError();
             n = d.sms / 2;
         }
@@ -178,6 +182,7 @@ struct WsLayout {
     float *part_lse = nullptr;
     int *item_off = nullptr;
     int4 *items = nullptr;
+    int32_t *cu_virtual = nullptr;  // paged cache: sequence offsets built from seq_lens
     size_t bytes = 0;
 };
 
@@ -197,6 +202,8 @@ WsLayout ws_layout(void *base, long long max_items, int num_heads, int batch) {
     off = align_up(off + off_bytes, 256);
     L.items = reinterpret_cast<int4 *>(p + off);
     off = align_up(off + it_bytes, 256);
+    L.cu_virtual = reinterpret_cast<int32_t *>(p + off);
+    off = align_up(off + off_bytes, 256);
     L.bytes = off;
     return L;
 }
@@ -223,12 +230,31 @@ int launch_status() {
     return e == cudaSuccess ? MLA_B200_OK : cuda_failure(e);
 }
 
+// A page pool [pool_rows / page_size, page_size, 576] with its block table
+// [batch, max_blocks] and per-sequence lengths (device int32 arrays).
+struct PagedArgs {
+    const int32_t *block_table;
+    const int32_t *seq_lens;
+    int max_blocks;
+    int page_size;
+    long long pool_rows;
+};
+
+template <int kSched, bool kBf16, bool kPaged>
+void launch_tc(int clusters, const CUtensorMap &cs, const CUtensorMap &co, const CUtensorMap &qm,
+               const tc::TcParams &tp, cudaStream_t stream) {
+    tc::tc_decode_kernel<kSched, kBf16, kPaged><<<2 * clusters, tc::kThreads, tc::kSmemBytes, stream>>>(cs, co, qm, tp);
+}
+
 // Shared driver of the split-KV paths: plan -> partial kernel -> combine.
+// pg (tensor-core path only): the cache is a page pool; cu_seqlens is ignored
+// and the sequences' offsets on a virtual packed axis are built from
+// pg->seq_lens by the plan kernel; total_tokens is an upper bound.
 template <typename T>
 int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int batch,
                      int num_heads, long long total_tokens, int max_seq_len, float scale,
                      int num_splits, void *out, int out_dtype, float *out_lse, void *workspace,
-                     size_t workspace_bytes, cudaStream_t stream) {
+                     size_t workspace_bytes, cudaStream_t stream, const PagedArgs *pg = nullptr) {
     int dev;
     DevInfo info;
     int st = current_device(&dev, &info);
@@ -241,14 +267,22 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
     const bool tc_path = !std::is_same<T, float>::value && num_heads <= 128;
     if (kBf16 && !tc_path) return MLA_B200_ERR_UNSUPPORTED;  // bf16 has no SIMT kernel
+    if (pg != nullptr && !tc_path) return MLA_B200_ERR_UNSUPPORTED;  // paged: tensor-core kernel only
     // (A single sequence splits evenly in the chunked schedule already.)
     const bool balanced = tc_path && num_splits <= 0 && batch > 1;
-    const int chunk = chunk_for(batch, total_tokens, max_seq_len, num_splits, info.sms);
+    int chunk = chunk_for(batch, total_tokens, max_seq_len, num_splits, info.sms);
+    // paged: items start on 96-token boundaries so every 32-row box sits in one page
+    if (pg != nullptr) chunk = (int)std::min<long long>(cdiv(chunk, kTile) * kTile, 1 << 30);
     const long long max_items = balanced ? (long long)batch + info.tc_clusters
                                          : max_items_for(batch, total_tokens, chunk);
     if (max_items > (1LL << 30)) return MLA_B200_ERR_UNSUPPORTED;
     WsLayout L = ws_layout(workspace, max_items, num_heads, batch);
     if (workspace == nullptr || workspace_bytes < L.bytes) return MLA_B200_ERR_WORKSPACE;
+    const int32_t *seq_lens = nullptr;
+    if (pg != nullptr) {
+        seq_lens = pg->seq_lens;
+        cu_seqlens = L.cu_virtual;  // written by the plan kernel below
+    }
 
     WorkList wl = {};
     wl.batch = batch;
@@ -279,7 +313,8 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
             wl.cu_seqlens = cu_seqlens;
             wl.nworkers = info.tc_clusters;
             bal_clusters = info.tc_clusters;
-            plan_balanced_kernel<<<1, 1024, 0, stream>>>(cu_seqlens, batch, L.item_off);
+            plan_balanced_kernel<<<1, 1024, 0, stream>>>(cu_seqlens, batch, L.item_off, seq_lens,
+                                                         max_seq_len, L.cu_virtual);
         }
     } else if (cu_seqlens == nullptr) {
         wl.items = nullptr;
@@ -293,15 +328,18 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
         wl.seq_len = 0;
         wl.cps = 0;
         wl.max_items = (int)max_items;
+        wl.cu_seqlens = cu_seqlens;  // read by the paged kernel
         plan_varlen_kernel<<<1, 1024, 0, stream>>>(cu_seqlens, batch, chunk, L.item_off, L.items,
-                                                   (int)max_items);
+                                                   (int)max_items, seq_lens, max_seq_len, L.cu_virtual);
     }
     bool tc_direct = false;  // the tcgen05 kernel wrote single-item sequences itself
     if (wl.max_items > 0 && (!balanced || bal_clusters > 0)) {
         if (tc_path) {
             CUtensorMap cmap_s, cmap_o, qmap;
-            st = make_tmap_576(&cmap_s, cache, total_tokens, tc::kTS, kBf16);
-            if (st == MLA_B200_OK) st = make_tmap_576(&cmap_o, cache, total_tokens, tc::kTO, kBf16);
+            // paged: both maps cover the whole pool, in 32-row boxes
+            const long long map_rows = pg != nullptr ? pg->pool_rows : total_tokens;
+            st = make_tmap_576(&cmap_s, cache, map_rows, pg != nullptr ? tc::kTO : tc::kTS, kBf16);
+            if (st == MLA_B200_OK) st = make_tmap_576(&cmap_o, cache, map_rows, tc::kTO, kBf16);
             if (st == MLA_B200_OK) st = make_tmap_576(&qmap, q, (long long)batch * num_heads, 128, kBf16);
             if (st != MLA_B200_OK) return st;
             tc::TcParams tp;
@@ -317,13 +355,19 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
             tp.out_kind = out_dtype == MLA_B200_OUT_F16 ? tc::kOutF16
                           : out_dtype == MLA_B200_OUT_BF16 ? tc::kOutBF16 : tc::kOutF32;
             tp.out_lse = out_lse;
+            tp.block_table = pg != nullptr ? pg->block_table : nullptr;
+            tp.max_blocks = pg != nullptr ? pg->max_blocks : 0;
+            tp.page_size = pg != nullptr ? pg->page_size : 0;
             tc_direct = true;
             const int clusters = balanced ? bal_clusters : std::min(info.tc_clusters, wl.max_items);
             timing_mark(t_ev_start, stream);
-            if (balanced)
-                tc::tc_decode_kernel<kSchedBalanced, kBf16><<<2 * clusters, tc::kThreads, tc::kSmemBytes, stream>>>(cmap_s, cmap_o, qmap, tp);
-            else
-                tc::tc_decode_kernel<kSchedChunked, kBf16><<<2 * clusters, tc::kThreads, tc::kSmemBytes, stream>>>(cmap_s, cmap_o, qmap, tp);
+            if (pg != nullptr) {
+                if (balanced) launch_tc<kSchedBalanced, kBf16, true>(clusters, cmap_s, cmap_o, qmap, tp, stream);
+                else launch_tc<kSchedChunked, kBf16, true>(clusters, cmap_s, cmap_o, qmap, tp, stream);
+            } else {
+                if (balanced) launch_tc<kSchedBalanced, kBf16, false>(clusters, cmap_s, cmap_o, qmap, tp, stream);
+                else launch_tc<kSchedChunked, kBf16, false>(clusters, cmap_s, cmap_o, qmap, tp, stream);
+            }
             timing_mark(t_ev_stop, stream);
         } else if constexpr (!kBf16) {
             dim3 grid(wl.max_items, (unsigned)cdiv(num_heads, kSimtHeads));
@@ -376,6 +420,49 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     return launch_status();
 }
 
+}  // namespace
+
+namespace {
+template <typename T>
+int decode_paged(const void *query, const void *kv_pages, const int32_t *block_table,
+                 const int32_t *seq_lens, int batch, int num_heads, int num_pages, int page_size,
+                 int max_blocks, int max_seq_len, float softmax_scale, int num_splits, void *out,
+                 int out_dtype, float *out_lse, void *workspace, size_t workspace_bytes,
+                 void *stream) {
+    constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+    if (batch < 0 || num_heads <= 0 || num_pages < 0 || page_size <= 0 || max_blocks < 0 ||
+        max_seq_len < 0)
+        return MLA_B200_ERR_INVALID_ARG;
+    if (batch > 0 && (query == nullptr || out == nullptr || block_table == nullptr || seq_lens == nullptr))
+        return MLA_B200_ERR_INVALID_ARG;
+    if (num_pages > 0 && kv_pages == nullptr) return MLA_B200_ERR_INVALID_ARG;
+    if (kBf16 ? (out_dtype != MLA_B200_OUT_BF16 && out_dtype != MLA_B200_OUT_F32)
+              : (out_dtype != MLA_B200_OUT_F16 && out_dtype != MLA_B200_OUT_F32))
+        return MLA_B200_ERR_INVALID_ARG;
+    if (!(softmax_scale > 0.f) || !isfinite(softmax_scale)) return MLA_B200_ERR_INVALID_ARG;
+    if (!aligned(query, 16) || !aligned(kv_pages, 16) || !aligned(out, 16) || !aligned(out_lse, 4) ||
+        !aligned(block_table, 4) || !aligned(seq_lens, 4))
+        return MLA_B200_ERR_INVALID_ARG;
+    if (page_size % tc::kTO != 0) return MLA_B200_ERR_UNSUPPORTED;
+    if ((long long)max_seq_len > (long long)max_blocks * page_size) return MLA_B200_ERR_INVALID_ARG;
+    const long long pool_rows = (long long)num_pages * page_size;
+    const long long bound = (long long)batch * max_seq_len;
+    if (pool_rows >= (1LL << 31) || bound >= (1LL << 31)) return MLA_B200_ERR_UNSUPPORTED;
+    if (num_heads > 128) return MLA_B200_ERR_UNSUPPORTED;
+    if (batch == 0) return MLA_B200_OK;
+    if (num_pages == 0 || max_seq_len == 0) {
+        // every sequence is empty: O* = 0 and LSE = -inf, through the merge of no partials
+        return run_split_decode<T>(static_cast<const T *>(query), static_cast<const T *>(kv_pages),
+                                   nullptr, batch, num_heads, 0, 0, softmax_scale, num_splits, out,
+                                   out_dtype, out_lse, workspace, workspace_bytes,
+                                   static_cast<cudaStream_t>(stream));
+    }
+    PagedArgs pg{block_table, seq_lens, max_blocks, page_size, pool_rows};
+    return run_split_decode<T>(static_cast<const T *>(query), static_cast<const T *>(kv_pages),
+                               nullptr, batch, num_heads, bound, max_seq_len, softmax_scale,
+                               num_splits, out, out_dtype, out_lse, workspace, workspace_bytes,
+                               static_cast<cudaStream_t>(stream), &pg);
+}
 }  // namespace
 
 extern "C" {
@@ -522,6 +609,27 @@ int mla_b200_decode_batched_bf16(const void *query, const void *cache, const int
                                            num_heads, total_tokens, max_seq_len, softmax_scale,
                                            num_splits, out, out_dtype, out_lse, workspace,
                                            workspace_bytes, static_cast<cudaStream_t>(stream));
+}
+
+int mla_b200_decode_paged_f16(const void *query, const void *kv_pages, const int32_t *block_table,
+                              const int32_t *seq_lens, int batch, int num_heads, int num_pages,
+                              int page_size, int max_blocks_per_seq, int max_seq_len,
+                              float softmax_scale, int num_splits, void *out, int out_dtype,
+                              float *out_lse, void *workspace, size_t workspace_bytes, void *stream) {
+    return decode_paged<__half>(query, kv_pages, block_table, seq_lens, batch, num_heads, num_pages,
+                                page_size, max_blocks_per_seq, max_seq_len, softmax_scale, num_splits,
+                                out, out_dtype, out_lse, workspace, workspace_bytes, stream);
+}
+
+int mla_b200_decode_paged_bf16(const void *query, const void *kv_pages, const int32_t *block_table,
+                               const int32_t *seq_lens, int batch, int num_heads, int num_pages,
+                               int page_size, int max_blocks_per_seq, int max_seq_len,
+                               float softmax_scale, int num_splits, void *out, int out_dtype,
+                               float *out_lse, void *workspace, size_t workspace_bytes, void *stream) {
+    return decode_paged<__nv_bfloat16>(query, kv_pages, block_table, seq_lens, batch, num_heads,
+                                       num_pages, page_size, max_blocks_per_seq, max_seq_len,
+                                       softmax_scale, num_splits, out, out_dtype, out_lse, workspace,
+                                       workspace_bytes, stream);
 }
 
 int mla_b200_decode_fused_f32(const float *query, const float *cache, float *out, int num_heads,

@@ -235,16 +235,66 @@ __global__ void __launch_bounds__(32 * kRowsPerCombineBlock) combine_rows_kernel
         out_lse[(size_t)b * num_heads + h] = wsum > 0.f ? mx + __logf(wsum) : -INFINITY;
 }
 
-// Expands cu_seqlens[B+1] into item_off[B+1] (exclusive prefix of per-sequence
-// item counts) and items[] = {b, row_begin, row_end, 0}.  One block.
-__global__ void __launch_bounds__(1024) plan_varlen_kernel(const int32_t *__restrict__ cu_seqlens,
-                                                           int batch, int chunk,
-                                                           int *__restrict__ item_off,
-                                                           int4 *__restrict__ items,
-                                                           int max_items) {
+// Paged cache: per-sequence lengths (clamped to max_len) into offsets cu[B+1] on
+// a virtual packed axis, which the schedules then walk like a packed batch.
+// Called by all 1024 threads of one block; cu is complete and visible to the
+// block on return.
+__device__ void lens_to_offsets(const int32_t *lens, int batch, int max_len, int32_t *cu) {
     __shared__ int warp_tot[32];
     __shared__ int carry_s;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (tid == 0) carry_s = 0;
+    __syncthreads();
+    for (int base = 0; base < batch; base += 1024) {
+        const int b = base + tid;
+        const int len = b < batch ? min(max(lens[b], 0), max_len) : 0;
+        int v = len;
+#pragma unroll
+        for (int o = 1; o < 32; o <<= 1) {
+            const int n = __shfl_up_sync(0xffffffffu, v, o);
+            if (lane >= o) v += n;
+        }
+        if (lane == 31) warp_tot[warp] = v;
+        __syncthreads();
+        if (warp == 0) {
+            int w = warp_tot[lane];
+#pragma unroll
+            for (int o = 1; o < 32; o <<= 1) {
+                const int n = __shfl_up_sync(0xffffffffu, w, o);
+                if (lane >= o) w += n;
+            }
+            warp_tot[lane] = w;
+        }
+        __syncthreads();
+        const int excl = carry_s + (warp > 0 ? warp_tot[warp - 1] : 0) + v - len;
+        if (b < batch) cu[b] = excl;
+        __syncthreads();
+        if (tid == 1023) carry_s = excl + len;
+        __syncthreads();
+    }
+    if (tid == 0) cu[batch] = carry_s;
+    __syncthreads();
+}
+
+// Expands cu_seqlens[B+1] into item_off[B+1] (exclusive prefix of per-sequence
+// item counts) and items[] = {b, row_begin, row_end, 0}.  One block.  With
+// seq_lens (paged cache) the offsets are first built into cu_out from the
+// lengths and used as cu_seqlens.
+__global__ void __launch_bounds__(1024) plan_varlen_kernel(const int32_t *cu_seqlens,
+                                                           int batch, int chunk,
+                                                           int *__restrict__ item_off,
+                                                           int4 *__restrict__ items,
+                                                           int max_items,
+                                                           const int32_t *seq_lens = nullptr,
+                                                           int max_len = 0,
+                                                           int32_t *cu_out = nullptr) {
+    __shared__ int warp_tot[32];
+    __shared__ int carry_s;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (seq_lens != nullptr) {
+        lens_to_offsets(seq_lens, batch, max_len, cu_out);
+        cu_seqlens = cu_out;
+    }
     if (tid == 0) carry_s = 0;
     __syncthreads();
     for (int base = 0; base < batch; base += 1024) {
@@ -294,11 +344,18 @@ __global__ void __launch_bounds__(1024) plan_varlen_kernel(const int32_t *__rest
 // Balanced schedule, varlen: cost_off[b] = sum over b' < b of the cost of
 // sequence b' (kItemCost + its 96-row tiles, 0 for an empty sequence), and
 // cost_off[B] the total.  One block; a block-wide scan per 1024 sequences.
-__global__ void __launch_bounds__(1024) plan_balanced_kernel(const int32_t *__restrict__ cu_seqlens,
-                                                             int batch, int *__restrict__ cost_off) {
+__global__ void __launch_bounds__(1024) plan_balanced_kernel(const int32_t *cu_seqlens,
+                                                             int batch, int *__restrict__ cost_off,
+                                                             const int32_t *seq_lens = nullptr,
+                                                             int max_len = 0,
+                                                             int32_t *cu_out = nullptr) {
     __shared__ int warp_tot[32];
     __shared__ int carry_s;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    if (seq_lens != nullptr) {
+        lens_to_offsets(seq_lens, batch, max_len, cu_out);
+        cu_seqlens = cu_out;
+    }
     if (tid == 0) carry_s = 0;
     __syncthreads();
     for (int base = 0; base < batch; base += 1024) {

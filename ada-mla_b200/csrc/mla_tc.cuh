@@ -92,7 +92,9 @@ enum BarId {
     kBarCorr = kBarPFull + kMsgSlots,  // [3] O-CTA: O ready for GEMM2     (count 128)
     kBarMmaDone = kBarCorr + kMsgSlots,// [3] O-CTA: GEMM2 of a message done (count 1, commit)
     kBarDrain = kBarMmaDone + kMsgSlots,// [2] an MMA issuer's ops retired (teardown)
-    kNumBars = kBarDrain + 2
+    kBarZReq = kBarDrain + 2,          //     O-CTA, paged: GEMM2 issuer asks for a tile's tail rows zeroed (count 1)
+    kBarZDone = kBarZReq + 1,          //     O-CTA, paged: tail rows zeroed (count 1)
+    kNumBars = kBarZDone + 1
 };
 
 // Shared-memory layout (offsets from a 1024-aligned base).  Each role has its
@@ -106,7 +108,8 @@ constexpr int kEndO = kOffMsgO + kMsgSlots * kMsgStride;         // 210944
 constexpr int kOffBar = kEndS > kEndO ? kEndS : kEndO;
 constexpr int kOffSlot = kOffBar + kNumBars * 8;
 constexpr int kOffAbort = kOffSlot + 4;
-constexpr int kOffEpi = (kOffAbort + 4 + 1023) / 1024 * 1024;    // O-CTA epilogue staging
+constexpr int kOffZArg = kOffAbort + 4;                          // paged zero request: {tile, tail rows, stop}
+constexpr int kOffEpi = (kOffZArg + 12 + 1023) / 1024 * 1024;    // O-CTA epilogue staging
 constexpr int kEpiWarpBytes = 32 * 128;                          // one warp's 32 rows x 128 bytes
 constexpr int kSmemBytes = kOffEpi + 4 * kEpiWarpBytes + 1024;   // + 1024 alignment slack
 static_assert(kSmemBytes <= 232448, "dynamic shared memory limit");
@@ -129,10 +132,29 @@ struct TcParams {
     void *part_o;      // [max_items, num_heads, 512], element type part_kind
     float *part_lse;   // [max_items, num_heads]
     int part_kind;     // partial element type: kOutF32 / kOutF16
+    int page_size;     // paged: a multiple of kTO
     void *out;         // [batch, num_heads, 512]: written directly for single-item sequences
     int out_kind;      // out element type: kOutF32 / kOutF16 / kOutBF16
+    int max_blocks;    // paged
     float *out_lse;    // [batch, num_heads] or null
+    // Paged cache (kPaged): the maps address the page pool as rows
+    // [num_pages * page_size, 576]; token t of sequence b lives in pool row
+    // block_table[b * max_blocks + t / page_size] * page_size + t % page_size,
+    // and wl.cu_seqlens holds the sequences' offsets on a virtual packed axis.
+    // (page_size and max_blocks sit in alignment padding: the kernel's code
+    // generation for the contiguous cache is sensitive to this struct's size.)
+    const int32_t *block_table;
 };
+
+// Pool row of the 32-row box starting at token t (a multiple of kTO) of
+// sequence b.  Boxes past the sequence's last token re-read its last box: the
+// softmax masks those columns, so the bytes only have to be addressable.
+__device__ __forceinline__ int paged_row(const TcParams &p, int b, int t, int seq_len) {
+    const int tc = min(t, (seq_len - 1) & ~(kTO - 1));
+    const int blk = tc / p.page_size;
+    const int pg = p.block_table[(long long)b * p.max_blocks + blk];
+    return pg * p.page_size + (tc - blk * p.page_size);
+}
 
 __device__ __forceinline__ uint32_t u32_of(float f) { return __float_as_uint(f); }
 __device__ __forceinline__ float f32_of(uint32_t u) { return __uint_as_float(u); }
@@ -163,13 +185,16 @@ struct Ring {
     }
 };
 
-// cmap_s: cache [rows, 576], box 64 x 96.  cmap_o: same cache, box 64 x 32.
-// qmap: query [B * n_h, 576], box 64 x 128.  All 128-byte swizzled.
+// cmap_s: cache [rows, 576], box 64 x 96 (paged: box 64 x 32, the S-CTA
+// loading each K-block of a tile as three boxes, one per 32-token piece of a
+// page).  cmap_o: same cache, box 64 x 32.  qmap: query [B * n_h, 576], box
+// 64 x 128.  All 128-byte swizzled.
 // kSched: the work-list schedule this instantiation serves (kSchedChunked or
 // kSchedBalanced); the other schedule's iteration code would cost registers in
 // every role.  kBf16: Q* and the cache are bf16 (P goes to GEMM2 as bf16 too:
-// the MMA takes A and B of one type); otherwise fp16.
-template <int kSched, bool kBf16>
+// the MMA takes A and B of one type); otherwise fp16.  kPaged: the cache is a
+// page pool addressed through p.block_table.
+template <int kSched, bool kBf16, bool kPaged>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tc_decode_kernel(const __grid_constant__ CUtensorMap cmap_s,
                      const __grid_constant__ CUtensorMap cmap_o,
@@ -207,6 +232,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             ptx::mbar_init(bar(kBarDrain + i), 1);
         }
         ptx::mbar_init(bar(kBarQReady), 1);
+        if constexpr (kPaged) {
+            ptx::mbar_init(bar(kBarZReq), 1);
+            ptx::mbar_init(bar(kBarZDone), 1);
+            reinterpret_cast<volatile int *>(smem + kOffZArg)[2] = 0;
+        }
         *abort_flag = 0;
         ptx::fence_mbarrier_init_cluster();
     }
@@ -253,27 +283,61 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     }
                     prev_b = it.b;
                 }
+                // paged: pool rows of the current tile's three 32-row pieces, and
+                // of the next tile's, read a tile ahead so the block-table
+                // latency stays off the refill path
+                int seq_len = 0, tok0 = 0, pr[kOPerS], pn[kOPerS];
+                if constexpr (kPaged) {
+                    const int c0 = wl.cu_seqlens[it.b];
+                    seq_len = wl.cu_seqlens[it.b + 1] - c0;
+                    tok0 = (int)it.row0 - c0;
+#pragma unroll
+                    for (int c = 0; c < kOPerS; ++c) pr[c] = paged_row(p, it.b, tok0 + c * kTO, seq_len);
+                }
                 for (int t0 = 0; ok && t0 < it.len; t0 += kTS) {
                     const int row = (int)(it.row0 + t0);
+                    if constexpr (kPaged) {
+#pragma unroll
+                        for (int c = 0; c < kOPerS; ++c) pn[c] = paged_row(p, it.b, tok0 + t0 + kTS + c * kTO, seq_len);
+                    }
                     if (role == 0) {
-                        for (int sl = 0; sl < kSlotsPerTile; ++sl) {
-                            if (!acquire()) { ok = false; break; }
-                            const uint32_t dst = sbase + kOffRing + rg.slot * kSlotS;
-                            ptx::mbar_arrive_expect_tx(bar(kBarFull + rg.slot), kSlotS);
-                            for (int j = 0; j < kKbPerSlot; ++j)
-                                ptx::tma_load_2d(dst + j * kBoxS, &cmap_s, (sl * kKbPerSlot + j) * 64, row, bar(kBarFull + rg.slot));
-                            rg.next(nslots);
+                        if constexpr (kPaged) {
+                            for (int sl = 0; sl < kSlotsPerTile; ++sl) {
+                                if (!acquire()) { ok = false; break; }
+                                const uint32_t dst = sbase + kOffRing + rg.slot * kSlotS;
+                                ptx::mbar_arrive_expect_tx(bar(kBarFull + rg.slot), kSlotS);
+                                for (int j = 0; j < kKbPerSlot; ++j)
+#pragma unroll
+                                    for (int c = 0; c < kOPerS; ++c)
+                                        ptx::tma_load_2d(dst + j * kBoxS + c * kBoxO, &cmap_s, (sl * kKbPerSlot + j) * 64, pr[c], bar(kBarFull + rg.slot));
+                                rg.next(nslots);
+                            }
+                        } else {
+                            for (int sl = 0; sl < kSlotsPerTile; ++sl) {
+                                if (!acquire()) { ok = false; break; }
+                                const uint32_t dst = sbase + kOffRing + rg.slot * kSlotS;
+                                ptx::mbar_arrive_expect_tx(bar(kBarFull + rg.slot), kSlotS);
+                                for (int j = 0; j < kKbPerSlot; ++j)
+                                    ptx::tma_load_2d(dst + j * kBoxS, &cmap_s, (sl * kKbPerSlot + j) * 64, row, bar(kBarFull + rg.slot));
+                                rg.next(nslots);
+                            }
                         }
                     } else {
                         const int nct = (min(kTS, it.len - t0) + kTO - 1) / kTO;
                         for (int ct = 0; ct < nct; ++ct) {
+                            int r = row + ct * kTO;
+                            if constexpr (kPaged) r = ct == 0 ? pr[0] : (ct == 1 ? pr[1] : pr[2]);
                             if (!acquire()) { ok = false; break; }
                             const uint32_t dst = sbase + kOffRing + rg.slot * kSlotO;
                             ptx::mbar_arrive_expect_tx(bar(kBarFull + rg.slot), kSlotO);
                             for (int kb = 0; kb < kVBlocks; ++kb)
-                                ptx::tma_load_2d(dst + kb * kBoxO, &cmap_o, kb * 64, row + ct * kTO, bar(kBarFull + rg.slot));
+                                ptx::tma_load_2d(dst + kb * kBoxO, &cmap_o, kb * 64, r, bar(kBarFull + rg.slot));
                             rg.next(nslots);
                         }
+                    }
+                    if constexpr (kPaged) {
+#pragma unroll
+                        for (int c = 0; c < kOPerS; ++c) pr[c] = pn[c];
                     }
                 }
             }
@@ -297,7 +361,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int nslots = role == 0 ? kSlotsS : kSlotsO;
             const uint32_t me = warp == 1 ? 0u : 1u;
             Ring rg;
-            uint32_t jt = 0, qphase = 0, nseq = 0, qready_seq = 0;
+            uint32_t jt = 0, qphase = 0, nseq = 0, qready_seq = 0, nzero = 0;
             int prev_b = -1;
             bool ok = true;
             ItemCursor cur = items_begin<kSched>(wl, cid, ncl);
@@ -306,6 +370,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             while (ok && items_next<kSched>(wl, cur, it, i)) {
                 const bool new_seq = role == 0 && it.b != prev_b;
                 prev_b = it.b;
+                bool at_end = false;  // paged: the item ends at its sequence's last token
+                if constexpr (kPaged) at_end = it.row0 + it.len == wl.cu_seqlens[it.b + 1];
                 for (int t0 = 0; ok && t0 < it.len; t0 += kTS, ++jt) {
                     if (role == 0) {
                         const bool mine = (jt & 1u) == me;
@@ -383,6 +449,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         const int nct = (min(kTS, it.len - t0) + kTO - 1) / kTO;
                         for (int ct = 0; ct < nct; ++ct) {
                             if (!ptx::mbar_spin(bar(kBarFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
+                            if constexpr (kPaged) {
+                                // the sequence's last tile: rows past its end are zeroed by warp 3
+                                const int tail = (it.len - t0) % kTO;
+                                if (at_end && ct == nct - 1 && t0 + kTS >= it.len && tail != 0) {
+                                    volatile int *za = reinterpret_cast<volatile int *>(smem + kOffZArg);
+                                    za[0] = (int)(sbase + kOffRing + rg.slot * kSlotO);
+                                    za[1] = tail;
+                                    ptx::mbar_arrive(bar(kBarZReq));
+                                    if (!ptx::mbar_wait(bar(kBarZDone), nzero & 1, kErrWaitMma)) { ok = false; break; }
+                                    ++nzero;
+                                    ptx::tc_fence_after();
+                                }
+                            }
                             const uint64_t c0 = ptx::sdesc_sw128(sbase + kOffRing + rg.slot * kSlotO, kBoxO, 1024);
                             const uint64_t pa = p0 + (uint64_t)(ct * (kSubP >> 4));
                             const uint32_t acc0 = (t0 > 0 || ct > 0) ? 1u : 0u;
@@ -404,9 +483,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 }
             }
             if (!ok) *abort_flag = 1;
+            if constexpr (kPaged) {
+                if (role == 1) {  // release the zeroing warp
+                    reinterpret_cast<volatile int *>(smem + kOffZArg)[2] = 1;
+                    ptx::mbar_arrive(bar(kBarZReq));
+                }
+            }
             // every MMA this thread issued has retired before TMEM is freed
             ptx::mma_commit(bar(kBarDrain + me));
             ptx::mbar_wait(bar(kBarDrain + me), 0, kErrWaitMma);
+        }
+    } else if (kPaged && warp == 3) {
+        // ------------------------------------------------------------ O-CTA, paged: tail zeroing
+        // Rows of a sequence's last C tile past its end hold whatever the page
+        // held, not necessarily finite numbers; P is 0 there, but 0 x NaN is NaN
+        // in GEMM2.  The GEMM2 issuer, holding such a tile (landed), posts its
+        // address and valid rows; this warp zeroes the rest and answers.  The
+        // request and answer phases alternate, so the parities never alias.
+        volatile int *za = reinterpret_cast<volatile int *>(smem + kOffZArg);
+        for (uint32_t n = 0;; ++n) {
+            const bool w = ptx::mbar_wait(bar(kBarZReq), n & 1, kErrWaitMma);
+            if (!__all_sync(0xffffffffu, w) || za[2] != 0) break;
+            const uint32_t base = (uint32_t)za[0];
+            const int tail = za[1];
+            const int pieces = (kTO - tail) * kVBlocks * 8;  // 16-byte pieces past the end
+            for (int q = lane; q < pieces; q += 32) {
+                const int rb = q >> 3;
+                ptx::st_shared_v4(base + (rb % kVBlocks) * kBoxO + (tail + rb / kVBlocks) * 128 + (q & 7) * 16, 0u, 0u, 0u, 0u);
+            }
+            ptx::fence_proxy_async_smem();  // the zeros before GEMM2's operand reads
+            __syncwarp();
+            if (lane == 0) ptx::mbar_arrive(bar(kBarZDone));
         }
     } else if (warp >= 4) {
         // ------------------------------------------------------------ math warpgroup

@@ -169,6 +169,35 @@ MLA_B200_API int mla_b200_decode_batched_bf16(const void *query, const void *cac
                                               void *out, int out_dtype, float *out_lse,
                                               void *workspace, size_t workspace_bytes, void *stream);
 
+/* Paged latent cache (no counterpart in the reference, whose cache is one
+ * contiguous [N, 576] tensor, csrc/mla_api.cpp:20).  The cache is a page pool
+ * kv_pages [num_pages, page_size, 576] (fp16 for _f16, bf16 for _bf16); token t
+ * of sequence b is row t % page_size of page block_table[b * max_blocks_per_seq
+ * + t / page_size].  block_table int32 [batch, max_blocks_per_seq] and seq_lens
+ * int32 [batch] are device arrays.  page_size is a multiple of 32 (64 and 128
+ * are the usual sizes); max_seq_len bounds every seq_lens[b] (longer lengths
+ * are clamped to it) and max_seq_len <= max_blocks_per_seq * page_size.  Page
+ * rows past a sequence's end may hold any bits (NaN included): they are never
+ * part of the result.  A page index outside [0, num_pages) reads zeros.
+ * Workspace: mla_b200_workspace_size(batch, num_heads, batch * max_seq_len,
+ * max_seq_len, num_splits).  Otherwise the contract of
+ * mla_b200_decode_batched_f16 / _bf16 (out_dtype F16 or F32 for _f16, BF16 or
+ * F32 for _bf16); num_heads <= 128. */
+MLA_B200_API int mla_b200_decode_paged_f16(const void *query, const void *kv_pages,
+                                           const int32_t *block_table, const int32_t *seq_lens,
+                                           int batch, int num_heads, int num_pages, int page_size,
+                                           int max_blocks_per_seq, int max_seq_len,
+                                           float softmax_scale, int num_splits, void *out,
+                                           int out_dtype, float *out_lse, void *workspace,
+                                           size_t workspace_bytes, void *stream);
+MLA_B200_API int mla_b200_decode_paged_bf16(const void *query, const void *kv_pages,
+                                            const int32_t *block_table, const int32_t *seq_lens,
+                                            int batch, int num_heads, int num_pages, int page_size,
+                                            int max_blocks_per_seq, int max_seq_len,
+                                            float softmax_scale, int num_splits, void *out,
+                                            int out_dtype, float *out_lse, void *workspace,
+                                            size_t workspace_bytes, void *stream);
+
 /* fp32 fused decode of ONE sequence, reference semantics (scale 1/sqrt(192),
  * 512 output columns).  Replaces run_mla_decode_fused (csrc/mla_decode.hpp:18-23,
  * csrc/mla_decode_fused_fwd_sm89.cu:6-60).  head_dim_c must be 576. */

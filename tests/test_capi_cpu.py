@@ -71,6 +71,16 @@ def test_invalid_arguments_rejected_before_launch():
                                             None, None, 0, None) == capi.ERR_INVALID_ARG
     assert lib.mla_b200_decode_batched_bf16(16, 16, None, 1, 256, 64, 64, 1.0, 0, 16, capi.OUT_BF16,
                                             None, None, 0, None) == capi.ERR_UNSUPPORTED
+    # paged: page size not a multiple of 32; max_seq_len beyond the block table;
+    # fp16 entry with a bf16 output dtype
+    assert lib.mla_b200_decode_paged_f16(16, 16, 16, 16, 1, 128, 4, 48, 4, 64, 1.0, 0, 16, capi.OUT_F16,
+                                         None, None, 0, None) == capi.ERR_UNSUPPORTED
+    assert lib.mla_b200_decode_paged_f16(16, 16, 16, 16, 1, 128, 4, 64, 2, 200, 1.0, 0, 16, capi.OUT_F16,
+                                         None, None, 0, None) == capi.ERR_INVALID_ARG
+    assert lib.mla_b200_decode_paged_f16(16, 16, 16, 16, 1, 128, 4, 64, 4, 64, 1.0, 0, 16, capi.OUT_BF16,
+                                         None, None, 0, None) == capi.ERR_INVALID_ARG
+    assert lib.mla_b200_decode_paged_bf16(16, 16, None, 16, 1, 128, 4, 64, 4, 64, 1.0, 0, 16,
+                                          capi.OUT_BF16, None, None, 0, None) == capi.ERR_INVALID_ARG
     # fused fp32 requires head_dim_c = 576
     assert lib.mla_b200_decode_fused_f32(16, 16, 16, 128, 512, 64, None, 0, None) == capi.ERR_UNSUPPORTED
     # naive needs all buffers

@@ -316,3 +316,120 @@ def test_bf16_rejects_mixed_dtypes(mla):
         mla.mla_decode_batched(q, c)
     with pytest.raises(ValueError):
         mla.mla_decode_batched(q, c.bfloat16(), out_dtype=torch.float16)
+
+
+# ---------------------------------------------------------------------------
+# Paged latent cache
+
+
+def _paged(lens, page_size, nh, seed, dtype=torch.float16, spare_pages=3):
+    """Packed per-sequence caches scattered over a shuffled page pool whose unused
+    rows hold NaN; block-table slots past a sequence's pages hold -1."""
+    g = torch.Generator().manual_seed(seed)
+    q = (torch.randn(len(lens), nh, 576, generator=g) / np.sqrt(192)).to(dtype)
+    packed = torch.randn(sum(lens), 576, generator=g).to(dtype)
+    npg = [-(-n // page_size) for n in lens]
+    num_pages = sum(npg) + spare_pages
+    perm = torch.randperm(num_pages, generator=g)
+    pool = torch.full((num_pages, page_size, 576), float("nan"), dtype=dtype)
+    max_blocks = max(max(npg), 1) + 1
+    bt = torch.full((len(lens), max_blocks), -1, dtype=torch.int32)
+    lo, used = 0, 0
+    for b, n in enumerate(lens):
+        for k in range(npg[b]):
+            pg = int(perm[used])
+            used += 1
+            bt[b, k] = pg
+            rows = packed[lo + k * page_size: lo + min(n, (k + 1) * page_size)]
+            pool[pg, :rows.shape[0]] = rows
+        lo += n
+    cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32)
+    return q, packed, cu, pool, bt, torch.tensor(lens, dtype=torch.int32)
+
+
+@pytest.mark.parametrize("page_size", [32, 64, 128])
+@pytest.mark.parametrize("nh", [128, 16])
+def test_paged_matches_packed_and_oracle(mla, page_size, nh):
+    """Automatic split: the paged decode runs the same schedule as the packed
+    varlen decode of the same sequences, so the outputs agree bit for bit; both
+    match the oracle.  NaN in unused page rows must not reach the result."""
+    lens = [1, 31, 32, 33, 0, 64, 95, 96, 97, 128, 129, 700, 2500]
+    q, packed, cu, pool, bt, sl = _paged(lens, page_size, nh, seed=40 + page_size + nh)
+    out_p, lse_p = mla.mla_decode_paged(q.cuda(), pool.cuda(), bt.cuda(), sl.cuda(),
+                                        max_seq_len=max(lens), softmax_scale=1.0, return_lse=True)
+    out_v, lse_v = mla.mla_decode_batched(q.cuda(), packed.cuda(), cu.cuda(), max_seq_len=max(lens),
+                                          softmax_scale=1.0, return_lse=True)
+    torch.cuda.synchronize()
+    assert torch.equal(out_p, out_v)
+    assert torch.equal(lse_p[sl.cuda() > 0], lse_v[sl.cuda() > 0])
+    lo = 0
+    for i, n in enumerate(lens):
+        if n == 0:
+            assert torch.count_nonzero(out_p[i]).item() == 0
+        else:
+            ref = oracle.mla_decode_oracle(_np(q[i]), _np(packed[lo:lo + n]), 1.0, threads=8)
+            assert_close_parity(_np(out_p[i]), ref, what=f"paged ps={page_size} b={i} n={n}")
+        lo += n
+    _no_device_error(mla)
+
+
+@pytest.mark.parametrize("num_splits", [-1, 1, 3, 7])
+def test_paged_single_long_sequence(mla, capi, num_splits):
+    lens = [20000 + 17]
+    q, packed, cu, pool, bt, sl = _paged(lens, 64, 128, seed=50)
+    ref = oracle.mla_decode_oracle(_np(q[0]), _np(packed), REF_SCALE, threads=8)
+    out = mla.mla_decode_paged(q.cuda(), pool.cuda(), bt.cuda(), sl.cuda(), max_seq_len=lens[0],
+                               softmax_scale=REF_SCALE, num_splits=num_splits)
+    out_c = capi.decode_paged(q.cuda(), pool.cuda(), bt.cuda(), sl.cuda(), lens[0], REF_SCALE,
+                              num_splits=num_splits, out_fp32=True)
+    torch.cuda.synchronize()
+    assert_close_parity(_np(out[0]), ref, what=f"paged long s={num_splits}")
+    assert_close_parity(_np(out_c[0]), ref, what=f"paged long capi s={num_splits}")
+    _no_device_error(mla)
+
+
+@pytest.mark.parametrize("num_splits", [1, 2, 5])
+def test_paged_explicit_splits_batch(mla, num_splits):
+    lens = [300, 0, 1, 4097, 96, 1000]
+    q, packed, cu, pool, bt, sl = _paged(lens, 128, 128, seed=51 + num_splits)
+    out = mla.mla_decode_paged(q.cuda(), pool.cuda(), bt.cuda(), sl.cuda(), max_seq_len=max(lens),
+                               softmax_scale=1.0, num_splits=num_splits)
+    torch.cuda.synchronize()
+    lo = 0
+    for i, n in enumerate(lens):
+        if n == 0:
+            assert torch.count_nonzero(out[i]).item() == 0
+        else:
+            ref = oracle.mla_decode_oracle(_np(q[i]), _np(packed[lo:lo + n]), 1.0, threads=8)
+            assert_close_parity(_np(out[i]), ref, what=f"paged splits={num_splits} b={i}")
+        lo += n
+    _no_device_error(mla)
+
+
+def test_paged_bf16(mla):
+    lens = [5, 0, 64, 97, 1500, 33]
+    q, packed, cu, pool, bt, sl = _paged(lens, 64, 128, seed=52, dtype=torch.bfloat16)
+    out = mla.mla_decode_paged(q.cuda(), pool.cuda(), bt.cuda(), sl.cuda(), softmax_scale=1.0,
+                               out_dtype=torch.float32)
+    out_v = mla.mla_decode_batched(q.cuda(), packed.cuda(), cu.cuda(), max_seq_len=max(lens),
+                                   softmax_scale=1.0, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    assert torch.equal(out, out_v)
+    lo = 0
+    for i, n in enumerate(lens):
+        if n:
+            ref = oracle.mla_decode_oracle(_np(q[i]), _np(packed[lo:lo + n]), 1.0, threads=8)
+            assert_close_parity(_np(out[i]), ref, what=f"paged bf16 b={i}")
+        lo += n
+    _no_device_error(mla)
+
+
+def test_paged_rejects_bad_shapes(mla):
+    q = torch.randn(2, 16, 576).half().cuda()
+    pool = torch.randn(4, 48, 576).half().cuda()   # page size not a multiple of 32
+    bt = torch.zeros(2, 2, dtype=torch.int32).cuda()
+    sl = torch.tensor([10, 20], dtype=torch.int32).cuda()
+    with pytest.raises(RuntimeError):
+        mla.mla_decode_paged(q, pool, bt, sl)
+    with pytest.raises(RuntimeError):
+        mla.mla_decode_paged(q, pool[:, :32].contiguous(), bt[:1], sl)  # block table rows != B
