@@ -126,21 +126,49 @@ PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
     return fn;
 }
 
-// 2-D view [rows, 576] fp16 with (64 x box_rows) boxes and 128-byte swizzle
-// (the UMMA K-major / MN-major SW128 operand layout).
-int make_tmap_576(CUtensorMap *map, const void *base, long long rows, int box_rows, bool bf16 = false) {
+int encode_tmap(CUtensorMap *map, const void *base, cuuint32_t rank, const cuuint64_t *dims,
+                const cuuint64_t *strides, const cuuint32_t *box, bool bf16) {
     auto enc = tmap_encoder();
     if (enc == nullptr) return cuda_failure(cudaErrorSymbolNotFound);
-    cuuint64_t dims[2] = {(cuuint64_t)kDK, (cuuint64_t)rows};
-    cuuint64_t strides[1] = {(cuuint64_t)kDK * 2};
-    cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
-    cuuint32_t estr[2] = {1, 1};
-    const CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, 2,
-                           const_cast<void *>(base), dims,
-                           strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                           CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    const cuuint32_t estr[4] = {1, 1, 1, 1};
+    const CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank,
+                           const_cast<void *>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
+                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? MLA_B200_OK : cuda_failure(cudaErrorInvalidValue);
+}
+
+// 2-D view [rows, 576] with (64 x box_rows) boxes and 128-byte swizzle (the
+// UMMA K-major / MN-major SW128 operand layout).
+int make_tmap_576(CUtensorMap *map, const void *base, long long rows, int box_rows, bool bf16 = false) {
+    const cuuint64_t dims[2] = {(cuuint64_t)kDK, (cuuint64_t)rows};
+    const cuuint64_t strides[1] = {(cuuint64_t)kDK * 2};
+    const cuuint32_t box[2] = {64, (cuuint32_t)box_rows};
+    return encode_tmap(map, base, 2, dims, strides, box, bf16);
+}
+
+// 3-D view (64 columns, rows, 9 column blocks) of the same [rows, 576] cache:
+// the block axis (stride 128 B) is outermost, so one box of (64, box_rows,
+// box_blocks) lands in shared memory as box_blocks consecutive [box_rows x 64]
+// SW128 K-blocks -- the layout of box_blocks separate 2-D loads, in one
+// instruction.
+int make_tmap_blocks(CUtensorMap *map, const void *base, long long rows, int box_rows, int box_blocks,
+                     bool bf16) {
+    const cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(kDK / 64)};
+    const cuuint64_t strides[2] = {(cuuint64_t)kDK * 2, 128};
+    const cuuint32_t box[3] = {64, (cuuint32_t)box_rows, (cuuint32_t)box_blocks};
+    return encode_tmap(map, base, 3, dims, strides, box, bf16);
+}
+
+// 4-D view (64 columns, 8 rows, 9 column blocks, rows / 8 row groups) of a page
+// pool with rows % 8 == 0.  A box (64, 8, 3, 4) takes 32 rows x 3 K-blocks and
+// lands as 4 row groups of 3 interleaved 1 KB SW128 atoms: K-block j's 8-row
+// groups sit 3 KB apart (the GEMM1 B descriptor's stride for paged tiles).
+int make_tmap_pool_groups(CUtensorMap *map, const void *base, long long rows, bool bf16) {
+    const cuuint64_t dims[4] = {64, 8, (cuuint64_t)(kDK / 64), (cuuint64_t)(rows / 8)};
+    const cuuint64_t strides[3] = {(cuuint64_t)kDK * 2, 128, (cuuint64_t)kDK * 2 * 8};
+    const cuuint32_t box[4] = {64, 8, (cuuint32_t)tc::kKbPerSlot, (cuuint32_t)(tc::kTO / 8)};
+    return encode_tmap(map, base, 4, dims, strides, box, bf16);
 }
 
 inline size_t align_up(size_t x, size_t a) { return (x + a - 1) / a * a; }
@@ -336,10 +364,14 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     if (wl.max_items > 0 && (!balanced || bal_clusters > 0)) {
         if (tc_path) {
             CUtensorMap cmap_s, cmap_o, qmap;
-            // paged: both maps cover the whole pool, in 32-row boxes
+            // S-CTA: one box per ring slot (3 K-blocks x 96 rows); paged, one per
+            // 32-row piece and slot.  O-CTA: one box per 32-row C tile (8 K-blocks).
             const long long map_rows = pg != nullptr ? pg->pool_rows : total_tokens;
-            st = make_tmap_576(&cmap_s, cache, map_rows, pg != nullptr ? tc::kTO : tc::kTS, kBf16);
-            if (st == MLA_B200_OK) st = make_tmap_576(&cmap_o, cache, map_rows, tc::kTO, kBf16);
+            if (pg != nullptr)
+                st = make_tmap_pool_groups(&cmap_s, cache, map_rows, kBf16);
+            else
+                st = make_tmap_blocks(&cmap_s, cache, map_rows, tc::kTS, tc::kKbPerSlot, kBf16);
+            if (st == MLA_B200_OK) st = make_tmap_blocks(&cmap_o, cache, map_rows, tc::kTO, tc::kVBlocks, kBf16);
             if (st == MLA_B200_OK) st = make_tmap_576(&qmap, q, (long long)batch * num_heads, 128, kBf16);
             if (st != MLA_B200_OK) return st;
             tc::TcParams tp;

@@ -277,7 +277,8 @@ __device__ void lens_to_offsets(const int32_t *lens, int batch, int max_len, int
 }
 
 // Expands cu_seqlens[B+1] into item_off[B+1] (exclusive prefix of per-sequence
-// item counts) and items[] = {b, row_begin, row_end, 0}.  One block.  With
+// item counts) and items[] = {b, row_begin, row_end, token offset in the
+// sequence}.  One block.  With
 // seq_lens (paged cache) the offsets are first built into cu_out from the
 // lengths and used as cu_seqlens.
 __global__ void __launch_bounds__(1024) plan_varlen_kernel(const int32_t *cu_seqlens,
@@ -331,7 +332,7 @@ __global__ void __launch_bounds__(1024) plan_varlen_kernel(const int32_t *cu_seq
             const int r1 = cu_seqlens[b + 1];
             for (int c = 0; c < cnt && excl + c < max_items; ++c) {
                 const int s = r0 + c * chunk;
-                items[excl + c] = make_int4(b, s, min(s + chunk, r1), 0);
+                items[excl + c] = make_int4(b, s, min(s + chunk, r1), c * chunk);
             }
         }
         __syncthreads();

@@ -69,6 +69,7 @@ struct Item {
     int b;
     long long row0;  // first cache row (index into the packed / dense cache)
     int len;         // rows in this item, 0 = empty
+    int tok0;        // first token's position in its sequence
 };
 
 __device__ __forceinline__ Item get_item(const WorkList &w, int i) {
@@ -79,6 +80,7 @@ __device__ __forceinline__ Item get_item(const WorkList &w, int i) {
         const int start = c * w.chunk;
         it.b = b;
         it.row0 = (long long)b * w.seq_len + start;
+        it.tok0 = start;
         const int rem = w.seq_len - start;
         it.len = b < w.batch ? max(0, min(w.chunk, rem)) : 0;
     } else {
@@ -88,10 +90,12 @@ __device__ __forceinline__ Item get_item(const WorkList &w, int i) {
             it.b = v.x;
             it.row0 = v.y;
             it.len = v.z - v.y;
+            it.tok0 = v.w;
         } else {
             it.b = 0;
             it.row0 = 0;
             it.len = 0;
+            it.tok0 = 0;
         }
     }
     return it;
@@ -207,6 +211,7 @@ __device__ __forceinline__ bool items_next(const WorkList &w, ItemCursor &c, Ite
             it.b = b;
             it.row0 = s.row0 + (long long)lo * kTile;
             it.len = min(hi * kTile, s.len) - lo * kTile;
+            it.tok0 = lo * kTile;
             return true;
         }
     }

@@ -60,6 +60,7 @@ constexpr int kBoxS = kTS * 128;                 // 12288: one K-block box [96 t
 constexpr int kKbPerSlot = 3;                    // K-blocks per S ring slot (12 MMAs per wait)
 constexpr int kSlotS = kKbPerSlot * kBoxS;       // 36864
 constexpr int kSlotsPerTile = kKBlocks / kKbPerSlot;  // 3
+constexpr int kPieceS = kKbPerSlot * kTO * 128;  // 12288: paged, one 32-row piece of a slot
 constexpr int kSlotsS = 5;
 constexpr int kBoxO = kTO * 128;                 // 4096: [32 tok x 64 col]
 constexpr int kSlotO = kVBlocks * kBoxO;         // 32768: C tile [32 x 512]
@@ -92,9 +93,7 @@ enum BarId {
     kBarCorr = kBarPFull + kMsgSlots,  // [3] O-CTA: O ready for GEMM2     (count 128)
     kBarMmaDone = kBarCorr + kMsgSlots,// [3] O-CTA: GEMM2 of a message done (count 1, commit)
     kBarDrain = kBarMmaDone + kMsgSlots,// [2] an MMA issuer's ops retired (teardown)
-    kBarZReq = kBarDrain + 2,          //     O-CTA, paged: GEMM2 issuer asks for a tile's tail rows zeroed (count 1)
-    kBarZDone = kBarZReq + 1,          //     O-CTA, paged: tail rows zeroed (count 1)
-    kNumBars = kBarZDone + 1
+    kNumBars = kBarDrain + 2
 };
 
 // Shared-memory layout (offsets from a 1024-aligned base).  Each role has its
@@ -146,11 +145,25 @@ struct TcParams {
     const int32_t *block_table;
 };
 
+// Zeroes rows [tail, 32) of a landed [32 x 512] C tile (8 SW128 K-blocks of
+// 32 rows; whole 128-byte rows, so the swizzle does not matter), this lane's
+// share of a warp's work, and orders the stores before the tensor core's
+// operand reads.
+__device__ __forceinline__ void zero_tail(uint32_t tile, int tail, int lane) {
+    const int pieces = (kTO - tail) * kVBlocks * 8;  // 16-byte pieces
+    for (int q = lane; q < pieces; q += 32) {
+        const int rb = q >> 3;
+        ptx::st_shared_v4(tile + (rb % kVBlocks) * kBoxO + (tail + rb / kVBlocks) * 128 + (q & 7) * 16, 0u, 0u, 0u, 0u);
+    }
+    ptx::fence_proxy_async_smem();
+}
+
 // Pool row of the 32-row box starting at token t (a multiple of kTO) of
-// sequence b.  Boxes past the sequence's last token re-read its last box: the
-// softmax masks those columns, so the bytes only have to be addressable.
-__device__ __forceinline__ int paged_row(const TcParams &p, int b, int t, int seq_len) {
-    const int tc = min(t, (seq_len - 1) & ~(kTO - 1));
+// sequence b.  Boxes past the item's last token `last` re-read its last box:
+// the softmax masks those columns, so the bytes only have to be addressable
+// (and no block-table entry past the sequence's pages is read).
+__device__ __forceinline__ int paged_row(const TcParams &p, int b, int t, int last) {
+    const int tc = min(t, last & ~(kTO - 1));
     const int blk = tc / p.page_size;
     const int pg = p.block_table[(long long)b * p.max_blocks + blk];
     return pg * p.page_size + (tc - blk * p.page_size);
@@ -232,11 +245,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             ptx::mbar_init(bar(kBarDrain + i), 1);
         }
         ptx::mbar_init(bar(kBarQReady), 1);
-        if constexpr (kPaged) {
-            ptx::mbar_init(bar(kBarZReq), 1);
-            ptx::mbar_init(bar(kBarZDone), 1);
-            reinterpret_cast<volatile int *>(smem + kOffZArg)[2] = 0;
-        }
+        if constexpr (kPaged) reinterpret_cast<volatile int *>(smem + kOffZArg)[2] = 0;
         *abort_flag = 0;
         ptx::fence_mbarrier_init_cluster();
     }
@@ -269,6 +278,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             Item it;
             int i;
             while (ok && items_next<kSched>(wl, cur, it, i)) {
+                // paged: pool rows of the current tile's three 32-row pieces, and
+                // of the next tile's, read a tile ahead so the block-table
+                // latency stays off the refill path (the first tile's overlaps
+                // the Q loads)
+                int last = 0, pr[kOPerS], pn[kOPerS];
+                if constexpr (kPaged) {
+                    last = it.tok0 + it.len - 1;
+#pragma unroll
+                    for (int c = 0; c < kOPerS; ++c) pr[c] = paged_row(p, it.b, it.tok0 + c * kTO, last);
+                }
                 if (role == 0 && it.b != prev_b) {
                     // Q of the new sequence: two 128 x 64 boxes per ring slot
                     const int qrow = it.b * p.num_heads;
@@ -283,22 +302,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                     }
                     prev_b = it.b;
                 }
-                // paged: pool rows of the current tile's three 32-row pieces, and
-                // of the next tile's, read a tile ahead so the block-table
-                // latency stays off the refill path
-                int seq_len = 0, tok0 = 0, pr[kOPerS], pn[kOPerS];
-                if constexpr (kPaged) {
-                    const int c0 = wl.cu_seqlens[it.b];
-                    seq_len = wl.cu_seqlens[it.b + 1] - c0;
-                    tok0 = (int)it.row0 - c0;
-#pragma unroll
-                    for (int c = 0; c < kOPerS; ++c) pr[c] = paged_row(p, it.b, tok0 + c * kTO, seq_len);
-                }
                 for (int t0 = 0; ok && t0 < it.len; t0 += kTS) {
                     const int row = (int)(it.row0 + t0);
                     if constexpr (kPaged) {
 #pragma unroll
-                        for (int c = 0; c < kOPerS; ++c) pn[c] = paged_row(p, it.b, tok0 + t0 + kTS + c * kTO, seq_len);
+                        for (int c = 0; c < kOPerS; ++c) pn[c] = paged_row(p, it.b, it.tok0 + t0 + kTS + c * kTO, last);
                     }
                     if (role == 0) {
                         if constexpr (kPaged) {
@@ -306,10 +314,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                 if (!acquire()) { ok = false; break; }
                                 const uint32_t dst = sbase + kOffRing + rg.slot * kSlotS;
                                 ptx::mbar_arrive_expect_tx(bar(kBarFull + rg.slot), kSlotS);
-                                for (int j = 0; j < kKbPerSlot; ++j)
 #pragma unroll
-                                    for (int c = 0; c < kOPerS; ++c)
-                                        ptx::tma_load_2d(dst + j * kBoxS + c * kBoxO, &cmap_s, (sl * kKbPerSlot + j) * 64, pr[c], bar(kBarFull + rg.slot));
+                                for (int c = 0; c < kOPerS; ++c)
+                                    ptx::tma_load_4d(dst + c * kPieceS, &cmap_s, 0, 0, sl * kKbPerSlot, pr[c] >> 3, bar(kBarFull + rg.slot));
                                 rg.next(nslots);
                             }
                         } else {
@@ -317,8 +324,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                 if (!acquire()) { ok = false; break; }
                                 const uint32_t dst = sbase + kOffRing + rg.slot * kSlotS;
                                 ptx::mbar_arrive_expect_tx(bar(kBarFull + rg.slot), kSlotS);
-                                for (int j = 0; j < kKbPerSlot; ++j)
-                                    ptx::tma_load_2d(dst + j * kBoxS, &cmap_s, (sl * kKbPerSlot + j) * 64, row, bar(kBarFull + rg.slot));
+                                ptx::tma_load_3d(dst, &cmap_s, 0, row, sl * kKbPerSlot, bar(kBarFull + rg.slot));
                                 rg.next(nslots);
                             }
                         }
@@ -330,8 +336,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                             if (!acquire()) { ok = false; break; }
                             const uint32_t dst = sbase + kOffRing + rg.slot * kSlotO;
                             ptx::mbar_arrive_expect_tx(bar(kBarFull + rg.slot), kSlotO);
-                            for (int kb = 0; kb < kVBlocks; ++kb)
-                                ptx::tma_load_2d(dst + kb * kBoxO, &cmap_o, kb * 64, r, bar(kBarFull + rg.slot));
+                            ptx::tma_load_3d(dst, &cmap_o, 0, r, 0, bar(kBarFull + rg.slot));
                             rg.next(nslots);
                         }
                     }
@@ -361,7 +366,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             const int nslots = role == 0 ? kSlotsS : kSlotsO;
             const uint32_t me = warp == 1 ? 0u : 1u;
             Ring rg;
-            uint32_t jt = 0, qphase = 0, nseq = 0, qready_seq = 0, nzero = 0;
+            uint32_t jt = 0, qphase = 0, nseq = 0, qready_seq = 0;
             int prev_b = -1;
             bool ok = true;
             ItemCursor cur = items_begin<kSched>(wl, cid, ncl);
@@ -370,8 +375,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             while (ok && items_next<kSched>(wl, cur, it, i)) {
                 const bool new_seq = role == 0 && it.b != prev_b;
                 prev_b = it.b;
-                bool at_end = false;  // paged: the item ends at its sequence's last token
-                if constexpr (kPaged) at_end = it.row0 + it.len == wl.cu_seqlens[it.b + 1];
                 for (int t0 = 0; ok && t0 < it.len; t0 += kTS, ++jt) {
                     if (role == 0) {
                         const bool mine = (jt & 1u) == me;
@@ -428,12 +431,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                             if (!ptx::mbar_spin(bar(kBarFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
                             // descriptor of the slot, plus compile-time offsets per K-step: a
                             // short issue sequence between MMAs
-                            const uint64_t b0 = ptx::sdesc_sw128(sbase + kOffRing + rg.slot * kSlotS, 16, 1024);
+                            // (paged slots interleave the K-blocks per 8-row group: stride 3 KB)
+                            const uint64_t b0 = ptx::sdesc_sw128(sbase + kOffRing + rg.slot * kSlotS, 16, kPaged ? kKbPerSlot * 1024 : 1024);
                             const uint32_t a0 = tmem + kTmemQ + sl * (kKbPerSlot * 32);
                             const uint32_t acc0 = sl > 0 ? 1u : 0u;
+                            constexpr int kKbStride = kPaged ? 1024 : kBoxS;
 #pragma unroll
                             for (int k = 0; k < kKbPerSlot * 4; ++k)
-                                ptx::mma_ts(d, a0 + k * 8, b0 + (uint64_t)(((k >> 2) * kBoxS + (k & 3) * 32) >> 4),
+                                ptx::mma_ts(d, a0 + k * 8, b0 + (uint64_t)(((k >> 2) * kKbStride + (k & 3) * 32) >> 4),
                                             idesc_s<kBf16>(), k > 0 ? 1u : acc0);
                             ptx::mma_commit(bar(kBarEmpty + rg.slot));
                             rg.next(nslots);
@@ -450,15 +455,20 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         for (int ct = 0; ct < nct; ++ct) {
                             if (!ptx::mbar_spin(bar(kBarFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
                             if constexpr (kPaged) {
-                                // the sequence's last tile: rows past its end are zeroed by warp 3
+                                // an item's last tile ending inside a 32-row piece: the rows past
+                                // its end are zeroed by the whole warp (the other lanes wait at
+                                // __syncwarp meanwhile).  Items split sequences on 96-token tile
+                                // boundaries, so this is a sequence's end; elsewhere it would
+                                // only zero rows whose P is 0.
                                 const int tail = (it.len - t0) % kTO;
-                                if (at_end && ct == nct - 1 && t0 + kTS >= it.len && tail != 0) {
+                                if (ct == nct - 1 && t0 + kTS >= it.len && tail != 0) {
                                     volatile int *za = reinterpret_cast<volatile int *>(smem + kOffZArg);
-                                    za[0] = (int)(sbase + kOffRing + rg.slot * kSlotO);
+                                    const uint32_t tile = sbase + kOffRing + rg.slot * kSlotO;
+                                    za[0] = (int)tile;
                                     za[1] = tail;
-                                    ptx::mbar_arrive(bar(kBarZReq));
-                                    if (!ptx::mbar_wait(bar(kBarZDone), nzero & 1, kErrWaitMma)) { ok = false; break; }
-                                    ++nzero;
+                                    __syncwarp();
+                                    zero_tail(tile, tail, 0);
+                                    __syncwarp();
                                     ptx::tc_fence_after();
                                 }
                             }
@@ -484,36 +494,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             }
             if (!ok) *abort_flag = 1;
             if constexpr (kPaged) {
-                if (role == 1) {  // release the zeroing warp
+                if (role == 1) {  // release the helper lanes (every path out of the loop gets here)
                     reinterpret_cast<volatile int *>(smem + kOffZArg)[2] = 1;
-                    ptx::mbar_arrive(bar(kBarZReq));
+                    __syncwarp();
                 }
             }
             // every MMA this thread issued has retired before TMEM is freed
             ptx::mma_commit(bar(kBarDrain + me));
             ptx::mbar_wait(bar(kBarDrain + me), 0, kErrWaitMma);
-        }
-    } else if (kPaged && warp == 3) {
-        // ------------------------------------------------------------ O-CTA, paged: tail zeroing
-        // Rows of a sequence's last C tile past its end hold whatever the page
-        // held, not necessarily finite numbers; P is 0 there, but 0 x NaN is NaN
-        // in GEMM2.  The GEMM2 issuer, holding such a tile (landed), posts its
-        // address and valid rows; this warp zeroes the rest and answers.  The
-        // request and answer phases alternate, so the parities never alias.
-        volatile int *za = reinterpret_cast<volatile int *>(smem + kOffZArg);
-        for (uint32_t n = 0;; ++n) {
-            const bool w = ptx::mbar_wait(bar(kBarZReq), n & 1, kErrWaitMma);
-            if (!__all_sync(0xffffffffu, w) || za[2] != 0) break;
-            const uint32_t base = (uint32_t)za[0];
-            const int tail = za[1];
-            const int pieces = (kTO - tail) * kVBlocks * 8;  // 16-byte pieces past the end
-            for (int q = lane; q < pieces; q += 32) {
-                const int rb = q >> 3;
-                ptx::st_shared_v4(base + (rb % kVBlocks) * kBoxO + (tail + rb / kVBlocks) * 128 + (q & 7) * 16, 0u, 0u, 0u, 0u);
+        } else if (kPaged && role == 1) {
+            // O-CTA, paged: lanes 1-31 of the GEMM2 warp.  Rows of a sequence's
+            // last C tile past its end hold whatever the page held, not
+            // necessarily finite numbers; P is 0 there, but 0 x NaN is NaN in
+            // GEMM2.  The issuing lane posts such a tile (landed) and these lanes
+            // zero its tail with it.  Between requests they wait inside
+            // __syncwarp, issuing nothing.
+            volatile int *za = reinterpret_cast<volatile int *>(smem + kOffZArg);
+            for (;;) {
+                __syncwarp();
+                if (za[2] != 0) break;
+                zero_tail((uint32_t)za[0], za[1], lane);
+                __syncwarp();
             }
-            ptx::fence_proxy_async_smem();  // the zeros before GEMM2's operand reads
-            __syncwarp();
-            if (lane == 0) ptx::mbar_arrive(bar(kBarZDone));
         }
     } else if (warp >= 4) {
         // ------------------------------------------------------------ math warpgroup
