@@ -120,3 +120,49 @@ def make_workload(cfg: int, seed: int = 0, device: str | torch.device = "cpu",
         cu = None
     return Workload(cfg=cfg, query=q, cache=cache, cu_seqlens=cu, seqlens=list(seqlens),
                     max_seq_len=max(seqlens) if seqlens else 0)
+
+
+@dataclass
+class PagedLayout:
+    """A page pool layout of a workload's sequences: sequence b's token t lives
+    in row t % page_size of page block_table[b, t // page_size]."""
+    page_size: int
+    num_pages: int
+    block_table: torch.Tensor  # int32 [B, max_blocks]
+    seq_lens: torch.Tensor     # int32 [B]
+    pool_rows: torch.Tensor    # int64 [T]: pool row of each packed cache row
+
+    def scatter(self, cache: torch.Tensor, pool: torch.Tensor | None = None) -> torch.Tensor:
+        """Copies a workload cache (dense or packed) into a [num_pages,
+        page_size, 576] pool (allocated when absent; rows past a sequence's end
+        are left as they were)."""
+        if pool is None:
+            pool = torch.empty((self.num_pages, self.page_size, HEAD_DIM_K), dtype=cache.dtype,
+                               device=cache.device)
+        pool.view(-1, HEAD_DIM_K).index_copy_(0, self.pool_rows.to(cache.device),
+                                              cache.reshape(-1, HEAD_DIM_K))
+        return pool
+
+
+def paged_layout(wl: Workload, page_size: int, seed: int = 0, spare_pages: int = 0) -> PagedLayout:
+    """Shuffled page assignment (seeded) for ``wl``'s sequences, as a serving
+    engine's page allocator would leave it after churn."""
+    npg = [-(-n // page_size) for n in wl.seqlens]
+    num_pages = sum(npg) + spare_pages
+    g = torch.Generator().manual_seed(seed + 104729)
+    perm = torch.randperm(num_pages, generator=g)
+    max_blocks = max(max(npg, default=0), 1)
+    bt = torch.full((wl.batch, max_blocks), -1, dtype=torch.int32)
+    rows = []
+    used = 0
+    for b, n in enumerate(wl.seqlens):
+        pages = perm[used:used + npg[b]]
+        used += npg[b]
+        bt[b, :npg[b]] = pages.to(torch.int32)
+        t = torch.arange(n, dtype=torch.int64)
+        rows.append(pages.to(torch.int64)[t // page_size] * page_size + t % page_size)
+    dev = wl.query.device
+    pool_rows = torch.cat(rows) if rows else torch.zeros(0, dtype=torch.int64)
+    return PagedLayout(page_size=page_size, num_pages=num_pages, block_table=bt.to(dev),
+                       seq_lens=torch.tensor(wl.seqlens, dtype=torch.int32).to(dev),
+                       pool_rows=pool_rows.to(dev))

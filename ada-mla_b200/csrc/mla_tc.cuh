@@ -198,10 +198,12 @@ struct Ring {
     }
 };
 
-// cmap_s: cache [rows, 576], box 64 x 96 (paged: box 64 x 32, the S-CTA
-// loading each K-block of a tile as three boxes, one per 32-token piece of a
-// page).  cmap_o: same cache, box 64 x 32.  qmap: query [B * n_h, 576], box
-// 64 x 128.  All 128-byte swizzled.
+// cmap_s: the cache as (64 columns, rows, 9 K-blocks), one box = 3 K-blocks x
+// 96 rows = one S ring slot; paged: the pool as (64, 8 rows, 9 K-blocks, row
+// groups), one box = 3 K-blocks x 32 rows of one page, three per slot (the
+// slot's K-blocks interleaved per 8-row group).  cmap_o: the cache as (64,
+// rows, 9), one box = 8 K-blocks x 32 rows = one O ring slot.  qmap: query
+// [B * n_h, 576], box 64 x 128.  All 128-byte swizzled.
 // kSched: the work-list schedule this instantiation serves (kSchedChunked or
 // kSchedBalanced); the other schedule's iteration code would cost registers in
 // every role.  kBf16: Q* and the cache are bf16 (P goes to GEMM2 as bf16 too:

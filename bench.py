@@ -14,6 +14,11 @@ inputs from a ring whose total size is >= 3x the L2, so each step streams its
 cache from HBM.  The timed region is a CUDA graph of exactly K steps launched
 through the C ABI (mla_b200_decode_batched_f16) with preallocated buffers.
 
+`--page-size P` (P a multiple of 32) runs the same step on a paged copy of
+the cache: shuffled pages of P tokens in a pool, addressed through a block
+table (mla_b200_decode_paged_f16); the metric still counts each sequence's own
+cache bytes.
+
 `--impl reference` times the reference's own FP32 CPU kernel
 (run_mla_decode_cpu, compiled from the reference sources into oracle/_ref, or
 our C restatement when that build is absent) on all host cores, rank 0 only.
@@ -247,7 +252,7 @@ def run_ours(args):
     torch.cuda.set_device(dev)
     import ada_mla
     from ada_mla import capi
-    from ada_mla.workloads import make_workload
+    from ada_mla.workloads import make_workload, paged_layout
 
     hbm_peak, _, peak_kind = _peaks()
     L2 = torch.cuda.get_device_properties(dev).L2_cache_size or (126 << 20)
@@ -266,12 +271,27 @@ def run_ours(args):
     out = torch.empty((b, nh, 512), dtype=torch.float16, device=dev)
     lib = capi.lib()
     cache_2d = [c.view(-1, HEAD_DIM_K) for c in cs]
+    paged = args.page_size > 0
+    if paged:
+        pl = paged_layout(wl, args.page_size, seed=rank)
+        pools = [pl.scatter(c) for c in cs]  # the ring's copies, each in its own pool
+        del cs, cache_2d
+        ws_bytes = capi.workspace_size(b, nh, b * maxlen, maxlen, args.splits)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        step_bytes = pools[0].numel() * pools[0].element_size() + wl.query.numel() * wl.query.element_size()
 
     def step(i, stream):
-        st = lib.mla_b200_decode_batched_f16(
-            qs[i % ring].data_ptr(), cache_2d[i % ring].data_ptr(),
-            None if cu is None else cu.data_ptr(), b, nh, total, maxlen, 1.0, args.splits,
-            out.data_ptr(), capi.OUT_F16, None, ws.data_ptr(), ws_bytes, stream)
+        if paged:
+            st = lib.mla_b200_decode_paged_f16(
+                qs[i % ring].data_ptr(), pools[i % ring].data_ptr(), pl.block_table.data_ptr(),
+                pl.seq_lens.data_ptr(), b, nh, pl.num_pages, pl.page_size, pl.block_table.shape[1],
+                maxlen, 1.0, args.splits, out.data_ptr(), capi.OUT_F16, None, ws.data_ptr(),
+                ws_bytes, stream)
+        else:
+            st = lib.mla_b200_decode_batched_f16(
+                qs[i % ring].data_ptr(), cache_2d[i % ring].data_ptr(),
+                None if cu is None else cu.data_ptr(), b, nh, total, maxlen, 1.0, args.splits,
+                out.data_ptr(), capi.OUT_F16, None, ws.data_ptr(), ws_bytes, stream)
         if st != 0:
             raise RuntimeError(f"decode failed: {capi.status_string(st)}")
 
@@ -331,16 +351,27 @@ def run_ours(args):
 
     # end-to-end through the public API: pinned host inputs -> device, decode,
     # result -> host, every step
+    # (paged: the pool, block table and lengths all cross from the host)
+    src = pools[0] if paged else wl.cache
     qh = [wl.query.cpu().pin_memory() for _ in range(2)]
-    ch = [wl.cache.cpu().pin_memory() for _ in range(2)]
-    qd, cd = torch.empty_like(wl.query), torch.empty_like(wl.cache)
+    ch = [src.cpu().pin_memory() for _ in range(2)]
+    qd, cd = torch.empty_like(wl.query), torch.empty_like(src)
     oh = torch.empty((b, nh, 512), dtype=torch.float16).pin_memory()
+    if paged:
+        bth, slh = pl.block_table.cpu().pin_memory(), pl.seq_lens.cpu().pin_memory()
+        btd, sld = torch.empty_like(pl.block_table), torch.empty_like(pl.seq_lens)
 
     def e2e_step(i):
         qd.copy_(qh[i % 2], non_blocking=True)
         cd.copy_(ch[i % 2], non_blocking=True)
-        o = ada_mla.mla_decode_batched(qd, cd, cu, max_seq_len=maxlen, softmax_scale=1.0,
-                                       num_splits=args.splits)
+        if paged:
+            btd.copy_(bth, non_blocking=True)
+            sld.copy_(slh, non_blocking=True)
+            o = ada_mla.mla_decode_paged(qd, cd, btd, sld, max_seq_len=maxlen, softmax_scale=1.0,
+                                         num_splits=args.splits)
+        else:
+            o = ada_mla.mla_decode_batched(qd, cd, cu, max_seq_len=maxlen, softmax_scale=1.0,
+                                           num_splits=args.splits)
         oh.copy_(o, non_blocking=True)
 
     e2e_steps = max(3, min(args.steps, 200))
@@ -358,6 +389,8 @@ def run_ours(args):
     e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / e2e_steps
     e2e_value = world * wl.cache_bytes / (e2e_ms * 1e-3) / 1e9
     h2d = qh[0].numel() * qh[0].element_size() + ch[0].numel() * ch[0].element_size()
+    if paged:
+        h2d += bth.numel() * 4 + slh.numel() * 4
     d2h = oh.numel() * oh.element_size()
 
     err = ada_mla.mla_get_device_error()
@@ -365,7 +398,7 @@ def run_ours(args):
         raise RuntimeError(f"device error word set: {err}")
 
     chunk, splits = capi.plan(b, nh, total, maxlen, torch.cuda.get_device_properties(dev).multi_processor_count)
-    kernels_per_step = 2 + (1 if cu is not None else 0)
+    kernels_per_step = 2 + (1 if cu is not None or paged else 0)
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
@@ -373,8 +406,11 @@ def run_ours(args):
             "us_per_step": ms_step * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "f16", "data": "synthetic",
             "config": {"workload": f"cfg{args.config}: B={b} n_h={nh} N={maxlen} per rank "
-                                   f"({'packed varlen' if cu is not None else 'dense'}), "
-                                   "softmax scale folded into Q*",
+                                   + (f"(paged cache: shuffled {args.page_size}-token pages, "
+                                      f"{pl.num_pages} pages), " if paged else
+                                      f"({'packed varlen' if cu is not None else 'dense'}), ")
+                                   + "softmax scale folded into Q*",
+                       "page_size": args.page_size if paged else None,
                        "cfg": args.config, "batch_per_rank": b, "num_heads": nh,
                        "seq_len": maxlen, "total_tokens_per_rank": total,
                        "num_splits": splits if args.splits <= 0 else args.splits,
@@ -384,12 +420,13 @@ def run_ours(args):
                              f">= 3x L2)" if ring > 1 else "no rotation"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved / hbm_peak, "peak_source": peak_kind,
-                         "traffic": NCU_TRAFFIC.get(args.config), "kernel": "mla::tc::tc_decode_kernel",
+                         "traffic": None if paged else NCU_TRAFFIC.get(args.config),
+                         "kernel": "mla::tc::tc_decode_kernel",
                          "launch_us": launch_ms * 1e3,
                          "algorithmic_bytes_per_launch": wl.cache_bytes},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "us_per_step": e2e_ms * 1e3,
-                    "api": "ada_mla.mla_decode_batched"},
+                    "api": "ada_mla.mla_decode_paged" if paged else "ada_mla.mla_decode_batched"},
             "gpu_launches": args.steps * kernels_per_step,
             "clocks": sampler.summary(),
         }
@@ -493,6 +530,8 @@ def main():
     ap.add_argument("--config", type=int, default=1, choices=[1, 2, 3, 4])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--splits", type=int, default=-1)
+    ap.add_argument("--page-size", type=int, default=0,
+                    help="decode a paged copy of the cache (pages of this many tokens)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-rotate", action="store_true")
