@@ -9,6 +9,7 @@
 #include <atomic>
 #include <mutex>
 #include <type_traits>
+#include <utility>
 
 #include <cudaTypedefs.h>
 
@@ -268,10 +269,33 @@ struct PagedArgs {
     long long pool_rows;
 };
 
+// Launch, with programmatic stream serialization when `dependent`: the kernel
+// may then start while its predecessor in the stream runs (the predecessor
+// allows it with griddep_launch) and waits for it (griddep_wait) before
+// touching the predecessor's results.  Used on the plan -> decode edge, where
+// the decode kernel's set-up overlaps the plan.  (On decode -> merge it
+// measured slower: the merge has no set-up to overlap.)
+template <typename... Params, typename... Args>
+void launch_dependent(void (*kernel)(Params...), dim3 grid, dim3 block, size_t smem,
+                      cudaStream_t stream, bool dependent, Args &&...args) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = grid;
+    cfg.blockDim = block;
+    cfg.dynamicSmemBytes = smem;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attr[0].val.programmaticStreamSerializationAllowed = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = dependent ? 1 : 0;
+    cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);  // errors: launch_status()
+}
+
 template <int kSched, bool kBf16, bool kPaged>
 void launch_tc(int clusters, const CUtensorMap &cs, const CUtensorMap &co, const CUtensorMap &qm,
-               const tc::TcParams &tp, cudaStream_t stream) {
-    tc::tc_decode_kernel<kSched, kBf16, kPaged><<<2 * clusters, tc::kThreads, tc::kSmemBytes, stream>>>(cs, co, qm, tp);
+               const tc::TcParams &tp, cudaStream_t stream, bool after_plan) {
+    launch_dependent(tc::tc_decode_kernel<kSched, kBf16, kPaged>, dim3(2 * clusters), dim3(tc::kThreads),
+                     tc::kSmemBytes, stream, after_plan, cs, co, qm, tp);
 }
 
 // Shared driver of the split-KV paths: plan -> partial kernel -> combine.
@@ -394,11 +418,11 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
             const int clusters = balanced ? bal_clusters : std::min(info.tc_clusters, wl.max_items);
             timing_mark(t_ev_start, stream);
             if (pg != nullptr) {
-                if (balanced) launch_tc<kSchedBalanced, kBf16, true>(clusters, cmap_s, cmap_o, qmap, tp, stream);
-                else launch_tc<kSchedChunked, kBf16, true>(clusters, cmap_s, cmap_o, qmap, tp, stream);
+                if (balanced) launch_tc<kSchedBalanced, kBf16, true>(clusters, cmap_s, cmap_o, qmap, tp, stream, cu_seqlens != nullptr);
+                else launch_tc<kSchedChunked, kBf16, true>(clusters, cmap_s, cmap_o, qmap, tp, stream, cu_seqlens != nullptr);
             } else {
-                if (balanced) launch_tc<kSchedBalanced, kBf16, false>(clusters, cmap_s, cmap_o, qmap, tp, stream);
-                else launch_tc<kSchedChunked, kBf16, false>(clusters, cmap_s, cmap_o, qmap, tp, stream);
+                if (balanced) launch_tc<kSchedBalanced, kBf16, false>(clusters, cmap_s, cmap_o, qmap, tp, stream, cu_seqlens != nullptr);
+                else launch_tc<kSchedChunked, kBf16, false>(clusters, cmap_s, cmap_o, qmap, tp, stream, cu_seqlens != nullptr);
             }
             timing_mark(t_ev_stop, stream);
         } else if constexpr (!kBf16) {
@@ -420,35 +444,37 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     if (batch >= 8) {
         const dim3 rgrid((unsigned)cdiv(num_heads, kRowsPerCombineBlock), (unsigned)batch);
         const dim3 rblock(32 * kRowsPerCombineBlock);
+        const float *po = L.part_o;
+        const __half *ph = reinterpret_cast<const __half *>(L.part_o);
         if (out_dtype == MLA_B200_OUT_BF16)
-            combine_rows_kernel<__nv_bfloat16, float><<<rgrid, rblock, 0, stream>>>(
-                L.part_o, L.part_lse, wl, num_heads, static_cast<__nv_bfloat16 *>(out), out_lse, skip);
+            launch_dependent(combine_rows_kernel<__nv_bfloat16, float>, rgrid, rblock, 0, stream, false, po,
+                             L.part_lse, wl, num_heads, static_cast<__nv_bfloat16 *>(out), out_lse, skip);
         else if (out_dtype == MLA_B200_OUT_F16 && tc_direct)
-            combine_rows_kernel<__half, __half><<<rgrid, rblock, 0, stream>>>(
-                reinterpret_cast<const __half *>(L.part_o), L.part_lse, wl, num_heads, static_cast<__half *>(out),
-                out_lse, skip);
+            launch_dependent(combine_rows_kernel<__half, __half>, rgrid, rblock, 0, stream, false, ph, L.part_lse,
+                             wl, num_heads, static_cast<__half *>(out), out_lse, skip);
         else if (out_dtype == MLA_B200_OUT_F16)
-            combine_rows_kernel<__half, float><<<rgrid, rblock, 0, stream>>>(
-                L.part_o, L.part_lse, wl, num_heads, static_cast<__half *>(out), out_lse, skip);
+            launch_dependent(combine_rows_kernel<__half, float>, rgrid, rblock, 0, stream, false, po, L.part_lse,
+                             wl, num_heads, static_cast<__half *>(out), out_lse, skip);
         else
-            combine_rows_kernel<float, float><<<rgrid, rblock, 0, stream>>>(
-                L.part_o, L.part_lse, wl, num_heads, static_cast<float *>(out), out_lse, skip);
+            launch_dependent(combine_rows_kernel<float, float>, rgrid, rblock, 0, stream, false, po, L.part_lse,
+                             wl, num_heads, static_cast<float *>(out), out_lse, skip);
         return launch_status();
     }
-    if (out_dtype == MLA_B200_OUT_BF16) {
-        combine_kernel<__nv_bfloat16, float><<<cgrid, kCombineThreads, 0, stream>>>(
-            L.part_o, L.part_lse, wl, num_heads, rows, static_cast<__nv_bfloat16 *>(out), out_lse, skip);
-    } else if (out_dtype == MLA_B200_OUT_F16 && tc_direct) {
-        combine_kernel<__half, __half><<<cgrid, kCombineThreads, 0, stream>>>(
-            reinterpret_cast<const __half *>(L.part_o), L.part_lse, wl, num_heads, rows,
-            static_cast<__half *>(out), out_lse, skip);
-    } else if (out_dtype == MLA_B200_OUT_F16) {
-        combine_kernel<__half, float><<<cgrid, kCombineThreads, 0, stream>>>(
-            L.part_o, L.part_lse, wl, num_heads, rows, static_cast<__half *>(out), out_lse, skip);
-    } else {
-        combine_kernel<float, float><<<cgrid, kCombineThreads, 0, stream>>>(
-            L.part_o, L.part_lse, wl, num_heads, rows, static_cast<float *>(out), out_lse, skip);
-    }
+    const float *po = L.part_o;
+    const __half *ph = reinterpret_cast<const __half *>(L.part_o);
+    const dim3 cblock(kCombineThreads);
+    if (out_dtype == MLA_B200_OUT_BF16)
+        launch_dependent(combine_kernel<__nv_bfloat16, float>, dim3(cgrid), cblock, 0, stream, false, po,
+                         L.part_lse, wl, num_heads, rows, static_cast<__nv_bfloat16 *>(out), out_lse, skip);
+    else if (out_dtype == MLA_B200_OUT_F16 && tc_direct)
+        launch_dependent(combine_kernel<__half, __half>, dim3(cgrid), cblock, 0, stream, false, ph, L.part_lse,
+                         wl, num_heads, rows, static_cast<__half *>(out), out_lse, skip);
+    else if (out_dtype == MLA_B200_OUT_F16)
+        launch_dependent(combine_kernel<__half, float>, dim3(cgrid), cblock, 0, stream, false, po, L.part_lse,
+                         wl, num_heads, rows, static_cast<__half *>(out), out_lse, skip);
+    else
+        launch_dependent(combine_kernel<float, float>, dim3(cgrid), cblock, 0, stream, false, po, L.part_lse,
+                         wl, num_heads, rows, static_cast<float *>(out), out_lse, skip);
     return launch_status();
 }
 

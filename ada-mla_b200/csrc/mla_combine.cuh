@@ -291,6 +291,7 @@ __global__ void __launch_bounds__(1024) plan_varlen_kernel(const int32_t *cu_seq
                                                            int32_t *cu_out = nullptr) {
     __shared__ int warp_tot[32];
     __shared__ int carry_s;
+    griddep_launch();  // the decode kernel may start its set-up now
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (seq_lens != nullptr) {
         lens_to_offsets(seq_lens, batch, max_len, cu_out);
@@ -352,6 +353,7 @@ __global__ void __launch_bounds__(1024) plan_balanced_kernel(const int32_t *cu_s
                                                              int32_t *cu_out = nullptr) {
     __shared__ int warp_tot[32];
     __shared__ int carry_s;
+    griddep_launch();  // the decode kernel may start its set-up now
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     if (seq_lens != nullptr) {
         lens_to_offsets(seq_lens, batch, max_len, cu_out);

@@ -50,6 +50,14 @@ constexpr float kLn2 = 0.6931471805599453f;
 // ---------------------------------------------------------------------------
 constexpr int kItemCost = 2;  // fixed cost of one work item, in 96-row tiles
 
+// Programmatic dependent launch.  A kernel launched with the programmatic
+// stream-serialization attribute may start while its predecessor in the stream
+// still runs (once every CTA of the predecessor has called griddep_launch() or
+// exited); griddep_wait() returns when the predecessor grid has completed and
+// its memory is visible.  Without the attribute both are no-ops.
+__device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
+
 struct WorkList {
     const int4 *items;
     const int *item_off;

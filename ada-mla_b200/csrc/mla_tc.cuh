@@ -263,6 +263,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     ptx::cluster_sync();
     ptx::tc_fence_after();
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(smem + kOffSlot);
+    // Set-up above overlaps the plan kernel (programmatic launch); the work list
+    // is read below.
+    griddep_wait();
 
     const WorkList &wl = p.wl;
 
