@@ -78,15 +78,16 @@ ext_path = EXT_PATH
 
 def mla_decode_batched(query, cache, cu_seqlens=None, max_seq_len: int = -1,
                        softmax_scale: float = SOFTMAX_SCALE, num_splits: int = -1,
-                       return_lse: bool = False, out_dtype=None):
-    """Batched / variable-length fp16 or bf16 decode.
+                       return_lse: bool = False, out_dtype=None, kv_scale: float = 1.0):
+    """Batched / variable-length decode: fp16 or bf16, or an fp8 (e4m3) cache.
 
-    query  [B, n_h, 576] fp16 or bf16 (bf16: n_h <= 128).
+    query  [B, n_h, 576] fp16 or bf16 (bf16 and fp8 cache: n_h <= 128).
     cache  dense [B, N, 576], or packed [T, 576] with ``cu_seqlens`` int32
            [B+1] (sequence b owns rows cu_seqlens[b]:cu_seqlens[b+1]), in the
-           query's dtype.  Pass ``max_seq_len`` to avoid a device->host read of
-           the longest length.
-    Returns O* [B, n_h, 512] (the input dtype, or fp32 when
+           query's dtype -- or torch.float8_e4m3fn with an fp16 query, the
+           cache then being ``cache * kv_scale``.  Pass ``max_seq_len`` to
+           avoid a device->host read of the longest length.
+    Returns O* [B, n_h, 512] (the query's dtype, or fp32 when
     ``out_dtype=torch.float32``) and, with ``return_lse``, the natural-log LSE
     [B, n_h] fp32 as a tuple.
     """
@@ -95,7 +96,7 @@ def mla_decode_batched(query, cache, cu_seqlens=None, max_seq_len: int = -1,
     out_fp32 = out_dtype == torch.float32
     out, lse = _ext.mla_decode_batched(query, cache, cu_seqlens, int(max_seq_len),
                                        float(softmax_scale), int(num_splits),
-                                       bool(return_lse), out_fp32)
+                                       bool(return_lse), out_fp32, float(kv_scale))
     return (out, lse) if return_lse else out
 
 

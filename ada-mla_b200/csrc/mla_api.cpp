@@ -124,14 +124,16 @@ std::vector<at::Tensor> mla_decode_batched(const at::Tensor &query, const at::Te
                                            const c10::optional<at::Tensor> &cu_seqlens,
                                            int64_t max_seq_len, double softmax_scale,
                                            int64_t num_splits, bool return_lse,
-                                           bool out_fp32) {
+                                           bool out_fp32, double kv_scale) {
     check_cuda(query, "query");
     check_cuda(cache, "cache");
     TORCH_CHECK(query.device() == cache.device(), "query and cache on different devices");
     const bool bf16 = query.scalar_type() == at::kBFloat16;
+    const bool fp8 = cache.scalar_type() == at::kFloat8_e4m3fn;
     TORCH_CHECK((query.scalar_type() == at::kHalf || bf16) &&
-                    cache.scalar_type() == query.scalar_type(),
-                "mla_decode_batched: float16 or bfloat16 inputs (query and cache alike) expected");
+                    (cache.scalar_type() == query.scalar_type() || (fp8 && !bf16)),
+                "mla_decode_batched: float16 or bfloat16 inputs (query and cache alike), or a "
+                "float16 query with a float8_e4m3fn cache, expected");
     TORCH_CHECK(query.dim() == 3 && query.size(2) == MLA_B200_HEAD_DIM_K,
                 "mla_decode_batched: query must be [B, n_h, 576]");
     const int64_t b = query.size(0), nh = query.size(1);
@@ -162,16 +164,24 @@ std::vector<at::Tensor> mla_decode_batched(const at::Tensor &query, const at::Te
                                                               : query.scalar_type()));
     at::Tensor lse = return_lse ? at::empty({b, nh}, query.options().dtype(at::kFloat))
                                 : at::Tensor();
-    const size_t ws = mla_b200_workspace_size((int)b, (int)nh, total, (int)max_seq_len,
-                                              (int)num_splits);
+    const size_t ws = (fp8 ? mla_b200_workspace_size_fp8 : mla_b200_workspace_size)(
+        (int)b, (int)nh, total, (int)max_seq_len, (int)num_splits);
     at::Tensor w = workspace(query, ws);
-    auto *fn = bf16 ? mla_b200_decode_batched_bf16 : mla_b200_decode_batched_f16;
     const int odt = out_fp32 ? MLA_B200_OUT_F32 : (bf16 ? MLA_B200_OUT_BF16 : MLA_B200_OUT_F16);
-    check_status(fn(query.data_ptr(), cache.data_ptr(), cu_ptr, (int)b, (int)nh, total,
-                    (int)max_seq_len, (float)softmax_scale, (int)num_splits, out.data_ptr(), odt,
-                    return_lse ? lse.data_ptr<float>() : nullptr, w.data_ptr(), w.numel(),
-                    stream_ptr()),
-                 "mla_decode_batched");
+    float *lse_ptr = return_lse ? lse.data_ptr<float>() : nullptr;
+    if (fp8) {
+        check_status(mla_b200_decode_batched_fp8(
+                         query.data_ptr(), cache.data_ptr(), (float)kv_scale, cu_ptr, (int)b, (int)nh,
+                         total, (int)max_seq_len, (float)softmax_scale, (int)num_splits,
+                         out.data_ptr(), odt, lse_ptr, w.data_ptr(), w.numel(), stream_ptr()),
+                     "mla_decode_batched");
+    } else {
+        auto *fn = bf16 ? mla_b200_decode_batched_bf16 : mla_b200_decode_batched_f16;
+        check_status(fn(query.data_ptr(), cache.data_ptr(), cu_ptr, (int)b, (int)nh, total,
+                        (int)max_seq_len, (float)softmax_scale, (int)num_splits, out.data_ptr(), odt,
+                        lse_ptr, w.data_ptr(), w.numel(), stream_ptr()),
+                     "mla_decode_batched");
+    }
     if (!return_lse) lse = at::empty({0}, query.options().dtype(at::kFloat));
     return {out, lse};
 }
@@ -268,10 +278,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("query"), py::arg("cache"));
     m.def("mla_decode_split", &mla_decode_split, "split-KV decode, reference semantics",
           py::arg("query"), py::arg("cache"), py::arg("num_splits") = -1);
-    m.def("mla_decode_batched", &mla_decode_batched, "batched / varlen fp16 decode",
+    m.def("mla_decode_batched", &mla_decode_batched, "batched / varlen decode (fp16, bf16, fp8 cache)",
           py::arg("query"), py::arg("cache"), py::arg("cu_seqlens") = py::none(),
           py::arg("max_seq_len") = -1, py::arg("softmax_scale") = 0.07216878364870322,
-          py::arg("num_splits") = -1, py::arg("return_lse") = false, py::arg("out_fp32") = false);
+          py::arg("num_splits") = -1, py::arg("return_lse") = false, py::arg("out_fp32") = false,
+          py::arg("kv_scale") = 1.0);
     m.def("mla_decode_paged", &mla_decode_paged, "decode over a paged latent cache",
           py::arg("query"), py::arg("kv_pages"), py::arg("block_table"), py::arg("seq_lens"),
           py::arg("max_seq_len") = -1, py::arg("softmax_scale") = 0.07216878364870322,

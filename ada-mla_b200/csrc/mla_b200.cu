@@ -15,6 +15,7 @@
 
 #include "mla_b200.h"
 #include "mla_combine.cuh"
+#include "mla_fp8.cuh"
 #include "mla_common.cuh"
 #include "mla_simt.cuh"
 #include "mla_tc.cuh"
@@ -45,11 +46,11 @@ int cuda_failure(cudaError_t e) {
 
 // Opts a tensor-core kernel instantiation (both schedules) into its dynamic
 // shared memory.
-template <bool kBf16, bool kPaged>
+template <bool kBf16, bool kPaged, bool kFp8 = false>
 bool set_tc_smem() {
-    return cudaFuncSetAttribute(tc::tc_decode_kernel<kSchedChunked, kBf16, kPaged>,
+    return cudaFuncSetAttribute(tc::tc_decode_kernel<kSchedChunked, kBf16, kPaged, kFp8>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmemBytes) == cudaSuccess &&
-           cudaFuncSetAttribute(tc::tc_decode_kernel<kSchedBalanced, kBf16, kPaged>,
+           cudaFuncSetAttribute(tc::tc_decode_kernel<kSchedBalanced, kBf16, kPaged, kFp8>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmemBytes) == cudaSuccess;
 }
 
@@ -86,7 +87,8 @@ int current_device(int *dev_out, DevInfo *info_out) {
     }
     if (d.tc_clusters == 0) {
         if (!set_tc_smem<false, false>() || !set_tc_smem<true, false>() ||
-            !set_tc_smem<false, true>() || !set_tc_smem<true, true>()) {
+            !set_tc_smem<false, true>() || !set_tc_smem<true, true>() ||
+            !set_tc_smem<false, false, true>()) {
             return cuda_failure(cudaGetLastError());
         }
         cudaLaunchConfig_t cfg = {};
@@ -101,7 +103,7 @@ int current_device(int *dev_out, DevInfo *info_out) {
         cfg.attrs = &attr;
         cfg.numAttrs = 1;
         int n = 0;
-        if (cudaOccupancyMaxActiveClusters(&n, tc::tc_decode_kernel<kSchedChunked, false, false>, &cfg) != cudaSuccess || n <= 0) {
+        if (cudaOccupancyMaxActiveClusters(&n, tc::tc_decode_kernel<kSchedChunked, false, false, false>, &cfg) != cudaSuccess || n <= 0) {
             cudaGetLastError();
             n = d.sms / 2;
         }
@@ -128,15 +130,43 @@ PFN_cuTensorMapEncodeTiled_v12000 tmap_encoder() {
 }
 
 int encode_tmap(CUtensorMap *map, const void *base, cuuint32_t rank, const cuuint64_t *dims,
-                const cuuint64_t *strides, const cuuint32_t *box, bool bf16) {
+                const cuuint64_t *strides, const cuuint32_t *box, bool bf16,
+                CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B, bool bytes = false) {
     auto enc = tmap_encoder();
     if (enc == nullptr) return cuda_failure(cudaErrorSymbolNotFound);
     const cuuint32_t estr[4] = {1, 1, 1, 1};
-    const CUresult r = enc(map, bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16, rank,
-                           const_cast<void *>(base), dims, strides, box, estr,
-                           CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B,
-                           CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    const CUtensorMapDataType dt = bytes ? CU_TENSOR_MAP_DATA_TYPE_UINT8
+                                   : bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const CUresult r = enc(map, dt, rank, const_cast<void *>(base), dims, strides, box, estr,
+                           CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                           CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
     return r == CUDA_SUCCESS ? MLA_B200_OK : cuda_failure(cudaErrorInvalidValue);
+}
+
+// e4m3 cache [rows, 576] (one byte per element), GEMM1 side: (64 B, rows, 9
+// K-blocks) with 64-byte swizzle, one box = 3 K-blocks x 96 rows (an fp8 S slot).
+int make_tmap_fp8_s(CUtensorMap *map, const void *base, long long rows) {
+    const cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(kDK / 64)};
+    const cuuint64_t strides[2] = {(cuuint64_t)kDK, 64};
+    const cuuint32_t box[3] = {64, (cuuint32_t)tc::kTS, (cuuint32_t)tc::kKbPerSlot};
+    return encode_tmap(map, base, 3, dims, strides, box, false, CU_TENSOR_MAP_SWIZZLE_64B, true);
+}
+
+// e4m3 cache, GEMM2 side: (128 B, rows, 4 column groups) over the first 512
+// columns, unswizzled, one box = a [32 x 512 B] C_N tile for the widening warps.
+int make_tmap_fp8_o(CUtensorMap *map, const void *base, long long rows) {
+    const cuuint64_t dims[3] = {128, (cuuint64_t)rows, (cuuint64_t)(kDV / 128)};
+    const cuuint64_t strides[2] = {(cuuint64_t)kDK, 128};
+    const cuuint32_t box[3] = {128, (cuuint32_t)tc::kTO, (cuuint32_t)(kDV / 128)};
+    return encode_tmap(map, base, 3, dims, strides, box, false, CU_TENSOR_MAP_SWIZZLE_NONE, true);
+}
+
+// Q8 [2 x rows, 576] e4m3 (hi plane then lo plane), box 64 B x 128 rows, SW64.
+int make_tmap_q8(CUtensorMap *map, const void *base, long long rows) {
+    const cuuint64_t dims[2] = {(cuuint64_t)kDK, (cuuint64_t)(2 * rows)};
+    const cuuint64_t strides[1] = {(cuuint64_t)kDK};
+    const cuuint32_t box[2] = {64, 128};
+    return encode_tmap(map, base, 2, dims, strides, box, false, CU_TENSOR_MAP_SWIZZLE_64B, true);
 }
 
 // 2-D view [rows, 576] with (64 x box_rows) boxes and 128-byte swizzle (the
@@ -212,10 +242,12 @@ struct WsLayout {
     int *item_off = nullptr;
     int4 *items = nullptr;
     int32_t *cu_virtual = nullptr;  // paged cache: sequence offsets built from seq_lens
+    uint8_t *q8 = nullptr;          // fp8 cache: Q* as e4m3 hi and lo planes [2, B * n_h, 576]
+    float *q_scale = nullptr;       // fp8 cache: [B * n_h]
     size_t bytes = 0;
 };
 
-WsLayout ws_layout(void *base, long long max_items, int num_heads, int batch) {
+WsLayout ws_layout(void *base, long long max_items, int num_heads, int batch, bool fp8 = false) {
     WsLayout L;
     size_t off = 0;
     const size_t o_bytes = (size_t)max_items * num_heads * kDV * sizeof(float);
@@ -233,6 +265,13 @@ WsLayout ws_layout(void *base, long long max_items, int num_heads, int batch) {
     off = align_up(off + it_bytes, 256);
     L.cu_virtual = reinterpret_cast<int32_t *>(p + off);
     off = align_up(off + off_bytes, 256);
+    if (fp8) {
+        const size_t rows = (size_t)batch * num_heads;
+        L.q8 = reinterpret_cast<uint8_t *>(p + off);
+        off = align_up(off + 2 * rows * kDK, 256);
+        L.q_scale = reinterpret_cast<float *>(p + off);
+        off = align_up(off + rows * sizeof(float), 256);
+    }
     L.bytes = off;
     return L;
 }
@@ -261,6 +300,13 @@ int launch_status() {
 
 // A page pool [pool_rows / page_size, page_size, 576] with its block table
 // [batch, max_blocks] and per-sequence lengths (device int32 arrays).
+// An e4m3 latent cache [total_tokens, 576] (dense or packed like the fp16 one)
+// and its per-tensor scale: C = C8 * kv_scale.
+struct Fp8Args {
+    const void *cache8;
+    float kv_scale;
+};
+
 struct PagedArgs {
     const int32_t *block_table;
     const int32_t *seq_lens;
@@ -291,10 +337,10 @@ void launch_dependent(void (*kernel)(Params...), dim3 grid, dim3 block, size_t s
     cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);  // errors: launch_status()
 }
 
-template <int kSched, bool kBf16, bool kPaged>
+template <int kSched, bool kBf16, bool kPaged, bool kFp8 = false>
 void launch_tc(int clusters, const CUtensorMap &cs, const CUtensorMap &co, const CUtensorMap &qm,
                const tc::TcParams &tp, cudaStream_t stream, bool after_plan) {
-    launch_dependent(tc::tc_decode_kernel<kSched, kBf16, kPaged>, dim3(2 * clusters), dim3(tc::kThreads),
+    launch_dependent(tc::tc_decode_kernel<kSched, kBf16, kPaged, kFp8>, dim3(2 * clusters), dim3(tc::kThreads),
                      tc::kSmemBytes, stream, after_plan, cs, co, qm, tp);
 }
 
@@ -306,7 +352,8 @@ template <typename T>
 int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int batch,
                      int num_heads, long long total_tokens, int max_seq_len, float scale,
                      int num_splits, void *out, int out_dtype, float *out_lse, void *workspace,
-                     size_t workspace_bytes, cudaStream_t stream, const PagedArgs *pg = nullptr) {
+                     size_t workspace_bytes, cudaStream_t stream, const PagedArgs *pg = nullptr,
+                     const Fp8Args *f8 = nullptr) {
     int dev;
     DevInfo info;
     int st = current_device(&dev, &info);
@@ -320,6 +367,7 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     const bool tc_path = !std::is_same<T, float>::value && num_heads <= 128;
     if (kBf16 && !tc_path) return MLA_B200_ERR_UNSUPPORTED;  // bf16 has no SIMT kernel
     if (pg != nullptr && !tc_path) return MLA_B200_ERR_UNSUPPORTED;  // paged: tensor-core kernel only
+    if (f8 != nullptr && (!tc_path || kBf16 || pg != nullptr)) return MLA_B200_ERR_UNSUPPORTED;
     // (A single sequence splits evenly in the chunked schedule already.)
     const bool balanced = tc_path && num_splits <= 0 && batch > 1;
     int chunk = chunk_for(batch, total_tokens, max_seq_len, num_splits, info.sms);
@@ -328,7 +376,7 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     const long long max_items = balanced ? (long long)batch + info.tc_clusters
                                          : max_items_for(batch, total_tokens, chunk);
     if (max_items > (1LL << 30)) return MLA_B200_ERR_UNSUPPORTED;
-    WsLayout L = ws_layout(workspace, max_items, num_heads, batch);
+    WsLayout L = ws_layout(workspace, max_items, num_heads, batch, f8 != nullptr);
     if (workspace == nullptr || workspace_bytes < L.bytes) return MLA_B200_ERR_WORKSPACE;
     const int32_t *seq_lens = nullptr;
     if (pg != nullptr) {
@@ -391,13 +439,25 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
             // S-CTA: one box per ring slot (3 K-blocks x 96 rows); paged, one per
             // 32-row piece and slot.  O-CTA: one box per 32-row C tile (8 K-blocks).
             const long long map_rows = pg != nullptr ? pg->pool_rows : total_tokens;
-            if (pg != nullptr)
-                st = make_tmap_pool_groups(&cmap_s, cache, map_rows, kBf16);
-            else
-                st = make_tmap_blocks(&cmap_s, cache, map_rows, tc::kTS, tc::kKbPerSlot, kBf16);
-            if (st == MLA_B200_OK) st = make_tmap_blocks(&cmap_o, cache, map_rows, tc::kTO, tc::kVBlocks, kBf16);
-            if (st == MLA_B200_OK) st = make_tmap_576(&qmap, q, (long long)batch * num_heads, 128, kBf16);
-            if (st != MLA_B200_OK) return st;
+            const long long qrows = (long long)batch * num_heads;
+            if (f8 != nullptr) {
+                st = make_tmap_fp8_s(&cmap_s, f8->cache8, map_rows);
+                if (st == MLA_B200_OK) st = make_tmap_fp8_o(&cmap_o, f8->cache8, map_rows);
+                if (st == MLA_B200_OK) st = make_tmap_q8(&qmap, L.q8, qrows);
+                if (st != MLA_B200_OK) return st;
+                // Q* -> e4m3 hi / lo planes and row scales; the decode kernel's
+                // set-up overlaps it (programmatic launch)
+                q8_prep_kernel<<<(unsigned)cdiv(qrows, 8), 256, 0, stream>>>(
+                    reinterpret_cast<const __half *>(q), (int)qrows, L.q8, L.q_scale);
+            } else {
+                if (pg != nullptr)
+                    st = make_tmap_pool_groups(&cmap_s, cache, map_rows, kBf16);
+                else
+                    st = make_tmap_blocks(&cmap_s, cache, map_rows, tc::kTS, tc::kKbPerSlot, kBf16);
+                if (st == MLA_B200_OK) st = make_tmap_blocks(&cmap_o, cache, map_rows, tc::kTO, tc::kVBlocks, kBf16);
+                if (st == MLA_B200_OK) st = make_tmap_576(&qmap, q, qrows, 128, kBf16);
+                if (st != MLA_B200_OK) return st;
+            }
             tc::TcParams tp;
             tp.wl = wl;
             tp.num_heads = num_heads;
@@ -411,13 +471,26 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
             tp.out_kind = out_dtype == MLA_B200_OUT_F16 ? tc::kOutF16
                           : out_dtype == MLA_B200_OUT_BF16 ? tc::kOutBF16 : tc::kOutF32;
             tp.out_lse = out_lse;
-            tp.block_table = pg != nullptr ? pg->block_table : nullptr;
             tp.max_blocks = pg != nullptr ? pg->max_blocks : 0;
-            tp.page_size = pg != nullptr ? pg->page_size : 0;
+            if (f8 != nullptr) {
+                // S = kv_scale * q_scale[row] * (Q8.C8); O = kv_scale * 2^8 * (P.C8w) / l,
+                // C8w being the widened tile (e4m3 value x 2^-8)
+                tp.scale_log2 = scale * kLog2e * f8->kv_scale;
+                tp.q_scale = L.q_scale;
+                tp.o_scale = f8->kv_scale * 256.f;
+            } else {
+                tp.block_table = pg != nullptr ? pg->block_table : nullptr;
+                tp.page_size = pg != nullptr ? pg->page_size : 0;
+            }
             tc_direct = true;
             const int clusters = balanced ? bal_clusters : std::min(info.tc_clusters, wl.max_items);
             timing_mark(t_ev_start, stream);
-            if (pg != nullptr) {
+            if (f8 != nullptr) {
+                if constexpr (!kBf16) {  // (fp8 runs with fp16 Q*; the prep kernel precedes)
+                    if (balanced) launch_tc<kSchedBalanced, false, false, true>(clusters, cmap_s, cmap_o, qmap, tp, stream, true);
+                    else launch_tc<kSchedChunked, false, false, true>(clusters, cmap_s, cmap_o, qmap, tp, stream, true);
+                }
+            } else if (pg != nullptr) {
                 if (balanced) launch_tc<kSchedBalanced, kBf16, true>(clusters, cmap_s, cmap_o, qmap, tp, stream, cu_seqlens != nullptr);
                 else launch_tc<kSchedChunked, kBf16, true>(clusters, cmap_s, cmap_o, qmap, tp, stream, cu_seqlens != nullptr);
             } else {
@@ -586,8 +659,9 @@ int mla_b200_plan(int batch, int num_heads, long long total_tokens, int max_seq_
     return MLA_B200_OK;
 }
 
-size_t mla_b200_workspace_size(int batch, int num_heads, long long total_tokens, int max_seq_len,
-                               int num_splits) {
+namespace {
+size_t workspace_bytes_for(int batch, int num_heads, long long total_tokens, int max_seq_len,
+                           int num_splits, bool fp8) {
     if (batch < 0 || num_heads <= 0 || total_tokens < 0) return 0;
     int num_sms = 0, dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess ||
@@ -600,7 +674,18 @@ size_t mla_b200_workspace_size(int batch, int num_heads, long long total_tokens,
     long long max_items = max_items_for(batch, total_tokens, chunk);
     // an automatic split may run the balanced schedule: batch + one item per cluster
     if (num_splits <= 0) max_items = std::max(max_items, (long long)batch + std::max(1, num_sms / 2));
-    return ws_layout(nullptr, max_items, num_heads, batch).bytes;
+    return ws_layout(nullptr, max_items, num_heads, batch, fp8).bytes;
+}
+}  // namespace
+
+size_t mla_b200_workspace_size(int batch, int num_heads, long long total_tokens, int max_seq_len,
+                               int num_splits) {
+    return workspace_bytes_for(batch, num_heads, total_tokens, max_seq_len, num_splits, false);
+}
+
+size_t mla_b200_workspace_size_fp8(int batch, int num_heads, long long total_tokens, int max_seq_len,
+                                   int num_splits) {
+    return workspace_bytes_for(batch, num_heads, total_tokens, max_seq_len, num_splits, true);
 }
 
 int mla_b200_decode_split_f16(const void *query, const void *cache, void *out, int num_heads,
@@ -688,6 +773,34 @@ int mla_b200_decode_paged_bf16(const void *query, const void *kv_pages, const in
                                        num_pages, page_size, max_blocks_per_seq, max_seq_len,
                                        softmax_scale, num_splits, out, out_dtype, out_lse, workspace,
                                        workspace_bytes, stream);
+}
+
+int mla_b200_decode_batched_fp8(const void *query, const void *cache, float kv_scale,
+                                const int32_t *cu_seqlens, int batch, int num_heads,
+                                long long total_tokens, int max_seq_len, float softmax_scale,
+                                int num_splits, void *out, int out_dtype, float *out_lse,
+                                void *workspace, size_t workspace_bytes, void *stream) {
+    if (batch < 0 || num_heads <= 0 || total_tokens < 0 || max_seq_len < 0)
+        return MLA_B200_ERR_INVALID_ARG;
+    if (batch > 0 && (query == nullptr || out == nullptr)) return MLA_B200_ERR_INVALID_ARG;
+    if (total_tokens > 0 && cache == nullptr) return MLA_B200_ERR_INVALID_ARG;
+    if (out_dtype != MLA_B200_OUT_F16 && out_dtype != MLA_B200_OUT_F32) return MLA_B200_ERR_INVALID_ARG;
+    if (!(softmax_scale > 0.f) || !isfinite(softmax_scale)) return MLA_B200_ERR_INVALID_ARG;
+    if (!(kv_scale > 0.f) || !isfinite(kv_scale)) return MLA_B200_ERR_INVALID_ARG;
+    if (!aligned(query, 16) || !aligned(cache, 16) || !aligned(out, 16) || !aligned(out_lse, 4))
+        return MLA_B200_ERR_INVALID_ARG;
+    if (cu_seqlens == nullptr && (long long)batch * max_seq_len != total_tokens)
+        return MLA_B200_ERR_INVALID_ARG;
+    if (cu_seqlens != nullptr && max_seq_len == 0 && total_tokens > 0)
+        return MLA_B200_ERR_INVALID_ARG;
+    if (total_tokens >= (1LL << 31)) return MLA_B200_ERR_UNSUPPORTED;
+    if (num_heads > 128) return MLA_B200_ERR_UNSUPPORTED;
+    Fp8Args f8{cache, kv_scale};
+    // (the fp16 cache pointer is unused on this path; query is fp16)
+    return run_split_decode<__half>(static_cast<const __half *>(query), nullptr, cu_seqlens, batch,
+                                    num_heads, total_tokens, max_seq_len, softmax_scale, num_splits,
+                                    out, out_dtype, out_lse, workspace, workspace_bytes,
+                                    static_cast<cudaStream_t>(stream), nullptr, &f8);
 }
 
 int mla_b200_decode_fused_f32(const float *query, const float *cache, float *out, int num_heads,

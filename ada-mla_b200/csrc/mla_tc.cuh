@@ -69,6 +69,22 @@ constexpr int kQBoxBytes = 128 * 128;            // Q box: 128 rows x 64 fp16
 constexpr int kQSlots = (kKBlocks + 1) / 2;      // 5 ring slots carry Q (two boxes each)
 static_assert(2 * kQBoxBytes <= kSlotS, "two Q boxes per ring slot");
 
+// FP8 (e4m3) cache.  S-CTA: C tiles as 64-byte K-blocks (SW64) in 18 KB slots
+// (3 K-blocks x 96 rows), ten of them in the fp16 ring's space; Q* as fp8 hi
+// and lo planes, one K-block of each per slot.  O-CTA: fp8 C_N tiles [32 x 512 B]
+// land in a 2-slot staging ring, the math warpgroup widens them into the
+// fp16 SW128 tiles GEMM2 reads (3 slots).
+constexpr int kBoxS8 = kTS * 64;                 // 6144: one fp8 K-block [96 tok x 64 B]
+constexpr int kSlotS8 = kKbPerSlot * kBoxS8;     // 18432
+constexpr int kSlotsS8 = 10;
+static_assert(kSlotsS8 * kSlotS8 <= kSlotsS * kSlotS, "fp8 S ring inside the fp16 one");
+constexpr int kQBox8 = 128 * 64;                 // 8192: Q8 box [128 rows x 64 B]
+static_assert(2 * kQBox8 <= kSlotS8, "Q8 hi + lo box per ring slot");
+constexpr int kSlotsO16 = 3;                     // widened fp16 C_N tiles
+constexpr int kStg8 = kTO * kDV;                 // 16384: fp8 C_N tile [32 x 512 B]
+constexpr int kSlotsStg8 = 2;
+constexpr int kTmemQLo = 144;                    // fp8: Q lo plane's TMEM columns
+
 // Message S-CTA -> O-CTA, one per S tile: P as three SW64 K-major sub-tiles of
 // [128 rows x 32 tokens] (8 KB each), then per-row alpha, l, m.
 constexpr int kSubP = 128 * kTO * 2;             // 8192
@@ -80,7 +96,8 @@ constexpr int kMsgBytes = kMsgP + 1536;          // 26112
 constexpr int kMsgStride = 26 * 1024;
 constexpr int kMsgSlots = 3;                     // O-CTA receive ring
 
-constexpr int kRingSlots = kSlotsS > kSlotsO ? kSlotsS : kSlotsO;
+constexpr int kRingSlots = kSlotsS8;             // the deepest ring (fp8 S-CTA)
+static_assert(kRingSlots >= kSlotsS && kRingSlots >= kSlotsO, "ring barriers");
 enum BarId {
     kBarFull = 0,                      // [4] ring slot landed            (count 1 + tx)
     kBarEmpty = kRingSlots,            // [4] ring slot consumed          (count 1, commit)
@@ -93,7 +110,9 @@ enum BarId {
     kBarCorr = kBarPFull + kMsgSlots,  // [3] O-CTA: O ready for GEMM2     (count 128)
     kBarMmaDone = kBarCorr + kMsgSlots,// [3] O-CTA: GEMM2 of a message done (count 1, commit)
     kBarDrain = kBarMmaDone + kMsgSlots,// [2] an MMA issuer's ops retired (teardown)
-    kNumBars = kBarDrain + 2
+    kBarCvtFull = kBarDrain + 2,       // [3] O-CTA, fp8: widened C_N tile ready (count 4, one per warp)
+    kBarCvtEmpty = kBarCvtFull + kSlotsO16, // [3] O-CTA, fp8: GEMM2 done with a widened tile (commit)
+    kNumBars = kBarCvtEmpty + kSlotsO16
 };
 
 // Shared-memory layout (offsets from a 1024-aligned base).  Each role has its
@@ -102,6 +121,8 @@ enum BarId {
 constexpr int kOffRing = 0;
 constexpr int kOffStgS = kSlotsS * kSlotS;                       // 184320: S staging
 constexpr int kOffMsgO = kSlotsO * kSlotO;                       // 131072: O receive ring [3]
+constexpr int kOffStg8 = kSlotsO16 * kSlotO;                     // 98304: fp8 C_N staging
+static_assert(kOffStg8 + kSlotsStg8 * kStg8 <= kOffMsgO, "fp8 staging inside the O ring");
 constexpr int kEndS = kOffStgS + kMsgStride;                     // 210944
 constexpr int kEndO = kOffMsgO + kMsgSlots * kMsgStride;         // 210944
 constexpr int kOffBar = kEndS > kEndO ? kEndS : kEndO;
@@ -123,6 +144,9 @@ constexpr float kRescaleLog2 = 8.0f;
 // GEMM1: M=128 heads, N=96 tokens; GEMM2: M=128 heads, N=256 dims, B MN-major.
 template <bool kBf16> __host__ __device__ constexpr uint32_t idesc_s() { return ptx::idesc_f16_f32(128, kTS, 0, 0, kBf16 ? 1 : 0); }
 template <bool kBf16> __host__ __device__ constexpr uint32_t idesc_o() { return ptx::idesc_f16_f32(128, 256, 0, 1, kBf16 ? 1 : 0); }
+// kind::f8f6f4 with A and B e4m3 (format code 0), f32 accumulate: the same bits
+// as the f16 descriptor.
+__host__ __device__ constexpr uint32_t idesc_s8() { return ptx::idesc_f16_f32(128, kTS, 0, 0, 0); }
 
 struct TcParams {
     WorkList wl;
@@ -131,7 +155,10 @@ struct TcParams {
     void *part_o;      // [max_items, num_heads, 512], element type part_kind
     float *part_lse;   // [max_items, num_heads]
     int part_kind;     // partial element type: kOutF32 / kOutF16
-    int page_size;     // paged: a multiple of kTO
+    union {
+        int page_size;     // paged: a multiple of kTO
+        float o_scale;     // fp8 cache: factor of the finished O (kv scale x 2^8)
+    };
     void *out;         // [batch, num_heads, 512]: written directly for single-item sequences
     int out_kind;      // out element type: kOutF32 / kOutF16 / kOutBF16
     int max_blocks;    // paged
@@ -142,7 +169,10 @@ struct TcParams {
     // and wl.cu_seqlens holds the sequences' offsets on a virtual packed axis.
     // (page_size and max_blocks sit in alignment padding: the kernel's code
     // generation for the contiguous cache is sensitive to this struct's size.)
-    const int32_t *block_table;
+    union {
+        const int32_t *block_table;
+        const float *q_scale;  // fp8 cache: per (sequence, head) row, Q* = Q8 x q_scale
+    };
 };
 
 // Zeroes rows [tail, 32) of a landed [32 x 512] C tile (8 SW128 K-blocks of
@@ -156,6 +186,40 @@ __device__ __forceinline__ void zero_tail(uint32_t tile, int tail, int lane) {
         ptx::st_shared_v4(tile + (rb % kVBlocks) * kBoxO + (tail + rb / kVBlocks) * 128 + (q & 7) * 16, 0u, 0u, 0u, 0u);
     }
     ptx::fence_proxy_async_smem();
+}
+
+// fp8 cache: widens one landed e4m3 C_N tile [32 rows x 512 B] (staging layout
+// [4 column groups][32 rows][128 B], unswizzled) into the fp16 SW128 tile GEMM2
+// reads ([8 K-blocks][32 rows][128 B]).  Each byte s.eeee.mmm becomes the half
+// s.0eeee.mmm0000000, whose value is the e4m3 value times 2^-8 exactly
+// (subnormals included; the 2^8 joins the output scale): integer ops at full
+// rate, where the hardware e4m3 -> f16 conversion measured 2.5x slower here.
+// Called by the 128 threads of a warpgroup; a warp's pass covers 4 rows x one
+// K-block: lane = (row in 4, 16-byte chunk in 8) reads 8 bytes and writes one
+// swizzled 16-byte chunk, so each store instruction fills four whole 128-byte
+// rows (no bank conflicts).  All 16 passes' loads go out first.
+__device__ __forceinline__ uint32_t e4m3_pair_to_half2(uint32_t w, uint32_t sel) {
+    const uint32_t y = __byte_perm(w, 0u, sel);         // lanes: byte << 8
+    const uint32_t a = (y & 0x7F007F00u) >> 1;          // exponent and mantissa
+    return a | (y & 0x80008000u);                       // + sign
+}
+
+__device__ __forceinline__ void widen_tile(uint32_t src, uint32_t dst, int t) {
+    const int lane = t & 31, w = t >> 5;
+    const int j = lane & 7, rr = lane >> 3;
+    uint2 v[16];
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const int wu = w + 4 * i, kb = wu & 7, row = (wu >> 3) * 4 + rr;
+        v[i] = ptx::ld_shared_v2(src + (kb >> 1) * 4096 + row * 128 + (kb & 1) * 64 + j * 8);
+    }
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+        const int wu = w + 4 * i, kb = wu & 7, row = (wu >> 3) * 4 + rr;
+        ptx::st_shared_v4(dst + kb * kBoxO + row * 128 + ((j ^ (row & 7)) << 4),
+                          e4m3_pair_to_half2(v[i].x, 0x1404u), e4m3_pair_to_half2(v[i].x, 0x3424u),
+                          e4m3_pair_to_half2(v[i].y, 0x1404u), e4m3_pair_to_half2(v[i].y, 0x3424u));
+    }
 }
 
 // Pool row of the 32-row box starting at token t (a multiple of kTO) of
@@ -208,8 +272,11 @@ struct Ring {
 // kSchedBalanced); the other schedule's iteration code would cost registers in
 // every role.  kBf16: Q* and the cache are bf16 (P goes to GEMM2 as bf16 too:
 // the MMA takes A and B of one type); otherwise fp16.  kPaged: the cache is a
-// page pool addressed through p.block_table.
-template <int kSched, bool kBf16, bool kPaged>
+// page pool addressed through p.block_table.  kFp8: the cache is e4m3 (cmap_s:
+// 64-byte K-blocks, box 3 x 96 rows, SW64; cmap_o: (128 B, rows, 4) box of one
+// [32 x 512 B] tile, unswizzled) and qmap addresses Q8 [2 x B * n_h, 576] e4m3
+// (hi plane, then lo plane), box 64 x 128, SW64.
+template <int kSched, bool kBf16, bool kPaged, bool kFp8>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tc_decode_kernel(const __grid_constant__ CUtensorMap cmap_s,
                      const __grid_constant__ CUtensorMap cmap_o,
@@ -230,7 +297,14 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (tid == 0) {
         for (int i = 0; i < kRingSlots; ++i) {
             ptx::mbar_init(bar(kBarFull + i), 1);
-            ptx::mbar_init(bar(kBarEmpty + i), 1);
+            // fp8 O-CTA: the staging ring is released by the four widening warps
+            ptx::mbar_init(bar(kBarEmpty + i), (kFp8 && role == 1) ? 4 : 1);
+        }
+        if constexpr (kFp8) {
+            for (int i = 0; i < kSlotsO16; ++i) {
+                ptx::mbar_init(bar(kBarCvtFull + i), 4);
+                ptx::mbar_init(bar(kBarCvtEmpty + i), 1);
+            }
         }
         for (int i = 0; i < 2; ++i) {
             ptx::mbar_init(bar(kBarSFull + i), 1);
@@ -272,7 +346,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
-            const int nslots = role == 0 ? kSlotsS : kSlotsO;
+            const int nslots = role == 0 ? (kFp8 ? kSlotsS8 : kSlotsS) : (kFp8 ? kSlotsStg8 : kSlotsO);
             Ring rg;
             int prev_b = -1;
             bool ok = true;
@@ -293,7 +367,19 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                     for (int c = 0; c < kOPerS; ++c) pr[c] = paged_row(p, it.b, it.tok0 + c * kTO, last);
                 }
-                if (role == 0 && it.b != prev_b) {
+                if (kFp8 && role == 0 && it.b != prev_b) {
+                    // Q8 of the new sequence: hi and lo boxes of one K-block per slot
+                    const int qrow = it.b * p.num_heads, lo_row = wl.batch * p.num_heads + qrow;
+                    for (int kb = 0; kb < kKBlocks; ++kb) {
+                        if (!acquire()) { ok = false; break; }
+                        const uint32_t dst = sbase + kOffRing + rg.slot * kSlotS8;
+                        ptx::mbar_arrive_expect_tx(bar(kBarFull + rg.slot), 2 * kQBox8);
+                        ptx::tma_load_2d(dst, &qmap, kb * 64, qrow, bar(kBarFull + rg.slot));
+                        ptx::tma_load_2d(dst + kQBox8, &qmap, kb * 64, lo_row, bar(kBarFull + rg.slot));
+                        rg.next(nslots);
+                    }
+                    prev_b = it.b;
+                } else if (role == 0 && it.b != prev_b) {
                     // Q of the new sequence: two 128 x 64 boxes per ring slot
                     const int qrow = it.b * p.num_heads;
                     for (int kb = 0; kb < kKBlocks; kb += 2) {
@@ -325,10 +411,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                 rg.next(nslots);
                             }
                         } else {
+                            constexpr int kSlotBytes = kFp8 ? kSlotS8 : kSlotS;
                             for (int sl = 0; sl < kSlotsPerTile; ++sl) {
                                 if (!acquire()) { ok = false; break; }
-                                const uint32_t dst = sbase + kOffRing + rg.slot * kSlotS;
-                                ptx::mbar_arrive_expect_tx(bar(kBarFull + rg.slot), kSlotS);
+                                const uint32_t dst = sbase + kOffRing + rg.slot * kSlotBytes;
+                                ptx::mbar_arrive_expect_tx(bar(kBarFull + rg.slot), kSlotBytes);
                                 ptx::tma_load_3d(dst, &cmap_s, 0, row, sl * kKbPerSlot, bar(kBarFull + rg.slot));
                                 rg.next(nslots);
                             }
@@ -339,8 +426,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                             int r = row + ct * kTO;
                             if constexpr (kPaged) r = ct == 0 ? pr[0] : (ct == 1 ? pr[1] : pr[2]);
                             if (!acquire()) { ok = false; break; }
-                            const uint32_t dst = sbase + kOffRing + rg.slot * kSlotO;
-                            ptx::mbar_arrive_expect_tx(bar(kBarFull + rg.slot), kSlotO);
+                            const uint32_t dst = kFp8 ? sbase + kOffStg8 + rg.slot * kStg8
+                                                      : sbase + kOffRing + rg.slot * kSlotO;
+                            ptx::mbar_arrive_expect_tx(bar(kBarFull + rg.slot), kFp8 ? kStg8 : kSlotO);
                             ptx::tma_load_3d(dst, &cmap_o, 0, r, 0, bar(kBarFull + rg.slot));
                             rg.next(nslots);
                         }
@@ -368,7 +456,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // same items and ring positions, skipping the other's slots.
         // O-CTA: lane 0 of warp 1 issues GEMM2.
         if (lane == 0) {
-            const int nslots = role == 0 ? kSlotsS : kSlotsO;
+            const int nslots = role == 0 ? (kFp8 ? kSlotsS8 : kSlotsS) : (kFp8 ? kSlotsO16 : kSlotsO);
             const uint32_t me = warp == 1 ? 0u : 1u;
             Ring rg;
             uint32_t jt = 0, qphase = 0, nseq = 0, qready_seq = 0;
@@ -400,15 +488,27 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                 // barrier's complete_tx orders the loaded bytes before the
                                 // copy / MMA reads them.  (A fence stalls this thread until
                                 // the tensor pipe drains, ~230 cycles.)
-                                for (int kb = 0; ok && kb < kKBlocks; kb += 2) {
+                                for (int kb = 0; ok && kb < kKBlocks; kb += kFp8 ? 1 : 2) {
                                     if (*abort_flag || !ptx::mbar_spin(bar(kBarFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
-                                    const uint32_t slot = sbase + kOffRing + rg.slot * kSlotS;
-                                    const int nb = min(2, kKBlocks - kb);
-                                    for (int j = 0; j < nb; ++j) {
+                                    if constexpr (kFp8) {
+                                        // K-block kb of the hi and lo planes: 64 B per row, 16 columns each
+                                        const uint32_t slot = sbase + kOffRing + rg.slot * kSlotS8;
 #pragma unroll
-                                        for (int c = 0; c < 4; ++c)
-                                            ptx::tmem_cp_128x256b(tmem + kTmemQ + ((kb + j) * 4 + c) * 8,
-                                                                  ptx::sdesc_sw128(slot + j * kQBoxBytes + c * 32, 16, 1024));
+                                        for (int c = 0; c < 2; ++c) {
+                                            ptx::tmem_cp_128x256b(tmem + kTmemQ + kb * 16 + c * 8,
+                                                                  ptx::sdesc_sw64(slot + c * 32, 16, 512));
+                                            ptx::tmem_cp_128x256b(tmem + kTmemQ + kTmemQLo + kb * 16 + c * 8,
+                                                                  ptx::sdesc_sw64(slot + kQBox8 + c * 32, 16, 512));
+                                        }
+                                    } else {
+                                        const uint32_t slot = sbase + kOffRing + rg.slot * kSlotS;
+                                        const int nb = min(2, kKBlocks - kb);
+                                        for (int j = 0; j < nb; ++j) {
+#pragma unroll
+                                            for (int c = 0; c < 4; ++c)
+                                                ptx::tmem_cp_128x256b(tmem + kTmemQ + ((kb + j) * 4 + c) * 8,
+                                                                      ptx::sdesc_sw128(slot + j * kQBoxBytes + c * 32, 16, 1024));
+                                        }
                                     }
                                     ptx::mma_commit(bar(kBarEmpty + rg.slot));
                                     rg.next(nslots);
@@ -417,7 +517,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                 ptx::mma_commit(bar(kBarQReady));
                                 qready_seq = nseq;
                             } else {
-                                for (int q = 0; q < kQSlots; ++q) rg.next(nslots);
+                                for (int q = 0; q < (kFp8 ? kKBlocks : kQSlots); ++q) rg.next(nslots);
                             }
                         }
                         if (!mine) {
@@ -436,15 +536,28 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                             if (!ptx::mbar_spin(bar(kBarFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
                             // descriptor of the slot, plus compile-time offsets per K-step: a
                             // short issue sequence between MMAs
-                            // (paged slots interleave the K-blocks per 8-row group: stride 3 KB)
-                            const uint64_t b0 = ptx::sdesc_sw128(sbase + kOffRing + rg.slot * kSlotS, 16, kPaged ? kKbPerSlot * 1024 : 1024);
-                            const uint32_t a0 = tmem + kTmemQ + sl * (kKbPerSlot * 32);
                             const uint32_t acc0 = sl > 0 ? 1u : 0u;
-                            constexpr int kKbStride = kPaged ? 1024 : kBoxS;
+                            if constexpr (kFp8) {
+                                // K-block j, K-step ks (32 e4m3): S += Q8hi.C8 + Q8lo.C8
+                                const uint64_t b0 = ptx::sdesc_sw64(sbase + kOffRing + rg.slot * kSlotS8, 16, 512);
+                                const uint32_t a0 = tmem + kTmemQ + sl * (kKbPerSlot * 16);
 #pragma unroll
-                            for (int k = 0; k < kKbPerSlot * 4; ++k)
-                                ptx::mma_ts(d, a0 + k * 8, b0 + (uint64_t)(((k >> 2) * kKbStride + (k & 3) * 32) >> 4),
-                                            idesc_s<kBf16>(), k > 0 ? 1u : acc0);
+                                for (int k = 0; k < kKbPerSlot * 2; ++k) {
+                                    const uint64_t bk = b0 + (uint64_t)(((k >> 1) * kBoxS8 + (k & 1) * 32) >> 4);
+                                    const uint32_t ak = a0 + (k >> 1) * 16 + (k & 1) * 8;
+                                    ptx::mma_ts_f8(d, ak, bk, idesc_s8(), k > 0 ? 1u : acc0);
+                                    ptx::mma_ts_f8(d, ak + kTmemQLo, bk, idesc_s8(), 1u);
+                                }
+                            } else {
+                                // (paged slots interleave the K-blocks per 8-row group: stride 3 KB)
+                                const uint64_t b0 = ptx::sdesc_sw128(sbase + kOffRing + rg.slot * kSlotS, 16, kPaged ? kKbPerSlot * 1024 : 1024);
+                                const uint32_t a0 = tmem + kTmemQ + sl * (kKbPerSlot * 32);
+                                constexpr int kKbStride = kPaged ? 1024 : kBoxS;
+#pragma unroll
+                                for (int k = 0; k < kKbPerSlot * 4; ++k)
+                                    ptx::mma_ts(d, a0 + k * 8, b0 + (uint64_t)(((k >> 2) * kKbStride + (k & 3) * 32) >> 4),
+                                                idesc_s<kBf16>(), k > 0 ? 1u : acc0);
+                            }
                             ptx::mma_commit(bar(kBarEmpty + rg.slot));
                             rg.next(nslots);
                         }
@@ -454,11 +567,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         const uint32_t ms = jt % kMsgSlots, mu = jt / kMsgSlots;
                         if (*abort_flag || !ptx::mbar_wait<true>(bar(kBarPFull + ms), mu & 1, kErrWaitPeer) ||
                             !ptx::mbar_spin(bar(kBarCorr + ms), mu & 1, kErrWaitMma)) { ok = false; break; }
-                        ptx::tc_fence_after();  // the correction's TMEM stores to O come first
-                        const uint64_t p0 = ptx::sdesc_sw64(sbase + kOffMsgO + ms * kMsgStride, 16, 512);
                         const int nct = (min(kTS, it.len - t0) + kTO - 1) / kTO;
+                        if constexpr (!kFp8) ptx::tc_fence_after();  // the correction's TMEM stores to O come first
+                        const uint64_t p0 = ptx::sdesc_sw64(sbase + kOffMsgO + ms * kMsgStride, 16, 512);
                         for (int ct = 0; ct < nct; ++ct) {
-                            if (!ptx::mbar_spin(bar(kBarFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
+                            if constexpr (kFp8) {
+                                // a widened C_N tile, stored by the math warpgroup (which shares
+                                // this SM's schedulers: sleep-backoff wait, not a tight spin); the
+                                // fence orders the MMAs after its stores and the O correction
+                                if (!ptx::mbar_wait(bar(kBarCvtFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
+                                ptx::tc_fence_after();
+                            } else if (!ptx::mbar_spin(bar(kBarFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
                             if constexpr (kPaged) {
                                 // an item's last tile ending inside a 32-row piece: the rows past
                                 // its end are zeroed by the whole warp (the other lanes wait at
@@ -488,7 +607,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                                 c0 + (uint64_t)((nh * 4 * kBoxO + kk * 16 * 128) >> 4), idesc_o<kBf16>(),
                                                 kk > 0 ? 1u : acc0);
                             }
-                            ptx::mma_commit(bar(kBarEmpty + rg.slot));
+                            ptx::mma_commit(bar((kFp8 ? kBarCvtEmpty : kBarEmpty) + rg.slot));
                             rg.next(nslots);
                         }
                         if (!ok) break;
@@ -538,6 +657,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             int i;
             while (ok && items_next<kSched>(wl, cur, it, i)) {
                 float m_used = -INFINITY, l_run = 0.f;
+                // fp8: this row's Q* scale joins the softmax scale
+                float sl2 = p.scale_log2;
+                if constexpr (kFp8) {
+                    if (h < p.num_heads) sl2 *= p.q_scale[(size_t)it.b * p.num_heads + h];
+                }
                 for (int t0 = 0; t0 < it.len; t0 += kTS, ++jt) {
                     const uint32_t sb = jt & 1, use = jt >> 1;
                     const uint32_t ms = jt % kMsgSlots, mu = jt / kMsgSlots;
@@ -578,7 +702,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                         for (int k = 8; k < kTS; ++k) m8[k & 7] = fmaxf(m8[k & 7], f32_of(r[k]));
                         const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                                               fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * p.scale_log2;
+                                               fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * sl2;
                         if (mx > m_used + kRescaleLog2) {
                             alpha = (m_used == -INFINITY) ? 0.f : ptx::ex2(m_used - mx);
                             m_used = mx;
@@ -588,8 +712,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                         for (int k = 0; k < kTS; k += 2) {
-                            const float p0 = ptx::ex2(fmaf(f32_of(r[k]), p.scale_log2, neg_m));
-                            const float p1 = ptx::ex2(fmaf(f32_of(r[k + 1]), p.scale_log2, neg_m));
+                            const float p0 = ptx::ex2(fmaf(f32_of(r[k]), sl2, neg_m));
+                            const float p1 = ptx::ex2(fmaf(f32_of(r[k + 1]), sl2, neg_m));
                             s4[(k >> 1) & 3] += p0 + p1;
                             pk[k >> 1] = pack2<kBf16>(p0, p1);
                         }
@@ -647,9 +771,29 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             ItemCursor cur = items_begin<kSched>(wl, cid, ncl);
             Item it;
             int i;
+            Ring stg, c16;  // fp8: staging ring (from TMA) and widened ring (to GEMM2)
             while (ok && items_next<kSched>(wl, cur, it, i)) {
                 for (int t0 = 0; t0 < it.len; t0 += kTS, ++jt) {
                     const uint32_t ms = jt % kMsgSlots, mu = jt / kMsgSlots;
+                    if constexpr (kFp8) {
+                        // widen the tile's C_N pieces while the S-CTA computes its P
+                        const int nct = (min(kTS, it.len - t0) + kTO - 1) / kTO;
+                        for (int ct = 0; ct < nct; ++ct) {
+                            bool wv = !*abort_flag && ptx::mbar_wait(bar(kBarFull + stg.slot), stg.phase, kErrWaitFull) &&
+                                      ptx::mbar_wait(bar(kBarCvtEmpty + c16.slot), c16.phase ^ 1, kErrWaitMma);
+                            if (!ptx::named_barrier_and(2, 128, wv)) { ok = false; break; }
+                            widen_tile(sbase + kOffStg8 + stg.slot * kStg8, sbase + kOffRing + c16.slot * kSlotO, h);
+                            ptx::fence_proxy_async_smem();
+                            __syncwarp();
+                            if (lane == 0) {
+                                ptx::mbar_arrive(bar(kBarCvtFull + c16.slot));
+                                ptx::mbar_arrive(bar(kBarEmpty + stg.slot));
+                            }
+                            stg.next(kSlotsStg8);
+                            c16.next(kSlotsO16);
+                        }
+                        if (!ok) break;
+                    }
                     // As in the S-CTA, every branch is warpgroup-uniform (bar.red).
                     bool w = !*abort_flag && ptx::mbar_wait<true>(bar(kBarPFull + ms), mu & 1, kErrWaitPeer);
                     if (!ptx::named_barrier_and(2, 128, w)) { ok = false; break; }
@@ -687,7 +831,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         int ni0, ni1;
                         item_range<kSched>(wl, it.b, ni0, ni1);
                         const bool single = ni1 - ni0 == 1;
-                        const float inv_l = l_fin > 0.f ? 1.f / l_fin : 0.f;
+                        float inv_l = l_fin > 0.f ? 1.f / l_fin : 0.f;
+                        if constexpr (kFp8) inv_l *= p.o_scale;
                         const float lse = l_fin > 0.f ? (m_fin + __log2f(l_fin)) * kLn2 : -INFINITY;
                         // 16-bit output: fp16 from fp16 inputs, bf16 from bf16 inputs
                         const bool f16 = (single ? p.out_kind : p.part_kind) != kOutF32;

@@ -198,6 +198,24 @@ MLA_B200_API int mla_b200_decode_paged_bf16(const void *query, const void *kv_pa
                                             int out_dtype, float *out_lse, void *workspace,
                                             size_t workspace_bytes, void *stream);
 
+/* FP8 latent cache (no counterpart in the reference, which lists fp8 as future
+ * work, README.md:407-408).  cache is e4m3 (OCP FP8, bias 7, no infinities)
+ * with the layout of mla_b200_decode_batched_f16's cache (dense or packed) and
+ * one per-tensor scale: C = cache * kv_scale.  query is fp16.  GEMM1 runs on
+ * the fp8 tensor-core path with Q* split into two e4m3 planes (hi + lo, per-row
+ * power-of-two scaling), GEMM2 on widened fp16 C_N tiles; accumulation and
+ * softmax state are fp32.  out_dtype MLA_B200_OUT_F16 or MLA_B200_OUT_F32;
+ * num_heads <= 128.  Workspace: mla_b200_workspace_size_fp8 (it adds the
+ * e4m3 Q* planes, 2 x batch x num_heads x 576 bytes). */
+MLA_B200_API size_t mla_b200_workspace_size_fp8(int batch, int num_heads, long long total_tokens,
+                                                int max_seq_len, int num_splits);
+MLA_B200_API int mla_b200_decode_batched_fp8(const void *query, const void *cache, float kv_scale,
+                                             const int32_t *cu_seqlens, int batch, int num_heads,
+                                             long long total_tokens, int max_seq_len,
+                                             float softmax_scale, int num_splits, void *out,
+                                             int out_dtype, float *out_lse, void *workspace,
+                                             size_t workspace_bytes, void *stream);
+
 /* fp32 fused decode of ONE sequence, reference semantics (scale 1/sqrt(192),
  * 512 output columns).  Replaces run_mla_decode_fused (csrc/mla_decode.hpp:18-23,
  * csrc/mla_decode_fused_fwd_sm89.cu:6-60).  head_dim_c must be 576. */

@@ -81,6 +81,13 @@ def test_invalid_arguments_rejected_before_launch():
                                          None, None, 0, None) == capi.ERR_INVALID_ARG
     assert lib.mla_b200_decode_paged_bf16(16, 16, None, 16, 1, 128, 4, 64, 4, 64, 1.0, 0, 16,
                                           capi.OUT_BF16, None, None, 0, None) == capi.ERR_INVALID_ARG
+    # fp8: bad kv scale; bf16 output is not offered
+    assert lib.mla_b200_decode_batched_fp8(16, 16, 0.0, None, 1, 128, 64, 64, 1.0, 0, 16, capi.OUT_F16,
+                                           None, None, 0, None) == capi.ERR_INVALID_ARG
+    assert lib.mla_b200_decode_batched_fp8(16, 16, 1.0, None, 1, 128, 64, 64, 1.0, 0, 16, capi.OUT_BF16,
+                                           None, None, 0, None) == capi.ERR_INVALID_ARG
+    assert lib.mla_b200_workspace_size_fp8(2, 128, 200, 100, 1) >= \
+        lib.mla_b200_workspace_size(2, 128, 200, 100, 1) + 2 * 2 * 128 * 576
     # fused fp32 requires head_dim_c = 576
     assert lib.mla_b200_decode_fused_f32(16, 16, 16, 128, 512, 64, None, 0, None) == capi.ERR_UNSUPPORTED
     # naive needs all buffers

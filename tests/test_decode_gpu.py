@@ -433,3 +433,73 @@ def test_paged_rejects_bad_shapes(mla):
         mla.mla_decode_paged(q, pool, bt, sl)
     with pytest.raises(RuntimeError):
         mla.mla_decode_paged(q, pool[:, :32].contiguous(), bt[:1], sl)  # block table rows != B
+
+
+# ---------------------------------------------------------------------------
+# FP8 (e4m3) latent cache: the oracle runs on the dequantized cache (the
+# e4m3 values times kv_scale, exact in fp32) with the same fp16 Q*.  The
+# kernel rounds Q* to two e4m3 planes (about 2^-8 relative, like bf16) and
+# keeps P fp16: the north-star bar applies unchanged.
+
+
+def _fp8_inputs(lens, nh, seed, kv_scale, dense_n=None):
+    g = torch.Generator().manual_seed(seed)
+    q = (torch.randn(len(lens), nh, 576, generator=g) / np.sqrt(192)).half()
+    total = sum(lens)
+    c = (torch.randn(total, 576, generator=g) / kv_scale).to(torch.float8_e4m3fn)
+    deq = c.float() * kv_scale
+    return q, c, deq
+
+
+@pytest.mark.parametrize("kv_scale", [1.0, 1.0 / 16])
+def test_fp8_dense(mla, kv_scale):
+    b, nh, n = 3, 128, 300
+    q, c, deq = _fp8_inputs([n] * b, nh, seed=61, kv_scale=kv_scale)
+    out32, lse = mla.mla_decode_batched(q.cuda(), c.view(b, n, 576).cuda(), softmax_scale=1.0,
+                                        return_lse=True, out_dtype=torch.float32, kv_scale=kv_scale)
+    out16 = mla.mla_decode_batched(q.cuda(), c.view(b, n, 576).cuda(), softmax_scale=1.0,
+                                   kv_scale=kv_scale)
+    torch.cuda.synchronize()
+    assert out16.dtype == torch.float16
+    for i in range(b):
+        rows = deq[i * n:(i + 1) * n].numpy()
+        ref = oracle.mla_decode_oracle(_np(q[i]), rows, 1.0, threads=8)
+        assert_close_parity(_np(out32[i]), ref, what=f"fp8 dense fp32-out b={i}")
+        assert_close_parity(_np(out16[i]), ref, what=f"fp8 dense fp16-out b={i}")
+        _, ref_lse = oracle.lse_partial_oracle(_np(q[i]), rows, 1.0)
+        np.testing.assert_allclose(_np(lse[i]), ref_lse, atol=2e-3, rtol=0)
+    _no_device_error(mla)
+
+
+@pytest.mark.parametrize("num_splits", [-1, 1, 3])
+def test_fp8_varlen(mla, capi, num_splits):
+    lens = [5, 0, 64, 95, 96, 97, 129, 1, 700, 2500]
+    q, c, deq = _fp8_inputs(lens, 128, seed=62, kv_scale=0.25)
+    cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32)
+    out = mla.mla_decode_batched(q.cuda(), c.cuda(), cu.cuda(), max_seq_len=max(lens),
+                                 softmax_scale=1.0, num_splits=num_splits, kv_scale=0.25)
+    out_c = capi.decode_batched_fp8(q.cuda(), c.cuda(), 0.25, cu.cuda(), max(lens), 1.0,
+                                    num_splits=num_splits, out_fp32=True)
+    torch.cuda.synchronize()
+    lo = 0
+    for i, n in enumerate(lens):
+        if n == 0:
+            assert torch.count_nonzero(out[i]).item() == 0
+        else:
+            ref = oracle.mla_decode_oracle(_np(q[i]), deq[lo:lo + n].numpy(), 1.0, threads=8)
+            assert_close_parity(_np(out[i]), ref, what=f"fp8 varlen b={i} n={n} s={num_splits}")
+            assert_close_parity(_np(out_c[i]), ref, what=f"fp8 varlen capi b={i}")
+        lo += n
+    _no_device_error(mla)
+
+
+@pytest.mark.parametrize("b,nh,n", [(40, 16, 257), (1, 128, 20017)])
+def test_fp8_batches_and_long(mla, b, nh, n):
+    q, c, deq = _fp8_inputs([n] * b, nh, seed=63 + b, kv_scale=0.5)
+    out = mla.mla_decode_batched(q.cuda(), c.view(b, n, 576).cuda(), softmax_scale=1.0,
+                                 out_dtype=torch.float32, kv_scale=0.5)
+    torch.cuda.synchronize()
+    for i in range(0, b, max(1, b // 8)):
+        ref = oracle.mla_decode_oracle(_np(q[i]), deq[i * n:(i + 1) * n].numpy(), 1.0, threads=8)
+        assert_close_parity(_np(out[i]), ref, what=f"fp8 b={i}")
+    _no_device_error(mla)
