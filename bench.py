@@ -19,6 +19,10 @@ the cache: shuffled pages of P tokens in a pool, addressed through a block
 table (mla_b200_decode_paged_f16); the metric still counts each sequence's own
 cache bytes.
 
+`--kv-dtype fp8` runs it on an e4m3 copy of the cache (kv scale 1;
+mla_b200_decode_batched_fp8); the metric then counts the e4m3 bytes (576 per
+token), so compare us/step with the fp16 line.
+
 `--impl reference` times the reference's own FP32 CPU kernel
 (run_mla_decode_cpu, compiled from the reference sources into oracle/_ref, or
 our C restatement when that build is absent) on all host cores, rank 0 only.
@@ -40,8 +44,8 @@ sys.path.insert(0, ROOT)
 HEAD_DIM_K = 576
 # DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of the
 # main decode kernel per config, from an `ncu --set full` capture of this kernel
-# on this workload (cfg 1: 4.95 MB read, 0 written; cfg 3: 151.9 + 4.7 MB).
-NCU_TRAFFIC = {1: 4.951e6, 3: 156.62e6}
+# on this workload (cfg 1: 4.95 MB read, 0 written; cfg 3: 152.0 + 4.0 MB).
+NCU_TRAFFIC = {1: 4.949e6, 3: 156.02e6}
 METRIC = "MLA decode latent-KV HBM GB/s (us/step alongside)"
 UNIT = "GB/s"
 
@@ -258,7 +262,7 @@ def run_ours(args):
     L2 = torch.cuda.get_device_properties(dev).L2_cache_size or (126 << 20)
 
     wl = make_workload(args.config, seed=1000 * rank, device=dev)
-    step_bytes = wl.cache_bytes + wl.query.numel() * wl.query.element_size()
+    step_bytes = wl.cache_bytes // (2 if args.kv_dtype == "fp8" else 1) + wl.query.numel() * wl.query.element_size()
     ring = max(2, -(-3 * L2 // step_bytes)) if not args.no_rotate else 1
     ring = min(ring, max(1, int(40e9 // step_bytes)))
     qs = [wl.query] + [wl.query.clone() for _ in range(ring - 1)]
@@ -272,6 +276,17 @@ def run_ours(args):
     lib = capi.lib()
     cache_2d = [c.view(-1, HEAD_DIM_K) for c in cs]
     paged = args.page_size > 0
+    fp8 = args.kv_dtype == "fp8"
+    if fp8 and paged:
+        raise SystemExit("--kv-dtype fp8 and --page-size do not combine")
+    cache_bytes = wl.cache_bytes // (2 if fp8 else 1)  # algorithmic bytes one step reads
+    if fp8:
+        cs8 = []
+        while cs:  # convert copy by copy (the fp16 ring need not exist at once in both forms)
+            cs8.append(cs.pop(0).view(-1, HEAD_DIM_K).to(torch.float8_e4m3fn))
+        del cache_2d
+        ws_bytes = lib.mla_b200_workspace_size_fp8(b, nh, total, maxlen, args.splits)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
     if paged:
         pl = paged_layout(wl, args.page_size, seed=rank)
         pools = [pl.scatter(c) for c in cs]  # the ring's copies, each in its own pool
@@ -281,7 +296,12 @@ def run_ours(args):
         step_bytes = pools[0].numel() * pools[0].element_size() + wl.query.numel() * wl.query.element_size()
 
     def step(i, stream):
-        if paged:
+        if fp8:
+            st = lib.mla_b200_decode_batched_fp8(
+                qs[i % ring].data_ptr(), cs8[i % ring].data_ptr(), 1.0,
+                None if cu is None else cu.data_ptr(), b, nh, total, maxlen, 1.0, args.splits,
+                out.data_ptr(), capi.OUT_F16, None, ws.data_ptr(), ws_bytes, stream)
+        elif paged:
             st = lib.mla_b200_decode_paged_f16(
                 qs[i % ring].data_ptr(), pools[i % ring].data_ptr(), pl.block_table.data_ptr(),
                 pl.seq_lens.data_ptr(), b, nh, pl.num_pages, pl.page_size, pl.block_table.shape[1],
@@ -323,7 +343,7 @@ def run_ours(args):
     barrier(world)
     ms_total = max_over_ranks(ev0.elapsed_time(ev1), world)
     ms_step = ms_total / args.steps
-    value = world * wl.cache_bytes / (ms_step * 1e-3) / 1e9
+    value = world * cache_bytes / (ms_step * 1e-3) / 1e9
 
     # per-launch duration of the dominant (main decode) kernel: the library
     # records these events immediately around that launch on its stream; in
@@ -347,12 +367,12 @@ def run_ours(args):
     torch.cuda.synchronize()
     launch_ms = statistics.mean(a.elapsed_time(e) for a, e in evs)
     del tgraph
-    achieved = wl.cache_bytes / (launch_ms * 1e-3) / 1e9
+    achieved = cache_bytes / (launch_ms * 1e-3) / 1e9
 
     # end-to-end through the public API: pinned host inputs -> device, decode,
     # result -> host, every step
     # (paged: the pool, block table and lengths all cross from the host)
-    src = pools[0] if paged else wl.cache
+    src = pools[0] if paged else (cs8[0].view(wl.cache.shape) if fp8 else wl.cache)
     qh = [wl.query.cpu().pin_memory() for _ in range(2)]
     ch = [src.cpu().pin_memory() for _ in range(2)]
     qd, cd = torch.empty_like(wl.query), torch.empty_like(src)
@@ -371,7 +391,7 @@ def run_ours(args):
                                          num_splits=args.splits)
         else:
             o = ada_mla.mla_decode_batched(qd, cd, cu, max_seq_len=maxlen, softmax_scale=1.0,
-                                           num_splits=args.splits)
+                                           num_splits=args.splits, kv_scale=1.0)
         oh.copy_(o, non_blocking=True)
 
     e2e_steps = max(3, min(args.steps, 200))
@@ -387,7 +407,7 @@ def run_ours(args):
     torch.cuda.synchronize()
     barrier(world)
     e2e_ms = max_over_ranks(e0.elapsed_time(e1), world) / e2e_steps
-    e2e_value = world * wl.cache_bytes / (e2e_ms * 1e-3) / 1e9
+    e2e_value = world * cache_bytes / (e2e_ms * 1e-3) / 1e9
     h2d = qh[0].numel() * qh[0].element_size() + ch[0].numel() * ch[0].element_size()
     if paged:
         h2d += bth.numel() * 4 + slh.numel() * 4
@@ -398,17 +418,18 @@ def run_ours(args):
         raise RuntimeError(f"device error word set: {err}")
 
     chunk, splits = capi.plan(b, nh, total, maxlen, torch.cuda.get_device_properties(dev).multi_processor_count)
-    kernels_per_step = 2 + (1 if cu is not None or paged else 0)
+    kernels_per_step = 2 + (1 if cu is not None or paged else 0) + (1 if fp8 else 0)
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "us_per_step": ms_step * 1e3, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+            "vs_baseline": None, "dtype": "f16" + (" (e4m3 cache)" if fp8 else ""), "data": "synthetic",
             "config": {"workload": f"cfg{args.config}: B={b} n_h={nh} N={maxlen} per rank "
                                    + (f"(paged cache: shuffled {args.page_size}-token pages, "
                                       f"{pl.num_pages} pages), " if paged else
-                                      f"({'packed varlen' if cu is not None else 'dense'}), ")
+                                      f"({'packed varlen' if cu is not None else 'dense'}"
+                                      f"{', e4m3 cache' if fp8 else ''}), ")
                                    + "softmax scale folded into Q*",
                        "page_size": args.page_size if paged else None,
                        "cfg": args.config, "batch_per_rank": b, "num_heads": nh,
@@ -420,10 +441,10 @@ def run_ours(args):
                              f">= 3x L2)" if ring > 1 else "no rotation"},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved / hbm_peak, "peak_source": peak_kind,
-                         "traffic": None if paged else NCU_TRAFFIC.get(args.config),
+                         "traffic": None if paged or fp8 else NCU_TRAFFIC.get(args.config),
                          "kernel": "mla::tc::tc_decode_kernel",
                          "launch_us": launch_ms * 1e3,
-                         "algorithmic_bytes_per_launch": wl.cache_bytes},
+                         "algorithmic_bytes_per_launch": cache_bytes},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "us_per_step": e2e_ms * 1e3,
                     "api": "ada_mla.mla_decode_paged" if paged else "ada_mla.mla_decode_batched"},
@@ -530,6 +551,8 @@ def main():
     ap.add_argument("--config", type=int, default=1, choices=[1, 2, 3, 4])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--splits", type=int, default=-1)
+    ap.add_argument("--kv-dtype", default="fp16", choices=["fp16", "fp8"],
+                    help="fp8: decode an e4m3 copy of the cache")
     ap.add_argument("--page-size", type=int, default=0,
                     help="decode a paged copy of the cache (pages of this many tokens)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
