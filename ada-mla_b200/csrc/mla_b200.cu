@@ -153,12 +153,12 @@ int make_tmap_fp8_s(CUtensorMap *map, const void *base, long long rows) {
 }
 
 // e4m3 cache, GEMM2 side: (128 B, rows, 4 column groups) over the first 512
-// columns, unswizzled, one box = a [32 x 512 B] C_N tile for the widening warps.
+// columns, 128-byte swizzle, one box = a [32 x 512 B] C_N tile, GEMM2's MN-major B.
 int make_tmap_fp8_o(CUtensorMap *map, const void *base, long long rows) {
     const cuuint64_t dims[3] = {128, (cuuint64_t)rows, (cuuint64_t)(kDV / 128)};
     const cuuint64_t strides[2] = {(cuuint64_t)kDK, 128};
     const cuuint32_t box[3] = {128, (cuuint32_t)tc::kTO, (cuuint32_t)(kDV / 128)};
-    return encode_tmap(map, base, 3, dims, strides, box, false, CU_TENSOR_MAP_SWIZZLE_NONE, true);
+    return encode_tmap(map, base, 3, dims, strides, box, false, CU_TENSOR_MAP_SWIZZLE_128B, true);
 }
 
 // Q8 [2 x rows, 576] e4m3 (hi plane then lo plane), box 64 B x 128 rows, SW64.
@@ -473,11 +473,10 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
             tp.out_lse = out_lse;
             tp.max_blocks = pg != nullptr ? pg->max_blocks : 0;
             if (f8 != nullptr) {
-                // S = kv_scale * q_scale[row] * (Q8.C8); O = kv_scale * 2^8 * (P.C8w) / l,
-                // C8w being the widened tile (e4m3 value x 2^-8)
+                // S = kv_scale * q_scale[row] * (Q8.C8); O = kv_scale * (P8.C8) / (kP8Scale * l)
                 tp.scale_log2 = scale * kLog2e * f8->kv_scale;
                 tp.q_scale = L.q_scale;
-                tp.o_scale = f8->kv_scale * 256.f;
+                tp.o_scale = f8->kv_scale / tc::kP8Scale;
             } else {
                 tp.block_table = pg != nullptr ? pg->block_table : nullptr;
                 tp.page_size = pg != nullptr ? pg->page_size : 0;

@@ -71,18 +71,19 @@ static_assert(2 * kQBoxBytes <= kSlotS, "two Q boxes per ring slot");
 
 // FP8 (e4m3) cache.  S-CTA: C tiles as 64-byte K-blocks (SW64) in 18 KB slots
 // (3 K-blocks x 96 rows), ten of them in the fp16 ring's space; Q* as fp8 hi
-// and lo planes, one K-block of each per slot.  O-CTA: fp8 C_N tiles [32 x 512 B]
-// land in a 2-slot staging ring, the math warpgroup widens them into the
-// fp16 SW128 tiles GEMM2 reads (3 slots).
+// and lo planes, one K-block of each per slot.  O-CTA: C8_N tiles [32 x 512 B]
+// (4 column groups of 128 B, SW128: GEMM2's MN-major B) in eight 16 KB slots;
+// the math warpgroup turns each fp16 P message into e4m3 hi and lo planes in
+// place (3 K-steps x [128 rows x 32 B], SW32), GEMM2's K-major A.
 constexpr int kBoxS8 = kTS * 64;                 // 6144: one fp8 K-block [96 tok x 64 B]
 constexpr int kSlotS8 = kKbPerSlot * kBoxS8;     // 18432
 constexpr int kSlotsS8 = 10;
 static_assert(kSlotsS8 * kSlotS8 <= kSlotsS * kSlotS, "fp8 S ring inside the fp16 one");
 constexpr int kQBox8 = 128 * 64;                 // 8192: Q8 box [128 rows x 64 B]
 static_assert(2 * kQBox8 <= kSlotS8, "Q8 hi + lo box per ring slot");
-constexpr int kSlotsO16 = 3;                     // widened fp16 C_N tiles
-constexpr int kStg8 = kTO * kDV;                 // 16384: fp8 C_N tile [32 x 512 B]
-constexpr int kSlotsStg8 = 2;
+constexpr int kSlotO8 = kTO * kDV;               // 16384: C8_N tile [32 x 512 B]
+constexpr int kSlotsO8 = 8;
+constexpr int kPlaneP8 = kOPerS * 128 * kTO;     // 12288: one e4m3 P plane of a message
 constexpr int kTmemQLo = 144;                    // fp8: Q lo plane's TMEM columns
 
 // Message S-CTA -> O-CTA, one per S tile: P as three SW64 K-major sub-tiles of
@@ -110,9 +111,7 @@ enum BarId {
     kBarCorr = kBarPFull + kMsgSlots,  // [3] O-CTA: O ready for GEMM2     (count 128)
     kBarMmaDone = kBarCorr + kMsgSlots,// [3] O-CTA: GEMM2 of a message done (count 1, commit)
     kBarDrain = kBarMmaDone + kMsgSlots,// [2] an MMA issuer's ops retired (teardown)
-    kBarCvtFull = kBarDrain + 2,       // [3] O-CTA, fp8: widened C_N tile ready (count 4, one per warp)
-    kBarCvtEmpty = kBarCvtFull + kSlotsO16, // [3] O-CTA, fp8: GEMM2 done with a widened tile (commit)
-    kNumBars = kBarCvtEmpty + kSlotsO16
+    kNumBars = kBarDrain + 2
 };
 
 // Shared-memory layout (offsets from a 1024-aligned base).  Each role has its
@@ -121,8 +120,8 @@ enum BarId {
 constexpr int kOffRing = 0;
 constexpr int kOffStgS = kSlotsS * kSlotS;                       // 184320: S staging
 constexpr int kOffMsgO = kSlotsO * kSlotO;                       // 131072: O receive ring [3]
-constexpr int kOffStg8 = kSlotsO16 * kSlotO;                     // 98304: fp8 C_N staging
-static_assert(kOffStg8 + kSlotsStg8 * kStg8 <= kOffMsgO, "fp8 staging inside the O ring");
+static_assert(kSlotsO8 * kSlotO8 <= kOffMsgO, "C8_N ring inside the O ring");
+static_assert(2 * kPlaneP8 <= kMsgAlpha, "e4m3 P planes inside the message's P");
 constexpr int kEndS = kOffStgS + kMsgStride;                     // 210944
 constexpr int kEndO = kOffMsgO + kMsgSlots * kMsgStride;         // 210944
 constexpr int kOffBar = kEndS > kEndO ? kEndS : kEndO;
@@ -140,6 +139,12 @@ constexpr uint32_t kTmemQ = 0;     // S-CTA: Q, 288 columns (2 fp16 per column)
 constexpr uint32_t kTmemS = 288;   // S-CTA: two S buffers of kTS columns
 static_assert(kTmemS + 2 * kTS <= kTmemCols, "TMEM budget");
 constexpr float kRescaleLog2 = 8.0f;
+// fp8 cache: P is scaled by 2^2 before its e4m3 hi/lo split (small weights
+// reach e4m3's subnormals 4x later: their absolute error drops to 2^-12), and
+// the lazy rescale keeps p <= 2^6: 2^2 * 64 = 256 stays under e4m3's 448.  (2^6
+// with p <= 4 measured slower: O corrections become frequent.)
+constexpr float kRescaleLog2Fp8 = 6.0f;
+constexpr float kP8Scale = 4.0f;
 
 // GEMM1: M=128 heads, N=96 tokens; GEMM2: M=128 heads, N=256 dims, B MN-major.
 template <bool kBf16> __host__ __device__ constexpr uint32_t idesc_s() { return ptx::idesc_f16_f32(128, kTS, 0, 0, kBf16 ? 1 : 0); }
@@ -157,7 +162,7 @@ struct TcParams {
     int part_kind;     // partial element type: kOutF32 / kOutF16
     union {
         int page_size;     // paged: a multiple of kTO
-        float o_scale;     // fp8 cache: factor of the finished O (kv scale x 2^8)
+        float o_scale;     // fp8 cache: factor of the finished O (kv scale / kP8Scale)
     };
     void *out;         // [batch, num_heads, 512]: written directly for single-item sequences
     int out_kind;      // out element type: kOutF32 / kOutF16 / kOutBF16
@@ -188,37 +193,69 @@ __device__ __forceinline__ void zero_tail(uint32_t tile, int tail, int lane) {
     ptx::fence_proxy_async_smem();
 }
 
-// fp8 cache: widens one landed e4m3 C_N tile [32 rows x 512 B] (staging layout
-// [4 column groups][32 rows][128 B], unswizzled) into the fp16 SW128 tile GEMM2
-// reads ([8 K-blocks][32 rows][128 B]).  Each byte s.eeee.mmm becomes the half
-// s.0eeee.mmm0000000, whose value is the e4m3 value times 2^-8 exactly
-// (subnormals included; the 2^8 joins the output scale): integer ops at full
-// rate, where the hardware e4m3 -> f16 conversion measured 2.5x slower here.
-// Called by the 128 threads of a warpgroup; a warp's pass covers 4 rows x one
-// K-block: lane = (row in 4, 16-byte chunk in 8) reads 8 bytes and writes one
-// swizzled 16-byte chunk, so each store instruction fills four whole 128-byte
-// rows (no bank conflicts).  All 16 passes' loads go out first.
-__device__ __forceinline__ uint32_t e4m3_pair_to_half2(uint32_t w, uint32_t sel) {
-    const uint32_t y = __byte_perm(w, 0u, sel);         // lanes: byte << 8
-    const uint32_t a = (y & 0x7F007F00u) >> 1;          // exponent and mantissa
-    return a | (y & 0x80008000u);                       // + sign
+// fp8 cache: turns row h of a landed fp16 P message (3 SW64 K-major sub-tiles
+// [128 x 32 tokens]) into e4m3 hi and lo planes of q = p * kP8Scale, hi =
+// e4m3(q), lo = e4m3(q - hi) (q to ~2^-8 relative; one e4m3 plane would be
+// 2^-4), written over the same bytes as GEMM2's A: plane x, K-step st at
+// x * kPlaneP8 + st * 4096, row h's 32 bytes with 32-byte swizzle.  All of the
+// warpgroup's reads must finish (a named barrier between the two halves)
+// before any write.
+struct P8Row {
+    uint4 v[kOPerS * 4];  // the row's 96 fp16 values
+};
+
+__device__ __forceinline__ void p8_read(const uint8_t *msg, int h, P8Row &r) {
+#pragma unroll
+    for (int st = 0; st < kOPerS; ++st)
+#pragma unroll
+        for (int c4 = 0; c4 < 4; ++c4)
+            r.v[st * 4 + c4] = *reinterpret_cast<const uint4 *>(msg + st * kSubP + h * 64 + ((c4 ^ ((h >> 1) & 3)) << 4));
 }
 
-__device__ __forceinline__ void widen_tile(uint32_t src, uint32_t dst, int t) {
-    const int lane = t & 31, w = t >> 5;
-    const int j = lane & 7, rr = lane >> 3;
-    uint2 v[16];
+__device__ __forceinline__ uint32_t e4m3x2_of(uint32_t h2) {  // two halves -> two e4m3 bytes
+    const __half2_raw hr = *reinterpret_cast<const __half2_raw *>(&h2);
+    return (uint32_t)__nv_cvt_halfraw2_to_fp8x2(hr, __NV_SATFINITE, __NV_E4M3);
+}
+
+__device__ __forceinline__ uint32_t half2_of_e4m3x2(uint32_t b2) {
+    const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2((__nv_fp8x2_storage_t)b2, __NV_E4M3);
+    return (uint32_t)hr.x | ((uint32_t)hr.y << 16);
+}
+
+__device__ __forceinline__ void p8_write(uint8_t *msg, int h, const P8Row &r) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        const int wu = w + 4 * i, kb = wu & 7, row = (wu >> 3) * 4 + rr;
-        v[i] = ptx::ld_shared_v2(src + (kb >> 1) * 4096 + row * 128 + (kb & 1) * 64 + j * 8);
-    }
+    for (int st = 0; st < kOPerS; ++st) {
+        uint32_t hi[8], lo[8];
 #pragma unroll
-    for (int i = 0; i < 16; ++i) {
-        const int wu = w + 4 * i, kb = wu & 7, row = (wu >> 3) * 4 + rr;
-        ptx::st_shared_v4(dst + kb * kBoxO + row * 128 + ((j ^ (row & 7)) << 4),
-                          e4m3_pair_to_half2(v[i].x, 0x1404u), e4m3_pair_to_half2(v[i].x, 0x3424u),
-                          e4m3_pair_to_half2(v[i].y, 0x1404u), e4m3_pair_to_half2(v[i].y, 0x3424u));
+        for (int c4 = 0; c4 < 4; ++c4) {
+            uint32_t in[4] = {r.v[st * 4 + c4].x, r.v[st * 4 + c4].y, r.v[st * 4 + c4].z, r.v[st * 4 + c4].w};
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {  // x kP8Scale: exact in fp16 (p <= 64)
+                const __half2 q = __hmul2(*reinterpret_cast<const __half2 *>(&in[k]), __float2half2_rn(kP8Scale));
+                in[k] = *reinterpret_cast<const uint32_t *>(&q);
+            }
+            uint32_t hb[4], lb[4];
+#pragma unroll
+            for (int k = 0; k < 4; ++k) {
+                hb[k] = e4m3x2_of(in[k]);
+                const __half2 d = __hsub2(*reinterpret_cast<const __half2 *>(&in[k]),
+                                          __halves2half2(__ushort_as_half((unsigned short)(half2_of_e4m3x2(hb[k]) & 0xFFFFu)),
+                                                         __ushort_as_half((unsigned short)(half2_of_e4m3x2(hb[k]) >> 16))));
+                lb[k] = e4m3x2_of(*reinterpret_cast<const uint32_t *>(&d));
+            }
+            hi[2 * c4] = hb[0] | (hb[1] << 16);
+            hi[2 * c4 + 1] = hb[2] | (hb[3] << 16);
+            lo[2 * c4] = lb[0] | (lb[1] << 16);
+            lo[2 * c4 + 1] = lb[2] | (lb[3] << 16);
+        }
+        const int sw = (h >> 2) & 1;  // 32-byte swizzle: chunk ^= address bit 7
+#pragma unroll
+        for (int x = 0; x < 2; ++x) {
+            const uint32_t *src = x == 0 ? hi : lo;
+            uint8_t *row = msg + x * kPlaneP8 + st * 4096 + h * 32;
+            *reinterpret_cast<uint4 *>(row + ((0 ^ sw) << 4)) = make_uint4(src[0], src[1], src[2], src[3]);
+            *reinterpret_cast<uint4 *>(row + ((1 ^ sw) << 4)) = make_uint4(src[4], src[5], src[6], src[7]);
+        }
     }
 }
 
@@ -297,14 +334,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (tid == 0) {
         for (int i = 0; i < kRingSlots; ++i) {
             ptx::mbar_init(bar(kBarFull + i), 1);
-            // fp8 O-CTA: the staging ring is released by the four widening warps
-            ptx::mbar_init(bar(kBarEmpty + i), (kFp8 && role == 1) ? 4 : 1);
-        }
-        if constexpr (kFp8) {
-            for (int i = 0; i < kSlotsO16; ++i) {
-                ptx::mbar_init(bar(kBarCvtFull + i), 4);
-                ptx::mbar_init(bar(kBarCvtEmpty + i), 1);
-            }
+            ptx::mbar_init(bar(kBarEmpty + i), 1);
         }
         for (int i = 0; i < 2; ++i) {
             ptx::mbar_init(bar(kBarSFull + i), 1);
@@ -346,7 +376,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
-            const int nslots = role == 0 ? (kFp8 ? kSlotsS8 : kSlotsS) : (kFp8 ? kSlotsStg8 : kSlotsO);
+            const int nslots = role == 0 ? (kFp8 ? kSlotsS8 : kSlotsS) : (kFp8 ? kSlotsO8 : kSlotsO);
             Ring rg;
             int prev_b = -1;
             bool ok = true;
@@ -426,9 +456,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                             int r = row + ct * kTO;
                             if constexpr (kPaged) r = ct == 0 ? pr[0] : (ct == 1 ? pr[1] : pr[2]);
                             if (!acquire()) { ok = false; break; }
-                            const uint32_t dst = kFp8 ? sbase + kOffStg8 + rg.slot * kStg8
-                                                      : sbase + kOffRing + rg.slot * kSlotO;
-                            ptx::mbar_arrive_expect_tx(bar(kBarFull + rg.slot), kFp8 ? kStg8 : kSlotO);
+                            const uint32_t dst = sbase + kOffRing + rg.slot * (kFp8 ? kSlotO8 : kSlotO);
+                            ptx::mbar_arrive_expect_tx(bar(kBarFull + rg.slot), kFp8 ? kSlotO8 : kSlotO);
                             ptx::tma_load_3d(dst, &cmap_o, 0, r, 0, bar(kBarFull + rg.slot));
                             rg.next(nslots);
                         }
@@ -456,7 +485,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         // same items and ring positions, skipping the other's slots.
         // O-CTA: lane 0 of warp 1 issues GEMM2.
         if (lane == 0) {
-            const int nslots = role == 0 ? (kFp8 ? kSlotsS8 : kSlotsS) : (kFp8 ? kSlotsO16 : kSlotsO);
+            const int nslots = role == 0 ? (kFp8 ? kSlotsS8 : kSlotsS) : (kFp8 ? kSlotsO8 : kSlotsO);
             const uint32_t me = warp == 1 ? 0u : 1u;
             Ring rg;
             uint32_t jt = 0, qphase = 0, nseq = 0, qready_seq = 0;
@@ -568,16 +597,12 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         if (*abort_flag || !ptx::mbar_wait<true>(bar(kBarPFull + ms), mu & 1, kErrWaitPeer) ||
                             !ptx::mbar_spin(bar(kBarCorr + ms), mu & 1, kErrWaitMma)) { ok = false; break; }
                         const int nct = (min(kTS, it.len - t0) + kTO - 1) / kTO;
-                        if constexpr (!kFp8) ptx::tc_fence_after();  // the correction's TMEM stores to O come first
+                        // the correction's TMEM stores to O (and fp8: the e4m3 P planes the
+                        // warpgroup wrote) come first
+                        ptx::tc_fence_after();
                         const uint64_t p0 = ptx::sdesc_sw64(sbase + kOffMsgO + ms * kMsgStride, 16, 512);
                         for (int ct = 0; ct < nct; ++ct) {
-                            if constexpr (kFp8) {
-                                // a widened C_N tile, stored by the math warpgroup (which shares
-                                // this SM's schedulers: sleep-backoff wait, not a tight spin); the
-                                // fence orders the MMAs after its stores and the O correction
-                                if (!ptx::mbar_wait(bar(kBarCvtFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
-                                ptx::tc_fence_after();
-                            } else if (!ptx::mbar_spin(bar(kBarFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
+                            if (!ptx::mbar_spin(bar(kBarFull + rg.slot), rg.phase, kErrWaitFull)) { ok = false; break; }
                             if constexpr (kPaged) {
                                 // an item's last tile ending inside a 32-row piece: the rows past
                                 // its end are zeroed by the whole warp (the other lanes wait at
@@ -596,18 +621,32 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                     ptx::tc_fence_after();
                                 }
                             }
-                            const uint64_t c0 = ptx::sdesc_sw128(sbase + kOffRing + rg.slot * kSlotO, kBoxO, 1024);
-                            const uint64_t pa = p0 + (uint64_t)(ct * (kSubP >> 4));
                             const uint32_t acc0 = (t0 > 0 || ct > 0) ? 1u : 0u;
+                            if constexpr (kFp8) {
+                                // O += P8hi.C8 + P8lo.C8 (K = 32 tokens); C8_N MN-major: 128-column
+                                // groups 4 KB apart (LBO), 8-row groups 1 KB apart (SBO)
+                                const uint64_t c0 = ptx::sdesc_sw128(sbase + kOffRing + rg.slot * kSlotO8, 4096, 1024);
+                                const uint32_t pm = sbase + kOffMsgO + ms * kMsgStride + ct * 4096;
 #pragma unroll
-                            for (int kk = 0; kk < kTO / 16; ++kk) {
+                                for (int x = 0; x < 2; ++x)
 #pragma unroll
-                                for (int nh = 0; nh < 2; ++nh)
-                                    ptx::mma_ss(tmem + nh * 256, pa + (uint64_t)((kk * 32) >> 4),
-                                                c0 + (uint64_t)((nh * 4 * kBoxO + kk * 16 * 128) >> 4), idesc_o<kBf16>(),
-                                                kk > 0 ? 1u : acc0);
+                                    for (int nh = 0; nh < 2; ++nh)
+                                        ptx::mma_ss_f8(tmem + nh * 256, ptx::sdesc_sw32(pm + x * kPlaneP8, 16, 256),
+                                                       c0 + (uint64_t)((nh * 2 * 4096) >> 4), idesc_o<false>(),
+                                                       x > 0 ? 1u : acc0);
+                            } else {
+                                const uint64_t c0 = ptx::sdesc_sw128(sbase + kOffRing + rg.slot * kSlotO, kBoxO, 1024);
+                                const uint64_t pa = p0 + (uint64_t)(ct * (kSubP >> 4));
+#pragma unroll
+                                for (int kk = 0; kk < kTO / 16; ++kk) {
+#pragma unroll
+                                    for (int nh = 0; nh < 2; ++nh)
+                                        ptx::mma_ss(tmem + nh * 256, pa + (uint64_t)((kk * 32) >> 4),
+                                                    c0 + (uint64_t)((nh * 4 * kBoxO + kk * 16 * 128) >> 4), idesc_o<kBf16>(),
+                                                    kk > 0 ? 1u : acc0);
+                                }
                             }
-                            ptx::mma_commit(bar((kFp8 ? kBarCvtEmpty : kBarEmpty) + rg.slot));
+                            ptx::mma_commit(bar(kBarEmpty + rg.slot));
                             rg.next(nslots);
                         }
                         if (!ok) break;
@@ -703,7 +742,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         for (int k = 8; k < kTS; ++k) m8[k & 7] = fmaxf(m8[k & 7], f32_of(r[k]));
                         const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
                                                fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * sl2;
-                        if (mx > m_used + kRescaleLog2) {
+                        if (mx > m_used + (kFp8 ? kRescaleLog2Fp8 : kRescaleLog2)) {
                             alpha = (m_used == -INFINITY) ? 0.f : ptx::ex2(m_used - mx);
                             m_used = mx;
                         }
@@ -771,33 +810,23 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             ItemCursor cur = items_begin<kSched>(wl, cid, ncl);
             Item it;
             int i;
-            Ring stg, c16;  // fp8: staging ring (from TMA) and widened ring (to GEMM2)
             while (ok && items_next<kSched>(wl, cur, it, i)) {
                 for (int t0 = 0; t0 < it.len; t0 += kTS, ++jt) {
                     const uint32_t ms = jt % kMsgSlots, mu = jt / kMsgSlots;
-                    if constexpr (kFp8) {
-                        // widen the tile's C_N pieces while the S-CTA computes its P
-                        const int nct = (min(kTS, it.len - t0) + kTO - 1) / kTO;
-                        for (int ct = 0; ct < nct; ++ct) {
-                            bool wv = !*abort_flag && ptx::mbar_wait(bar(kBarFull + stg.slot), stg.phase, kErrWaitFull) &&
-                                      ptx::mbar_wait(bar(kBarCvtEmpty + c16.slot), c16.phase ^ 1, kErrWaitMma);
-                            if (!ptx::named_barrier_and(2, 128, wv)) { ok = false; break; }
-                            widen_tile(sbase + kOffStg8 + stg.slot * kStg8, sbase + kOffRing + c16.slot * kSlotO, h);
-                            ptx::fence_proxy_async_smem();
-                            __syncwarp();
-                            if (lane == 0) {
-                                ptx::mbar_arrive(bar(kBarCvtFull + c16.slot));
-                                ptx::mbar_arrive(bar(kBarEmpty + stg.slot));
-                            }
-                            stg.next(kSlotsStg8);
-                            c16.next(kSlotsO16);
-                        }
-                        if (!ok) break;
-                    }
                     // As in the S-CTA, every branch is warpgroup-uniform (bar.red).
                     bool w = !*abort_flag && ptx::mbar_wait<true>(bar(kBarPFull + ms), mu & 1, kErrWaitPeer);
                     if (!ptx::named_barrier_and(2, 128, w)) { ok = false; break; }
                     const uint8_t *msg = smem + kOffMsgO + ms * kMsgStride;
+                    if constexpr (kFp8) {
+                        // P (fp16) -> e4m3 hi / lo planes in place, before Corr releases GEMM2.
+                        // (A message slot is rewritten only after its GEMM2 finished: the
+                        // S-CTA sends message x+3 after GEMM2 x freed the slot.)
+                        P8Row pr;
+                        p8_read(msg, h, pr);
+                        ptx::named_barrier(2, 128);
+                        p8_write(const_cast<uint8_t *>(msg), h, pr);
+                        ptx::fence_proxy_async_smem();
+                    }
                     const float alpha = reinterpret_cast<const float *>(msg + kMsgAlpha)[h];
                     const bool last = t0 + kTS >= it.len;
                     float l_fin = 0.f, m_fin = 0.f;

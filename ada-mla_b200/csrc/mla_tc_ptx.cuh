@@ -349,6 +349,16 @@ __device__ __forceinline__ void mma_ts_f8(uint32_t d_tmem, uint32_t a_tmem, uint
         : "memory");
 }
 
+// D[tmem] (+)= A[smem desc] * B[smem desc]^T, kind::f8f6f4, K = 32, fp32 accumulate.
+__device__ __forceinline__ void mma_ss_f8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc,
+                                          uint32_t idesc, uint32_t accumulate) {
+    asm volatile(
+        "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+        "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+        "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+        : "memory");
+}
+
 // Arrive on a local mbarrier once all prior tcgen05 async ops of this thread finish.
 __device__ __forceinline__ void mma_commit(uint32_t bar) {
     asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(
@@ -432,6 +442,17 @@ __device__ __forceinline__ uint64_t sdesc_sw64(uint32_t addr, uint32_t lbo, uint
     d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
     d |= (uint64_t)1 << 46;
     d |= (uint64_t)4 << 61;                        // layout: SWIZZLE_64B
+    return d;
+}
+
+// Same with 32-byte swizzle (rows of 32 B, 8-row atoms of 256 B).
+__device__ __forceinline__ uint64_t sdesc_sw32(uint32_t addr, uint32_t lbo, uint32_t sbo) {
+    uint64_t d = 0;
+    d |= (uint64_t)((addr >> 4) & 0x3FFF);
+    d |= (uint64_t)((lbo >> 4) & 0x3FFF) << 16;
+    d |= (uint64_t)((sbo >> 4) & 0x3FFF) << 32;
+    d |= (uint64_t)1 << 46;
+    d |= (uint64_t)6 << 61;                        // layout: SWIZZLE_32B
     return d;
 }
 
