@@ -33,7 +33,7 @@ from ._build import EXT_NAME, EXT_PATH, LIB_PATH
 
 __all__ = [
     "mla_decode_naive", "mla_decode_fused", "mla_decode_split", "mla_decode_batched",
-    "mla_decode_paged",
+    "mla_decode_paged", "mla_decode_mtp",
     "mla_combine", "mla_get_device_error", "NUM_HEADS", "HEAD_DIM", "HEAD_DIM_C",
     "HEAD_DIM_ROPE", "HEAD_DIM_K", "HEAD_DIM_V", "SOFTMAX_SCALE", "lib_path", "ext_path",
 ]
@@ -121,4 +121,25 @@ def mla_decode_paged(query, kv_pages, block_table, seq_lens, max_seq_len: int = 
     out, lse = _ext.mla_decode_paged(query, kv_pages, block_table, seq_lens, int(max_seq_len),
                                      float(softmax_scale), int(num_splits), bool(return_lse),
                                      out_dtype == torch.float32)
+    return (out, lse) if return_lse else out
+
+
+def mla_decode_mtp(query, cache, cu_seqlens=None, max_seq_len: int = -1,
+                   softmax_scale: float = SOFTMAX_SCALE, num_splits: int = -1,
+                   return_lse: bool = False, out_dtype=None):
+    """Multi-token (speculative / MTP draft) decode.
+
+    query  [B, k, n_h, 576] fp16 or bf16 with k * n_h <= 128: k draft tokens per
+           sequence whose own latent rows are the sequence's last k cache rows.
+    cache  as for ``mla_decode_batched`` (dense [B, N, 576] or packed with
+           ``cu_seqlens``), same dtype.  Draft token i of a sequence of length L
+           sees its first L - (k - 1 - i) tokens.
+    The k drafts share every cache tile (rows token * n_h + head of one MMA
+    tile): one pass over the cache for k tokens.  Returns O* [B, k, n_h, 512]
+    (and the LSE [B, k, n_h] with ``return_lse``).
+    """
+    if out_dtype not in (None, torch.float32, query.dtype):
+        raise ValueError(f"mla_decode_mtp: out_dtype must be None, float32 or {query.dtype}")
+    out, lse = _ext.mla_decode_mtp(query, cache, cu_seqlens, int(max_seq_len), float(softmax_scale),
+                                   int(num_splits), bool(return_lse), out_dtype == torch.float32)
     return (out, lse) if return_lse else out

@@ -48,6 +48,10 @@ SIGNATURES = {
                                               _c_int, _vp, _c_int, _vp, _vp, _c_size, _vp]),
     "mla_b200_decode_batched_fp8": (_c_int, [_vp, _vp, _c_float, _vp, _c_int, _c_int, _c_ll, _c_int,
                                              _c_float, _c_int, _vp, _c_int, _vp, _vp, _c_size, _vp]),
+    "mla_b200_decode_mtp_f16": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _c_ll, _c_int, _c_float,
+                                         _c_int, _vp, _c_int, _vp, _vp, _c_size, _vp]),
+    "mla_b200_decode_mtp_bf16": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _c_ll, _c_int, _c_float,
+                                          _c_int, _vp, _c_int, _vp, _vp, _c_size, _vp]),
     "mla_b200_decode_paged_f16": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int,
                                            _c_int, _c_float, _c_int, _vp, _c_int, _vp, _vp, _c_size, _vp]),
     "mla_b200_decode_paged_bf16": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _c_int, _c_int,

@@ -186,6 +186,61 @@ std::vector<at::Tensor> mla_decode_batched(const at::Tensor &query, const at::Te
     return {out, lse};
 }
 
+// Multi-token decode (no reference counterpart).
+//   query [B, k, n_h, 576] fp16 or bf16 (k * n_h <= 128), cache as in
+//   mla_decode_batched (same dtype); draft token i of sequence b sees its first
+//   len_b - (k - 1 - i) tokens.  Returns (out [B, k, n_h, 512], lse [B, k, n_h] or empty).
+std::vector<at::Tensor> mla_decode_mtp(const at::Tensor &query, const at::Tensor &cache,
+                                       const c10::optional<at::Tensor> &cu_seqlens,
+                                       int64_t max_seq_len, double softmax_scale,
+                                       int64_t num_splits, bool return_lse, bool out_fp32) {
+    check_cuda(query, "query");
+    check_cuda(cache, "cache");
+    TORCH_CHECK(query.device() == cache.device(), "query and cache on different devices");
+    const bool bf16 = query.scalar_type() == at::kBFloat16;
+    TORCH_CHECK((query.scalar_type() == at::kHalf || bf16) && cache.scalar_type() == query.scalar_type(),
+                "mla_decode_mtp: float16 or bfloat16 inputs (query and cache alike) expected");
+    TORCH_CHECK(query.dim() == 4 && query.size(3) == MLA_B200_HEAD_DIM_K,
+                "mla_decode_mtp: query must be [B, k, n_h, 576]");
+    const int64_t b = query.size(0), k = query.size(1), nh = query.size(2);
+    c10::cuda::CUDAGuard g(query.device());
+    const int32_t *cu_ptr = nullptr;
+    int64_t total = 0;
+    if (cu_seqlens.has_value() && cu_seqlens->defined()) {
+        const at::Tensor &cu = *cu_seqlens;
+        check_cuda(cu, "cu_seqlens");
+        TORCH_CHECK(cu.device() == query.device(), "cu_seqlens on a different device");
+        TORCH_CHECK(cu.scalar_type() == at::kInt && cu.dim() == 1 && cu.size(0) == b + 1,
+                    "cu_seqlens must be int32 [B+1]");
+        TORCH_CHECK(cache.dim() == 2 && cache.size(1) == MLA_B200_HEAD_DIM_K,
+                    "packed cache must be [T, 576]");
+        total = cache.size(0);
+        if (max_seq_len < 0)
+            max_seq_len = b > 0 ? (cu.slice(0, 1) - cu.slice(0, 0, b)).max().item<int64_t>() : 0;
+        cu_ptr = cu.data_ptr<int32_t>();
+    } else {
+        TORCH_CHECK(cache.dim() == 3 && cache.size(0) == b && cache.size(2) == MLA_B200_HEAD_DIM_K,
+                    "dense cache must be [B, N, 576]");
+        max_seq_len = cache.size(1);
+        total = b * max_seq_len;
+    }
+    at::Tensor out = at::empty({b, k, nh, MLA_B200_HEAD_DIM_V},
+                               query.options().dtype(out_fp32 ? at::kFloat : query.scalar_type()));
+    at::Tensor lse = return_lse ? at::empty({b, k, nh}, query.options().dtype(at::kFloat)) : at::Tensor();
+    const size_t ws = mla_b200_workspace_size((int)b, (int)(k * nh), total, (int)max_seq_len,
+                                              (int)num_splits);
+    at::Tensor w = workspace(query, ws);
+    auto *fn = bf16 ? mla_b200_decode_mtp_bf16 : mla_b200_decode_mtp_f16;
+    const int odt = out_fp32 ? MLA_B200_OUT_F32 : (bf16 ? MLA_B200_OUT_BF16 : MLA_B200_OUT_F16);
+    check_status(fn(query.data_ptr(), cache.data_ptr(), cu_ptr, (int)b, (int)k, (int)nh, total,
+                    (int)max_seq_len, (float)softmax_scale, (int)num_splits, out.data_ptr(), odt,
+                    return_lse ? lse.data_ptr<float>() : nullptr, w.data_ptr(), w.numel(),
+                    stream_ptr()),
+                 "mla_decode_mtp");
+    if (!return_lse) lse = at::empty({0}, query.options().dtype(at::kFloat));
+    return {out, lse};
+}
+
 // Paged decode (no reference counterpart).
 //   query [B, n_h, 576] fp16 or bf16; kv_pages [num_pages, page_size, 576] in the
 //   same dtype; block_table int32 [B, max_blocks]; seq_lens int32 [B]; all on
@@ -283,6 +338,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
           py::arg("max_seq_len") = -1, py::arg("softmax_scale") = 0.07216878364870322,
           py::arg("num_splits") = -1, py::arg("return_lse") = false, py::arg("out_fp32") = false,
           py::arg("kv_scale") = 1.0);
+    m.def("mla_decode_mtp", &mla_decode_mtp, "multi-token (draft) decode sharing each cache tile",
+          py::arg("query"), py::arg("cache"), py::arg("cu_seqlens") = py::none(),
+          py::arg("max_seq_len") = -1, py::arg("softmax_scale") = 0.07216878364870322,
+          py::arg("num_splits") = -1, py::arg("return_lse") = false, py::arg("out_fp32") = false);
     m.def("mla_decode_paged", &mla_decode_paged, "decode over a paged latent cache",
           py::arg("query"), py::arg("kv_pages"), py::arg("block_table"), py::arg("seq_lens"),
           py::arg("max_seq_len") = -1, py::arg("softmax_scale") = 0.07216878364870322,

@@ -46,11 +46,11 @@ int cuda_failure(cudaError_t e) {
 
 // Opts a tensor-core kernel instantiation (both schedules) into its dynamic
 // shared memory.
-template <bool kBf16, bool kPaged, bool kFp8 = false>
+template <bool kBf16, bool kPaged, bool kFp8 = false, bool kMtp = false>
 bool set_tc_smem() {
-    return cudaFuncSetAttribute(tc::tc_decode_kernel<kSchedChunked, kBf16, kPaged, kFp8>,
+    return cudaFuncSetAttribute(tc::tc_decode_kernel<kSchedChunked, kBf16, kPaged, kFp8, kMtp>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmemBytes) == cudaSuccess &&
-           cudaFuncSetAttribute(tc::tc_decode_kernel<kSchedBalanced, kBf16, kPaged, kFp8>,
+           cudaFuncSetAttribute(tc::tc_decode_kernel<kSchedBalanced, kBf16, kPaged, kFp8, kMtp>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmemBytes) == cudaSuccess;
 }
 
@@ -88,7 +88,8 @@ int current_device(int *dev_out, DevInfo *info_out) {
     if (d.tc_clusters == 0) {
         if (!set_tc_smem<false, false>() || !set_tc_smem<true, false>() ||
             !set_tc_smem<false, true>() || !set_tc_smem<true, true>() ||
-            !set_tc_smem<false, false, true>()) {
+            !set_tc_smem<false, false, true>() || !set_tc_smem<false, false, false, true>() ||
+            !set_tc_smem<true, false, false, true>()) {
             return cuda_failure(cudaGetLastError());
         }
         cudaLaunchConfig_t cfg = {};
@@ -307,6 +308,13 @@ struct Fp8Args {
     float kv_scale;
 };
 
+// Multi-token decode: each sequence carries `tokens` draft-token queries of
+// `heads` heads each (rows token * heads + head); see tc_decode_kernel.
+struct MtpArgs {
+    int tokens;
+    int heads;
+};
+
 struct PagedArgs {
     const int32_t *block_table;
     const int32_t *seq_lens;
@@ -337,11 +345,11 @@ void launch_dependent(void (*kernel)(Params...), dim3 grid, dim3 block, size_t s
     cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);  // errors: launch_status()
 }
 
-template <int kSched, bool kBf16, bool kPaged, bool kFp8 = false>
+template <int kSched, bool kBf16, bool kPaged, bool kFp8 = false, bool kMtp = false>
 void launch_tc(int clusters, const CUtensorMap &cs, const CUtensorMap &co, const CUtensorMap &qm,
                const tc::TcParams &tp, cudaStream_t stream, bool after_plan) {
-    launch_dependent(tc::tc_decode_kernel<kSched, kBf16, kPaged, kFp8>, dim3(2 * clusters), dim3(tc::kThreads),
-                     tc::kSmemBytes, stream, after_plan, cs, co, qm, tp);
+    launch_dependent(tc::tc_decode_kernel<kSched, kBf16, kPaged, kFp8, kMtp>, dim3(2 * clusters),
+                     dim3(tc::kThreads), tc::kSmemBytes, stream, after_plan, cs, co, qm, tp);
 }
 
 // Shared driver of the split-KV paths: plan -> partial kernel -> combine.
@@ -353,7 +361,7 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
                      int num_heads, long long total_tokens, int max_seq_len, float scale,
                      int num_splits, void *out, int out_dtype, float *out_lse, void *workspace,
                      size_t workspace_bytes, cudaStream_t stream, const PagedArgs *pg = nullptr,
-                     const Fp8Args *f8 = nullptr) {
+                     const Fp8Args *f8 = nullptr, const MtpArgs *mtp = nullptr) {
     int dev;
     DevInfo info;
     int st = current_device(&dev, &info);
@@ -368,6 +376,7 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     if (kBf16 && !tc_path) return MLA_B200_ERR_UNSUPPORTED;  // bf16 has no SIMT kernel
     if (pg != nullptr && !tc_path) return MLA_B200_ERR_UNSUPPORTED;  // paged: tensor-core kernel only
     if (f8 != nullptr && (!tc_path || kBf16 || pg != nullptr)) return MLA_B200_ERR_UNSUPPORTED;
+    if (mtp != nullptr && (!tc_path || pg != nullptr || f8 != nullptr)) return MLA_B200_ERR_UNSUPPORTED;
     // (A single sequence splits evenly in the chunked schedule already.)
     const bool balanced = tc_path && num_splits <= 0 && batch > 1;
     int chunk = chunk_for(batch, total_tokens, max_seq_len, num_splits, info.sms);
@@ -472,6 +481,7 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
                           : out_dtype == MLA_B200_OUT_BF16 ? tc::kOutBF16 : tc::kOutF32;
             tp.out_lse = out_lse;
             tp.max_blocks = pg != nullptr ? pg->max_blocks : 0;
+            if (mtp != nullptr) tp.mtp = (mtp->tokens << 16) | mtp->heads;
             if (f8 != nullptr) {
                 // S = kv_scale * q_scale[row] * (Q8.C8); O = kv_scale * (P8.C8) / (kP8Scale * l)
                 tp.scale_log2 = scale * kLog2e * f8->kv_scale;
@@ -484,7 +494,10 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
             tc_direct = true;
             const int clusters = balanced ? bal_clusters : std::min(info.tc_clusters, wl.max_items);
             timing_mark(t_ev_start, stream);
-            if (f8 != nullptr) {
+            if (mtp != nullptr) {
+                if (balanced) launch_tc<kSchedBalanced, kBf16, false, false, true>(clusters, cmap_s, cmap_o, qmap, tp, stream, cu_seqlens != nullptr);
+                else launch_tc<kSchedChunked, kBf16, false, false, true>(clusters, cmap_s, cmap_o, qmap, tp, stream, cu_seqlens != nullptr);
+            } else if (f8 != nullptr) {
                 if constexpr (!kBf16) {  // (fp8 runs with fp16 Q*; the prep kernel precedes)
                     if (balanced) launch_tc<kSchedBalanced, false, false, true>(clusters, cmap_s, cmap_o, qmap, tp, stream, true);
                     else launch_tc<kSchedChunked, false, false, true>(clusters, cmap_s, cmap_o, qmap, tp, stream, true);
@@ -592,6 +605,37 @@ int decode_paged(const void *query, const void *kv_pages, const int32_t *block_t
                                nullptr, batch, num_heads, bound, max_seq_len, softmax_scale,
                                num_splits, out, out_dtype, out_lse, workspace, workspace_bytes,
                                static_cast<cudaStream_t>(stream), &pg);
+}
+}  // namespace
+
+namespace {
+template <typename T>
+int decode_mtp(const void *query, const void *cache, const int32_t *cu_seqlens, int batch,
+               int num_tokens, int num_heads, long long total_tokens, int max_seq_len,
+               float softmax_scale, int num_splits, void *out, int out_dtype, float *out_lse,
+               void *workspace, size_t workspace_bytes, void *stream) {
+    constexpr bool kBf16 = std::is_same<T, __nv_bfloat16>::value;
+    if (batch < 0 || num_tokens <= 0 || num_heads <= 0 || total_tokens < 0 || max_seq_len < 0)
+        return MLA_B200_ERR_INVALID_ARG;
+    if (batch > 0 && (query == nullptr || out == nullptr)) return MLA_B200_ERR_INVALID_ARG;
+    if (total_tokens > 0 && cache == nullptr) return MLA_B200_ERR_INVALID_ARG;
+    if (kBf16 ? (out_dtype != MLA_B200_OUT_BF16 && out_dtype != MLA_B200_OUT_F32)
+              : (out_dtype != MLA_B200_OUT_F16 && out_dtype != MLA_B200_OUT_F32))
+        return MLA_B200_ERR_INVALID_ARG;
+    if (!(softmax_scale > 0.f) || !isfinite(softmax_scale)) return MLA_B200_ERR_INVALID_ARG;
+    if (!aligned(query, 16) || !aligned(cache, 16) || !aligned(out, 16) || !aligned(out_lse, 4))
+        return MLA_B200_ERR_INVALID_ARG;
+    if (cu_seqlens == nullptr && (long long)batch * max_seq_len != total_tokens)
+        return MLA_B200_ERR_INVALID_ARG;
+    if (cu_seqlens != nullptr && max_seq_len == 0 && total_tokens > 0)
+        return MLA_B200_ERR_INVALID_ARG;
+    if (total_tokens >= (1LL << 31)) return MLA_B200_ERR_UNSUPPORTED;
+    if ((long long)num_tokens * num_heads > 128) return MLA_B200_ERR_UNSUPPORTED;
+    MtpArgs m{num_tokens, num_heads};
+    return run_split_decode<T>(static_cast<const T *>(query), static_cast<const T *>(cache),
+                               cu_seqlens, batch, num_tokens * num_heads, total_tokens, max_seq_len,
+                               softmax_scale, num_splits, out, out_dtype, out_lse, workspace,
+                               workspace_bytes, static_cast<cudaStream_t>(stream), nullptr, nullptr, &m);
 }
 }  // namespace
 
@@ -772,6 +816,26 @@ int mla_b200_decode_paged_bf16(const void *query, const void *kv_pages, const in
                                        num_pages, page_size, max_blocks_per_seq, max_seq_len,
                                        softmax_scale, num_splits, out, out_dtype, out_lse, workspace,
                                        workspace_bytes, stream);
+}
+
+int mla_b200_decode_mtp_f16(const void *query, const void *cache, const int32_t *cu_seqlens,
+                            int batch, int num_tokens, int num_heads, long long total_tokens,
+                            int max_seq_len, float softmax_scale, int num_splits, void *out,
+                            int out_dtype, float *out_lse, void *workspace, size_t workspace_bytes,
+                            void *stream) {
+    return decode_mtp<__half>(query, cache, cu_seqlens, batch, num_tokens, num_heads, total_tokens,
+                              max_seq_len, softmax_scale, num_splits, out, out_dtype, out_lse,
+                              workspace, workspace_bytes, stream);
+}
+
+int mla_b200_decode_mtp_bf16(const void *query, const void *cache, const int32_t *cu_seqlens,
+                             int batch, int num_tokens, int num_heads, long long total_tokens,
+                             int max_seq_len, float softmax_scale, int num_splits, void *out,
+                             int out_dtype, float *out_lse, void *workspace, size_t workspace_bytes,
+                             void *stream) {
+    return decode_mtp<__nv_bfloat16>(query, cache, cu_seqlens, batch, num_tokens, num_heads,
+                                     total_tokens, max_seq_len, softmax_scale, num_splits, out,
+                                     out_dtype, out_lse, workspace, workspace_bytes, stream);
 }
 
 int mla_b200_decode_batched_fp8(const void *query, const void *cache, float kv_scale,

@@ -166,7 +166,10 @@ struct TcParams {
     };
     void *out;         // [batch, num_heads, 512]: written directly for single-item sequences
     int out_kind;      // out element type: kOutF32 / kOutF16 / kOutBF16
-    int max_blocks;    // paged
+    union {
+        int max_blocks;    // paged
+        int mtp;           // multi-token: (draft tokens << 16) | heads per token
+    };
     float *out_lse;    // [batch, num_heads] or null
     // Paged cache (kPaged): the maps address the page pool as rows
     // [num_pages * page_size, 576]; token t of sequence b lives in pool row
@@ -309,11 +312,14 @@ struct Ring {
 // kSchedBalanced); the other schedule's iteration code would cost registers in
 // every role.  kBf16: Q* and the cache are bf16 (P goes to GEMM2 as bf16 too:
 // the MMA takes A and B of one type); otherwise fp16.  kPaged: the cache is a
-// page pool addressed through p.block_table.  kFp8: the cache is e4m3 (cmap_s:
+// page pool addressed through p.block_table.  kMtp: each sequence's rows are
+// (draft token i, head) pairs, row = i * heads + head, and draft token i of k
+// sees the sequence's first len - (k - 1 - i) tokens (its own KV being the
+// cache's last k rows).  kFp8: the cache is e4m3 (cmap_s:
 // 64-byte K-blocks, box 3 x 96 rows, SW64; cmap_o: (128 B, rows, 4) box of one
 // [32 x 512 B] tile, unswizzled) and qmap addresses Q8 [2 x B * n_h, 576] e4m3
 // (hi plane, then lo plane), box 64 x 128, SW64.
-template <int kSched, bool kBf16, bool kPaged, bool kFp8>
+template <int kSched, bool kBf16, bool kPaged, bool kFp8, bool kMtp = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tc_decode_kernel(const __grid_constant__ CUtensorMap cmap_s,
                      const __grid_constant__ CUtensorMap cmap_o,
@@ -701,6 +707,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                 if constexpr (kFp8) {
                     if (h < p.num_heads) sl2 *= p.q_scale[(size_t)it.b * p.num_heads + h];
                 }
+                // multi-token: this row's causal limit, as a token offset within the item
+                int lim = 0;
+                if constexpr (kMtp) {
+                    const int mk = p.mtp >> 16, mnh = p.mtp & 0xFFFF;
+                    const int tok = min(h / mnh, mk - 1);
+                    const int slen = wl.cu_seqlens != nullptr ? wl.cu_seqlens[it.b + 1] - wl.cu_seqlens[it.b]
+                                                              : wl.seq_len;
+                    lim = slen - (mk - 1 - tok) - it.tok0;
+                }
                 for (int t0 = 0; t0 < it.len; t0 += kTS, ++jt) {
                     const uint32_t sb = jt & 1, use = jt >> 1;
                     const uint32_t ms = jt % kMsgSlots, mu = jt / kMsgSlots;
@@ -729,7 +744,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
                         // Row max of the raw logits (scale > 0 commutes with max), with
                         // masked tail columns at -inf; 8 independent chains.
-                        const int valid = min(kTS, it.len - t0);
+                        // (multi-token: per row; a row may see none of a tile)
+                        const int valid = kMtp ? max(0, min(min(kTS, it.len - t0), lim - t0)) : min(kTS, it.len - t0);
                         if (valid < kTS) {
 #pragma unroll
                             for (int k = 0; k < kTS; ++k)
@@ -747,7 +763,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                             m_used = mx;
                         }
                         // p = 2^(s * scale_log2 - m_used): one FFMA + one EX2 per logit.
-                        const float neg_m = -m_used;
+                        // (a row that has seen nothing yet keeps m_used = -inf: its p are 0)
+                        const float neg_m = (kMtp && m_used == -INFINITY) ? 0.f : -m_used;
                         float s4[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                         for (int k = 0; k < kTS; k += 2) {

@@ -23,6 +23,10 @@ cache bytes.
 mla_b200_decode_batched_fp8); the metric then counts the e4m3 bytes (576 per
 token), so compare us/step with the fp16 line.
 
+`--mtp K` decodes K draft tokens per sequence in one pass over the cache
+(mla_b200_decode_mtp_f16, K x n_h <= 128): the same bytes per step for K times
+the tokens (config keys `draft_tokens`, `tokens_per_step`).
+
 `--impl reference` times the reference's own FP32 CPU kernel
 (run_mla_decode_cpu, compiled from the reference sources into oracle/_ref, or
 our C restatement when that build is absent) on all host cores, rank 0 only.
@@ -277,6 +281,18 @@ def run_ours(args):
     cache_2d = [c.view(-1, HEAD_DIM_K) for c in cs]
     paged = args.page_size > 0
     fp8 = args.kv_dtype == "fp8"
+    mtp = args.mtp > 1
+    if mtp and (paged or fp8):
+        raise SystemExit("--mtp combines with neither --page-size nor --kv-dtype fp8")
+    if mtp:
+        if args.mtp * nh > 128:
+            raise SystemExit(f"--mtp {args.mtp} x {nh} heads exceeds 128 rows")
+        g = torch.Generator(device=dev).manual_seed(77 + rank)
+        qm = (torch.randn((b, args.mtp, nh, HEAD_DIM_K), generator=g, device=dev) / 192 ** 0.5).half()
+        qs = [qm] + [qm.clone() for _ in range(ring - 1)]
+        ws_bytes = capi.workspace_size(b, args.mtp * nh, total, maxlen, args.splits)
+        ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
+        out = torch.empty((b, args.mtp, nh, 512), dtype=torch.float16, device=dev)
     if fp8 and paged:
         raise SystemExit("--kv-dtype fp8 and --page-size do not combine")
     cache_bytes = wl.cache_bytes // (2 if fp8 else 1)  # algorithmic bytes one step reads
@@ -296,7 +312,12 @@ def run_ours(args):
         step_bytes = pools[0].numel() * pools[0].element_size() + wl.query.numel() * wl.query.element_size()
 
     def step(i, stream):
-        if fp8:
+        if mtp:
+            st = lib.mla_b200_decode_mtp_f16(
+                qs[i % ring].data_ptr(), cache_2d[i % ring].data_ptr(),
+                None if cu is None else cu.data_ptr(), b, args.mtp, nh, total, maxlen, 1.0,
+                args.splits, out.data_ptr(), capi.OUT_F16, None, ws.data_ptr(), ws_bytes, stream)
+        elif fp8:
             st = lib.mla_b200_decode_batched_fp8(
                 qs[i % ring].data_ptr(), cs8[i % ring].data_ptr(), 1.0,
                 None if cu is None else cu.data_ptr(), b, nh, total, maxlen, 1.0, args.splits,
@@ -373,10 +394,10 @@ def run_ours(args):
     # result -> host, every step
     # (paged: the pool, block table and lengths all cross from the host)
     src = pools[0] if paged else (cs8[0].view(wl.cache.shape) if fp8 else wl.cache)
-    qh = [wl.query.cpu().pin_memory() for _ in range(2)]
+    qh = [(qs[0] if mtp else wl.query).cpu().pin_memory() for _ in range(2)]
     ch = [src.cpu().pin_memory() for _ in range(2)]
-    qd, cd = torch.empty_like(wl.query), torch.empty_like(src)
-    oh = torch.empty((b, nh, 512), dtype=torch.float16).pin_memory()
+    qd, cd = torch.empty_like(qh[0], device=dev), torch.empty_like(src)
+    oh = torch.empty(tuple(out.shape), dtype=torch.float16).pin_memory()
     if paged:
         bth, slh = pl.block_table.cpu().pin_memory(), pl.seq_lens.cpu().pin_memory()
         btd, sld = torch.empty_like(pl.block_table), torch.empty_like(pl.seq_lens)
@@ -384,7 +405,10 @@ def run_ours(args):
     def e2e_step(i):
         qd.copy_(qh[i % 2], non_blocking=True)
         cd.copy_(ch[i % 2], non_blocking=True)
-        if paged:
+        if mtp:
+            o = ada_mla.mla_decode_mtp(qd, cd, cu, max_seq_len=maxlen, softmax_scale=1.0,
+                                       num_splits=args.splits)
+        elif paged:
             btd.copy_(bth, non_blocking=True)
             sld.copy_(slh, non_blocking=True)
             o = ada_mla.mla_decode_paged(qd, cd, btd, sld, max_seq_len=maxlen, softmax_scale=1.0,
@@ -432,6 +456,8 @@ def run_ours(args):
                                       f"{', e4m3 cache' if fp8 else ''}), ")
                                    + "softmax scale folded into Q*",
                        "page_size": args.page_size if paged else None,
+                       "draft_tokens": args.mtp if mtp else 1,
+                       "tokens_per_step": b * (args.mtp if mtp else 1) * world,
                        "cfg": args.config, "batch_per_rank": b, "num_heads": nh,
                        "seq_len": maxlen, "total_tokens_per_rank": total,
                        "num_splits": splits if args.splits <= 0 else args.splits,
@@ -447,7 +473,8 @@ def run_ours(args):
                          "algorithmic_bytes_per_launch": cache_bytes},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "us_per_step": e2e_ms * 1e3,
-                    "api": "ada_mla.mla_decode_paged" if paged else "ada_mla.mla_decode_batched"},
+                    "api": ("ada_mla.mla_decode_mtp" if mtp else "ada_mla.mla_decode_paged" if paged
+                            else "ada_mla.mla_decode_batched")},
             "gpu_launches": args.steps * kernels_per_step,
             "clocks": sampler.summary(),
         }
@@ -551,6 +578,8 @@ def main():
     ap.add_argument("--config", type=int, default=1, choices=[1, 2, 3, 4])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--splits", type=int, default=-1)
+    ap.add_argument("--mtp", type=int, default=1,
+                    help="draft tokens per sequence decoded in one pass (multi-token decode)")
     ap.add_argument("--kv-dtype", default="fp16", choices=["fp16", "fp8"],
                     help="fp8: decode an e4m3 copy of the cache")
     ap.add_argument("--page-size", type=int, default=0,

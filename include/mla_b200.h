@@ -198,6 +198,29 @@ MLA_B200_API int mla_b200_decode_paged_bf16(const void *query, const void *kv_pa
                                             int out_dtype, float *out_lse, void *workspace,
                                             size_t workspace_bytes, void *stream);
 
+/* Multi-token decode (speculative / MTP drafts; no counterpart in the
+ * reference): every sequence carries num_tokens queries, query [batch,
+ * num_tokens, num_heads, 576], whose own latent rows are the last num_tokens
+ * rows of the sequence's cache; draft token i sees the sequence's first
+ * len - (num_tokens - 1 - i) tokens (len >= num_tokens).  The drafts share
+ * every cache tile: rows token * num_heads + head fill one 128-row MMA tile, so
+ * num_tokens * num_heads <= 128.  out [batch, num_tokens, num_heads, 512],
+ * out_lse [batch, num_tokens, num_heads] or NULL; otherwise the contract of
+ * mla_b200_decode_batched_f16 / _bf16 (workspace: mla_b200_workspace_size with
+ * num_heads = num_tokens * num_heads). */
+MLA_B200_API int mla_b200_decode_mtp_f16(const void *query, const void *cache,
+                                         const int32_t *cu_seqlens, int batch, int num_tokens,
+                                         int num_heads, long long total_tokens, int max_seq_len,
+                                         float softmax_scale, int num_splits, void *out,
+                                         int out_dtype, float *out_lse, void *workspace,
+                                         size_t workspace_bytes, void *stream);
+MLA_B200_API int mla_b200_decode_mtp_bf16(const void *query, const void *cache,
+                                          const int32_t *cu_seqlens, int batch, int num_tokens,
+                                          int num_heads, long long total_tokens, int max_seq_len,
+                                          float softmax_scale, int num_splits, void *out,
+                                          int out_dtype, float *out_lse, void *workspace,
+                                          size_t workspace_bytes, void *stream);
+
 /* FP8 latent cache (no counterpart in the reference, which lists fp8 as future
  * work, README.md:407-408).  cache is e4m3 (OCP FP8, bias 7, no infinities)
  * with the layout of mla_b200_decode_batched_f16's cache (dense or packed) and

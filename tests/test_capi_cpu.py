@@ -88,6 +88,11 @@ def test_invalid_arguments_rejected_before_launch():
                                            None, None, 0, None) == capi.ERR_INVALID_ARG
     assert lib.mla_b200_workspace_size_fp8(2, 128, 200, 100, 1) >= \
         lib.mla_b200_workspace_size(2, 128, 200, 100, 1) + 2 * 2 * 128 * 576
+    # multi-token: more than 128 rows per sequence, zero tokens
+    assert lib.mla_b200_decode_mtp_f16(16, 16, None, 1, 2, 128, 64, 64, 1.0, 0, 16, capi.OUT_F16,
+                                       None, None, 0, None) == capi.ERR_UNSUPPORTED
+    assert lib.mla_b200_decode_mtp_f16(16, 16, None, 1, 0, 16, 64, 64, 1.0, 0, 16, capi.OUT_F16,
+                                       None, None, 0, None) == capi.ERR_INVALID_ARG
     # fused fp32 requires head_dim_c = 576
     assert lib.mla_b200_decode_fused_f32(16, 16, 16, 128, 512, 64, None, 0, None) == capi.ERR_UNSUPPORTED
     # naive needs all buffers

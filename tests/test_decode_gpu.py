@@ -503,3 +503,60 @@ def test_fp8_batches_and_long(mla, b, nh, n):
         ref = oracle.mla_decode_oracle(_np(q[i]), deq[i * n:(i + 1) * n].numpy(), 1.0, threads=8)
         assert_close_parity(_np(out[i]), ref, what=f"fp8 b={i}")
     _no_device_error(mla)
+
+
+# ---------------------------------------------------------------------------
+# Multi-token (draft) decode: draft token i of k sees the first L - (k-1-i)
+# tokens of its sequence; the oracle runs each (sequence, token) separately.
+
+
+def _mtp_check(mla, q, c_rows, lens, out, what, lse=None):
+    k = q.shape[1]
+    lo = 0
+    for b, n in enumerate(lens):
+        for i in range(k):
+            vis = n - (k - 1 - i)
+            if vis <= 0:
+                assert torch.count_nonzero(out[b, i]).item() == 0, f"{what} b={b} i={i}"
+                continue
+            rows = c_rows[lo:lo + vis]
+            ref = oracle.mla_decode_oracle(_np(q[b, i]), _np(rows), 1.0, threads=8)
+            assert_close_parity(_np(out[b, i]), ref, what=f"{what} b={b} i={i} n={n}")
+            if lse is not None and i == k - 1 and b % 3 == 0:
+                _, ref_lse = oracle.lse_partial_oracle(_np(q[b, i]), _np(rows), 1.0)
+                np.testing.assert_allclose(_np(lse[b, i]), ref_lse, atol=2e-3, rtol=0)
+        lo += n
+
+
+@pytest.mark.parametrize("k,nh", [(8, 16), (2, 64), (1, 128)])
+def test_mtp_dense(mla, k, nh):
+    b, n = 12, 700
+    g = torch.Generator().manual_seed(71 + k)
+    q = (torch.randn(b, k, nh, 576, generator=g) / np.sqrt(192)).half()
+    c = torch.randn(b, n, 576, generator=g).half()
+    out, lse = mla.mla_decode_mtp(q.cuda(), c.cuda(), softmax_scale=1.0, return_lse=True)
+    torch.cuda.synchronize()
+    assert out.shape == (b, k, nh, 512)
+    _mtp_check(mla, q, c.view(-1, 576), [n] * b, out, f"mtp dense k={k}", lse)
+    if k == 1:  # one draft token is the plain batched decode, bit for bit
+        ref = mla.mla_decode_batched(q[:, 0].contiguous().cuda(), c.cuda(), softmax_scale=1.0)
+        torch.cuda.synchronize()
+        assert torch.equal(out[:, 0], ref)
+    _no_device_error(mla)
+
+
+@pytest.mark.parametrize("num_splits", [-1, 1, 4])
+def test_mtp_varlen_short_and_split(mla, num_splits):
+    """Sequences shorter than, equal to and just past the draft count, a split
+    landing inside the last k-1 tokens (97 = 96 + 1), and long ones."""
+    k, nh = 8, 16
+    lens = [3, 8, 9, 96, 97, 100, 1500, 40]
+    g = torch.Generator().manual_seed(72)
+    q = (torch.randn(len(lens), k, nh, 576, generator=g) / np.sqrt(192)).bfloat16()
+    c = torch.randn(sum(lens), 576, generator=g).bfloat16()
+    cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32)
+    out = mla.mla_decode_mtp(q.cuda(), c.cuda(), cu.cuda(), max_seq_len=max(lens), softmax_scale=1.0,
+                             num_splits=num_splits, out_dtype=torch.float32)
+    torch.cuda.synchronize()
+    _mtp_check(mla, q, c, lens, out, f"mtp varlen s={num_splits}")
+    _no_device_error(mla)
