@@ -560,3 +560,34 @@ def test_mtp_varlen_short_and_split(mla, num_splits):
     torch.cuda.synchronize()
     _mtp_check(mla, q, c, lens, out, f"mtp varlen s={num_splits}")
     _no_device_error(mla)
+
+
+# ---------------------------------------------------------------------------
+# Weight absorption around the decode: the absorbed pipeline equals per-head
+# attention over up-projected keys and values (fp32 torch reference).
+
+
+def test_absorbed_pipeline_matches_unabsorbed_attention(mla):
+    from ada_mla import absorbed
+
+    torch.manual_seed(81)
+    b, nh, n, dn, dv = 4, 16, 300, 128, 128
+    scale = 1.0 / np.sqrt(dn + 64)
+    c = torch.randn(b, n, 576) * 0.5
+    q_nope = torch.randn(b, nh, dn) * 0.5
+    q_rope = torch.randn(b, nh, 64) * 0.5
+    w_uk = torch.randn(nh, dn, 512) / np.sqrt(512)
+    w_uv = torch.randn(nh, 512, dv) / np.sqrt(512)
+    # reference: keys k_j,i = c_j,N W_UK_i^T, values v_j,i = c_j,N W_UV_i, rope part shared
+    k_nope = torch.einsum("bnc,hdc->bhnd", c[:, :, :512], w_uk)           # [b, h, n, d]
+    v = torch.einsum("bnc,hcv->bhnv", c[:, :, :512], w_uv)                # [b, h, n, dv]
+    logits = (torch.einsum("bhd,bhnd->bhn", q_nope, k_nope) +
+              torch.einsum("bhr,bnr->bhn", q_rope, c[:, :, 512:])) * scale
+    ref = torch.einsum("bhn,bhnv->bhv", torch.softmax(logits, dim=-1), v)
+    out = absorbed.mla_decode_absorbed(q_nope.half().cuda(), q_rope.half().cuda(), w_uk.half().cuda(),
+                                       c.half().cuda(), w_uv.half().cuda(), softmax_scale=scale)
+    torch.cuda.synchronize()
+    assert out.shape == (b, nh, dv)
+    # fp16 operands and an fp16 O* between the steps: relative error ~1e-3 of |ref| ~ 0.1-1
+    assert_close_parity(_np(out), ref.numpy(), max_tol=2e-2, mean_tol=2e-3, what="absorbed pipeline")
+    _no_device_error(mla)
