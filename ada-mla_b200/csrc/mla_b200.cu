@@ -473,9 +473,10 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
             tp.scale_log2 = scale * kLog2e;
             tp.part_o = L.part_o;
             tp.part_lse = L.part_lse;
-            // fp16 partials for fp16 output; bf16 runs keep fp32 partials (bf16 data
-            // may exceed the fp16 range)
-            tp.part_kind = out_dtype == MLA_B200_OUT_F16 ? tc::kOutF16 : tc::kOutF32;
+            // 16-bit partials for 16-bit output (fp16, or bf16 for bf16: its data may
+            // exceed the fp16 range), fp32 partials for fp32 output
+            tp.part_kind = out_dtype == MLA_B200_OUT_F16 ? tc::kOutF16
+                           : out_dtype == MLA_B200_OUT_BF16 ? tc::kOutBF16 : tc::kOutF32;
             tp.out = out;
             tp.out_kind = out_dtype == MLA_B200_OUT_F16 ? tc::kOutF16
                           : out_dtype == MLA_B200_OUT_BF16 ? tc::kOutBF16 : tc::kOutF32;
@@ -523,7 +524,8 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     const long long rows = (long long)batch * num_heads;
     const unsigned cgrid = (unsigned)rows;
     const int skip = tc_direct ? 1 : 0;
-    // The tcgen05 kernel keeps fp16 partials for fp16 output; the SIMT kernel's are fp32.
+    // The tcgen05 kernel keeps 16-bit partials for 16-bit output (fp16 or bf16); the
+    // SIMT kernel's are fp32.
     // Batches merge row-parallel (a warp per row, few splits each); a few long
     // sequences merge split-parallel (a block per row, many splits).
     if (batch >= 8) {
@@ -532,8 +534,9 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
         const float *po = L.part_o;
         const __half *ph = reinterpret_cast<const __half *>(L.part_o);
         if (out_dtype == MLA_B200_OUT_BF16)
-            launch_dependent(combine_rows_kernel<__nv_bfloat16, float>, rgrid, rblock, 0, stream, false, po,
-                             L.part_lse, wl, num_heads, static_cast<__nv_bfloat16 *>(out), out_lse, skip);
+            launch_dependent(combine_rows_kernel<__nv_bfloat16, __nv_bfloat16>, rgrid, rblock, 0, stream, false,
+                             reinterpret_cast<const __nv_bfloat16 *>(L.part_o), L.part_lse, wl, num_heads,
+                             static_cast<__nv_bfloat16 *>(out), out_lse, skip);
         else if (out_dtype == MLA_B200_OUT_F16 && tc_direct)
             launch_dependent(combine_rows_kernel<__half, __half>, rgrid, rblock, 0, stream, false, ph, L.part_lse,
                              wl, num_heads, static_cast<__half *>(out), out_lse, skip);
@@ -549,8 +552,9 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     const __half *ph = reinterpret_cast<const __half *>(L.part_o);
     const dim3 cblock(kCombineThreads);
     if (out_dtype == MLA_B200_OUT_BF16)
-        launch_dependent(combine_kernel<__nv_bfloat16, float>, dim3(cgrid), cblock, 0, stream, false, po,
-                         L.part_lse, wl, num_heads, rows, static_cast<__nv_bfloat16 *>(out), out_lse, skip);
+        launch_dependent(combine_kernel<__nv_bfloat16, __nv_bfloat16>, dim3(cgrid), cblock, 0, stream, false,
+                         reinterpret_cast<const __nv_bfloat16 *>(L.part_o), L.part_lse, wl, num_heads, rows,
+                         static_cast<__nv_bfloat16 *>(out), out_lse, skip);
     else if (out_dtype == MLA_B200_OUT_F16 && tc_direct)
         launch_dependent(combine_kernel<__half, __half>, dim3(cgrid), cblock, 0, stream, false, ph, L.part_lse,
                          wl, num_heads, rows, static_cast<__half *>(out), out_lse, skip);

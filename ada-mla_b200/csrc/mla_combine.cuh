@@ -49,6 +49,23 @@ __device__ __forceinline__ void unpack16(const uint4 u, float (&v)[8]) {
     }
 }
 
+// The same for bf16 partials, and the choice by partial type.
+__device__ __forceinline__ void unpack16_bf16(const uint4 u, float (&v)[8]) {
+    const uint32_t w[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+    for (int j = 0; j < 4; ++j) {
+        const float2 f = __bfloat1622float2(*reinterpret_cast<const __nv_bfloat162 *>(&w[j]));
+        v[2 * j] = f.x;
+        v[2 * j + 1] = f.y;
+    }
+}
+
+template <typename PartT, int N>
+__device__ __forceinline__ void unpack_part(const uint4 u, float (&v)[N]) {
+    if constexpr (std::is_same<PartT, __nv_bfloat16>::value) unpack16_bf16(u, v);
+    else unpack16(u, v);
+}
+
 // rows = batch * num_heads; one block per row r = (b, h).  Partial i of row
 // (b, h) lives at part_o[(i * num_heads + h) * 512] and part_lse[i * num_heads
 // + h], for i in item_range(b).  Normalized partials: O_i = sum_j p_j C_j / l_i
@@ -115,7 +132,7 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(
                 for (int j = 0; j < 8; ++j) {
                     if (k + j * kGroups < n) {
                         float v[kVec];
-                        unpack16(u[j], v);
+                        unpack_part<PartT>(u[j], v);
                         const float w = w_s[k + j * kGroups];
 #pragma unroll
                         for (int e = 0; e < kVec; ++e) acc[e] = fmaf(w, v[e], acc[e]);
@@ -209,7 +226,7 @@ __global__ void __launch_bounds__(32 * kRowsPerCombineBlock) combine_rows_kernel
 #pragma unroll
                         for (int q = 0; q < kU; ++q) {
                             float v[16 / kU];
-                            unpack16(u[k][q], v);
+                            unpack_part<PartT>(u[k][q], v);
 #pragma unroll
                             for (int e = 0; e < 16 / kU; ++e) acc[q * (16 / kU) + e] = fmaf(wk, v[e], acc[q * (16 / kU) + e]);
                         }

@@ -159,7 +159,7 @@ struct TcParams {
     float scale_log2;  // softmax scale * log2(e)
     void *part_o;      // [max_items, num_heads, 512], element type part_kind
     float *part_lse;   // [max_items, num_heads]
-    int part_kind;     // partial element type: kOutF32 / kOutF16
+    int part_kind;     // partial element type: kOutF32 / kOutF16 / kOutBF16
     union {
         int page_size;     // paged: a multiple of kTO
         float o_scale;     // fp8 cache: factor of the finished O (kv scale / kP8Scale)

@@ -235,8 +235,9 @@ def test_balanced_schedule_dense(mla, b, n):
 
 # bf16 inputs: O* is checked at the north-star bar with fp32 output (P enters the
 # second GEMM as bf16, a 2^-9 relative rounding against fp16's 2^-11).  bf16
-# output adds its own rounding of up to half a bf16 ulp, 2^-9 * |O*|, so that
-# check is elementwise |got - ref| <= 1e-2 + 2^-8 * |ref| with mean-abs <= 2e-3.
+# output adds the rounding of the bf16 split partials and of the output, each up
+# to half a bf16 ulp (2^-9 * |O*|), so that check is elementwise
+# |got - ref| <= 1e-2 + 2^-8 * |ref| with mean-abs <= 2e-3.
 def _assert_bf16_out(got, ref, what):
     g = np.asarray(got, dtype=np.float64)
     r = np.asarray(ref, dtype=np.float64)
