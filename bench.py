@@ -27,6 +27,9 @@ token), so compare us/step with the fp16 line.
 (mla_b200_decode_mtp_f16, K x n_h <= 128): the same bytes per step for K times
 the tokens (config keys `draft_tokens`, `tokens_per_step`).
 
+`--dtype bf16` runs the step on bf16 copies of Q* and the cache
+(mla_b200_decode_batched_bf16, bf16 output); same bytes per token.
+
 `--impl reference` times the reference's own FP32 CPU kernel
 (run_mla_decode_cpu, compiled from the reference sources into oracle/_ref, or
 our C restatement when that build is absent) on all host cores, rank 0 only.
@@ -295,6 +298,14 @@ def run_ours(args):
         out = torch.empty((b, args.mtp, nh, 512), dtype=torch.float16, device=dev)
     if fp8 and paged:
         raise SystemExit("--kv-dtype fp8 and --page-size do not combine")
+    bf16 = args.dtype == "bf16"
+    if bf16 and (paged or fp8 or mtp):
+        raise SystemExit("--dtype bf16 combines with none of --page-size, --kv-dtype fp8, --mtp")
+    if bf16:
+        qs = [x.bfloat16() for x in qs]
+        cs = [x.bfloat16() for x in cs]
+        cache_2d = [c.view(-1, HEAD_DIM_K) for c in cs]
+        out = torch.empty((b, nh, 512), dtype=torch.bfloat16, device=dev)
     cache_bytes = wl.cache_bytes // (2 if fp8 else 1)  # algorithmic bytes one step reads
     if fp8:
         cs8 = []
@@ -322,6 +333,11 @@ def run_ours(args):
                 qs[i % ring].data_ptr(), cs8[i % ring].data_ptr(), 1.0,
                 None if cu is None else cu.data_ptr(), b, nh, total, maxlen, 1.0, args.splits,
                 out.data_ptr(), capi.OUT_F16, None, ws.data_ptr(), ws_bytes, stream)
+        elif bf16:
+            st = lib.mla_b200_decode_batched_bf16(
+                qs[i % ring].data_ptr(), cache_2d[i % ring].data_ptr(),
+                None if cu is None else cu.data_ptr(), b, nh, total, maxlen, 1.0, args.splits,
+                out.data_ptr(), capi.OUT_BF16, None, ws.data_ptr(), ws_bytes, stream)
         elif paged:
             st = lib.mla_b200_decode_paged_f16(
                 qs[i % ring].data_ptr(), pools[i % ring].data_ptr(), pl.block_table.data_ptr(),
@@ -393,11 +409,12 @@ def run_ours(args):
     # end-to-end through the public API: pinned host inputs -> device, decode,
     # result -> host, every step
     # (paged: the pool, block table and lengths all cross from the host)
-    src = pools[0] if paged else (cs8[0].view(wl.cache.shape) if fp8 else wl.cache)
-    qh = [(qs[0] if mtp else wl.query).cpu().pin_memory() for _ in range(2)]
+    src = pools[0] if paged else (cs8[0].view(wl.cache.shape) if fp8 else
+                                  (cs[0] if bf16 else wl.cache))
+    qh = [(qs[0] if mtp or bf16 else wl.query).cpu().pin_memory() for _ in range(2)]
     ch = [src.cpu().pin_memory() for _ in range(2)]
     qd, cd = torch.empty_like(qh[0], device=dev), torch.empty_like(src)
-    oh = torch.empty(tuple(out.shape), dtype=torch.float16).pin_memory()
+    oh = torch.empty(tuple(out.shape), dtype=out.dtype).pin_memory()
     if paged:
         bth, slh = pl.block_table.cpu().pin_memory(), pl.seq_lens.cpu().pin_memory()
         btd, sld = torch.empty_like(pl.block_table), torch.empty_like(pl.seq_lens)
@@ -448,7 +465,8 @@ def run_ours(args):
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms_step,
             "us_per_step": ms_step * 1e3, "higher_is_better": True, "scaling": "weak",
-            "vs_baseline": None, "dtype": "f16" + (" (e4m3 cache)" if fp8 else ""), "data": "synthetic",
+            "vs_baseline": None, "dtype": "bf16" if bf16 else "f16" + (" (e4m3 cache)" if fp8 else ""),
+            "data": "synthetic",
             "config": {"workload": f"cfg{args.config}: B={b} n_h={nh} N={maxlen} per rank "
                                    + (f"(paged cache: shuffled {args.page_size}-token pages, "
                                       f"{pl.num_pages} pages), " if paged else
@@ -578,6 +596,8 @@ def main():
     ap.add_argument("--config", type=int, default=1, choices=[1, 2, 3, 4])
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--splits", type=int, default=-1)
+    ap.add_argument("--dtype", default="fp16", choices=["fp16", "bf16"],
+                    help="bf16: decode bf16 copies of Q* and the cache")
     ap.add_argument("--mtp", type=int, default=1,
                     help="draft tokens per sequence decoded in one pass (multi-token decode)")
     ap.add_argument("--kv-dtype", default="fp16", choices=["fp16", "fp8"],
