@@ -35,6 +35,7 @@ SIGNATURES = {
     "mla_b200_version": (ctypes.c_char_p, []),
     "mla_b200_constant": (_c_int, [ctypes.c_char_p]),
     "mla_b200_set_kernel_timing": (_c_int, [_vp, _vp]),
+    "mla_b200_set_kernel_span": (_c_int, [_vp, _c_int]),
     "mla_b200_device_info": (_c_int, [ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
     "mla_b200_plan": (_c_int, [_c_int, _c_int, _c_ll, _c_int, _c_int,
                                ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
@@ -59,6 +60,7 @@ SIGNATURES = {
     "mla_b200_decode_fused_f32": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _vp, _c_size, _vp]),
     "mla_b200_decode_naive_f32": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _vp]),
     "mla_b200_combine_f32": (_c_int, [_vp, _vp, _c_int, _c_ll, _vp, _c_int, _vp, _vp]),
+    "mla_b200_combine_packed_f32": (_c_int, [_vp, _c_int, _c_ll, _c_ll, _vp, _c_int, _vp, _vp]),
     "mla_b200_get_device_error": (_c_int, [ctypes.POINTER(_c_int), _vp]),
     "mla_b200_last_cuda_error": (_c_int, []),
 }
@@ -116,6 +118,16 @@ def set_kernel_timing(start: "torch.cuda.Event | None", stop: "torch.cuda.Event 
     a = None if start is None else start.cuda_event
     b = None if stop is None else stop.cuda_event
     _check("mla_b200_set_kernel_timing", lib().mla_b200_set_kernel_timing(a, b))
+
+
+def set_kernel_span(span: "torch.Tensor | None") -> None:
+    """Record the device-side span of each later main decode-kernel launch of
+    this host thread into `span` (int64 CUDA tensor [slots, 2], each pair set
+    to (UINT64_MAX, 0) beforehand); None turns it off."""
+    if span is None:
+        _check("mla_b200_set_kernel_span", lib().mla_b200_set_kernel_span(None, 0))
+    else:
+        _check("mla_b200_set_kernel_span", lib().mla_b200_set_kernel_span(span.data_ptr(), span.shape[0]))
 
 
 def device_info():

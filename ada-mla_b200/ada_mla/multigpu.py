@@ -8,11 +8,11 @@ layer scales the same decode across the G GPUs of a node, one process per GPU:
   collective on the data path (``shard_sequences`` + ``decode_sharded``).  An
   optional all-gather returns the full batch of outputs to every rank.
 * **KV-length split** (batch < G): rank r owns cache rows
-  ``kv_split_bounds(N, G)[r]`` of every sequence, decodes them into a partial
-  ``(O normalized, LSE)`` in fp32, and one ``all_gather_into_tensor`` of
-  ``n_h x (512 + 1)`` floats per sequence gives every rank all G partials,
-  which the LSE-merge kernel (``mla_combine``) reduces to the exact result
-  (``KvSplitDecoder``).
+  ``kv_split_bounds(N, G)[r]`` of every sequence and decodes them straight
+  into a packed exchange buffer (O normalized, then LSE, fp32); one
+  ``all_gather_into_tensor`` of ``n_h x (512 + 1)`` floats per sequence gives
+  every rank all G partials, which the LSE-merge kernel reads in place and
+  reduces to the exact result (``KvSplitDecoder``).
 
 The per-rank decode and the merge are injectable so that the host logic
 (partitioning, packing, the collective, unpacking) can be exercised by CPU
@@ -72,22 +72,55 @@ def kv_split_bounds(n: int, world: int, align: int = KV_ALIGN) -> list[tuple[int
 # ---------------------------------------------------------------------------
 # defaults: the CUDA kernels
 # ---------------------------------------------------------------------------
-def _cuda_partial(query: torch.Tensor, cache: torch.Tensor, softmax_scale: float):
-    """(O [B, n_h, 512] fp32 normalized, LSE [B, n_h] fp32) of one KV slice."""
-    import ada_mla
+def packed_stride(rows: int) -> int:
+    """Floats per rank in the packed (O, LSE) exchange buffer: O [rows, 512]
+    then LSE [rows], padded to a multiple of 4 floats so that every rank's O
+    starts on a 16-byte boundary."""
+    return -(-rows * (HEAD_DIM_V + 1) // 4) * 4
+
+
+def _cuda_partial(query: torch.Tensor, cache: torch.Tensor, softmax_scale: float,
+                  o_out: torch.Tensor, lse_out: torch.Tensor, workspace: torch.Tensor) -> None:
+    """Decodes one dense KV slice into o_out [B, n_h, 512] fp32 (normalized) and
+    lse_out [B, n_h] fp32, in place (views into the exchange buffer)."""
+    from ada_mla import capi
 
     if not (query.is_cuda and cache.is_cuda):
         raise RuntimeError("the multi-GPU decode runs on CUDA tensors")
-    return ada_mla.mla_decode_batched(query, cache, softmax_scale=softmax_scale, return_lse=True,
-                                      out_dtype=torch.float32)
+    b, nh, n = query.shape[0], query.shape[1], cache.shape[1]
+    bf16 = query.dtype == torch.bfloat16
+    name = "mla_b200_decode_batched_bf16" if bf16 else "mla_b200_decode_batched_f16"
+    st = getattr(capi.lib(), name)(
+        query.data_ptr(), cache.data_ptr(), None, b, nh, b * n, n, float(softmax_scale), -1,
+        o_out.data_ptr(), capi.OUT_F32, lse_out.data_ptr(), workspace.data_ptr(),
+        workspace.numel(), torch.cuda.current_stream().cuda_stream)
+    if st != capi.OK:
+        raise capi.MlaError(name, st)
 
 
-def _cuda_merge(part_o: torch.Tensor, part_lse: torch.Tensor, out_dtype: torch.dtype):
-    import ada_mla
+def _cuda_workspace(query: torch.Tensor, cache: torch.Tensor) -> torch.Tensor:
+    from ada_mla import capi
 
-    if not part_o.is_cuda:
+    b, nh, n = query.shape[0], query.shape[1], cache.shape[1]
+    return torch.empty(max(256, capi.workspace_size(b, nh, b * n, n, -1)), dtype=torch.uint8,
+                       device=query.device)
+
+
+def _cuda_merge(packed: torch.Tensor, parts: int, rows: int, stride: int, out_dtype: torch.dtype):
+    """LSE merge straight from the gathered exchange buffer (mla_b200_combine_packed_f32)."""
+    from ada_mla import capi
+
+    if not packed.is_cuda:
         raise RuntimeError("the LSE merge runs on CUDA tensors")
-    out, lse = ada_mla.mla_combine(part_o, part_lse, out_fp32=out_dtype == torch.float32)
+    out = torch.empty((rows, HEAD_DIM_V), dtype=torch.float32 if out_dtype == torch.float32
+                      else torch.float16, device=packed.device)
+    lse = torch.empty((rows,), dtype=torch.float32, device=packed.device)
+    st = capi.lib().mla_b200_combine_packed_f32(
+        packed.data_ptr(), parts, rows, stride, out.data_ptr(),
+        capi.OUT_F32 if out_dtype == torch.float32 else capi.OUT_F16, lse.data_ptr(),
+        torch.cuda.current_stream().cuda_stream)
+    if st != capi.OK:
+        raise capi.MlaError("mla_b200_combine_packed_f32", st)
     return out, lse
 
 
@@ -95,29 +128,74 @@ def _cuda_merge(part_o: torch.Tensor, part_lse: torch.Tensor, out_dtype: torch.d
 class KvSplitDecoder:
     """KV-length-split decode across the ranks of ``group``.
 
-    ``local_decode(query, cache_slice, scale) -> (O fp32 [B, n_h, 512], LSE
-    fp32 [B, n_h])`` and ``merge(part_o [G, rows, 512], part_lse [G, rows],
-    out_dtype) -> (out [rows, 512], lse [rows])`` default to the CUDA kernels.
+    Each rank decodes its slice straight into its part of a packed exchange
+    buffer (O [rows, 512] fp32 then LSE [rows] fp32, rows = B x n_h), one
+    ``all_gather_into_tensor`` gives every rank all G parts, and the merge reads
+    the gathered buffer in place: no concatenation or unpacking copies.
+
+    ``local_decode(query, cache_slice, scale, o_out, lse_out, workspace)``
+    writes in place; ``merge(packed [G * stride], G, rows, stride, out_dtype) ->
+    (out [rows, 512], lse [rows])``.  Both default to the CUDA kernels and are
+    injectable (the CPU tests run the host logic on gloo ranks).
     """
 
     group: dist.ProcessGroup | None = None
     local_decode: Callable | None = None
     merge: Callable | None = None
+    make_workspace: Callable | None = None
 
     def __post_init__(self):
         self.local_decode = self.local_decode or _cuda_partial
         self.merge = self.merge or _cuda_merge
+        self.make_workspace = self.make_workspace or _cuda_workspace
+        self._bufs: dict = {}
 
     @property
     def world(self) -> int:
-        return dist.get_world_size(self.group)
+        return dist.get_world_size(self.group) if dist.is_initialized() else 1
 
     @property
     def rank(self) -> int:
-        return dist.get_rank(self.group)
+        return dist.get_rank(self.group) if dist.is_initialized() else 0
 
     def bounds(self, n: int) -> tuple[int, int]:
         return kv_split_bounds(n, self.world)[self.rank]
+
+    def _gather(self, recv: torch.Tensor, send: torch.Tensor) -> None:
+        if self.world > 1:
+            dist.all_gather_into_tensor(recv, send, group=self.group)
+        else:  # a single rank: its own part is the whole exchange
+            recv.copy_(send)
+
+    def _barrier(self) -> None:
+        if self.world > 1:
+            dist.barrier(group=self.group)
+
+    def _buffers(self, query: torch.Tensor, cache_slice: torch.Tensor):
+        """Exchange buffers and the decode workspace, allocated once per shape
+        (so the step can be captured in a CUDA graph)."""
+        b, nh = query.shape[0], query.shape[1]
+        key = (b, nh, cache_slice.shape[1], query.dtype, query.device)
+        if key not in self._bufs:
+            stride = packed_stride(b * nh)
+            send = torch.empty(stride, dtype=torch.float32, device=query.device)
+            recv = torch.empty(self.world * stride, dtype=torch.float32, device=query.device)
+            ws = self.make_workspace(query, cache_slice) if cache_slice.shape[1] > 0 else None
+            self._bufs[key] = (stride, send, recv, ws)
+        return self._bufs[key]
+
+    def _local(self, query, cache_slice, softmax_scale):
+        b, nh = query.shape[0], query.shape[1]
+        rows = b * nh
+        stride, send, recv, ws = self._buffers(query, cache_slice)
+        o = send[:rows * HEAD_DIM_V].view(b, nh, HEAD_DIM_V)
+        lse = send[rows * HEAD_DIM_V:rows * (HEAD_DIM_V + 1)].view(b, nh)
+        if cache_slice.shape[1] > 0:
+            self.local_decode(query, cache_slice, softmax_scale, o, lse, ws)
+        else:  # an empty slice contributes nothing to the merge
+            o.zero_()
+            lse.fill_(float("-inf"))
+        return stride, send, recv
 
     def __call__(self, query: torch.Tensor, cache_slice: torch.Tensor, softmax_scale: float,
                  out_dtype: torch.dtype = torch.float16, return_lse: bool = False):
@@ -125,22 +203,37 @@ class KvSplitDecoder:
         [B, N_r, 576] = this rank's rows of a dense cache (N_r may be 0).
         Returns O* [B, n_h, 512] on every rank."""
         b, nh = query.shape[0], query.shape[1]
-        rows = b * nh
-        if cache_slice.shape[1] > 0:
-            o, lse = self.local_decode(query, cache_slice, softmax_scale)
-        else:  # an empty slice contributes nothing to the merge
-            o = torch.zeros((b, nh, HEAD_DIM_V), dtype=torch.float32, device=query.device)
-            lse = torch.full((b, nh), float("-inf"), dtype=torch.float32, device=query.device)
-        packed = torch.cat([o.reshape(rows, HEAD_DIM_V).float(), lse.reshape(rows, 1).float()], dim=1)
-        gathered = torch.empty((self.world * rows, HEAD_DIM_V + 1), dtype=packed.dtype,
-                               device=packed.device)
-        dist.all_gather_into_tensor(gathered, packed.contiguous(), group=self.group)
-        gathered = gathered.view(self.world, rows, HEAD_DIM_V + 1)
-        part_o = gathered[:, :, :HEAD_DIM_V].contiguous()
-        part_lse = gathered[:, :, HEAD_DIM_V].contiguous()
-        out, out_lse = self.merge(part_o, part_lse, out_dtype)
+        stride, send, recv = self._local(query, cache_slice, softmax_scale)
+        self._gather(recv, send)
+        out, out_lse = self.merge(recv, self.world, b * nh, stride, out_dtype)
         out = out.reshape(b, nh, HEAD_DIM_V)
         return (out, out_lse.reshape(b, nh)) if return_lse else out
+
+    def stage_times_us(self, query: torch.Tensor, cache_slice: torch.Tensor, softmax_scale: float,
+                       reps: int = 20) -> dict:
+        """Device time of each stage (local decode, all-gather, merge), each run
+        `reps` times back to back between CUDA events on this rank's stream.
+        Every rank must call it (the all-gather stage is collective)."""
+        b, nh = query.shape[0], query.shape[1]
+        stride, send, recv = self._local(query, cache_slice, softmax_scale)
+        times = {}
+        stages = {
+            "local_decode": lambda: self._local(query, cache_slice, softmax_scale),
+            "all_gather": lambda: self._gather(recv, send),
+            "merge": lambda: self.merge(recv, self.world, b * nh, stride, torch.float16),
+        }
+        for name, fn in stages.items():
+            fn()
+            torch.cuda.synchronize()
+            self._barrier()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            for _ in range(reps):
+                fn()
+            e1.record()
+            torch.cuda.synchronize()
+            times[name] = e0.elapsed_time(e1) * 1e3 / reps
+        return times
 
 
 def decode_sharded(query_local: torch.Tensor, cache_local: torch.Tensor,

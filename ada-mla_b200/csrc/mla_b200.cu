@@ -208,29 +208,30 @@ inline long long cdiv(long long a, long long b) { return (a + b - 1) / b; }
 
 // Split plan: rows per work item.  `units` is the number of workers one wave
 // of the decode kernel has; the chunk is an even share of the batch's tiles
-// plus the fixed per-item cost (the balanced schedule's quota, mla_common.cuh),
-// but never longer than a sequence.
-int plan_chunk(int batch, long long total_tokens, int max_seq_len, int num_sms) {
+// plus the fixed per-item cost, which grows with the head count (the balanced
+// schedule's quota, mla_common.cuh), but never longer than a sequence.
+int plan_chunk(int batch, long long total_tokens, int max_seq_len, int num_sms, int num_heads) {
     const long long units = num_sms > 1 ? num_sms / 2 : 1;  // 2-CTA clusters per wave
-    const long long cost = cdiv(total_tokens > 0 ? total_tokens : 1, kTile) + (long long)kItemCost * (batch > 0 ? batch : 1);
+    const long long cost = cdiv(total_tokens > 0 ? total_tokens : 1, kTile) +
+                           (long long)item_cost_for(num_heads) * (batch > 0 ? batch : 1);
     long long chunk = cdiv(cost, units) * kTile;
     if (chunk < kTile) chunk = kTile;
     if (max_seq_len > 0) {
         const long long cap = cdiv(max_seq_len, kTile) * kTile;
         if (chunk > cap) chunk = cap;
     }
-    (void)batch;
     if (chunk > (1 << 30)) chunk = 1 << 30;
     return (int)chunk;
 }
 
-int chunk_for(int batch, long long total_tokens, int max_seq_len, int num_splits, int num_sms) {
+int chunk_for(int batch, long long total_tokens, int max_seq_len, int num_splits, int num_sms,
+              int num_heads) {
     if (num_splits > 0) {
         const long long n = max_seq_len > 0 ? max_seq_len : 1;
         long long c = cdiv(n, num_splits);
         return (int)(c < 1 ? 1 : c);
     }
-    return plan_chunk(batch, total_tokens, max_seq_len, num_sms);
+    return plan_chunk(batch, total_tokens, max_seq_len, num_sms, num_heads);
 }
 
 long long max_items_for(int batch, long long total_tokens, int chunk) {
@@ -279,6 +280,15 @@ WsLayout ws_layout(void *base, long long max_items, int num_heads, int batch, bo
 
 thread_local cudaEvent_t t_ev_start = nullptr;  // mla_b200_set_kernel_timing
 thread_local cudaEvent_t t_ev_stop = nullptr;
+thread_local unsigned long long *t_span = nullptr;  // mla_b200_set_kernel_span
+thread_local int t_span_slots = 0, t_span_next = 0;
+
+unsigned long long *next_span() {
+    if (t_span == nullptr || t_span_slots <= 0) return nullptr;
+    unsigned long long *p = t_span + 2 * (t_span_next % t_span_slots);
+    t_span_next = (t_span_next + 1) % t_span_slots;
+    return p;
+}
 
 // Inside stream capture a plain record only orders the capture; the external
 // flag makes it a real event-record node of the graph, timed at replay.
@@ -345,11 +355,14 @@ void launch_dependent(void (*kernel)(Params...), dim3 grid, dim3 block, size_t s
     cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);  // errors: launch_status()
 }
 
+struct TcMaps {
+    CUtensorMap cmap_s, cmap_o, qmap;
+};
+
 template <int kSched, bool kBf16, bool kPaged, bool kFp8 = false, bool kMtp = false>
-void launch_tc(int clusters, const CUtensorMap &cs, const CUtensorMap &co, const CUtensorMap &qm,
-               const tc::TcParams &tp, cudaStream_t stream, bool after_plan) {
+void launch_tc(int clusters, const TcMaps &m, const tc::TcParams &tp, cudaStream_t stream, bool after_plan) {
     launch_dependent(tc::tc_decode_kernel<kSched, kBf16, kPaged, kFp8, kMtp>, dim3(2 * clusters),
-                     dim3(tc::kThreads), tc::kSmemBytes, stream, after_plan, cs, co, qm, tp);
+                     dim3(tc::kThreads), tc::kSmemBytes, stream, after_plan, m.cmap_s, m.cmap_o, m.qmap, tp);
 }
 
 // Shared driver of the split-KV paths: plan -> partial kernel -> combine.
@@ -379,7 +392,7 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     if (mtp != nullptr && (!tc_path || pg != nullptr || f8 != nullptr)) return MLA_B200_ERR_UNSUPPORTED;
     // (A single sequence splits evenly in the chunked schedule already.)
     const bool balanced = tc_path && num_splits <= 0 && batch > 1;
-    int chunk = chunk_for(batch, total_tokens, max_seq_len, num_splits, info.sms);
+    int chunk = chunk_for(batch, total_tokens, max_seq_len, num_splits, info.sms, num_heads);
     // paged: items start on 96-token boundaries so every 32-row box sits in one page
     if (pg != nullptr) chunk = (int)std::min<long long>(cdiv(chunk, kTile) * kTile, 1 << 30);
     const long long max_items = balanced ? (long long)batch + info.tc_clusters
@@ -387,6 +400,7 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     if (max_items > (1LL << 30)) return MLA_B200_ERR_UNSUPPORTED;
     WsLayout L = ws_layout(workspace, max_items, num_heads, batch, f8 != nullptr);
     if (workspace == nullptr || workspace_bytes < L.bytes) return MLA_B200_ERR_WORKSPACE;
+    if (!aligned(workspace, 16)) return MLA_B200_ERR_INVALID_ARG;
     const int32_t *seq_lens = nullptr;
     if (pg != nullptr) {
         seq_lens = pg->seq_lens;
@@ -396,6 +410,7 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     WorkList wl = {};
     wl.batch = batch;
     wl.chunk = balanced ? 0 : chunk;
+    wl.item_cost = item_cost_for(num_heads);
     int bal_clusters = 0;      // balanced: clusters to launch
     bool bal_split = true;     // balanced: some sequence has more than one item
     if (balanced) {
@@ -403,7 +418,7 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
         if (cu_seqlens == nullptr) {
             wl.seq_len = max_seq_len;
             const long long tiles = cdiv(max_seq_len, kTile);
-            const long long cost = tiles > 0 ? tiles + kItemCost : 0;
+            const long long cost = tiles > 0 ? tiles + wl.item_cost : 0;
             const long long total = (long long)batch * cost;
             if (total >= (1LL << 31)) return MLA_B200_ERR_UNSUPPORTED;
             const long long q = std::max(1LL, cdiv(total, info.tc_clusters));
@@ -411,7 +426,7 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
             bal_clusters = total > 0 ? (int)cdiv(total, q) : 0;
             bal_split = total == 0;  // empty sequences get their zeros from the combine
             for (long long b = 0; b < batch && tiles > 0; ++b) {
-                const long long base = b * cost + kItemCost;
+                const long long base = b * cost + wl.item_cost;
                 if (base / q != (base + tiles - 1) / q) {
                     bal_split = true;
                     break;
@@ -422,7 +437,7 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
             wl.cu_seqlens = cu_seqlens;
             wl.nworkers = info.tc_clusters;
             bal_clusters = info.tc_clusters;
-            plan_balanced_kernel<<<1, 1024, 0, stream>>>(cu_seqlens, batch, L.item_off, seq_lens,
+            plan_balanced_kernel<<<1, 1024, 0, stream>>>(cu_seqlens, batch, wl.item_cost, L.item_off, seq_lens,
                                                          max_seq_len, L.cu_virtual);
         }
     } else if (cu_seqlens == nullptr) {
@@ -444,7 +459,8 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     bool tc_direct = false;  // the tcgen05 kernel wrote single-item sequences itself
     if (wl.max_items > 0 && (!balanced || bal_clusters > 0)) {
         if (tc_path) {
-            CUtensorMap cmap_s, cmap_o, qmap;
+            TcMaps maps;
+            CUtensorMap &cmap_s = maps.cmap_s, &cmap_o = maps.cmap_o, &qmap = maps.qmap;
             // S-CTA: one box per ring slot (3 K-blocks x 96 rows); paged, one per
             // 32-row piece and slot.  O-CTA: one box per 32-row C tile (8 K-blocks).
             const long long map_rows = pg != nullptr ? pg->pool_rows : total_tokens;
@@ -492,23 +508,24 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
                 tp.block_table = pg != nullptr ? pg->block_table : nullptr;
                 tp.page_size = pg != nullptr ? pg->page_size : 0;
             }
+            tp.span = next_span();
             tc_direct = true;
             const int clusters = balanced ? bal_clusters : std::min(info.tc_clusters, wl.max_items);
             timing_mark(t_ev_start, stream);
             if (mtp != nullptr) {
-                if (balanced) launch_tc<kSchedBalanced, kBf16, false, false, true>(clusters, cmap_s, cmap_o, qmap, tp, stream, cu_seqlens != nullptr);
-                else launch_tc<kSchedChunked, kBf16, false, false, true>(clusters, cmap_s, cmap_o, qmap, tp, stream, cu_seqlens != nullptr);
+                if (balanced) launch_tc<kSchedBalanced, kBf16, false, false, true>(clusters, maps, tp, stream, cu_seqlens != nullptr);
+                else launch_tc<kSchedChunked, kBf16, false, false, true>(clusters, maps, tp, stream, cu_seqlens != nullptr);
             } else if (f8 != nullptr) {
                 if constexpr (!kBf16) {  // (fp8 runs with fp16 Q*; the prep kernel precedes)
-                    if (balanced) launch_tc<kSchedBalanced, false, false, true>(clusters, cmap_s, cmap_o, qmap, tp, stream, true);
-                    else launch_tc<kSchedChunked, false, false, true>(clusters, cmap_s, cmap_o, qmap, tp, stream, true);
+                    if (balanced) launch_tc<kSchedBalanced, false, false, true>(clusters, maps, tp, stream, true);
+                    else launch_tc<kSchedChunked, false, false, true>(clusters, maps, tp, stream, true);
                 }
             } else if (pg != nullptr) {
-                if (balanced) launch_tc<kSchedBalanced, kBf16, true>(clusters, cmap_s, cmap_o, qmap, tp, stream, cu_seqlens != nullptr);
-                else launch_tc<kSchedChunked, kBf16, true>(clusters, cmap_s, cmap_o, qmap, tp, stream, cu_seqlens != nullptr);
+                if (balanced) launch_tc<kSchedBalanced, kBf16, true>(clusters, maps, tp, stream, cu_seqlens != nullptr);
+                else launch_tc<kSchedChunked, kBf16, true>(clusters, maps, tp, stream, cu_seqlens != nullptr);
             } else {
-                if (balanced) launch_tc<kSchedBalanced, kBf16, false>(clusters, cmap_s, cmap_o, qmap, tp, stream, cu_seqlens != nullptr);
-                else launch_tc<kSchedChunked, kBf16, false>(clusters, cmap_s, cmap_o, qmap, tp, stream, cu_seqlens != nullptr);
+                if (balanced) launch_tc<kSchedBalanced, kBf16, false>(clusters, maps, tp, stream, cu_seqlens != nullptr);
+                else launch_tc<kSchedChunked, kBf16, false>(clusters, maps, tp, stream, cu_seqlens != nullptr);
             }
             timing_mark(t_ev_stop, stream);
         } else if constexpr (!kBf16) {
@@ -551,19 +568,20 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     const float *po = L.part_o;
     const __half *ph = reinterpret_cast<const __half *>(L.part_o);
     const dim3 cblock(kCombineThreads);
+    const size_t ps = (size_t)num_heads * kDV, ls = (size_t)num_heads;
     if (out_dtype == MLA_B200_OUT_BF16)
         launch_dependent(combine_kernel<__nv_bfloat16, __nv_bfloat16>, dim3(cgrid), cblock, 0, stream, false,
                          reinterpret_cast<const __nv_bfloat16 *>(L.part_o), L.part_lse, wl, num_heads, rows,
-                         static_cast<__nv_bfloat16 *>(out), out_lse, skip);
+                         static_cast<__nv_bfloat16 *>(out), out_lse, skip, ps, ls);
     else if (out_dtype == MLA_B200_OUT_F16 && tc_direct)
         launch_dependent(combine_kernel<__half, __half>, dim3(cgrid), cblock, 0, stream, false, ph, L.part_lse,
-                         wl, num_heads, rows, static_cast<__half *>(out), out_lse, skip);
+                         wl, num_heads, rows, static_cast<__half *>(out), out_lse, skip, ps, ls);
     else if (out_dtype == MLA_B200_OUT_F16)
         launch_dependent(combine_kernel<__half, float>, dim3(cgrid), cblock, 0, stream, false, po, L.part_lse,
-                         wl, num_heads, rows, static_cast<__half *>(out), out_lse, skip);
+                         wl, num_heads, rows, static_cast<__half *>(out), out_lse, skip, ps, ls);
     else
         launch_dependent(combine_kernel<float, float>, dim3(cgrid), cblock, 0, stream, false, po, L.part_lse,
-                         wl, num_heads, rows, static_cast<float *>(out), out_lse, skip);
+                         wl, num_heads, rows, static_cast<float *>(out), out_lse, skip, ps, ls);
     return launch_status();
 }
 
@@ -678,6 +696,13 @@ int mla_b200_set_kernel_timing(void *ev_start, void *ev_stop) {
     return MLA_B200_OK;
 }
 
+int mla_b200_set_kernel_span(unsigned long long *span, int slots) {
+    t_span = slots > 0 ? span : nullptr;
+    t_span_slots = span != nullptr && slots > 0 ? slots : 0;
+    t_span_next = 0;
+    return MLA_B200_OK;
+}
+
 int mla_b200_device_info(int *num_sms, int *decode_clusters) {
     int dev;
     DevInfo info;
@@ -700,7 +725,7 @@ int mla_b200_plan(int batch, int num_heads, long long total_tokens, int max_seq_
             num_sms = 148;
         }
     }
-    const int chunk = plan_chunk(batch, total_tokens, max_seq_len, num_sms);
+    const int chunk = plan_chunk(batch, total_tokens, max_seq_len, num_sms, num_heads);
     if (chunk_tokens) *chunk_tokens = chunk;
     if (num_splits) *num_splits = max_seq_len > 0 ? (int)cdiv(max_seq_len, chunk) : 0;
     return MLA_B200_OK;
@@ -717,7 +742,7 @@ size_t workspace_bytes_for(int batch, int num_heads, long long total_tokens, int
         num_sms = 148;
     }
     if (max_seq_len <= 0 && batch > 0) max_seq_len = (int)cdiv(total_tokens, batch);
-    const int chunk = chunk_for(batch, total_tokens, max_seq_len, num_splits, num_sms);
+    const int chunk = chunk_for(batch, total_tokens, max_seq_len, num_splits, num_sms, num_heads);
     long long max_items = max_items_for(batch, total_tokens, chunk);
     // an automatic split may run the balanced schedule: batch + one item per cluster
     if (num_splits <= 0) max_items = std::max(max_items, (long long)batch + std::max(1, num_sms / 2));
@@ -923,7 +948,7 @@ int mla_b200_combine_f32(const float *part_o, const float *part_lse, int num_par
     DevInfo info;
     int st = current_device(&dev, &info);
     if (st != MLA_B200_OK) return st;
-    WorkList wl;
+    WorkList wl = {};
     wl.items = nullptr;
     wl.item_off = nullptr;
     wl.batch = 1;
@@ -933,12 +958,47 @@ int mla_b200_combine_f32(const float *part_o, const float *part_lse, int num_par
     wl.max_items = num_parts;
     const unsigned cgrid = (unsigned)rows;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const size_t ps = (size_t)rows * kDV, ls = (size_t)rows;
     if (out_dtype == MLA_B200_OUT_F16)
         combine_kernel<__half, float><<<cgrid, kCombineThreads, 0, s>>>(
-            part_o, part_lse, wl, (int)rows, rows, static_cast<__half *>(out), out_lse, 0);
+            part_o, part_lse, wl, (int)rows, rows, static_cast<__half *>(out), out_lse, 0, ps, ls);
     else
         combine_kernel<float, float><<<cgrid, kCombineThreads, 0, s>>>(
-            part_o, part_lse, wl, (int)rows, rows, static_cast<float *>(out), out_lse, 0);
+            part_o, part_lse, wl, (int)rows, rows, static_cast<float *>(out), out_lse, 0, ps, ls);
+    return launch_status();
+}
+
+int mla_b200_combine_packed_f32(const float *parts, int num_parts, long long rows,
+                                long long part_stride, void *out, int out_dtype, float *out_lse,
+                                void *stream) {
+    if (num_parts < 0 || rows < 0 || rows >= (1LL << 31)) return MLA_B200_ERR_INVALID_ARG;
+    if (rows == 0) return MLA_B200_OK;
+    if (out == nullptr || (num_parts > 0 && parts == nullptr)) return MLA_B200_ERR_INVALID_ARG;
+    if (part_stride < rows * (kDV + 1) || part_stride % 4 != 0) return MLA_B200_ERR_INVALID_ARG;
+    if (out_dtype != MLA_B200_OUT_F16 && out_dtype != MLA_B200_OUT_F32)
+        return MLA_B200_ERR_INVALID_ARG;
+    if (!aligned(parts, 16) || !aligned(out, 16)) return MLA_B200_ERR_INVALID_ARG;
+    int dev;
+    DevInfo info;
+    int st = current_device(&dev, &info);
+    if (st != MLA_B200_OK) return st;
+    WorkList wl = {};
+    wl.batch = 1;
+    wl.seq_len = num_parts;  // one "row" per part: item_range(0) = [0, num_parts)
+    wl.chunk = 1;
+    wl.cps = num_parts;
+    wl.max_items = num_parts;
+    const unsigned cgrid = (unsigned)rows;
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const float *lse0 = parts + (size_t)rows * kDV;
+    if (out_dtype == MLA_B200_OUT_F16)
+        combine_kernel<__half, float><<<cgrid, kCombineThreads, 0, s>>>(
+            parts, lse0, wl, (int)rows, rows, static_cast<__half *>(out), out_lse, 0,
+            (size_t)part_stride, (size_t)part_stride);
+    else
+        combine_kernel<float, float><<<cgrid, kCombineThreads, 0, s>>>(
+            parts, lse0, wl, (int)rows, rows, static_cast<float *>(out), out_lse, 0,
+            (size_t)part_stride, (size_t)part_stride);
     return launch_status();
 }
 
@@ -980,25 +1040,29 @@ int mla_b200_decode_split_f16_noalloc(const void *query, const void *cache, void
     if (!aligned(query, 16) || !aligned(cache, 16) || !aligned(out, 16))
         return MLA_B200_ERR_INVALID_ARG;
     const size_t cap = MLA_B200_NOALLOC_SCRATCH_BYTES;
-    int splits = num_splits;
-    if (splits > 0) {
-        if (mla_b200_workspace_size(1, num_heads, seq_length, seq_length, splits) > cap)
-            return MLA_B200_ERR_WORKSPACE;
-    } else {
-        int chunk = 0;
-        int st = mla_b200_plan(1, num_heads, seq_length, seq_length, 0, &chunk, &splits);
-        if (st != MLA_B200_OK) return st;
-        if (splits < 1) splits = 1;
-        while (splits > 1 &&
-               mla_b200_workspace_size(1, num_heads, seq_length, seq_length, splits) > cap)
-            --splits;
-        if (mla_b200_workspace_size(1, num_heads, seq_length, seq_length, splits) > cap)
-            return MLA_B200_ERR_WORKSPACE;
-    }
+    // Scratch bytes of an explicit split count (pure workspace arithmetic).
+    auto bytes_for = [&](int splits) -> size_t {
+        const int chunk = chunk_for(1, seq_length, seq_length, splits, 0, num_heads);
+        return ws_layout(nullptr, max_items_for(1, seq_length, chunk), num_heads, 1).bytes;
+    };
     int dev;
     DevInfo info;
     int st = current_device(&dev, &info);
     if (st != MLA_B200_OK) return st;
+    int splits = num_splits;
+    if (splits > 0) {
+        if (bytes_for(splits) > cap) return MLA_B200_ERR_WORKSPACE;
+    } else {
+        // the planned split, clamped to the most items whose partials fit:
+        // per item num_heads x 512 fp32 (+ its LSE and work-list entry)
+        const int chunk = plan_chunk(1, seq_length, seq_length, info.sms, num_heads);
+        splits = seq_length > 0 ? (int)cdiv(seq_length, chunk) : 1;
+        const long long per_item = (long long)num_heads * (kDV + 1) * 4 + 16;
+        const long long fit = std::max(1LL, ((long long)cap - 5 * 256) / per_item - 1);
+        splits = (int)std::max(1LL, std::min((long long)splits, fit));
+        while (splits > 1 && bytes_for(splits) > cap) --splits;  // alignment slack: at most a step or two
+        if (bytes_for(splits) > cap) return MLA_B200_ERR_WORKSPACE;
+    }
     void *scratch = nullptr;
     st = noalloc_scratch(dev, &scratch);
     if (st != MLA_B200_OK) return st;

@@ -77,11 +77,14 @@ __device__ __forceinline__ void unpack_part(const uint4 u, float (&v)[N]) {
 // splits with 8 loads in flight each, and their sums meet in shared memory.
 // skip_single: rows of sequences with exactly one item were already written
 // by the decode kernel itself and are left alone.
+// part_stride: elements from one partial's [num_heads, 512] block to the next
+// (num_heads * 512 in the workspace; larger in a packed exchange buffer, where
+// each part's LSE follows its O), lse_stride likewise for part_lse.
 template <typename OutT, typename PartT>
 __global__ void __launch_bounds__(kCombineThreads) combine_kernel(
     const PartT *__restrict__ part_o, const float *__restrict__ part_lse, WorkList wl,
     int num_heads, long long rows, OutT *__restrict__ out, float *__restrict__ out_lse,
-    int skip_single) {
+    int skip_single, size_t part_stride, size_t lse_stride) {
     constexpr int kVec = 16 / (int)sizeof(PartT);       // partial elements per thread
     constexpr int kTpr = kDV / kVec;                    // threads covering one row
     constexpr int kGroups = kCombineThreads / kTpr;     // split groups per block
@@ -99,7 +102,7 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(
     if (skip_single && i1 - i0 == 1) return;
 
     float mx = -INFINITY;
-    for (int i = i0 + tid; i < i1; i += kCombineThreads) mx = fmaxf(mx, part_lse[(size_t)i * num_heads + h]);
+    for (int i = i0 + tid; i < i1; i += kCombineThreads) mx = fmaxf(mx, part_lse[(size_t)i * lse_stride + h]);
     mx = warp_max(mx);
     if (lane == 0) red[warp] = mx;
     __syncthreads();
@@ -111,17 +114,17 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(
     for (int j = 0; j < kVec; ++j) acc[j] = 0.f;
     float wsum = 0.f;  // identical in every thread (same weights, same order)
     if (mx != -INFINITY) {
-        const size_t step = (size_t)num_heads * (kDV / kVec);  // one split, in 16-byte vectors
+        const size_t step = part_stride / kVec;  // one split, in 16-byte vectors
         for (int c0 = i0; c0 < i1; c0 += kCombineChunk) {
             const int n = min(kCombineChunk, i1 - c0);
             __syncthreads();
             for (int k = tid; k < n; k += kCombineThreads) {
-                const float lse = part_lse[(size_t)(c0 + k) * num_heads + h];
+                const float lse = part_lse[(size_t)(c0 + k) * lse_stride + h];
                 w_s[k] = lse == -INFINITY ? 0.f : __expf(lse - mx);
             }
             __syncthreads();
             for (int k = 0; k < n; ++k) wsum += w_s[k];
-            const uint4 *src = reinterpret_cast<const uint4 *>(part_o + ((size_t)c0 * num_heads + h) * kDV) + col;
+            const uint4 *src = reinterpret_cast<const uint4 *>(part_o + (size_t)c0 * part_stride + (size_t)h * kDV) + col;
             // up to 8 splits' loads in flight per thread (predicated at the end)
             for (int k = g; k < n; k += 8 * kGroups) {
                 uint4 u[8];
@@ -361,10 +364,11 @@ __global__ void __launch_bounds__(1024) plan_varlen_kernel(const int32_t *cu_seq
 }
 
 // Balanced schedule, varlen: cost_off[b] = sum over b' < b of the cost of
-// sequence b' (kItemCost + its 96-row tiles, 0 for an empty sequence), and
+// sequence b' (item_cost + its 96-row tiles, 0 for an empty sequence), and
 // cost_off[B] the total.  One block; a block-wide scan per 1024 sequences.
 __global__ void __launch_bounds__(1024) plan_balanced_kernel(const int32_t *cu_seqlens,
-                                                             int batch, int *__restrict__ cost_off,
+                                                             int batch, int item_cost,
+                                                             int *__restrict__ cost_off,
                                                              const int32_t *seq_lens = nullptr,
                                                              int max_len = 0,
                                                              int32_t *cu_out = nullptr) {
@@ -383,7 +387,7 @@ __global__ void __launch_bounds__(1024) plan_balanced_kernel(const int32_t *cu_s
         int cost = 0;
         if (b < batch) {
             const int len = cu_seqlens[b + 1] - cu_seqlens[b];
-            cost = len > 0 ? (len + kTile - 1) / kTile + kItemCost : 0;
+            cost = len > 0 ? (len + kTile - 1) / kTile + item_cost : 0;
         }
         int v = cost;
 #pragma unroll

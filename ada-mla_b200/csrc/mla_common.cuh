@@ -37,7 +37,7 @@ constexpr float kLn2 = 0.6931471805599453f;
 //
 // Balanced (chunk == 0, tensor-core kernel with an automatic split): the
 //   batch is laid out on a cost line.  Sequence b occupies the interval
-//   [cost0_b, cost0_b + kItemCost + tiles_b): kItemCost units stand for the
+//   [cost0_b, cost0_b + item_cost + tiles_b): item_cost units stand for the
 //   fixed cost of a work item (Q load, epilogue), then one unit per 96-row
 //   tile.  Worker c owns the units [c*quota, (c+1)*quota) and decodes, as one
 //   item, the tiles of each sequence that fall into its units.  So every
@@ -45,11 +45,15 @@ constexpr float kLn2 = 0.6931471805599453f;
 //   only where a worker's share ends.  The item of (sequence b, worker c) has
 //   id b + c: the ids of one sequence are consecutive and all ids are below
 //   batch + workers (some ids stay unused).
-//    dense : cost0_b = b * (kItemCost + tiles), quota given by the host.
+//    dense : cost0_b = b * (item_cost + tiles), quota given by the host.
 //    varlen: cost0_b = cost_off[b] (prefix computed by plan_balanced_kernel),
 //            quota = ceil(cost_off[B] / nworkers), derived on the device.
 // ---------------------------------------------------------------------------
-constexpr int kItemCost = 2;  // fixed cost of one work item, in 96-row tiles
+// Fixed cost of one work item, in 96-row tiles: its Q load (n_h x 1152 B) and
+// its partial write (n_h x 1024 B; one SM writes ~45 GB/s) both scale with the
+// head count.  2 tiles at 128 heads (measured: 3 or 4 moved nothing), 1 for 64
+// heads or fewer, where a split costs little.
+__host__ __device__ constexpr int item_cost_for(int num_heads) { return 1 + num_heads / 128; }
 
 // Programmatic dependent launch.  A kernel launched with the programmatic
 // stream-serialization attribute may start while its predecessor in the stream
@@ -72,6 +76,7 @@ struct WorkList {
     const int32_t *cu_seqlens;  // varlen: row offsets [batch + 1]
     int quota;                  // dense: cost units per worker
     int nworkers;               // varlen: workers the cost line is divided among
+    int item_cost;              // fixed cost of an item in tiles (item_cost_for(num_heads))
 };
 
 struct Item {
@@ -113,7 +118,7 @@ __device__ __forceinline__ Item get_item(const WorkList &w, int i) {
 // Balanced schedule: one sequence's place on the cost line.
 struct SeqSpan {
     int cost0;       // first cost unit
-    int tiles;       // 96-row tiles (its units after the kItemCost fixed ones)
+    int tiles;       // 96-row tiles (its units after the item_cost fixed ones)
     long long row0;  // first cache row
     int len;         // rows
 };
@@ -123,7 +128,7 @@ __device__ __forceinline__ SeqSpan seq_span(const WorkList &w, int b) {
     if (w.cost_off == nullptr) {
         s.len = w.seq_len;
         s.tiles = (w.seq_len + kTile - 1) / kTile;
-        s.cost0 = b * (s.tiles > 0 ? s.tiles + kItemCost : 0);
+        s.cost0 = b * (s.tiles > 0 ? s.tiles + w.item_cost : 0);
         s.row0 = (long long)b * w.seq_len;
     } else {
         s.cost0 = w.cost_off[b];
@@ -137,7 +142,7 @@ __device__ __forceinline__ SeqSpan seq_span(const WorkList &w, int b) {
 __device__ __forceinline__ int bal_total(const WorkList &w) {
     if (w.cost_off == nullptr) {
         const int t = (w.seq_len + kTile - 1) / kTile;
-        return w.batch * (t > 0 ? t + kItemCost : 0);
+        return w.batch * (t > 0 ? t + w.item_cost : 0);
     }
     return w.cost_off[w.batch];
 }
@@ -152,7 +157,7 @@ __device__ __forceinline__ int bal_quota(const WorkList &w) {
 __device__ __forceinline__ int bal_seq_at(const WorkList &w, int x) {
     if (w.cost_off == nullptr) {
         const int t = (w.seq_len + kTile - 1) / kTile;
-        return x / (t + kItemCost);
+        return x / (t + w.item_cost);
     }
     int lo = 0, hi = w.batch - 1;  // largest b with cost_off[b] <= x
     while (lo < hi) {
@@ -213,7 +218,7 @@ __device__ __forceinline__ bool items_next(const WorkList &w, ItemCursor &c, Ite
                 c.next = w.batch;
                 return false;
             }
-            const int base = s.cost0 + kItemCost;  // cost unit of tile 0
+            const int base = s.cost0 + w.item_cost;  // cost unit of tile 0
             const int lo = max(c.x0 - base, 0), hi = min(c.x1 - base, s.tiles);
             if (hi <= lo) continue;
             id = b + c.wid;
@@ -237,7 +242,7 @@ __device__ __forceinline__ void item_range(const WorkList &w, int b, int &i0, in
             return;
         }
         const int q = bal_quota(w);
-        const int base = s.cost0 + kItemCost;
+        const int base = s.cost0 + w.item_cost;
         i0 = b + base / q;
         i1 = b + (base + s.tiles - 1) / q + 1;
     } else if (w.items == nullptr) {

@@ -171,6 +171,7 @@ struct TcParams {
         int mtp;           // multi-token: (draft tokens << 16) | heads per token
     };
     float *out_lse;    // [batch, num_heads] or null
+    unsigned long long *span;  // or null: {first CTA start, last CTA end} %globaltimer of this launch
     // Paged cache (kPaged): the maps address the page pool as rows
     // [num_pages * page_size, 576]; token t of sequence b lives in pool row
     // block_table[b * max_blocks + t / page_size] * page_size + t % page_size,
@@ -333,6 +334,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
+    if (tid == 0 && p.span != nullptr) atomicMin(p.span, (unsigned long long)globaltimer_ns());
     const uint32_t role = ptx::cluster_ctarank();  // 0 = S-CTA, 1 = O-CTA
     const int cid = (int)ptx::cluster_id_x();
     const int ncl = (int)ptx::nclusters_x();
@@ -887,7 +889,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                               : static_cast<uint8_t *>(p.part_o) + (size_t)i * p.num_heads * row_bytes;
                         // Each pass moves a 128-byte segment of every row (64 fp16 or 32 fp32
                         // columns) through a per-warp swizzled 32-row staging tile, so that
-                        // each store instruction covers 4 rows x 128 contiguous bytes.
+                        // each store instruction covers 4 rows x 128 contiguous bytes.  (One
+                        // SM writes global memory at ~45 GB/s whatever the pattern or the
+                        // store path -- TMA stores measured slower -- so a 128 KB partial
+                        // needs ~3 us; the stores are issued at once and drain meanwhile.)
                         const uint32_t stg = sbase + kOffEpi + (warp & 3) * kEpiWarpBytes;
                         const uint32_t srow = stg + lane * 128;
                         const int row0 = (warp & 3) * 32;  // first head of this warp
@@ -947,14 +952,17 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     }
 
     // ---------------------------------------------------------------- teardown
+    // (lane 0 of the producer and MMA warps arrives after its role loop: the
+    // warp reconverges before the CTA and cluster barriers, which are .aligned)
     ptx::tc_fence_before();
-    __syncthreads();
     __syncwarp();
+    __syncthreads();
     ptx::cluster_sync();  // neither CTA leaves while its partner may still target it
     if (warp == 2) {
         ptx::tc_fence_after();
         ptx::tmem_dealloc(tmem, kTmemCols);
     }
+    if (tid == 0 && p.span != nullptr) atomicMax(p.span + 1, (unsigned long long)globaltimer_ns());
 }
 
 }  // namespace tc

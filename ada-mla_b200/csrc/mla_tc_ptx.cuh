@@ -76,12 +76,18 @@ __device__ __forceinline__ bool elect_one() {
     return pred != 0;
 }
 
+// bar.sync / bar.red are .aligned: every lane of a warp must reach the same
+// barrier instruction together, or the warp's arrival is miscounted.  Their
+// callers come out of per-thread spin loops (mbarrier waits) and lane-divergent
+// branches, so each helper first reconverges the warp.
 __device__ __forceinline__ void named_barrier(uint32_t id, uint32_t count) {
+    __syncwarp();
     asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(count) : "memory");
 }
 
 // bar.red.or: returns true in every participating thread if any passed true.
 __device__ __forceinline__ bool named_barrier_or(uint32_t id, uint32_t count, bool v) {
+    __syncwarp();
     uint32_t r;
     asm volatile(
         "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %3, 0;\n\t"
@@ -94,6 +100,7 @@ __device__ __forceinline__ bool named_barrier_or(uint32_t id, uint32_t count, bo
 
 // bar.red.and: true in every participating thread iff all passed true.
 __device__ __forceinline__ bool named_barrier_and(uint32_t id, uint32_t count, bool v) {
+    __syncwarp();
     uint32_t r;
     asm volatile(
         "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %3, 0;\n\t"

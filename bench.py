@@ -6,13 +6,24 @@ One step = one weight-absorbed decode O* = softmax(Q* C^T) C[:, :512] of the
 configured batch with inputs already resident in HBM.  Default workload is
 BASELINE config 1 (B=1, n_h=128, N=4096, fp16) on every rank: with N GPUs each
 rank decodes its own sequence (sequence sharding, no data-path collective), so
-per-GPU work is fixed ("scaling": "weak").
+per-GPU work is fixed ("scaling": "weak").  Every run (any N) also measures the
+two multi-GPU layouts of the north star and reports them under "multi_gpu":
+config 3 with its KV length split over the N ranks (local decode + one NCCL
+all-gather of the (O, LSE) partials + LSE merge, strong scaling) and config 2
+with its 128 sequences sharded over the ranks (strong scaling, no collective).
 
 Metric: latent-KV HBM GB/s = algorithmic cache bytes of all ranks / step time
 (max over ranks), plus us/step.  L2: every step reads a different copy of the
 inputs from a ring whose total size is >= 3x the L2, so each step streams its
-cache from HBM.  The timed region is a CUDA graph of exactly K steps launched
-through the C ABI (mla_b200_decode_batched_f16) with preallocated buffers.
+cache from HBM.  The timed region is one replay of a CUDA graph of exactly K
+steps launched through the C ABI (mla_b200_decode_batched_f16) with
+preallocated buffers; NVML clock readings are taken back to back from just
+before that replay until it has finished.
+
+roofline.launch_us is the average duration of the main decode kernel: CUDA
+events recorded by the library immediately around that launch on its stream,
+in an eager run whose launches were queued behind a device-side sleep (so no
+host latency and no graph event nodes sit inside the interval).
 
 `--page-size P` (P a multiple of 32) runs the same step on a paged copy of
 the cache: shuffled pages of P tokens in a pool, addressed through a block
@@ -24,37 +35,40 @@ mla_b200_decode_batched_fp8); the metric then counts the e4m3 bytes (576 per
 token), so compare us/step with the fp16 line.
 
 `--mtp K` decodes K draft tokens per sequence in one pass over the cache
-(mla_b200_decode_mtp_f16, K x n_h <= 128): the same bytes per step for K times
-the tokens (config keys `draft_tokens`, `tokens_per_step`).
+(mla_b200_decode_mtp_f16): the same bytes per step for K times the tokens
+(config keys `draft_tokens`, `tokens_per_step`).
 
 `--dtype bf16` runs the step on bf16 copies of Q* and the cache
 (mla_b200_decode_batched_bf16, bf16 output); same bytes per token.
 
 `--impl reference` times the reference's own FP32 CPU kernel
 (run_mla_decode_cpu, compiled from the reference sources into oracle/_ref, or
-our C restatement when that build is absent) on all host cores, rank 0 only.
+our C restatement when that build is absent) on all host cores, rank 0 only,
+on the same workload and `config`.  That arm never loads this repository's
+CUDA libraries (the workload generators are loaded by file path, not through
+the ada_mla package).
 """
 from __future__ import annotations
 
 import argparse
+import importlib.util
 import json
 import os
+import re
 import statistics
 import sys
 import threading
 import time
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
-sys.path.insert(0, os.path.join(ROOT, "ada-mla_b200"))
+PKG_PARENT = os.path.join(ROOT, "ada-mla_b200")
+sys.path.insert(0, PKG_PARENT)
 sys.path.insert(0, ROOT)
 
 HEAD_DIM_K = 576
-# DRAM bytes (dram__bytes_read.sum + dram__bytes_write.sum) of one launch of the
-# main decode kernel per config, from an `ncu --set full` capture of this kernel
-# on this workload (cfg 1: 4.95 MB read, 0 written; cfg 3: 152.0 + 4.0 MB).
-NCU_TRAFFIC = {1: 4.949e6, 3: 156.02e6}
 METRIC = "MLA decode latent-KV HBM GB/s (us/step alongside)"
 UNIT = "GB/s"
+PROFILES = os.path.join(ROOT, "profiles")
 
 
 def _peaks():
@@ -64,6 +78,62 @@ def _peaks():
         return float(p["hbm_gbs"]), float(p["bf16_tflops"]), "measured"
     except Exception:
         return 6650.0, 1590.0, "fallback"
+
+
+def load_workloads():
+    """The synthetic workload generators (ada_mla/workloads.py), loaded by path
+    so that the package's __init__ -- which loads the CUDA libraries -- does not
+    run.  The module itself imports only torch."""
+    name = "_mla_bench_workloads"
+    if name in sys.modules:
+        return sys.modules[name]
+    spec = importlib.util.spec_from_file_location(
+        name, os.path.join(PKG_PARENT, "ada_mla", "workloads.py"))
+    mod = importlib.util.module_from_spec(spec)
+    sys.modules[name] = mod
+    spec.loader.exec_module(mod)
+    return mod
+
+
+def ncu_traffic(cfg: int):
+    """DRAM bytes (read + write) of one launch of the main decode kernel on this
+    config, as recorded in its committed ncu summary (profiles/), with the
+    summary's file name and the commit the capture ran on."""
+    path = os.path.join(PROFILES, f"tc_decode_cfg{cfg}_ncu.md")
+    try:
+        with open(path) as f:
+            text = f.read()
+    except OSError:
+        return None, None
+    m = re.search(r"^traffic_bytes_per_launch:\s*([0-9.eE+]+)", text, re.M)
+    c = re.search(r"^captured_at_commit:\s*(\S+)", text, re.M)
+    if not m:
+        return None, None
+    return float(m.group(1)), f"profiles/{os.path.basename(path)} (commit {c.group(1) if c else '?'})"
+
+
+def workload_config(args, wl, world: int) -> dict:
+    """The `config` object of the JSON line: the workload only, identical for
+    both arms at the same arguments and world size."""
+    variant = ("dense" if wl.cu_seqlens is None else "packed varlen")
+    if args.page_size > 0:
+        variant = f"paged cache: shuffled {args.page_size}-token pages"
+    if args.kv_dtype == "fp8":
+        variant += ", e4m3 cache"
+    if args.dtype == "bf16":
+        variant += ", bf16"
+    return {
+        "workload": f"cfg{args.config}: B={wl.batch} n_h={wl.num_heads} N={wl.max_seq_len} per rank "
+                    f"({variant}), softmax scale folded into Q*",
+        "cfg": args.config, "batch_per_rank": wl.batch, "num_heads": wl.num_heads,
+        "seq_len": wl.max_seq_len, "total_tokens_per_rank": wl.total_tokens,
+        "page_size": args.page_size if args.page_size > 0 else None,
+        "draft_tokens": args.mtp if args.mtp > 1 else 1,
+        "tokens_per_step": wl.batch * max(args.mtp, 1) * world,
+        "parallelism": f"sequence-sharded x{world}" if world > 1 else "single GPU",
+        "l2": "GPU arm: every timed step reads its own copy of the inputs from a rotating ring "
+              ">= 3x L2 (inputs larger than L2)",
+    }
 
 
 # ---------------------------------------------------------------------------
@@ -76,7 +146,8 @@ class ClockSampler:
         0x40: "hw_thermal_slowdown", 0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting",
     }
 
-    def __init__(self, device_index: int):
+    def __init__(self, device_index: int, interval_s: float = 0.002):
+        self.interval_s = interval_s
         self.samples: list[tuple[int, int]] = []
         self.max_mhz = None
         self._stop = threading.Event()
@@ -106,10 +177,15 @@ class ClockSampler:
                 self._sample()
             except Exception:
                 return
-            time.sleep(0.002)
+            if self.interval_s > 0:
+                time.sleep(self.interval_s)
 
     def __enter__(self):
         if self._nvml is not None:
+            try:
+                self._sample()  # one reading just before the timed region starts
+            except Exception:
+                pass
             self._t = threading.Thread(target=self._run, daemon=True)
             self._t.start()
         return self
@@ -137,7 +213,7 @@ class ClockSampler:
 # ---------------------------------------------------------------------------
 # distributed plumbing
 # ---------------------------------------------------------------------------
-def dist_init(n_gpus: int):
+def dist_init():
     import torch
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
@@ -173,26 +249,62 @@ def max_over_ranks(x: float, world: int) -> float:
     return float(t.item())
 
 
+def timed_replay(graph, steps: int, world: int, local: int):
+    """Times ONE replay of `graph` (exactly `steps` steps) with CUDA events,
+    bracketed by a barrier and a synchronize; returns (ms per step, max over
+    ranks, clocks sampled by NVML while that replay runs)."""
+    import torch
+
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    sampler = ClockSampler(local, interval_s=0.0)
+    barrier(world)
+    torch.cuda.synchronize()
+    with sampler:
+        ev0.record()
+        graph.replay()
+        ev1.record()
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = max_over_ranks(ev0.elapsed_time(ev1), world) / steps
+    return ms, sampler.summary()
+
+
+def native_libs_loaded() -> list[str]:
+    """Shared objects of this repository mapped into this process."""
+    try:
+        with open("/proc/self/maps") as f:
+            paths = {line.split()[-1] for line in f if line.rstrip().endswith(".so")}
+    except OSError:
+        return []
+    return sorted(p for p in paths if p.startswith(ROOT) or "ada_mla" in p or "mla_b200" in p)
+
+
 # ---------------------------------------------------------------------------
 # CPU baseline / reference arm
 # ---------------------------------------------------------------------------
-def cpu_decode_sample(wl_cpu, impl: str, threads: int, min_seconds: float):
-    """Runs the reference CPU kernel on the whole (small) workload until
-    min_seconds of wall time have passed.  Returns (GB/s, sample description)."""
+def _cpu_decode(wl_cpu, seqs, impl: str, threads: int):
     import numpy as np
 
     import oracle
 
     q = wl_cpu.query.float().numpy()
+    nbytes = 0
+    for b in seqs:
+        c = wl_cpu.cache_rows(b).float().numpy()
+        qs = (q[b].astype(np.float64) * np.sqrt(HEAD_DIM_K)).astype(np.float32)
+        oracle.run_mla_decode_cpu(qs, c, impl=impl, threads=threads)
+        nbytes += c.shape[0] * HEAD_DIM_K * 2
+    return nbytes
+
+
+def cpu_decode_sample(wl_cpu, impl: str, threads: int, min_seconds: float):
+    """Runs the reference CPU kernel on the whole (small) workload until
+    min_seconds of wall time have passed.  Returns (GB/s, seconds, repetitions)."""
     bytes_done = 0
     t0 = time.perf_counter()
     reps = 0
     while True:
-        for b in range(wl_cpu.batch):
-            c = wl_cpu.cache_rows(b).float().numpy()
-            qs = (q[b].astype(np.float64) * np.sqrt(HEAD_DIM_K)).astype(np.float32)
-            oracle.run_mla_decode_cpu(qs, c, impl=impl, threads=threads)
-            bytes_done += c.shape[0] * HEAD_DIM_K * 2
+        bytes_done += _cpu_decode(wl_cpu, range(wl_cpu.batch), impl, threads)
         reps += 1
         el = time.perf_counter() - t0
         if el >= min_seconds:
@@ -206,48 +318,70 @@ def cpu_kind():
     return "reference" if oracle.have_ref() else "port"
 
 
+def cpu_cores() -> int:
+    try:
+        return len(os.sched_getaffinity(0))
+    except Exception:
+        return os.cpu_count() or 1
+
+
+def cpu_model() -> str:
+    try:
+        with open("/proc/cpuinfo") as f:
+            for line in f:
+                if line.startswith("model name"):
+                    return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    return "unknown"
+
+
 def run_reference_arm(args):
-    """--impl reference: the reference's FP32 CPU kernel on all host cores."""
+    """--impl reference: the reference's FP32 CPU kernel on all host cores,
+    rank 0 only, on the whole job's workload (world x the per-rank sequences of
+    the GPU arm); each step is that decode, or a bounded sample of its
+    sequences for the large configs."""
     rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    from ada_mla.workloads import make_workload
-
-    wl = make_workload(args.config, seed=0, device="cpu")
+    W = load_workloads()
+    wl = W.make_workload(args.config, seed=0, device="cpu")
     kind = cpu_kind()
     impl = "reference" if kind == "reference" else "oracle"
-    threads = os.cpu_count() or 1
-    import numpy as np
-
-    import oracle
-
-    q = wl.query.float().numpy()
-    cbytes = wl.cache_bytes
-
-    def one_step():
-        for b in range(wl.batch):
-            c = wl.cache_rows(b).float().numpy()
-            qs = (q[b].astype(np.float64) * np.sqrt(HEAD_DIM_K)).astype(np.float32)
-            oracle.run_mla_decode_cpu(qs, c, impl=impl, threads=threads)
-
+    threads = cpu_cores()
+    # whole-job work = world copies of the per-rank workload; a step decodes a
+    # bounded sample of it (every sequence of cfg1, the first sequences of the
+    # others) so that the run ends within minutes
+    limit = 1 if args.config == 3 else (2 if args.config == 2 else 8)
+    seqs = list(range(min(wl.batch, limit)))
     for _ in range(args.warmup):
-        one_step()
+        _cpu_decode(wl, seqs, impl, threads)
     t0 = time.perf_counter()
+    nbytes = 0
     for _ in range(args.steps):
-        one_step()
+        nbytes += _cpu_decode(wl, seqs, impl, threads)
     el = time.perf_counter() - t0
-    ms = el / args.steps * 1e3
-    gbs = cbytes * args.steps / el / 1e9
+    gbs = nbytes / el / 1e9
+    # us per step of the whole job's decode at this throughput
+    job_bytes = wl.cache_bytes * world
+    ms = job_bytes / (gbs * 1e9) * 1e3
+    loaded = native_libs_loaded()
+    if any("mla_b200" in p or "_ada_mla_ext" in p for p in loaded):
+        raise SystemExit(f"reference arm loaded this repository's CUDA libraries: {loaded}")
+    sample = (f"{len(seqs)} of {wl.batch} sequence(s) of cfg{args.config} per step "
+              f"({sum(wl.seqlens[b] for b in seqs)} tokens), {args.steps} steps, {el:.2f} s; "
+              f"ms_per_step scaled to the whole job ({world} x {wl.batch} sequences)")
     line = {
         "impl": "reference", "metric": METRIC, "value": gbs, "unit": UNIT,
         "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": ms, "us_per_step": ms * 1e3, "higher_is_better": True,
         "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": f"cfg{args.config}: B={wl.batch} n_h={wl.num_heads} "
-                               f"N={wl.max_seq_len} (full decode per step)", "cfg": args.config},
+        "config": workload_config(args, wl, world),
         "cpu_baseline": {"value": gbs, "unit": UNIT, "cores": threads, "kind": kind,
-                         "sample": f"whole cfg{args.config} decode per step, {args.steps} steps"},
+                         "cpu": cpu_model(), "sample": sample},
         "e2e": {"value": gbs, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "native_libs_loaded": loaded,
     }
     print(json.dumps(line), flush=True)
 
@@ -255,10 +389,73 @@ def run_reference_arm(args):
 # ---------------------------------------------------------------------------
 # our arm
 # ---------------------------------------------------------------------------
+def kernel_launch_us(step, n_launch: int) -> float:
+    """Average duration of the main decode kernel over n_launch eager steps.
+
+    The library records the events immediately around that launch on its
+    stream (mla_b200_set_kernel_timing).  A device-side sleep queued first
+    keeps the GPU busy while the host enqueues every step, so the steps then
+    run back to back and no host latency falls between the two events."""
+    import torch
+
+    from ada_mla import capi
+
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(n_launch)]
+    for a, e in evs:  # torch creates the CUDA event at its first record
+        a.record()
+        e.record()
+    s = torch.cuda.current_stream()
+    # one pass to learn the host enqueue time, then a sleep that covers it
+    t0 = time.perf_counter()
+    for i in range(n_launch):
+        step(i, s.cuda_stream)
+    host_s = time.perf_counter() - t0
+    torch.cuda.synchronize()
+    torch.cuda._sleep(int(max(host_s * 2.0, 1e-3) * 2.0e9))  # ~2 GHz cycles
+    for i in range(n_launch):
+        capi.set_kernel_timing(*evs[i])
+        step(i, s.cuda_stream)
+    capi.set_kernel_timing(None, None)
+    torch.cuda.synchronize()
+    return statistics.mean(a.elapsed_time(e) for a, e in evs) * 1e3
+
+
+def kernel_span_us(step, steps: int, cap) -> float:
+    """Mean device-side span of the main decode kernel over a graph of `steps`
+    steps (mla_b200_set_kernel_span: %globaltimer at its first CTA's start
+    and its last CTA's end, one slot per captured launch)."""
+    import torch
+
+    from ada_mla import capi
+
+    span = torch.empty((steps, 2), dtype=torch.int64, device="cuda")
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(cap):
+        capi.set_kernel_span(span)
+        try:
+            with torch.cuda.graph(g, stream=cap):
+                for i in range(steps):
+                    step(i, cap.cuda_stream)
+        finally:
+            capi.set_kernel_span(None)
+    vals = []
+    for _ in range(3):
+        span[:, 0].fill_(-1)  # UINT64_MAX
+        span[:, 1].fill_(0)
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+        d = (span[:, 1] - span[:, 0]).double()
+        vals.append(float(d.mean()) / 1e3)
+    del g
+    return min(vals)
+
+
 def run_ours(args):
     import torch
 
-    rank, world, local = dist_init(args.gpus)
+    rank, world, local = dist_init()
     dev = torch.device("cuda", local)
     torch.cuda.set_device(dev)
     import ada_mla
@@ -288,8 +485,6 @@ def run_ours(args):
     if mtp and (paged or fp8):
         raise SystemExit("--mtp combines with neither --page-size nor --kv-dtype fp8")
     if mtp:
-        if args.mtp * nh > 128:
-            raise SystemExit(f"--mtp {args.mtp} x {nh} heads exceeds 128 rows")
         g = torch.Generator(device=dev).manual_seed(77 + rank)
         qm = (torch.randn((b, args.mtp, nh, HEAD_DIM_K), generator=g, device=dev) / 192 ** 0.5).half()
         qs = [qm] + [qm.clone() for _ in range(ring - 1)]
@@ -367,44 +562,17 @@ def run_ours(args):
                 step(i, cap.cuda_stream)
     graph.replay()  # warm the graph itself
     torch.cuda.synchronize()
-
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler(local)
-    barrier(world)
-    torch.cuda.synchronize()
-    with sampler:
-        ev0.record()
-        graph.replay()
-        ev1.record()
-        torch.cuda.synchronize()
-    barrier(world)
-    ms_total = max_over_ranks(ev0.elapsed_time(ev1), world)
-    ms_step = ms_total / args.steps
+    ms_step, clocks = timed_replay(graph, args.steps, world, local)
     value = world * cache_bytes / (ms_step * 1e-3) / 1e9
+    del graph
 
-    # per-launch duration of the dominant (main decode) kernel: the library
-    # records these events immediately around that launch on its stream; in
-    # stream capture they become event-record nodes, so a second graph of the
-    # same steps times every launch at replay (no host launch latency inside)
-    n_launch = max(args.steps, 50)
-    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-           for _ in range(n_launch)]
-    for a, e in evs:  # torch creates its CUDA event on first record
-        a.record()
-        e.record()
-    torch.cuda.synchronize()
-    tgraph = torch.cuda.CUDAGraph()
-    with torch.cuda.stream(cap):
-        with torch.cuda.graph(tgraph, stream=cap):
-            for i in range(n_launch):
-                capi.set_kernel_timing(*evs[i])
-                step(i, cap.cuda_stream)
-            capi.set_kernel_timing(None, None)
-    tgraph.replay()
-    torch.cuda.synchronize()
-    launch_ms = statistics.mean(a.elapsed_time(e) for a, e in evs)
-    del tgraph
-    achieved = cache_bytes / (launch_ms * 1e-3) / 1e9
+    # per-launch duration of the dominant (main decode) kernel: its device-side
+    # span (first CTA start to last CTA end) in a second capture of the same K
+    # steps, and CUDA events around each launch (which add its launch latency)
+    kernel_us = kernel_span_us(step, args.steps, cap)
+    launch_us = kernel_launch_us(step, max(args.steps, 50))
+    achieved = cache_bytes / (kernel_us * 1e-6) / 1e9
+    traffic, traffic_src = (None, None) if (paged or fp8 or mtp or bf16) else ncu_traffic(args.config)
 
     # end-to-end through the public API: pinned host inputs -> device, decode,
     # result -> host, every step
@@ -453,6 +621,7 @@ def run_ours(args):
     if paged:
         h2d += bth.numel() * 4 + slh.numel() * 4
     d2h = oh.numel() * oh.element_size()
+    del qh, ch, qd, cd
 
     err = ada_mla.mla_get_device_error()
     if err != 0:
@@ -460,6 +629,8 @@ def run_ours(args):
 
     chunk, splits = capi.plan(b, nh, total, maxlen, torch.cuda.get_device_properties(dev).multi_processor_count)
     kernels_per_step = 2 + (1 if cu is not None or paged else 0) + (1 if fp8 else 0)
+    config = workload_config(args, wl, world)
+    line = None
     if rank == 0:
         line = {
             "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world,
@@ -467,123 +638,180 @@ def run_ours(args):
             "us_per_step": ms_step * 1e3, "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16" if bf16 else "f16" + (" (e4m3 cache)" if fp8 else ""),
             "data": "synthetic",
-            "config": {"workload": f"cfg{args.config}: B={b} n_h={nh} N={maxlen} per rank "
-                                   + (f"(paged cache: shuffled {args.page_size}-token pages, "
-                                      f"{pl.num_pages} pages), " if paged else
-                                      f"({'packed varlen' if cu is not None else 'dense'}"
-                                      f"{', e4m3 cache' if fp8 else ''}), ")
-                                   + "softmax scale folded into Q*",
-                       "page_size": args.page_size if paged else None,
-                       "draft_tokens": args.mtp if mtp else 1,
-                       "tokens_per_step": b * (args.mtp if mtp else 1) * world,
-                       "cfg": args.config, "batch_per_rank": b, "num_heads": nh,
-                       "seq_len": maxlen, "total_tokens_per_rank": total,
-                       "num_splits": splits if args.splits <= 0 else args.splits,
-                       "chunk_tokens": chunk,
-                       "parallelism": f"sequence-sharded x{world}" if world > 1 else "single GPU",
-                       "l2": f"rotating ring of {ring} input copies ({ring * step_bytes / 2**20:.0f} MiB "
-                             f">= 3x L2)" if ring > 1 else "no rotation"},
+            "config": config,
+            "run": {"num_splits": splits if args.splits <= 0 else args.splits, "chunk_tokens": chunk,
+                    "ring_copies": ring, "ring_mib": round(ring * step_bytes / 2**20)},
             "roofline": {"bound": "hbm", "achieved": achieved, "peak": hbm_peak, "unit": "GB/s",
                          "frac": achieved / hbm_peak, "peak_source": peak_kind,
-                         "traffic": None if paged or fp8 else NCU_TRAFFIC.get(args.config),
+                         "traffic": traffic, "traffic_source": traffic_src,
                          "kernel": "mla::tc::tc_decode_kernel",
-                         "launch_us": launch_ms * 1e3,
+                         "kernel_us": kernel_us,
+                         "timing": "achieved = algorithmic bytes / kernel_us; kernel_us = mean device-side "
+                                   "span of the kernel (first CTA start to last CTA end, %globaltimer) over "
+                                   "a graph of the K steps; launch_us = mean CUDA-event interval around each "
+                                   "launch on its stream (adds the launch latency)",
+                         "launch_us": launch_us,
                          "algorithmic_bytes_per_launch": cache_bytes},
             "e2e": {"value": e2e_value, "unit": UNIT, "h2d_bytes_per_step": h2d,
                     "d2h_bytes_per_step": d2h, "us_per_step": e2e_ms * 1e3,
                     "api": ("ada_mla.mla_decode_mtp" if mtp else "ada_mla.mla_decode_paged" if paged
                             else "ada_mla.mla_decode_batched")},
             "gpu_launches": args.steps * kernels_per_step,
-            "clocks": sampler.summary(),
+            "clocks": clocks,
         }
         if not args.no_cpu_baseline and world == 1:
-            from ada_mla.workloads import make_workload as mk
-
-            wl_cpu = mk(args.config, seed=0, device="cpu") if args.config in (0, 1) else None
+            wl_cpu = load_workloads().make_workload(args.config, seed=0, device="cpu") \
+                if args.config in (0, 1) else None
             if wl_cpu is not None:
-                threads = os.cpu_count() or 1
+                threads = cpu_cores()
                 kind = cpu_kind()
                 gbs, el, reps = cpu_decode_sample(wl_cpu, "reference" if kind == "reference" else "oracle",
                                                   threads, args.cpu_seconds)
                 line["cpu_baseline"] = {"value": gbs, "unit": UNIT, "cores": threads, "kind": kind,
+                                        "cpu": cpu_model(),
                                         "sample": f"{reps} full cfg{args.config} decodes "
                                                   f"({el:.1f} s wall)"}
+    del qs, wl
+    if not args.no_multi:
+        mg = multi_gpu_lines(args, rank, world, local)
+        if line is not None:
+            line["multi_gpu"] = mg
+    if line is not None:
         print(json.dumps(line), flush=True)
-    del graph
     if world > 1:
         import torch.distributed as dist
 
+        dist.barrier()
         dist.destroy_process_group()
 
 
-def run_kv(args):
-    """--mode kv: ONE workload (identical on every rank) whose KV length is split
-    across the ranks; each step = local decode of the rank's slice + NCCL
-    all-gather of the (O, LSE) partials + LSE merge, captured in one CUDA graph.
-    Total work is fixed as N grows ("scaling": "strong")."""
+# ---------------------------------------------------------------------------
+# the multi-GPU layouts (strong scaling over the ranks of this run)
+# ---------------------------------------------------------------------------
+def _ring_len(step_bytes: int, dev) -> int:
+    """Copies of a step's inputs so that consecutive steps read >= 3x L2 of
+    distinct data (capped at 40 GB)."""
     import torch
 
-    rank, world, local = dist_init(args.gpus)
-    dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    import torch.distributed as dist
+    l2 = torch.cuda.get_device_properties(dev).L2_cache_size or (126 << 20)
+    return max(1, min(-(-3 * l2 // max(step_bytes, 1)), int(40e9 // max(step_bytes, 1))))
 
-    from ada_mla import multigpu
-    from ada_mla.workloads import make_workload
 
-    wl = make_workload(args.config, seed=0, device=dev)
-    assert wl.cu_seqlens is None, "kv mode takes a dense config (1 or 3)"
-    n = wl.max_seq_len
-    dec = multigpu.KvSplitDecoder() if world > 1 else None
-    lo, hi = dec.bounds(n) if dec else (0, n)
-    cache_slice = wl.cache[:, lo:hi].contiguous()
+def _graph_of(fn, steps):
+    import torch
 
-    def step():
-        if dec is None:
-            import ada_mla
-
-            return ada_mla.mla_decode_batched(wl.query, cache_slice, softmax_scale=1.0)
-        return dec(wl.query, cache_slice, 1.0)
-
-    for _ in range(args.warmup):
-        step()
+    for _ in range(3):
+        fn()
     torch.cuda.synchronize()
     graph = torch.cuda.CUDAGraph()
     cap = torch.cuda.Stream()
     cap.wait_stream(torch.cuda.current_stream())
     with torch.cuda.stream(cap):
-        step()
+        fn()
         torch.cuda.synchronize()
         with torch.cuda.graph(graph, stream=cap):
-            for _ in range(args.steps):
-                step()
+            for _ in range(steps):
+                fn()
     graph.replay()
     torch.cuda.synchronize()
-    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    sampler = ClockSampler(local)
-    barrier(world)
-    torch.cuda.synchronize()
-    with sampler:
-        ev0.record()
-        graph.replay()
-        ev1.record()
-        torch.cuda.synchronize()
-    barrier(world)
-    ms_step = max_over_ranks(ev0.elapsed_time(ev1), world) / args.steps
-    value = wl.cache_bytes / (ms_step * 1e-3) / 1e9
-    if rank == 0:
-        print(json.dumps({
-            "metric": METRIC, "value": value, "unit": UNIT, "n_gpus": world, "steps": args.steps,
-            "warmup": args.warmup, "ms_per_step": ms_step, "us_per_step": ms_step * 1e3,
-            "higher_is_better": True, "scaling": "strong", "vs_baseline": None, "dtype": "f16",
-            "data": "synthetic",
-            "config": {"workload": f"cfg{args.config}: B={wl.batch} n_h={wl.num_heads} N={n}, KV length "
-                                   f"split over {world} GPU(s), (O, LSE) all-gather + LSE merge",
-                       "cfg": args.config, "parallelism": f"kv-split x{world}",
-                       "l2": "single copy (no rotation)"},
-            "clocks": sampler.summary()}), flush=True)
+    return graph
+
+
+def kv_split_line(cfg: int, steps: int, rank: int, world: int, local: int) -> dict:
+    """One sequence's KV length split over the ranks: local decode of the rank's
+    slice into a packed (O, LSE) buffer, one NCCL all-gather, LSE merge."""
+    import torch
+
+    from ada_mla import multigpu
+    from ada_mla.workloads import make_workload
+
+    dev = torch.device("cuda", local)
+    wl = make_workload(cfg, seed=0, device=dev)
+    n = wl.max_seq_len
+    dec = multigpu.KvSplitDecoder()
+    lo, hi = dec.bounds(n)
+    slice_bytes = max(1, (hi - lo) * wl.batch * HEAD_DIM_K * 2)
+    ring = _ring_len(slice_bytes, dev)
+    slices = [wl.cache[:, lo:hi].clone() for _ in range(ring)]
+    it = [0]
+
+    def fn():
+        dec(wl.query, slices[it[0] % ring], 1.0)
+        it[0] += 1
+
+    graph = _graph_of(fn, steps)
+    ms, clocks = timed_replay(graph, steps, world, local)
     del graph
+    stages = dec.stage_times_us(wl.query, slices[0], 1.0, reps=20)
+    return {"workload": f"cfg{cfg}: B={wl.batch} n_h={wl.num_heads} N={n}, KV length split over "
+                        f"{world} GPU(s): local decode + all-gather of (O, LSE) + LSE merge",
+            "scaling": "strong", "us_per_step": ms * 1e3,
+            "value": wl.cache_bytes / (ms * 1e-3) / 1e9, "unit": UNIT,
+            "stages_us_rank0": stages, "clocks_sm_mhz": clocks.get("sm_mhz")}
+
+
+def sharded_line(cfg: int, steps: int, rank: int, world: int, local: int) -> dict:
+    """A batch's sequences sharded over the ranks (LPT on length), each rank
+    decoding its own with no collective on the data path."""
+    import torch
+
+    import ada_mla
+    from ada_mla import multigpu
+    from ada_mla.workloads import make_workload, seqlens_for
+
+    dev = torch.device("cuda", local)
+    lens = seqlens_for(cfg, seed=0)
+    mine = multigpu.shard_sequences(lens, world)[rank]
+    wl = make_workload(cfg, seed=0, device=dev, seqlens=[lens[i] for i in mine])
+    ring = _ring_len(wl.cache_bytes, dev)
+    caches = [wl.cache] + [wl.cache.clone() for _ in range(ring - 1)]
+    it = [0]
+
+    def fn():
+        ada_mla.mla_decode_batched(wl.query, caches[it[0] % ring], wl.cu_seqlens,
+                                   max_seq_len=wl.max_seq_len, softmax_scale=1.0)
+        it[0] += 1
+
+    graph = _graph_of(fn, steps)
+    ms, clocks = timed_replay(graph, steps, world, local)
+    del graph
+    total_bytes = sum(lens) * HEAD_DIM_K * 2
+    return {"workload": f"cfg{cfg}: {len(lens)} sequences sharded over {world} GPU(s) by LPT on "
+                        f"length (rank 0: {len(mine)} sequences, {wl.total_tokens} tokens), no collective",
+            "scaling": "strong", "us_per_step": ms * 1e3,
+            "value": total_bytes / (ms * 1e-3) / 1e9, "unit": UNIT,
+            "clocks_sm_mhz": clocks.get("sm_mhz")}
+
+
+def multi_gpu_lines(args, rank, world, local) -> dict:
+    import torch
+
+    out = {}
+    steps = max(10, min(args.steps, 50))
+    out["cfg3_kv_split"] = kv_split_line(3, steps, rank, world, local)
+    torch.cuda.empty_cache()
+    out["cfg2_sharded"] = sharded_line(2, steps, rank, world, local)
+    torch.cuda.empty_cache()
+    return out
+
+
+def run_kv(args):
+    """--mode kv: only the KV-split line of the configured (dense) config."""
+    rank, world, local = dist_init()
+    import torch
+
+    torch.cuda.set_device(local)
+    line = kv_split_line(args.config, args.steps, rank, world, local)
+    if rank == 0:
+        line.update({"metric": METRIC, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+                     "ms_per_step": line["us_per_step"] / 1e3, "higher_is_better": True,
+                     "vs_baseline": None, "dtype": "f16", "data": "synthetic",
+                     "config": {"workload": line["workload"], "cfg": args.config,
+                                "parallelism": f"kv-split x{world}"}})
+        print(json.dumps(line), flush=True)
     if world > 1:
+        import torch.distributed as dist
+
         dist.barrier()
         dist.destroy_process_group()
 
@@ -606,10 +834,12 @@ def main():
                     help="decode a paged copy of the cache (pages of this many tokens)")
     ap.add_argument("--cpu-seconds", type=float, default=10.0)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-multi", action="store_true",
+                    help="skip the multi_gpu lines (cfg3 KV split, cfg2 sharded)")
     ap.add_argument("--no-rotate", action="store_true")
     ap.add_argument("--mode", default="shard", choices=["shard", "kv"],
                     help="shard: every rank decodes its own sequence(s), no collective (default); "
-                         "kv: one sequence's KV length split across the ranks")
+                         "kv: only the KV-split line of --config")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

@@ -91,6 +91,17 @@ MLA_B200_API int mla_b200_device_info(int *num_sms, int *decode_clusters);
  * the hook off. */
 MLA_B200_API int mla_b200_set_kernel_timing(void *ev_start, void *ev_stop);
 
+/* Device-side span of the main tensor-core decode kernel (no reference
+ * counterpart).  While set on the calling host thread, the k-th later launch
+ * of that kernel (k counting from 0, wrapping after `slots`) records, in
+ * span[2k] and span[2k+1], the %globaltimer (ns) of its first CTA's start
+ * (atomic min) and of its last CTA's end (atomic max); the caller initialises
+ * each pair to {UINT64_MAX, 0} before the launch runs.  The span excludes the
+ * launch latency that an event pair around the launch includes.  `span` is a
+ * device array of 2 * slots uint64; NULL (or slots <= 0) turns it off.  Under
+ * stream capture the pointer is baked into each captured launch. */
+MLA_B200_API int mla_b200_set_kernel_span(unsigned long long *span, int slots);
+
 /* ------------------------------------------------------------------------ */
 /* Planning                                                                  */
 /* ------------------------------------------------------------------------ */
@@ -298,6 +309,17 @@ MLA_B200_API int mla_b200_decode_split_f16_noalloc(const void *query, const void
 MLA_B200_API int mla_b200_combine_f32(const float *part_o, const float *part_lse, int num_parts,
                                       long long rows, void *out, int out_dtype, float *out_lse,
                                       void *stream);
+
+/* The same merge read from a packed exchange buffer, the layout one
+ * all-gather of every rank's (O, LSE) produces: part g occupies floats
+ * [g * part_stride, (g + 1) * part_stride) of `parts`, its O [rows, 512] fp32
+ * first and its LSE [rows] fp32 right after (at g * part_stride + rows * 512).
+ * part_stride >= rows * 513 and a multiple of 4 (each part's O 16-byte
+ * aligned).  Saves the unpacking copies of a split-KV multi-GPU step
+ * (no reference counterpart: the reference runs on one GPU). */
+MLA_B200_API int mla_b200_combine_packed_f32(const float *parts, int num_parts, long long rows,
+                                             long long part_stride, void *out, int out_dtype,
+                                             float *out_lse, void *stream);
 
 /* ------------------------------------------------------------------------ */
 /* Device error word                                                         */

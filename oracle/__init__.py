@@ -40,12 +40,24 @@ _libs: dict[str, ctypes.CDLL | None] = {}
 _F32P = ctypes.POINTER(ctypes.c_float)
 
 
+def reference_dir(ref_dir: str | None = None) -> str | None:
+    """The reference checkout: the argument, else $MLA_REFERENCE_DIR, else a
+    checkout named ``reference`` beside this repository.  None when its CPU
+    kernel's source is not there (e.g. on a machine that only runs the tests)."""
+    cands = [ref_dir, os.environ.get("MLA_REFERENCE_DIR"),
+             os.path.join(os.path.dirname(os.path.dirname(_HERE)), "reference")]
+    for d in cands:
+        if d and os.path.isfile(os.path.join(d, "csrc", "mla_decode_naive_fp32_cpu.cpp")):
+            return os.path.abspath(d)
+    return None
+
+
 def build(ref_dir: str | None = None) -> None:
     """Compile the oracle (and the reference CPU kernel when its sources exist)."""
     subprocess.run(["make", "-s", "-C", _HERE, "all"], check=True)
-    ref_dir = ref_dir or "/root/reference"
-    if os.path.isfile(os.path.join(ref_dir, "csrc", "mla_decode_naive_fp32_cpu.cpp")):
-        subprocess.run(["make", "-s", "-C", _HERE, "ref", f"REF={ref_dir}"], check=True)
+    ref = reference_dir(ref_dir)
+    if ref is not None:
+        subprocess.run(["make", "-s", "-C", _HERE, "ref", f"REF={ref}"], check=True)
 
 
 def _load(path: str, build_if_missing: bool) -> ctypes.CDLL | None:

@@ -25,6 +25,12 @@ def test_shard_sequences_lpt_balance_and_coverage():
         assert plan == multigpu.shard_sequences(lens, world)  # deterministic
 
 
+def test_packed_stride_aligns_every_part():
+    for rows in (1, 3, 16, 128, 129, 2048):
+        st = multigpu.packed_stride(rows)
+        assert st >= rows * 513 and st % 4 == 0 and st - rows * 513 < 4
+
+
 def test_kv_split_bounds_cover_and_align():
     for n in (0, 1, 95, 96, 4096, 131072, 131071):
         for world in (1, 2, 4, 8):
@@ -42,18 +48,22 @@ def _free_port():
         return s.getsockname()[1]
 
 
-def _cpu_partial(query, cache, scale):
+def _cpu_partial(query, cache, scale, o_out, lse_out, workspace):
+    """In-place per-rank decode (float64 oracle partials) into the exchange buffer's views."""
     q = query.numpy()
     c = cache.numpy()
-    outs, lses = [], []
     for b in range(q.shape[0]):
         o, lse = oracle.lse_partial_oracle(q[b], c[b], scale)
-        outs.append(o)
-        lses.append(lse)
-    return torch.tensor(np.stack(outs), dtype=torch.float32), torch.tensor(np.stack(lses), dtype=torch.float32)
+        o_out[b] = torch.tensor(o, dtype=torch.float32)
+        lse_out[b] = torch.tensor(lse, dtype=torch.float32)
 
 
-def _cpu_merge(part_o, part_lse, out_dtype):
+def _cpu_merge(packed, parts, rows, stride, out_dtype):
+    """LSE merge read straight from the gathered buffer: part g's O at
+    g * stride, its LSE right after the O block."""
+    views = packed.view(parts, stride)
+    part_o = views[:, :rows * 512].reshape(parts, rows, 512)
+    part_lse = views[:, rows * 512:rows * 513]
     lse = part_lse.double()
     m = lse.max(dim=0).values
     m = torch.where(torch.isfinite(m), m, torch.zeros_like(m))
@@ -72,7 +82,8 @@ def _kv_worker(rank, world, port, n, seed, results):
         b, nh = 2, 8
         q = torch.randn(b, nh, 576, generator=g) / 192 ** 0.5
         c = torch.randn(b, n, 576, generator=g)
-        dec = multigpu.KvSplitDecoder(local_decode=_cpu_partial, merge=_cpu_merge)
+        dec = multigpu.KvSplitDecoder(local_decode=_cpu_partial, merge=_cpu_merge,
+                                      make_workspace=lambda q, c: None)
         lo, hi = dec.bounds(n)
         out, lse = dec(q, c[:, lo:hi].contiguous(), 1.0, out_dtype=torch.float64, return_lse=True)
         full = [oracle.lse_partial_oracle(q[i].numpy(), c[i].numpy(), 1.0) for i in range(b)]

@@ -3,18 +3,24 @@ Python from its definition (csrc/mla_common.cuh: the cost line, each cluster's
 quota, item ids b + cluster) and checked for the properties the kernels rely
 on: every tile of every sequence is decoded exactly once, a sequence's item ids
 are consecutive and below batch + clusters, no cluster exceeds its quota, and
-the combine's id range for a sequence is exactly the ids its items used."""
+the combine's id range for a sequence is exactly the ids its items used.
+The fixed cost of an item is 1 + n_h // 128 tiles (item_cost_for), so both
+head-count regimes are checked."""
 import numpy as np
 import pytest
 
-TILE, ITEM_COST = 96, 2
+TILE = 96
+
+
+def item_cost_for(num_heads):
+    return 1 + num_heads // 128
 
 
 def cdiv(a, b):
     return -(-a // b)
 
 
-def schedule(lens, clusters):
+def schedule(lens, clusters, ITEM_COST=2):
     tiles = [cdiv(n, TILE) for n in lens]
     cost = [t + ITEM_COST if t > 0 else 0 for t in tiles]
     off = np.concatenate([[0], np.cumsum(cost)]).astype(int)
@@ -38,10 +44,12 @@ def schedule(lens, clusters):
 
 @pytest.mark.parametrize("seed", range(6))
 @pytest.mark.parametrize("clusters", [1, 7, 74])
-def test_balanced_schedule_properties(seed, clusters):
+@pytest.mark.parametrize("num_heads", [16, 128])
+def test_balanced_schedule_properties(seed, clusters, num_heads):
+    ITEM_COST = item_cost_for(num_heads)
     rng = np.random.default_rng(seed)
     lens = [int(x) for x in rng.integers(0, 9000, size=int(rng.integers(1, 300)))]
-    items, ranges, q, off = schedule(lens, clusters)
+    items, ranges, q, off = schedule(lens, clusters, ITEM_COST)
     covered = {b: np.zeros(cdiv(n, TILE), dtype=int) for b, n in enumerate(lens)}
     per_cluster = {}
     for c, i, b, lo, hi in items:
@@ -62,6 +70,10 @@ def test_balanced_schedule_properties(seed, clusters):
         assert load <= q + ITEM_COST, "a cluster's work is its quota plus at most one item's fixed cost"
 
 
+def test_item_cost_grows_with_heads():
+    assert item_cost_for(128) == 2 and item_cost_for(64) == 1 and item_cost_for(16) == 1
+
+
 def test_balanced_schedule_single_sequence_matches_even_split():
-    items, ranges, q, _ = schedule([131072], 74)
+    items, ranges, q, _ = schedule([131072], 74, item_cost_for(128))
     assert len(items) == 72 and max(hi - lo for *_, lo, hi in items) == q

@@ -41,6 +41,34 @@ def test_noalloc_matches_workspace_entry_on_two_calls():
     assert capi.get_device_error() == 0
 
 
+@pytest.mark.parametrize("splits", [1, 4, 16])
+def test_noalloc_explicit_splits_match_workspace_entry_and_oracle(splits):
+    import numpy as np
+
+    import oracle
+    from ada_mla import capi
+
+    lib = capi.lib()
+    stream = torch.cuda.current_stream().cuda_stream
+    q, c = _inputs(128, 4000, seed=200 + splits)
+    ref = capi.decode_split_f16(q, c, splits)
+    want = oracle.mla_decode_oracle(q.float().cpu().numpy(), c.float().cpu().numpy(),
+                                    1.0 / np.sqrt(192.0), threads=8)
+    out = torch.full((128, 512), float("nan"), dtype=torch.float16, device="cuda")
+    for call in range(2):
+        st = lib.mla_b200_decode_split_f16_noalloc(q.data_ptr(), c.data_ptr(), out.data_ptr(), 128, 4000,
+                                                   splits, stream)
+        assert st == capi.OK, capi.status_string(st)
+        torch.cuda.synchronize()
+        if call == 0:
+            free0, _ = torch.cuda.mem_get_info()
+    free1, _ = torch.cuda.mem_get_info()
+    assert free1 == free0  # the second call took no device memory
+    got = out.float().cpu().numpy()
+    assert_close_parity(got, ref.float().cpu().numpy(), MAX_ABS_TOL, MEAN_ABS_TOL, what=f"splits={splits}")
+    assert_close_parity(got, want, MAX_ABS_TOL, MEAN_ABS_TOL, what=f"splits={splits} vs oracle")
+
+
 def test_noalloc_rejects_oversized_split_request():
     from ada_mla import capi
 
