@@ -129,14 +129,16 @@ def mla_decode_mtp(query, cache, cu_seqlens=None, max_seq_len: int = -1,
                    return_lse: bool = False, out_dtype=None):
     """Multi-token (speculative / MTP draft) decode.
 
-    query  [B, k, n_h, 576] fp16 or bf16 with k * n_h <= 128: k draft tokens per
+    query  [B, k, n_h, 576] fp16 or bf16, n_h <= 128: k draft tokens per
            sequence whose own latent rows are the sequence's last k cache rows.
     cache  as for ``mla_decode_batched`` (dense [B, N, 576] or packed with
            ``cu_seqlens``), same dtype.  Draft token i of a sequence of length L
            sees its first L - (k - 1 - i) tokens.
-    The k drafts share every cache tile (rows token * n_h + head of one MMA
-    tile): one pass over the cache for k tokens.  Returns O* [B, k, n_h, 512]
-    (and the LSE [B, k, n_h] with ``return_lse``).
+    With k * n_h <= 128 the k drafts share every cache tile (rows token * n_h +
+    head of one MMA tile): one pass over the cache for k tokens.  Above that
+    (e.g. 128 heads) each draft is decoded as its own 128-row sequence next to
+    the sequence's other drafts, whose repeated tile reads hit L2.  Returns O*
+    [B, k, n_h, 512] (and the LSE [B, k, n_h] with ``return_lse``).
     """
     if out_dtype not in (None, torch.float32, query.dtype):
         raise ValueError(f"mla_decode_mtp: out_dtype must be None, float32 or {query.dtype}")

@@ -41,6 +41,7 @@ SIGNATURES = {
                                ctypes.POINTER(_c_int), ctypes.POINTER(_c_int)]),
     "mla_b200_workspace_size": (_c_size, [_c_int, _c_int, _c_ll, _c_int, _c_int]),
     "mla_b200_workspace_size_fp8": (_c_size, [_c_int, _c_int, _c_ll, _c_int, _c_int]),
+    "mla_b200_workspace_size_mtp": (_c_size, [_c_int, _c_int, _c_int, _c_ll, _c_int, _c_int]),
     "mla_b200_decode_split_f16": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _vp, _c_size, _vp]),
     "mla_b200_decode_split_f16_noalloc": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _vp]),
     "mla_b200_decode_batched_f16": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_ll, _c_int, _c_float,

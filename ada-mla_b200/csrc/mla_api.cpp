@@ -187,7 +187,7 @@ std::vector<at::Tensor> mla_decode_batched(const at::Tensor &query, const at::Te
 }
 
 // Multi-token decode (no reference counterpart).
-//   query [B, k, n_h, 576] fp16 or bf16 (k * n_h <= 128), cache as in
+//   query [B, k, n_h, 576] fp16 or bf16 (n_h <= 128), cache as in
 //   mla_decode_batched (same dtype); draft token i of sequence b sees its first
 //   len_b - (k - 1 - i) tokens.  Returns (out [B, k, n_h, 512], lse [B, k, n_h] or empty).
 std::vector<at::Tensor> mla_decode_mtp(const at::Tensor &query, const at::Tensor &cache,
@@ -227,8 +227,8 @@ std::vector<at::Tensor> mla_decode_mtp(const at::Tensor &query, const at::Tensor
     at::Tensor out = at::empty({b, k, nh, MLA_B200_HEAD_DIM_V},
                                query.options().dtype(out_fp32 ? at::kFloat : query.scalar_type()));
     at::Tensor lse = return_lse ? at::empty({b, k, nh}, query.options().dtype(at::kFloat)) : at::Tensor();
-    const size_t ws = mla_b200_workspace_size((int)b, (int)(k * nh), total, (int)max_seq_len,
-                                              (int)num_splits);
+    const size_t ws = mla_b200_workspace_size_mtp((int)b, (int)k, (int)nh, total, (int)max_seq_len,
+                                                  (int)num_splits);
     at::Tensor w = workspace(query, ws);
     auto *fn = bf16 ? mla_b200_decode_mtp_bf16 : mla_b200_decode_mtp_f16;
     const int odt = out_fp32 ? MLA_B200_OUT_F32 : (bf16 ? MLA_B200_OUT_BF16 : MLA_B200_OUT_F16);

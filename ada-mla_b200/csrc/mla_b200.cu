@@ -374,7 +374,7 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
                      int num_heads, long long total_tokens, int max_seq_len, float scale,
                      int num_splits, void *out, int out_dtype, float *out_lse, void *workspace,
                      size_t workspace_bytes, cudaStream_t stream, const PagedArgs *pg = nullptr,
-                     const Fp8Args *f8 = nullptr, const MtpArgs *mtp = nullptr) {
+                     const Fp8Args *f8 = nullptr, const MtpArgs *mtp = nullptr, int group = 1) {
     int dev;
     DevInfo info;
     int st = current_device(&dev, &info);
@@ -390,13 +390,20 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     if (pg != nullptr && !tc_path) return MLA_B200_ERR_UNSUPPORTED;  // paged: tensor-core kernel only
     if (f8 != nullptr && (!tc_path || kBf16 || pg != nullptr)) return MLA_B200_ERR_UNSUPPORTED;
     if (mtp != nullptr && (!tc_path || pg != nullptr || f8 != nullptr)) return MLA_B200_ERR_UNSUPPORTED;
+    // group > 1: `batch` virtual sequences, `group` per real sequence, read the
+    // real sequences' rows (seq_len_of); they always take a planned schedule
+    // (work table or cost line), and plan with group x the real tokens.
+    const bool virt = group > 1;
+    if (virt && (!tc_path || pg != nullptr || f8 != nullptr || mtp != nullptr || batch % group != 0))
+        return MLA_B200_ERR_UNSUPPORTED;
+    const long long plan_total = virt ? total_tokens * group : total_tokens;
     // (A single sequence splits evenly in the chunked schedule already.)
     const bool balanced = tc_path && num_splits <= 0 && batch > 1;
-    int chunk = chunk_for(batch, total_tokens, max_seq_len, num_splits, info.sms, num_heads);
+    int chunk = chunk_for(batch, plan_total, max_seq_len, num_splits, info.sms, num_heads);
     // paged: items start on 96-token boundaries so every 32-row box sits in one page
     if (pg != nullptr) chunk = (int)std::min<long long>(cdiv(chunk, kTile) * kTile, 1 << 30);
     const long long max_items = balanced ? (long long)batch + info.tc_clusters
-                                         : max_items_for(batch, total_tokens, chunk);
+                                         : max_items_for(batch, plan_total, chunk);
     if (max_items > (1LL << 30)) return MLA_B200_ERR_UNSUPPORTED;
     WsLayout L = ws_layout(workspace, max_items, num_heads, batch, f8 != nullptr);
     if (workspace == nullptr || workspace_bytes < L.bytes) return MLA_B200_ERR_WORKSPACE;
@@ -411,11 +418,13 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     wl.batch = batch;
     wl.chunk = balanced ? 0 : chunk;
     wl.item_cost = item_cost_for(num_heads);
+    wl.group = group;
+    const bool planned = cu_seqlens != nullptr || virt;  // a plan kernel precedes the decode
     int bal_clusters = 0;      // balanced: clusters to launch
     bool bal_split = true;     // balanced: some sequence has more than one item
     if (balanced) {
         wl.max_items = (int)max_items;
-        if (cu_seqlens == nullptr) {
+        if (!planned) {
             wl.seq_len = max_seq_len;
             const long long tiles = cdiv(max_seq_len, kTile);
             const long long cost = tiles > 0 ? tiles + wl.item_cost : 0;
@@ -435,12 +444,13 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
         } else {
             wl.cost_off = L.item_off;
             wl.cu_seqlens = cu_seqlens;
+            wl.seq_len = max_seq_len;  // the dense length of virtual sequences without cu_seqlens
             wl.nworkers = info.tc_clusters;
             bal_clusters = info.tc_clusters;
             plan_balanced_kernel<<<1, 1024, 0, stream>>>(cu_seqlens, batch, wl.item_cost, L.item_off, seq_lens,
-                                                         max_seq_len, L.cu_virtual);
+                                                         max_seq_len, L.cu_virtual, group, max_seq_len);
         }
-    } else if (cu_seqlens == nullptr) {
+    } else if (!planned) {
         wl.items = nullptr;
         wl.item_off = nullptr;
         wl.seq_len = max_seq_len;
@@ -454,7 +464,8 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
         wl.max_items = (int)max_items;
         wl.cu_seqlens = cu_seqlens;  // read by the paged kernel
         plan_varlen_kernel<<<1, 1024, 0, stream>>>(cu_seqlens, batch, chunk, L.item_off, L.items,
-                                                   (int)max_items, seq_lens, max_seq_len, L.cu_virtual);
+                                                   (int)max_items, seq_lens, max_seq_len, L.cu_virtual,
+                                                   group, max_seq_len);
     }
     bool tc_direct = false;  // the tcgen05 kernel wrote single-item sequences itself
     if (wl.max_items > 0 && (!balanced || bal_clusters > 0)) {
@@ -513,19 +524,19 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
             const int clusters = balanced ? bal_clusters : std::min(info.tc_clusters, wl.max_items);
             timing_mark(t_ev_start, stream);
             if (mtp != nullptr) {
-                if (balanced) launch_tc<kSchedBalanced, kBf16, false, false, true>(clusters, maps, tp, stream, cu_seqlens != nullptr);
-                else launch_tc<kSchedChunked, kBf16, false, false, true>(clusters, maps, tp, stream, cu_seqlens != nullptr);
+                if (balanced) launch_tc<kSchedBalanced, kBf16, false, false, true>(clusters, maps, tp, stream, planned);
+                else launch_tc<kSchedChunked, kBf16, false, false, true>(clusters, maps, tp, stream, planned);
             } else if (f8 != nullptr) {
                 if constexpr (!kBf16) {  // (fp8 runs with fp16 Q*; the prep kernel precedes)
                     if (balanced) launch_tc<kSchedBalanced, false, false, true>(clusters, maps, tp, stream, true);
                     else launch_tc<kSchedChunked, false, false, true>(clusters, maps, tp, stream, true);
                 }
             } else if (pg != nullptr) {
-                if (balanced) launch_tc<kSchedBalanced, kBf16, true>(clusters, maps, tp, stream, cu_seqlens != nullptr);
-                else launch_tc<kSchedChunked, kBf16, true>(clusters, maps, tp, stream, cu_seqlens != nullptr);
+                if (balanced) launch_tc<kSchedBalanced, kBf16, true>(clusters, maps, tp, stream, planned);
+                else launch_tc<kSchedChunked, kBf16, true>(clusters, maps, tp, stream, planned);
             } else {
-                if (balanced) launch_tc<kSchedBalanced, kBf16, false>(clusters, maps, tp, stream, cu_seqlens != nullptr);
-                else launch_tc<kSchedChunked, kBf16, false>(clusters, maps, tp, stream, cu_seqlens != nullptr);
+                if (balanced) launch_tc<kSchedBalanced, kBf16, false>(clusters, maps, tp, stream, planned);
+                else launch_tc<kSchedChunked, kBf16, false>(clusters, maps, tp, stream, planned);
             }
             timing_mark(t_ev_stop, stream);
         } else if constexpr (!kBf16) {
@@ -537,7 +548,7 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
         }
     }
     // A dense batch decoded as one item per sequence is complete already.
-    if (tc_direct && cu_seqlens == nullptr && (balanced ? !bal_split : wl.cps == 1)) return launch_status();
+    if (tc_direct && !planned && (balanced ? !bal_split : wl.cps == 1)) return launch_status();
     const long long rows = (long long)batch * num_heads;
     const unsigned cgrid = (unsigned)rows;
     const int skip = tc_direct ? 1 : 0;
@@ -652,12 +663,25 @@ int decode_mtp(const void *query, const void *cache, const int32_t *cu_seqlens, 
     if (cu_seqlens != nullptr && max_seq_len == 0 && total_tokens > 0)
         return MLA_B200_ERR_INVALID_ARG;
     if (total_tokens >= (1LL << 31)) return MLA_B200_ERR_UNSUPPORTED;
-    if ((long long)num_tokens * num_heads > 128) return MLA_B200_ERR_UNSUPPORTED;
-    MtpArgs m{num_tokens, num_heads};
-    return run_split_decode<T>(static_cast<const T *>(query), static_cast<const T *>(cache),
-                               cu_seqlens, batch, num_tokens * num_heads, total_tokens, max_seq_len,
-                               softmax_scale, num_splits, out, out_dtype, out_lse, workspace,
-                               workspace_bytes, static_cast<cudaStream_t>(stream), nullptr, nullptr, &m);
+    if (num_heads > 128) return MLA_B200_ERR_UNSUPPORTED;
+    if ((long long)num_tokens * num_heads <= 128) {
+        // every draft token's rows in one 128-row tile: one pass over the cache
+        MtpArgs m{num_tokens, num_heads};
+        return run_split_decode<T>(static_cast<const T *>(query), static_cast<const T *>(cache),
+                                   cu_seqlens, batch, num_tokens * num_heads, total_tokens, max_seq_len,
+                                   softmax_scale, num_splits, out, out_dtype, out_lse, workspace,
+                                   workspace_bytes, static_cast<cudaStream_t>(stream), nullptr, nullptr, &m);
+    }
+    // More rows than one tile: each draft token runs as its own sequence of
+    // num_heads rows (query [batch, k, n_h] = [batch * k, n_h] sequences) over the
+    // real sequence's rows up to its causal limit.  The drafts of a sequence are
+    // neighbours on the balanced cost line, so their clusters read the same cache
+    // tiles at about the same time and the second read comes from L2.
+    if ((long long)batch * num_tokens >= (1LL << 31)) return MLA_B200_ERR_UNSUPPORTED;
+    return run_split_decode<T>(static_cast<const T *>(query), static_cast<const T *>(cache), cu_seqlens,
+                               batch * num_tokens, num_heads, total_tokens, max_seq_len, softmax_scale,
+                               num_splits, out, out_dtype, out_lse, workspace, workspace_bytes,
+                               static_cast<cudaStream_t>(stream), nullptr, nullptr, nullptr, num_tokens);
 }
 }  // namespace
 
@@ -758,6 +782,16 @@ size_t mla_b200_workspace_size(int batch, int num_heads, long long total_tokens,
 size_t mla_b200_workspace_size_fp8(int batch, int num_heads, long long total_tokens, int max_seq_len,
                                    int num_splits) {
     return workspace_bytes_for(batch, num_heads, total_tokens, max_seq_len, num_splits, true);
+}
+
+size_t mla_b200_workspace_size_mtp(int batch, int num_tokens, int num_heads, long long total_tokens,
+                                   int max_seq_len, int num_splits) {
+    if (batch < 0 || num_tokens <= 0 || num_heads <= 0 || total_tokens < 0) return 0;
+    if ((long long)num_tokens * num_heads <= 128)
+        return workspace_bytes_for(batch, num_tokens * num_heads, total_tokens, max_seq_len, num_splits, false);
+    if (max_seq_len <= 0 && batch > 0) max_seq_len = (int)cdiv(total_tokens, batch);
+    return workspace_bytes_for(batch * num_tokens, num_heads, total_tokens * num_tokens, max_seq_len,
+                               num_splits, false);
 }
 
 int mla_b200_decode_split_f16(const void *query, const void *cache, void *out, int num_heads,

@@ -308,7 +308,8 @@ __global__ void __launch_bounds__(1024) plan_varlen_kernel(const int32_t *cu_seq
                                                            int max_items,
                                                            const int32_t *seq_lens = nullptr,
                                                            int max_len = 0,
-                                                           int32_t *cu_out = nullptr) {
+                                                           int32_t *cu_out = nullptr,
+                                                           int group = 1, int dense_len = 0) {
     __shared__ int warp_tot[32];
     __shared__ int carry_s;
     griddep_launch();  // the decode kernel may start its set-up now
@@ -323,7 +324,7 @@ __global__ void __launch_bounds__(1024) plan_varlen_kernel(const int32_t *cu_seq
         const int b = base + tid;
         int cnt = 0;
         if (b < batch) {
-            const int len = cu_seqlens[b + 1] - cu_seqlens[b];
+            const int len = seq_len_of(cu_seqlens, dense_len, group, b);
             cnt = len > 0 ? (len + chunk - 1) / chunk : 0;
         }
         // block-wide inclusive scan of cnt
@@ -349,8 +350,8 @@ __global__ void __launch_bounds__(1024) plan_varlen_kernel(const int32_t *cu_seq
         const int excl = carry + (warp > 0 ? warp_tot[warp - 1] : 0) + v - cnt;
         if (b < batch) {
             item_off[b] = min(excl, max_items);
-            const int r0 = cu_seqlens[b];
-            const int r1 = cu_seqlens[b + 1];
+            const int r0 = (int)seq_row0_of(cu_seqlens, dense_len, group, b);
+            const int r1 = r0 + seq_len_of(cu_seqlens, dense_len, group, b);
             for (int c = 0; c < cnt && excl + c < max_items; ++c) {
                 const int s = r0 + c * chunk;
                 items[excl + c] = make_int4(b, s, min(s + chunk, r1), c * chunk);
@@ -371,7 +372,8 @@ __global__ void __launch_bounds__(1024) plan_balanced_kernel(const int32_t *cu_s
                                                              int *__restrict__ cost_off,
                                                              const int32_t *seq_lens = nullptr,
                                                              int max_len = 0,
-                                                             int32_t *cu_out = nullptr) {
+                                                             int32_t *cu_out = nullptr,
+                                                             int group = 1, int dense_len = 0) {
     __shared__ int warp_tot[32];
     __shared__ int carry_s;
     griddep_launch();  // the decode kernel may start its set-up now
@@ -386,7 +388,7 @@ __global__ void __launch_bounds__(1024) plan_balanced_kernel(const int32_t *cu_s
         const int b = base + tid;
         int cost = 0;
         if (b < batch) {
-            const int len = cu_seqlens[b + 1] - cu_seqlens[b];
+            const int len = seq_len_of(cu_seqlens, dense_len, group, b);
             cost = len > 0 ? (len + kTile - 1) / kTile + item_cost : 0;
         }
         int v = cost;

@@ -77,7 +77,29 @@ struct WorkList {
     int quota;                  // dense: cost units per worker
     int nworkers;               // varlen: workers the cost line is divided among
     int item_cost;              // fixed cost of an item in tiles (item_cost_for(num_heads))
+    int group;                  // >= 1; see seq_len_of
 };
+
+// Length of (virtual) sequence b.  group == 1: sequence b itself (cu_seqlens,
+// or dense_len for a dense cache).  group > 1 (multi-token decode with more
+// draft tokens than one 128-row tile holds): sequence b is draft token
+// d = b % group of real sequence b / group, reading that sequence's cache
+// rows up to its causal limit len - (group - 1 - d).
+__host__ __device__ __forceinline__ int seq_len_of(const int32_t *cu, int dense_len, int group, int b) {
+    const int r = group > 1 ? b / group : b;
+    int len = cu != nullptr ? cu[r + 1] - cu[r] : dense_len;
+    if (group > 1) {
+        len -= group - 1 - (b - r * group);
+        if (len < 0) len = 0;
+    }
+    return len;
+}
+
+// First cache row of (virtual) sequence b.
+__host__ __device__ __forceinline__ long long seq_row0_of(const int32_t *cu, int dense_len, int group, int b) {
+    const int r = group > 1 ? b / group : b;
+    return cu != nullptr ? (long long)cu[r] : (long long)r * dense_len;
+}
 
 struct Item {
     int b;
@@ -132,8 +154,8 @@ __device__ __forceinline__ SeqSpan seq_span(const WorkList &w, int b) {
         s.row0 = (long long)b * w.seq_len;
     } else {
         s.cost0 = w.cost_off[b];
-        s.row0 = w.cu_seqlens[b];
-        s.len = w.cu_seqlens[b + 1] - w.cu_seqlens[b];
+        s.row0 = seq_row0_of(w.cu_seqlens, w.seq_len, w.group, b);
+        s.len = seq_len_of(w.cu_seqlens, w.seq_len, w.group, b);
         s.tiles = (s.len + kTile - 1) / kTile;
     }
     return s;

@@ -34,9 +34,10 @@ cache bytes.
 mla_b200_decode_batched_fp8); the metric then counts the e4m3 bytes (576 per
 token), so compare us/step with the fp16 line.
 
-`--mtp K` decodes K draft tokens per sequence in one pass over the cache
-(mla_b200_decode_mtp_f16): the same bytes per step for K times the tokens
-(config keys `draft_tokens`, `tokens_per_step`).
+`--mtp K` decodes K draft tokens per sequence (mla_b200_decode_mtp_f16): one
+pass over the cache when K x n_h <= 128, else one 128-row pass per draft with
+the repeated reads served by L2; the metric counts each sequence's cache bytes
+once (config keys `draft_tokens`, `tokens_per_step`).
 
 `--dtype bf16` runs the step on bf16 copies of Q* and the cache
 (mla_b200_decode_batched_bf16, bf16 output); same bytes per token.
@@ -488,7 +489,7 @@ def run_ours(args):
         g = torch.Generator(device=dev).manual_seed(77 + rank)
         qm = (torch.randn((b, args.mtp, nh, HEAD_DIM_K), generator=g, device=dev) / 192 ** 0.5).half()
         qs = [qm] + [qm.clone() for _ in range(ring - 1)]
-        ws_bytes = capi.workspace_size(b, args.mtp * nh, total, maxlen, args.splits)
+        ws_bytes = lib.mla_b200_workspace_size_mtp(b, args.mtp, nh, total, maxlen, args.splits)
         ws = torch.empty(ws_bytes, dtype=torch.uint8, device=dev)
         out = torch.empty((b, args.mtp, nh, 512), dtype=torch.float16, device=dev)
     if fp8 and paged:

@@ -213,12 +213,18 @@ MLA_B200_API int mla_b200_decode_paged_bf16(const void *query, const void *kv_pa
  * reference): every sequence carries num_tokens queries, query [batch,
  * num_tokens, num_heads, 576], whose own latent rows are the last num_tokens
  * rows of the sequence's cache; draft token i sees the sequence's first
- * len - (num_tokens - 1 - i) tokens (len >= num_tokens).  The drafts share
- * every cache tile: rows token * num_heads + head fill one 128-row MMA tile, so
- * num_tokens * num_heads <= 128.  out [batch, num_tokens, num_heads, 512],
- * out_lse [batch, num_tokens, num_heads] or NULL; otherwise the contract of
- * mla_b200_decode_batched_f16 / _bf16 (workspace: mla_b200_workspace_size with
- * num_heads = num_tokens * num_heads). */
+ * len - (num_tokens - 1 - i) tokens (len >= num_tokens).  num_heads <= 128.
+ * When num_tokens * num_heads <= 128 the drafts share every cache tile (rows
+ * token * num_heads + head fill one 128-row MMA tile: one pass over the
+ * cache).  Above that (e.g. 128 heads) each draft token is decoded as its own
+ * sequence of num_heads rows over the same cache rows, scheduled next to the
+ * sequence's other drafts so their repeated tile reads come from L2.
+ * out [batch, num_tokens, num_heads, 512], out_lse [batch, num_tokens,
+ * num_heads] or NULL; otherwise the contract of mla_b200_decode_batched_f16 /
+ * _bf16.  Workspace: mla_b200_workspace_size_mtp. */
+MLA_B200_API size_t mla_b200_workspace_size_mtp(int batch, int num_tokens, int num_heads,
+                                                long long total_tokens, int max_seq_len,
+                                                int num_splits);
 MLA_B200_API int mla_b200_decode_mtp_f16(const void *query, const void *cache,
                                          const int32_t *cu_seqlens, int batch, int num_tokens,
                                          int num_heads, long long total_tokens, int max_seq_len,

@@ -88,9 +88,15 @@ def test_invalid_arguments_rejected_before_launch():
                                            None, None, 0, None) == capi.ERR_INVALID_ARG
     assert lib.mla_b200_workspace_size_fp8(2, 128, 200, 100, 1) >= \
         lib.mla_b200_workspace_size(2, 128, 200, 100, 1) + 2 * 2 * 128 * 576
-    # multi-token: more than 128 rows per sequence, zero tokens
-    assert lib.mla_b200_decode_mtp_f16(16, 16, None, 1, 2, 128, 64, 64, 1.0, 0, 16, capi.OUT_F16,
+    # multi-token: more than 128 heads, zero tokens
+    assert lib.mla_b200_decode_mtp_f16(16, 16, None, 1, 2, 256, 64, 64, 1.0, 0, 16, capi.OUT_F16,
                                        None, None, 0, None) == capi.ERR_UNSUPPORTED
+    # multi-token workspace: k x n_h <= 128 shares tiles (one sequence of k x n_h rows);
+    # above, one sequence of n_h rows per draft token
+    assert lib.mla_b200_workspace_size_mtp(3, 8, 16, 3000, 1000, -1) == \
+        lib.mla_b200_workspace_size(3, 128, 3000, 1000, -1)
+    assert lib.mla_b200_workspace_size_mtp(3, 4, 128, 3000, 1000, -1) == \
+        lib.mla_b200_workspace_size(12, 128, 12000, 1000, -1)
     assert lib.mla_b200_decode_mtp_f16(16, 16, None, 1, 0, 16, 64, 64, 1.0, 0, 16, capi.OUT_F16,
                                        None, None, 0, None) == capi.ERR_INVALID_ARG
     # fused fp32 requires head_dim_c = 576
