@@ -62,6 +62,10 @@ SIGNATURES = {
     "mla_b200_decode_naive_f32": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _vp]),
     "mla_b200_combine_f32": (_c_int, [_vp, _vp, _c_int, _c_ll, _vp, _c_int, _vp, _vp]),
     "mla_b200_combine_packed_f32": (_c_int, [_vp, _c_int, _c_ll, _c_ll, _vp, _c_int, _vp, _vp]),
+    "mla_b200_absorb_q_f16": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _vp]),
+    "mla_b200_absorb_q_bf16": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_int, _vp]),
+    "mla_b200_project_o_f16": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _vp]),
+    "mla_b200_project_o_bf16": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _vp]),
     "mla_b200_get_device_error": (_c_int, [ctypes.POINTER(_c_int), _vp]),
     "mla_b200_last_cuda_error": (_c_int, []),
 }
@@ -274,6 +278,28 @@ def combine_f32(part_o: torch.Tensor, part_lse: torch.Tensor, out_fp32: bool = T
         _ptr(part_o), _ptr(part_lse), p, rows, _ptr(out), OUT_F32 if out_fp32 else OUT_F16,
         _ptr(lse), _stream()))
     return out, lse
+
+
+def absorb_q(q_nope: torch.Tensor, q_rope: torch.Tensor, w_uk: torch.Tensor,
+             out: torch.Tensor | None = None) -> torch.Tensor:
+    """Q* [B, n_h, 576] = [q_nope . W_UK[h], q_rope] (mla_b200_absorb_q_f16 / _bf16)."""
+    b, nh, d = q_nope.shape
+    if out is None:
+        out = torch.empty((b, nh, 576), dtype=q_nope.dtype, device=q_nope.device)
+    name = "mla_b200_absorb_q_bf16" if q_nope.dtype == torch.bfloat16 else "mla_b200_absorb_q_f16"
+    _check(name, getattr(lib(), name)(_ptr(q_nope), _ptr(q_rope), _ptr(w_uk), _ptr(out), b, nh, d, _stream()))
+    return out
+
+
+def project_o(o_star: torch.Tensor, w_uv: torch.Tensor, out: torch.Tensor | None = None) -> torch.Tensor:
+    """out [B, n_h, d_v] = O*[b, h, :] . W_UV[h] (mla_b200_project_o_f16 / _bf16)."""
+    b, nh, _ = o_star.shape
+    dv = w_uv.shape[2]
+    if out is None:
+        out = torch.empty((b, nh, dv), dtype=o_star.dtype, device=o_star.device)
+    name = "mla_b200_project_o_bf16" if o_star.dtype == torch.bfloat16 else "mla_b200_project_o_f16"
+    _check(name, getattr(lib(), name)(_ptr(o_star), _ptr(w_uv), _ptr(out), b, nh, dv, _stream()))
+    return out
 
 
 def get_device_error() -> int:

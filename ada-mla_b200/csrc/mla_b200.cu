@@ -17,6 +17,7 @@
 #include "mla_combine.cuh"
 #include "mla_fp8.cuh"
 #include "mla_common.cuh"
+#include "mla_proj.cuh"
 #include "mla_simt.cuh"
 #include "mla_tc.cuh"
 
@@ -31,6 +32,7 @@ struct DevInfo {
     int sms = 0;
     int major = 0;
     bool simt_attr_set = false;
+    bool proj_attr_set = false;
     int tc_clusters = 0;  // co-resident 2-CTA clusters of the tcgen05 decode kernel
 };
 
@@ -84,6 +86,12 @@ int current_device(int *dev_out, DevInfo *info_out) {
             return cuda_failure(cudaGetLastError());
         }
         d.simt_attr_set = true;
+    }
+    if (!d.proj_attr_set) {
+        if (cudaFuncSetAttribute(proj::proj_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                 proj::kSmemBudget + 4096) != cudaSuccess)
+            return cuda_failure(cudaGetLastError());
+        d.proj_attr_set = true;
     }
     if (d.tc_clusters == 0) {
         if (!set_tc_smem<false, false>() || !set_tc_smem<true, false>() ||
@@ -685,7 +693,103 @@ int decode_mtp(const void *query, const void *cache, const int32_t *cu_seqlens, 
 }
 }  // namespace
 
+namespace {
+// Y[b, h, m] = sum_k X[b, h, k] W[h, k, m] for every head (proj::proj_kernel):
+// X [batch, heads, k_total], W [heads, k_total, m_total], Y element (b, h, m)
+// at out[b * out_b + h * out_h + m]; rope (or null): [batch, heads, 64] copied
+// to out[b * out_b + h * out_h + m_total + j].
+template <bool kBf16>
+int run_proj(const void *x, const void *w, const void *rope, void *out, int batch, int heads, int k_total,
+             int m_total, long long out_b, long long out_h, cudaStream_t stream) {
+    if (batch < 0 || heads <= 0 || k_total <= 0 || m_total <= 0) return MLA_B200_ERR_INVALID_ARG;
+    if (batch > 0 && (x == nullptr || w == nullptr || out == nullptr)) return MLA_B200_ERR_INVALID_ARG;
+    if (!aligned(x, 16) || !aligned(w, 16) || !aligned(out, 16) || !aligned(rope, 16))
+        return MLA_B200_ERR_INVALID_ARG;
+    if (k_total % proj::kStageK != 0 || m_total % proj::kTileM != 0) return MLA_B200_ERR_UNSUPPORTED;
+    if ((long long)batch * heads * (long long)(k_total > m_total ? k_total : m_total) >= (1LL << 40))
+        return MLA_B200_ERR_UNSUPPORTED;
+    int dev;
+    DevInfo info;
+    int st = current_device(&dev, &info);
+    if (st != MLA_B200_OK) return st;
+    if (batch == 0) return MLA_B200_OK;
+    auto enc = tmap_encoder();
+    if (enc == nullptr) return cuda_failure(cudaErrorSymbolNotFound);
+    proj::ProjParams p;
+    p.batch = batch;
+    p.heads = heads;
+    p.k_total = k_total;
+    p.m_total = m_total;
+    p.n_box = std::min(256, (batch + 15) / 16 * 16);
+    p.units_m = m_total / proj::kTileM;
+    p.units_n = (int)cdiv(batch, p.n_box);
+    const long long units = (long long)heads * p.units_m * p.units_n;
+    if (units >= (1LL << 31)) return MLA_B200_ERR_UNSUPPORTED;
+    p.units = (int)units;
+    p.stage_bytes = 2 * proj::kBoxA + p.n_box * 128;
+    p.stages = std::max(2, std::min(proj::kMaxStages, proj::kSmemBudget / p.stage_bytes));
+    p.out = out;
+    p.out_b = out_b;
+    p.out_h = out_h;
+    p.bf16 = kBf16 ? 1 : 0;
+    p.rope = rope;
+    const CUtensorMapDataType dt = kBf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+    const cuuint32_t estr[3] = {1, 1, 1};
+    CUtensorMap wmap, xmap;
+    {
+        const cuuint64_t dims[3] = {(cuuint64_t)m_total, (cuuint64_t)k_total, (cuuint64_t)heads};
+        const cuuint64_t strides[2] = {(cuuint64_t)m_total * 2, (cuuint64_t)k_total * m_total * 2};
+        const cuuint32_t box[3] = {64, (cuuint32_t)proj::kStageK, 1};
+        if (enc(&wmap, dt, 3, const_cast<void *>(w), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cuda_failure(cudaErrorInvalidValue);
+    }
+    {
+        const cuuint64_t dims[3] = {(cuuint64_t)k_total, (cuuint64_t)heads, (cuuint64_t)batch};
+        const cuuint64_t strides[2] = {(cuuint64_t)k_total * 2, (cuuint64_t)heads * k_total * 2};
+        const cuuint32_t box[3] = {(cuuint32_t)proj::kStageK, 1, (cuuint32_t)p.n_box};
+        if (enc(&xmap, dt, 3, const_cast<void *>(x), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) != CUDA_SUCCESS)
+            return cuda_failure(cudaErrorInvalidValue);
+    }
+    const size_t smem = (size_t)p.stages * p.stage_bytes + proj::kNumBars * 8 + 16 + 1024;
+    const int grid = std::min(p.units, info.sms);
+    timing_mark(t_ev_start, stream);
+    launch_dependent(proj::proj_kernel, dim3(grid), dim3(proj::kThreads), smem, stream, false, wmap, xmap, p);
+    timing_mark(t_ev_stop, stream);
+    return launch_status();
+}
+}  // namespace
+
 extern "C" {
+
+int mla_b200_absorb_q_f16(const void *q_nope, const void *q_rope, const void *w_uk, void *q_star, int batch,
+                          int num_heads, int head_dim, void *stream) {
+    if (batch > 0 && q_rope == nullptr) return MLA_B200_ERR_INVALID_ARG;
+    return run_proj<false>(q_nope, w_uk, q_rope, q_star, batch, num_heads, head_dim, kDV,
+                           (long long)num_heads * kDK, kDK, static_cast<cudaStream_t>(stream));
+}
+
+int mla_b200_absorb_q_bf16(const void *q_nope, const void *q_rope, const void *w_uk, void *q_star, int batch,
+                           int num_heads, int head_dim, void *stream) {
+    if (batch > 0 && q_rope == nullptr) return MLA_B200_ERR_INVALID_ARG;
+    return run_proj<true>(q_nope, w_uk, q_rope, q_star, batch, num_heads, head_dim, kDV,
+                          (long long)num_heads * kDK, kDK, static_cast<cudaStream_t>(stream));
+}
+
+int mla_b200_project_o_f16(const void *o_star, const void *w_uv, void *out, int batch, int num_heads,
+                           int head_dim_v, void *stream) {
+    return run_proj<false>(o_star, w_uv, nullptr, out, batch, num_heads, kDV, head_dim_v,
+                           (long long)num_heads * head_dim_v, head_dim_v, static_cast<cudaStream_t>(stream));
+}
+
+int mla_b200_project_o_bf16(const void *o_star, const void *w_uv, void *out, int batch, int num_heads,
+                            int head_dim_v, void *stream) {
+    return run_proj<true>(o_star, w_uv, nullptr, out, batch, num_heads, kDV, head_dim_v,
+                          (long long)num_heads * head_dim_v, head_dim_v, static_cast<cudaStream_t>(stream));
+}
 
 const char *mla_b200_status_string(int status) {
     switch (status) {

@@ -817,6 +817,74 @@ def run_kv(args):
         dist.destroy_process_group()
 
 
+def run_absorbed(args):
+    """--mode absorbed: the projections on either side of the decode, on the
+    tcgen05 projection kernel, for config --config's batch at 128 heads (d = d_v
+    = 128): Q absorption alone, O projection alone (weight-read GB/s: each layer
+    has its own weights, so a ring of weight copies >= 3x L2 is cycled), and the
+    whole step absorb -> decode -> project.  The same products through torch.bmm
+    (cuBLAS) are timed alongside."""
+    import torch
+
+    rank, world, local = dist_init()
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    from ada_mla import absorbed, capi
+    from ada_mla.workloads import make_workload
+
+    wl = make_workload(args.config, seed=0, device=dev)
+    b, nh, d, dv = wl.batch, wl.num_heads, 128, 128
+    g = torch.Generator(device=dev).manual_seed(5)
+    q_nope = (torch.randn((b, nh, d), generator=g, device=dev)).half()
+    q_rope = (torch.randn((b, nh, 64), generator=g, device=dev) / 192 ** 0.5).half()
+    w_bytes = nh * d * 512 * 2
+    ring = _ring_len(2 * w_bytes, dev)
+    w_uk = [(torch.randn((nh, d, 512), generator=g, device=dev) / 512 ** 0.5).half() for _ in range(ring)]
+    w_uv = [(torch.randn((nh, 512, dv), generator=g, device=dev) / 512 ** 0.5).half() for _ in range(ring)]
+    o_star = torch.randn((b, nh, 512), generator=g, device=dev).half()
+    q_star = torch.empty((b, nh, 576), dtype=torch.float16, device=dev)
+    out = torch.empty((b, nh, dv), dtype=torch.float16, device=dev)
+    it = [0]
+    steps = max(10, min(args.steps, 100))
+
+    def timed(fn):
+        it[0] = 0
+
+        def step():
+            fn(it[0] % ring)
+            it[0] += 1
+
+        graph = _graph_of(step, steps)
+        ms, clocks = timed_replay(graph, steps, world, local)
+        del graph
+        return ms * 1e3, clocks.get("sm_mhz")
+
+    res = {}
+    us, mhz = timed(lambda i: capi.absorb_q(q_nope, q_rope, w_uk[i], q_star))
+    res["absorb_q"] = {"us": us, "weight_GBps": w_bytes / (us * 1e-6) / 1e9, "sm_mhz": mhz}
+    us, mhz = timed(lambda i: capi.project_o(o_star, w_uv[i], out))
+    res["project_o"] = {"us": us, "weight_GBps": w_bytes / (us * 1e-6) / 1e9, "sm_mhz": mhz}
+    us, _ = timed(lambda i: torch.bmm(q_nope.transpose(0, 1), w_uk[i], out=q_star.new_empty((nh, b, 512))))
+    res["absorb_q_torch_bmm"] = {"us": us, "weight_GBps": w_bytes / (us * 1e-6) / 1e9}
+    us, _ = timed(lambda i: torch.bmm(o_star.transpose(0, 1), w_uv[i]))
+    res["project_o_torch_bmm"] = {"us": us, "weight_GBps": w_bytes / (us * 1e-6) / 1e9}
+    cache = wl.cache
+    us_dec, _ = timed(lambda i: absorbed.mla_decode_batched(q_star, cache, wl.cu_seqlens,
+                                                            max_seq_len=wl.max_seq_len, softmax_scale=1.0))
+    us, mhz = timed(lambda i: absorbed.mla_decode_absorbed(
+        q_nope, q_rope, w_uk[i], cache, w_uv[i], wl.cu_seqlens, max_seq_len=wl.max_seq_len, softmax_scale=1.0))
+    res["pipeline"] = {"us": us, "decode_only_us": us_dec, "sm_mhz": mhz}
+    if rank == 0:
+        print(json.dumps({"mode": "absorbed", "config": {"workload": f"cfg{args.config}: B={b} n_h={nh} d={d} "
+                                                                     f"d_v={dv} fp16, weights ring x{ring}"},
+                          "hbm_peak_GBps": _peaks()[0], "results": res}), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+        dist.destroy_process_group()
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -838,9 +906,10 @@ def main():
     ap.add_argument("--no-multi", action="store_true",
                     help="skip the multi_gpu lines (cfg3 KV split, cfg2 sharded)")
     ap.add_argument("--no-rotate", action="store_true")
-    ap.add_argument("--mode", default="shard", choices=["shard", "kv"],
+    ap.add_argument("--mode", default="shard", choices=["shard", "kv", "absorbed"],
                     help="shard: every rank decodes its own sequence(s), no collective (default); "
-                         "kv: only the KV-split line of --config")
+                         "kv: only the KV-split line of --config; absorbed: the projections around "
+                         "the decode and the whole absorbed step")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
@@ -848,6 +917,8 @@ def main():
         run_reference_arm(args)
     elif args.mode == "kv":
         run_kv(args)
+    elif args.mode == "absorbed":
+        run_absorbed(args)
     else:
         run_ours(args)
 

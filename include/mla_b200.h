@@ -301,6 +301,37 @@ MLA_B200_API int mla_b200_decode_split_f16_noalloc(const void *query, const void
                                                    void *stream);
 
 /* ------------------------------------------------------------------------ */
+/* The per-head projections on either side of the decode                     */
+/* ------------------------------------------------------------------------ */
+
+/* Q absorption (no kernel counterpart in the reference, whose README.md:74-110
+ * derives it and leaves it to the caller):
+ *   q_star[b, h, 0:512]   = q_nope[b, h, :] . w_uk[h]     (fp32 accumulate)
+ *   q_star[b, h, 512:576] = q_rope[b, h, :]
+ * q_nope [batch, num_heads, head_dim], q_rope [batch, num_heads, 64],
+ * w_uk [num_heads, head_dim, 512], q_star [batch, num_heads, 576], all fp16
+ * (_f16) or all bf16 (_bf16), 16-byte aligned; head_dim a multiple of 64.
+ * A tcgen05 kernel streams every weight byte from HBM once (swap-AB: weights on
+ * the MMA's M side, the batch on N).  It signals programmatic launch
+ * completion early, so a decode launched after it may overlap its set-up. */
+MLA_B200_API int mla_b200_absorb_q_f16(const void *q_nope, const void *q_rope, const void *w_uk,
+                                       void *q_star, int batch, int num_heads, int head_dim,
+                                       void *stream);
+MLA_B200_API int mla_b200_absorb_q_bf16(const void *q_nope, const void *q_rope, const void *w_uk,
+                                        void *q_star, int batch, int num_heads, int head_dim,
+                                        void *stream);
+
+/* Per-head value projection of O* (no reference counterpart):
+ *   out[b, h, :] = o_star[b, h, :] . w_uv[h]
+ * o_star [batch, num_heads, 512], w_uv [num_heads, 512, head_dim_v],
+ * out [batch, num_heads, head_dim_v]; fp16 or bf16 throughout; head_dim_v a
+ * multiple of 128.  Same kernel as mla_b200_absorb_q_*. */
+MLA_B200_API int mla_b200_project_o_f16(const void *o_star, const void *w_uv, void *out, int batch,
+                                        int num_heads, int head_dim_v, void *stream);
+MLA_B200_API int mla_b200_project_o_bf16(const void *o_star, const void *w_uv, void *out, int batch,
+                                         int num_heads, int head_dim_v, void *stream);
+
+/* ------------------------------------------------------------------------ */
 /* Log-sum-exp merge of partial results                                      */
 /* ------------------------------------------------------------------------ */
 

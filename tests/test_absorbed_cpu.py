@@ -1,11 +1,22 @@
 """CPU check of the weight-absorption algebra around the decode
 (ada_mla.absorbed): absorbing W_UK into Q* and projecting O* by W_UV equals
 per-head attention over up-projected keys and values.  The decode step itself
-is a torch fp32 restatement here (the kernel's parity is covered on the GPU)."""
+is a torch fp32 restatement here, and so are the two projections (the
+definitions the tcgen05 projection kernels implement; their parity is covered
+on the GPU)."""
 import numpy as np
 import torch
 
-from ada_mla import absorbed
+
+
+def absorb_ref(q_nope, q_rope, w_uk):
+    """Q*[b, h] = [q_nope[b, h] . W_UK[h], q_rope[b, h]]"""
+    return torch.cat([torch.einsum("bhd,hdc->bhc", q_nope, w_uk), q_rope], dim=-1)
+
+
+def project_ref(o_star, w_uv):
+    """o[b, h] = O*[b, h] . W_UV[h]"""
+    return torch.einsum("bhc,hcv->bhv", o_star, w_uv)
 
 
 def _decode_fp32(q_star, c, scale):
@@ -22,9 +33,9 @@ def test_absorption_algebra():
     q_rope = torch.randn(b, nh, 64, dtype=torch.float64)
     w_uk = torch.randn(nh, dn, 512, dtype=torch.float64) / 512 ** 0.5
     w_uv = torch.randn(nh, 512, dv, dtype=torch.float64) / 512 ** 0.5
-    q_star = absorbed.absorb_query(q_nope, q_rope, w_uk)
+    q_star = absorb_ref(q_nope, q_rope, w_uk)
     assert q_star.shape == (b, nh, 576)
-    out = absorbed.project_output(_decode_fp32(q_star, c, scale), w_uv)
+    out = project_ref(_decode_fp32(q_star, c, scale), w_uv)
     k_nope = torch.einsum("bnc,hdc->bhnd", c[:, :, :512], w_uk)
     v = torch.einsum("bnc,hcv->bhnv", c[:, :, :512], w_uv)
     logits = (torch.einsum("bhd,bhnd->bhn", q_nope, k_nope)
@@ -36,7 +47,11 @@ def test_absorption_algebra():
 def test_shape_errors():
     import pytest
 
+    from ada_mla import absorbed
+
     with pytest.raises(ValueError):
         absorbed.absorb_query(torch.zeros(1, 4, 128), torch.zeros(1, 4, 64), torch.zeros(4, 64, 512))
     with pytest.raises(ValueError):
         absorbed.project_output(torch.zeros(1, 4, 512), torch.zeros(3, 512, 128))
+    with pytest.raises(ValueError):  # the kernels take CUDA tensors only: no CPU path
+        absorbed.absorb_query(torch.zeros(1, 4, 128), torch.zeros(1, 4, 64), torch.zeros(4, 128, 512))
