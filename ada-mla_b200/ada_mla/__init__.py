@@ -78,15 +78,18 @@ ext_path = EXT_PATH
 
 def mla_decode_batched(query, cache, cu_seqlens=None, max_seq_len: int = -1,
                        softmax_scale: float = SOFTMAX_SCALE, num_splits: int = -1,
-                       return_lse: bool = False, out_dtype=None, kv_scale: float = 1.0):
+                       return_lse: bool = False, out_dtype=None, kv_scale=1.0):
     """Batched / variable-length decode: fp16 or bf16, or an fp8 (e4m3) cache.
 
     query  [B, n_h, 576] fp16 or bf16 (bf16 and fp8 cache: n_h <= 128).
     cache  dense [B, N, 576], or packed [T, 576] with ``cu_seqlens`` int32
            [B+1] (sequence b owns rows cu_seqlens[b]:cu_seqlens[b+1]), in the
            query's dtype -- or torch.float8_e4m3fn with an fp16 query, the
-           cache then being ``cache * kv_scale``.  Pass ``max_seq_len`` to
-           avoid a device->host read of the longest length.
+           cache then being ``cache * kv_scale``: a float (one scale for the
+           tensor) or an fp32 CUDA tensor with one scale per cache row
+           ([T] packed, [B, N] dense; a per-page or per-tile scale is its value
+           repeated over the rows).  Pass ``max_seq_len`` to avoid a
+           device->host read of the longest length.
     Returns O* [B, n_h, 512] (the query's dtype, or fp32 when
     ``out_dtype=torch.float32``) and, with ``return_lse``, the natural-log LSE
     [B, n_h] fp32 as a tuple.
@@ -94,6 +97,23 @@ def mla_decode_batched(query, cache, cu_seqlens=None, max_seq_len: int = -1,
     if out_dtype not in (None, torch.float32, query.dtype):
         raise ValueError(f"mla_decode_batched: out_dtype must be None, float32 or {query.dtype}")
     out_fp32 = out_dtype == torch.float32
+    if isinstance(kv_scale, torch.Tensor):
+        from . import capi
+
+        if cache.dtype != torch.float8_e4m3fn or query.dtype != torch.float16:
+            raise ValueError("mla_decode_batched: per-row kv scales need an e4m3 cache and an fp16 query")
+        rows = cache.shape[0] * (cache.shape[1] if cu_seqlens is None else 1)
+        if (not kv_scale.is_cuda or kv_scale.dtype != torch.float32 or kv_scale.numel() != rows
+                or not kv_scale.is_contiguous()):
+            raise ValueError("mla_decode_batched: kv_scale tensor must be contiguous fp32 CUDA, one per cache row")
+        if cu_seqlens is None:
+            max_seq_len = cache.shape[1]
+        elif max_seq_len < 0:
+            max_seq_len = int((cu_seqlens[1:] - cu_seqlens[:-1]).max().item()) if cache.shape[0] else 0
+        c2 = cache.reshape(-1, cache.shape[-1]) if cu_seqlens is None else cache
+        res = capi.decode_batched_fp8_scaled(query, c2, kv_scale, cu_seqlens, int(max_seq_len), float(softmax_scale),
+                                             int(num_splits), out_fp32=out_fp32, return_lse=return_lse)
+        return res
     out, lse = _ext.mla_decode_batched(query, cache, cu_seqlens, int(max_seq_len),
                                        float(softmax_scale), int(num_splits),
                                        bool(return_lse), out_fp32, float(kv_scale))

@@ -50,6 +50,8 @@ SIGNATURES = {
                                               _c_int, _vp, _c_int, _vp, _vp, _c_size, _vp]),
     "mla_b200_decode_batched_fp8": (_c_int, [_vp, _vp, _c_float, _vp, _c_int, _c_int, _c_ll, _c_int,
                                              _c_float, _c_int, _vp, _c_int, _vp, _vp, _c_size, _vp]),
+    "mla_b200_decode_batched_fp8_scaled": (_c_int, [_vp, _vp, _vp, _vp, _c_int, _c_int, _c_ll, _c_int,
+                                                    _c_float, _c_int, _vp, _c_int, _vp, _vp, _c_size, _vp]),
     "mla_b200_decode_mtp_f16": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _c_ll, _c_int, _c_float,
                                          _c_int, _vp, _c_int, _vp, _vp, _c_size, _vp]),
     "mla_b200_decode_mtp_bf16": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _c_ll, _c_int, _c_float,
@@ -68,6 +70,7 @@ SIGNATURES = {
     "mla_b200_project_o_bf16": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_int, _vp]),
     "mla_b200_get_device_error": (_c_int, [ctypes.POINTER(_c_int), _vp]),
     "mla_b200_last_cuda_error": (_c_int, []),
+    "mla_b200_selftest_wait_timeout": (_c_int, [ctypes.c_ulonglong, _vp, _vp]),
 }
 
 _lib: ctypes.CDLL | None = None
@@ -223,6 +226,22 @@ def decode_batched_fp8(query: torch.Tensor, cache: torch.Tensor, kv_scale: float
     ws = _workspace(ws_bytes, query.device)
     _check("mla_b200_decode_batched_fp8", lib().mla_b200_decode_batched_fp8(
         _ptr(query), _ptr(cache), float(kv_scale), _ptr(cu_seqlens), b, nh, total, max_seq_len,
+        float(softmax_scale), num_splits, _ptr(out), OUT_F32 if out_fp32 else OUT_F16, _ptr(lse),
+        _ptr(ws), ws.numel(), _stream()))
+    return (out, lse) if return_lse else out
+
+
+def decode_batched_fp8_scaled(query: torch.Tensor, cache: torch.Tensor, kv_scales: torch.Tensor,
+                              cu_seqlens: torch.Tensor | None, max_seq_len: int, softmax_scale: float,
+                              num_splits: int = -1, out_fp32: bool = False, return_lse: bool = False):
+    """Decode over an e4m3 cache with one scale per cache row (C[t] = cache[t] * kv_scales[t])."""
+    b, nh = query.shape[0], query.shape[1]
+    total = cache.shape[0] if cu_seqlens is not None else b * max_seq_len
+    out = torch.empty((b, nh, 512), dtype=torch.float32 if out_fp32 else torch.float16, device=query.device)
+    lse = torch.empty((b, nh), dtype=torch.float32, device=query.device) if return_lse else None
+    ws = _workspace(lib().mla_b200_workspace_size_fp8(b, nh, total, max_seq_len, num_splits), query.device)
+    _check("mla_b200_decode_batched_fp8_scaled", lib().mla_b200_decode_batched_fp8_scaled(
+        _ptr(query), _ptr(cache), _ptr(kv_scales), _ptr(cu_seqlens), b, nh, total, max_seq_len,
         float(softmax_scale), num_splits, _ptr(out), OUT_F32 if out_fp32 else OUT_F16, _ptr(lse),
         _ptr(ws), ws.numel(), _stream()))
     return (out, lse) if return_lse else out

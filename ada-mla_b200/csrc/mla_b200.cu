@@ -154,6 +154,8 @@ int encode_tmap(CUtensorMap *map, const void *base, cuuint32_t rank, const cuuin
 
 // e4m3 cache [rows, 576] (one byte per element), GEMM1 side: (64 B, rows, 9
 // K-blocks) with 64-byte swizzle, one box = 3 K-blocks x 96 rows (an fp8 S slot).
+// (Boxes of 128-byte rows with 128-byte swizzle, one K-block per 12 KB slot,
+// measured slower: cfg3 89.8 vs 77.1 us per step.)
 int make_tmap_fp8_s(CUtensorMap *map, const void *base, long long rows) {
     const cuuint64_t dims[3] = {64, (cuuint64_t)rows, (cuuint64_t)(kDK / 64)};
     const cuuint64_t strides[2] = {(cuuint64_t)kDK, 64};
@@ -324,6 +326,7 @@ int launch_status() {
 struct Fp8Args {
     const void *cache8;
     float kv_scale;
+    const float *kv_scales;  // or null: per cache row scales [rows]
 };
 
 // Multi-token decode: each sequence carries `tokens` draft-token queries of
@@ -476,6 +479,13 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
                                                    group, max_seq_len);
     }
     bool tc_direct = false;  // the tcgen05 kernel wrote single-item sequences itself
+    // A few long sequences chain decode -> merge -> next decode with programmatic
+    // launches (each kernel waits before it touches its predecessor's data): the
+    // merge is one short wave there, and its launch gap is a tenth of the step.
+    // Batches do not: the next decode's early CTAs would hold SMs that their
+    // larger merge still needs (same-box A/B: cfg1 -1.2 us, cfg3 -1.4 us, cfg2
+    // B=128 +3 us).
+    const bool chain = batch < 8;
     if (wl.max_items > 0 && (!balanced || bal_clusters > 0)) {
         if (tc_path) {
             TcMaps maps;
@@ -519,32 +529,35 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
             tp.max_blocks = pg != nullptr ? pg->max_blocks : 0;
             if (mtp != nullptr) tp.mtp = (mtp->tokens << 16) | mtp->heads;
             if (f8 != nullptr) {
-                // S = kv_scale * q_scale[row] * (Q8.C8); O = kv_scale * (P8.C8) / (kP8Scale * l)
-                tp.scale_log2 = scale * kLog2e * f8->kv_scale;
+                // S = kv_scale * q_scale[row] * (Q8.C8); O = kv_scale * (P8.C8) / l, the
+                // weights' factor kP8Scale in l too (per-row scales: applied per column in
+                // the kernel, kv_scale = 1 here)
+                tp.scale_log2 = scale * kLog2e * (f8->kv_scales != nullptr ? 1.f : f8->kv_scale);
                 tp.q_scale = L.q_scale;
-                tp.o_scale = f8->kv_scale / tc::kP8Scale;
+                tp.o_scale = f8->kv_scales != nullptr ? 1.f : f8->kv_scale;
             } else {
                 tp.block_table = pg != nullptr ? pg->block_table : nullptr;
                 tp.page_size = pg != nullptr ? pg->page_size : 0;
             }
             tp.span = next_span();
+            tp.kv_scales = f8 != nullptr ? f8->kv_scales : nullptr;
             tc_direct = true;
             const int clusters = balanced ? bal_clusters : std::min(info.tc_clusters, wl.max_items);
             timing_mark(t_ev_start, stream);
             if (mtp != nullptr) {
-                if (balanced) launch_tc<kSchedBalanced, kBf16, false, false, true>(clusters, maps, tp, stream, planned);
-                else launch_tc<kSchedChunked, kBf16, false, false, true>(clusters, maps, tp, stream, planned);
+                if (balanced) launch_tc<kSchedBalanced, kBf16, false, false, true>(clusters, maps, tp, stream, planned || chain);
+                else launch_tc<kSchedChunked, kBf16, false, false, true>(clusters, maps, tp, stream, planned || chain);
             } else if (f8 != nullptr) {
                 if constexpr (!kBf16) {  // (fp8 runs with fp16 Q*; the prep kernel precedes)
                     if (balanced) launch_tc<kSchedBalanced, false, false, true>(clusters, maps, tp, stream, true);
                     else launch_tc<kSchedChunked, false, false, true>(clusters, maps, tp, stream, true);
                 }
             } else if (pg != nullptr) {
-                if (balanced) launch_tc<kSchedBalanced, kBf16, true>(clusters, maps, tp, stream, planned);
-                else launch_tc<kSchedChunked, kBf16, true>(clusters, maps, tp, stream, planned);
+                if (balanced) launch_tc<kSchedBalanced, kBf16, true>(clusters, maps, tp, stream, planned || chain);
+                else launch_tc<kSchedChunked, kBf16, true>(clusters, maps, tp, stream, planned || chain);
             } else {
-                if (balanced) launch_tc<kSchedBalanced, kBf16, false>(clusters, maps, tp, stream, planned);
-                else launch_tc<kSchedChunked, kBf16, false>(clusters, maps, tp, stream, planned);
+                if (balanced) launch_tc<kSchedBalanced, kBf16, false>(clusters, maps, tp, stream, planned || chain);
+                else launch_tc<kSchedChunked, kBf16, false>(clusters, maps, tp, stream, planned || chain);
             }
             timing_mark(t_ev_stop, stream);
         } else if constexpr (!kBf16) {
@@ -570,17 +583,17 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
         const float *po = L.part_o;
         const __half *ph = reinterpret_cast<const __half *>(L.part_o);
         if (out_dtype == MLA_B200_OUT_BF16)
-            launch_dependent(combine_rows_kernel<__nv_bfloat16, __nv_bfloat16>, rgrid, rblock, 0, stream, false,
+            launch_dependent(combine_rows_kernel<__nv_bfloat16, __nv_bfloat16>, rgrid, rblock, 0, stream, chain,
                              reinterpret_cast<const __nv_bfloat16 *>(L.part_o), L.part_lse, wl, num_heads,
                              static_cast<__nv_bfloat16 *>(out), out_lse, skip);
         else if (out_dtype == MLA_B200_OUT_F16 && tc_direct)
-            launch_dependent(combine_rows_kernel<__half, __half>, rgrid, rblock, 0, stream, false, ph, L.part_lse,
+            launch_dependent(combine_rows_kernel<__half, __half>, rgrid, rblock, 0, stream, chain, ph, L.part_lse,
                              wl, num_heads, static_cast<__half *>(out), out_lse, skip);
         else if (out_dtype == MLA_B200_OUT_F16)
-            launch_dependent(combine_rows_kernel<__half, float>, rgrid, rblock, 0, stream, false, po, L.part_lse,
+            launch_dependent(combine_rows_kernel<__half, float>, rgrid, rblock, 0, stream, chain, po, L.part_lse,
                              wl, num_heads, static_cast<__half *>(out), out_lse, skip);
         else
-            launch_dependent(combine_rows_kernel<float, float>, rgrid, rblock, 0, stream, false, po, L.part_lse,
+            launch_dependent(combine_rows_kernel<float, float>, rgrid, rblock, 0, stream, chain, po, L.part_lse,
                              wl, num_heads, static_cast<float *>(out), out_lse, skip);
         return launch_status();
     }
@@ -589,17 +602,17 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     const dim3 cblock(kCombineThreads);
     const size_t ps = (size_t)num_heads * kDV, ls = (size_t)num_heads;
     if (out_dtype == MLA_B200_OUT_BF16)
-        launch_dependent(combine_kernel<__nv_bfloat16, __nv_bfloat16>, dim3(cgrid), cblock, 0, stream, false,
+        launch_dependent(combine_kernel<__nv_bfloat16, __nv_bfloat16>, dim3(cgrid), cblock, 0, stream, chain,
                          reinterpret_cast<const __nv_bfloat16 *>(L.part_o), L.part_lse, wl, num_heads, rows,
                          static_cast<__nv_bfloat16 *>(out), out_lse, skip, ps, ls);
     else if (out_dtype == MLA_B200_OUT_F16 && tc_direct)
-        launch_dependent(combine_kernel<__half, __half>, dim3(cgrid), cblock, 0, stream, false, ph, L.part_lse,
+        launch_dependent(combine_kernel<__half, __half>, dim3(cgrid), cblock, 0, stream, chain, ph, L.part_lse,
                          wl, num_heads, rows, static_cast<__half *>(out), out_lse, skip, ps, ls);
     else if (out_dtype == MLA_B200_OUT_F16)
-        launch_dependent(combine_kernel<__half, float>, dim3(cgrid), cblock, 0, stream, false, po, L.part_lse,
+        launch_dependent(combine_kernel<__half, float>, dim3(cgrid), cblock, 0, stream, chain, po, L.part_lse,
                          wl, num_heads, rows, static_cast<__half *>(out), out_lse, skip, ps, ls);
     else
-        launch_dependent(combine_kernel<float, float>, dim3(cgrid), cblock, 0, stream, false, po, L.part_lse,
+        launch_dependent(combine_kernel<float, float>, dim3(cgrid), cblock, 0, stream, chain, po, L.part_lse,
                          wl, num_heads, rows, static_cast<float *>(out), out_lse, skip, ps, ls);
     return launch_status();
 }
@@ -690,6 +703,21 @@ int decode_mtp(const void *query, const void *cache, const int32_t *cu_seqlens, 
                                batch * num_tokens, num_heads, total_tokens, max_seq_len, softmax_scale,
                                num_splits, out, out_dtype, out_lse, workspace, workspace_bytes,
                                static_cast<cudaStream_t>(stream), nullptr, nullptr, nullptr, num_tokens);
+}
+}  // namespace
+
+namespace {
+// Bounded-wait self test: one thread waits on an mbarrier that nothing will
+// complete, with the given limit, through the same wait loop the decode kernels
+// use; the wait records kErrSelfTest in the device error word and returns,
+// and the kernel writes whether it returned to *done.
+__global__ void wait_selftest_kernel(uint64_t limit_ns, int *done) {
+    __shared__ __align__(8) uint64_t bar;
+    const uint32_t b = ptx::smem_u32(&bar);
+    ptx::mbar_init(b, 1);
+    asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+    const bool ok = ptx::mbar_wait(b, 0, kErrSelfTest, limit_ns);  // phase 0 never completes
+    *done = ok ? 2 : 1;
 }
 }  // namespace
 
@@ -1005,11 +1033,39 @@ int mla_b200_decode_mtp_bf16(const void *query, const void *cache, const int32_t
                                      out_dtype, out_lse, workspace, workspace_bytes, stream);
 }
 
+namespace {
+int decode_fp8(const void *query, const void *cache, float kv_scale, const float *kv_scales,
+               const int32_t *cu_seqlens, int batch, int num_heads, long long total_tokens, int max_seq_len,
+               float softmax_scale, int num_splits, void *out, int out_dtype, float *out_lse, void *workspace,
+               size_t workspace_bytes, void *stream);
+}  // namespace
+
 int mla_b200_decode_batched_fp8(const void *query, const void *cache, float kv_scale,
                                 const int32_t *cu_seqlens, int batch, int num_heads,
                                 long long total_tokens, int max_seq_len, float softmax_scale,
                                 int num_splits, void *out, int out_dtype, float *out_lse,
                                 void *workspace, size_t workspace_bytes, void *stream) {
+    return decode_fp8(query, cache, kv_scale, nullptr, cu_seqlens, batch, num_heads, total_tokens, max_seq_len,
+                      softmax_scale, num_splits, out, out_dtype, out_lse, workspace, workspace_bytes, stream);
+}
+
+int mla_b200_decode_batched_fp8_scaled(const void *query, const void *cache, const float *kv_scales,
+                                       const int32_t *cu_seqlens, int batch, int num_heads,
+                                       long long total_tokens, int max_seq_len, float softmax_scale,
+                                       int num_splits, void *out, int out_dtype, float *out_lse,
+                                       void *workspace, size_t workspace_bytes, void *stream) {
+    if (total_tokens > 0 && (kv_scales == nullptr || !aligned(kv_scales, 4))) return MLA_B200_ERR_INVALID_ARG;
+    return decode_fp8(query, cache, 1.f, kv_scales, cu_seqlens, batch, num_heads, total_tokens, max_seq_len,
+                      softmax_scale, num_splits, out, out_dtype, out_lse, workspace, workspace_bytes, stream);
+}
+
+}  // extern "C"
+
+namespace {
+int decode_fp8(const void *query, const void *cache, float kv_scale, const float *kv_scales,
+               const int32_t *cu_seqlens, int batch, int num_heads, long long total_tokens, int max_seq_len,
+               float softmax_scale, int num_splits, void *out, int out_dtype, float *out_lse, void *workspace,
+               size_t workspace_bytes, void *stream) {
     if (batch < 0 || num_heads <= 0 || total_tokens < 0 || max_seq_len < 0)
         return MLA_B200_ERR_INVALID_ARG;
     if (batch > 0 && (query == nullptr || out == nullptr)) return MLA_B200_ERR_INVALID_ARG;
@@ -1025,13 +1081,16 @@ int mla_b200_decode_batched_fp8(const void *query, const void *cache, float kv_s
         return MLA_B200_ERR_INVALID_ARG;
     if (total_tokens >= (1LL << 31)) return MLA_B200_ERR_UNSUPPORTED;
     if (num_heads > 128) return MLA_B200_ERR_UNSUPPORTED;
-    Fp8Args f8{cache, kv_scale};
+    Fp8Args f8{cache, kv_scale, kv_scales};
     // (the fp16 cache pointer is unused on this path; query is fp16)
     return run_split_decode<__half>(static_cast<const __half *>(query), nullptr, cu_seqlens, batch,
                                     num_heads, total_tokens, max_seq_len, softmax_scale, num_splits,
                                     out, out_dtype, out_lse, workspace, workspace_bytes,
                                     static_cast<cudaStream_t>(stream), nullptr, &f8);
 }
+}  // namespace
+
+extern "C" {
 
 int mla_b200_decode_fused_f32(const float *query, const float *cache, float *out, int num_heads,
                               int head_dim_c, int seq_length, void *workspace,
@@ -1233,5 +1292,15 @@ int mla_b200_get_device_error(int *code, void *stream) {
 }
 
 int mla_b200_last_cuda_error(void) { return t_last_cuda_error; }
+
+int mla_b200_selftest_wait_timeout(unsigned long long limit_ns, int *done, void *stream) {
+    if (done == nullptr || limit_ns == 0 || limit_ns > 100000000ull) return MLA_B200_ERR_INVALID_ARG;
+    int dev;
+    DevInfo info;
+    const int st = current_device(&dev, &info);
+    if (st != MLA_B200_OK) return st;
+    wait_selftest_kernel<<<1, 1, 0, static_cast<cudaStream_t>(stream)>>>(limit_ns, done);
+    return launch_status();
+}
 
 }  // extern "C"

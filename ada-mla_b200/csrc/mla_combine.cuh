@@ -91,6 +91,8 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(
     __shared__ float w_s[kCombineChunk];
     __shared__ float red[kCombineThreads / 32];
     __shared__ __align__(16) float acc_s[kGroups - 1][kDV];
+    griddep_launch();  // the next decode may place its CTAs and set up
+    griddep_wait();    // the partials are complete and visible
     const long long row = blockIdx.x;
     if (row >= rows) return;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
@@ -192,6 +194,8 @@ __global__ void __launch_bounds__(32 * kRowsPerCombineBlock) combine_rows_kernel
     const PartT *__restrict__ part_o, const float *__restrict__ part_lse, WorkList wl, int num_heads,
     OutT *__restrict__ out, float *__restrict__ out_lse, int skip_single) {
     constexpr int kU = 16 * (int)sizeof(PartT) / 16;  // 16-byte vectors per lane per split
+    griddep_launch();
+    griddep_wait();
     const int lane = threadIdx.x & 31;
     const int b = blockIdx.y;
     const int h = blockIdx.x * kRowsPerCombineBlock + (threadIdx.x >> 5);

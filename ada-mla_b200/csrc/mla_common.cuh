@@ -61,6 +61,10 @@ __host__ __device__ constexpr int item_cost_for(int num_heads) { return 1 + num_
 // exited); griddep_wait() returns when the predecessor grid has completed and
 // its memory is visible.  Without the attribute both are no-ops.
 __device__ __forceinline__ void griddep_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// The decode and merge kernels call griddep_launch() at their start, so that
+// a successor launched with the attribute (the host chains decode -> merge ->
+// next decode for a few long sequences) can place its CTAs and set up early.
 __device__ __forceinline__ void griddep_launch() { asm volatile("griddepcontrol.launch_dependents;" ::: "memory"); }
 
 struct WorkList {
@@ -288,6 +292,7 @@ enum DeviceError : int {
     kErrWaitMma = 3,       // waited too long for an MMA commit
     kErrWaitPeer = 4,      // waited too long for the partner CTA of a cluster
     kErrBadShape = 5,      // a kernel saw a shape its host checks should have rejected
+    kErrSelfTest = 6,      // the bounded-wait self test's wait ran out (expected)
 };
 
 __device__ int g_mla_error = 0;  // one translation unit (mla_b200.cu) includes this

@@ -74,7 +74,10 @@ static_assert(2 * kQBoxBytes <= kSlotS, "two Q boxes per ring slot");
 // and lo planes, one K-block of each per slot.  O-CTA: C8_N tiles [32 x 512 B]
 // (4 column groups of 128 B, SW128: GEMM2's MN-major B) in eight 16 KB slots;
 // the math warpgroup turns each fp16 P message into e4m3 hi and lo planes in
-// place (3 K-steps x [128 rows x 32 B], SW32), GEMM2's K-major A.
+// place (3 K-steps x [128 rows x 32 B], SW32), GEMM2's K-major A.  (Splitting
+// P in the S-CTA's softmax instead, from fp32 registers, measured slower: cfg3
+// 85.7 vs 67 us.  The softmax warpgroup bounds the tile period and the
+// conversions share the exp2 pipe; the O-CTA's warpgroup is otherwise idle.)
 constexpr int kBoxS8 = kTS * 64;                 // 6144: one fp8 K-block [96 tok x 64 B]
 constexpr int kSlotS8 = kKbPerSlot * kBoxS8;     // 18432
 constexpr int kSlotsS8 = 10;
@@ -145,6 +148,25 @@ constexpr float kRescaleLog2 = 8.0f;
 // with p <= 4 measured slower: O corrections become frequent.)
 constexpr float kRescaleLog2Fp8 = 6.0f;
 constexpr float kP8Scale = 4.0f;
+// Per-row scales: the scale's exponent joins the softmax exponent, so within a
+// tile the weights of small-scale rows sit lower by the tiles' scale spread.  A
+// lower lazy-rescale threshold (2^3) leaves room for a larger factor: q = 16 *
+// w * mantissa <= 16 * 8 * 2 = 256.  (2^4 with a factor of 8 left a 2^4.6
+// scale spread at max-abs 0.0107, just over the bar.)
+constexpr float kRescaleLog2Fp8Rows = 3.0f;
+constexpr float kP8ScaleRows = 16.0f;  // times the scale's mantissa in [1, 2)
+constexpr float kP8Log2Scale = 2.0f;      // log2 kP8Scale
+constexpr float kP8Log2ScaleRows = 4.0f;  // log2 kP8ScaleRows
+
+// s = 2^e * f with f in [1, 2), for a positive normal float (bit fields; e is
+// clamped to +-125 so that 2^-e stays a normal float).
+__device__ __forceinline__ int scale_exp(float s) {
+    return min(125, max(-125, ((__float_as_int(s) >> 23) & 0xFF) - 127));
+}
+__device__ __forceinline__ float scale_mant(float s) {
+    return __int_as_float((__float_as_int(s) & 0x007FFFFF) | 0x3F800000);
+}
+__device__ __forceinline__ float scale_pow2_inv(float s) { return __int_as_float((127 - scale_exp(s)) << 23); }
 
 // GEMM1: M=128 heads, N=96 tokens; GEMM2: M=128 heads, N=256 dims, B MN-major.
 template <bool kBf16> __host__ __device__ constexpr uint32_t idesc_s() { return ptx::idesc_f16_f32(128, kTS, 0, 0, kBf16 ? 1 : 0); }
@@ -162,7 +184,7 @@ struct TcParams {
     int part_kind;     // partial element type: kOutF32 / kOutF16 / kOutBF16
     union {
         int page_size;     // paged: a multiple of kTO
-        float o_scale;     // fp8 cache: factor of the finished O (kv scale / kP8Scale)
+        float o_scale;     // fp8 cache: factor of the finished O (kv scale; 1 with per-row scales)
     };
     void *out;         // [batch, num_heads, 512]: written directly for single-item sequences
     int out_kind;      // out element type: kOutF32 / kOutF16 / kOutBF16
@@ -172,6 +194,7 @@ struct TcParams {
     };
     float *out_lse;    // [batch, num_heads] or null
     unsigned long long *span;  // or null: {first CTA start, last CTA end} %globaltimer of this launch
+    const float *kv_scales;    // fp8 cache: per cache row dequantisation scale (or null: per tensor)
     // Paged cache (kPaged): the maps address the page pool as rows
     // [num_pages * page_size, 576]; token t of sequence b lives in pool row
     // block_table[b * max_blocks + t / page_size] * page_size + t % page_size,
@@ -198,12 +221,12 @@ __device__ __forceinline__ void zero_tail(uint32_t tile, int tail, int lane) {
 }
 
 // fp8 cache: turns row h of a landed fp16 P message (3 SW64 K-major sub-tiles
-// [128 x 32 tokens]) into e4m3 hi and lo planes of q = p * kP8Scale, hi =
-// e4m3(q), lo = e4m3(q - hi) (q to ~2^-8 relative; one e4m3 plane would be
-// 2^-4), written over the same bytes as GEMM2's A: plane x, K-step st at
-// x * kPlaneP8 + st * 4096, row h's 32 bytes with 32-byte swizzle.  All of the
-// warpgroup's reads must finish (a named barrier between the two halves)
-// before any write.
+// [128 x 32 tokens]) into e4m3 hi and lo planes of q (the weights as the
+// softmax sent them, already times kP8Scale / kP8ScaleRows): hi and lo = e4m3(q
+// - hi) carry q to ~2^-8 relative (one e4m3 plane would be 2^-4), written over
+// the same bytes as GEMM2's A: plane x, K-step st at x * kPlaneP8 + st * 4096,
+// row h's 32 bytes with 32-byte swizzle.  All of the warpgroup's reads must
+// finish (a named barrier between the two halves) before any write.
 struct P8Row {
     uint4 v[kOPerS * 4];  // the row's 96 fp16 values
 };
@@ -226,25 +249,34 @@ __device__ __forceinline__ uint32_t half2_of_e4m3x2(uint32_t b2) {
     return (uint32_t)hr.x | ((uint32_t)hr.y << 16);
 }
 
+// hi: kExact, e4m3(q) decoded back (one conversion more per pair); else q
+// rounded to 3 mantissa bits on the integer pipe (half an ulp added at bit 6 of
+// each fp16, bits 0-6 cleared; q >= 0 so the low half cannot carry into the
+// high one), which is exact in e4m3's normal range [2^-6, 448].  Below 2^-6
+// (weights under 2^-8 of the running maximum) e4m3 is subnormal and the
+// rounded hi may not be representable: an error of at most 2^-10 on such a q,
+// as for the exact split.  Per-row cache scales push small-scale rows' weights
+// lower, so they take the exact split.
+template <bool kExact>
 __device__ __forceinline__ void p8_write(uint8_t *msg, int h, const P8Row &r) {
 #pragma unroll
     for (int st = 0; st < kOPerS; ++st) {
         uint32_t hi[8], lo[8];
 #pragma unroll
         for (int c4 = 0; c4 < 4; ++c4) {
-            uint32_t in[4] = {r.v[st * 4 + c4].x, r.v[st * 4 + c4].y, r.v[st * 4 + c4].z, r.v[st * 4 + c4].w};
-#pragma unroll
-            for (int k = 0; k < 4; ++k) {  // x kP8Scale: exact in fp16 (p <= 64)
-                const __half2 q = __hmul2(*reinterpret_cast<const __half2 *>(&in[k]), __float2half2_rn(kP8Scale));
-                in[k] = *reinterpret_cast<const uint32_t *>(&q);
-            }
+            const uint32_t in[4] = {r.v[st * 4 + c4].x, r.v[st * 4 + c4].y, r.v[st * 4 + c4].z, r.v[st * 4 + c4].w};
             uint32_t hb[4], lb[4];
 #pragma unroll
             for (int k = 0; k < 4; ++k) {
-                hb[k] = e4m3x2_of(in[k]);
-                const __half2 d = __hsub2(*reinterpret_cast<const __half2 *>(&in[k]),
-                                          __halves2half2(__ushort_as_half((unsigned short)(half2_of_e4m3x2(hb[k]) & 0xFFFFu)),
-                                                         __ushort_as_half((unsigned short)(half2_of_e4m3x2(hb[k]) >> 16))));
+                uint32_t hh;  // hi as two fp16
+                if constexpr (kExact) {
+                    hb[k] = e4m3x2_of(in[k]);
+                    hh = half2_of_e4m3x2(hb[k]);
+                } else {
+                    hh = (in[k] + 0x00400040u) & 0xFF80FF80u;
+                    hb[k] = e4m3x2_of(hh);
+                }
+                const __half2 d = __hsub2(*reinterpret_cast<const __half2 *>(&in[k]), *reinterpret_cast<const __half2 *>(&hh));
                 lb[k] = e4m3x2_of(*reinterpret_cast<const uint32_t *>(&d));
             }
             hi[2 * c4] = hb[0] | (hb[1] << 16);
@@ -334,7 +366,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
-    if (tid == 0 && p.span != nullptr) atomicMin(p.span, (unsigned long long)globaltimer_ns());
     const uint32_t role = ptx::cluster_ctarank();  // 0 = S-CTA, 1 = O-CTA
     const int cid = (int)ptx::cluster_id_x();
     const int ncl = (int)ptx::nclusters_x();
@@ -377,7 +408,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(smem + kOffSlot);
     // Set-up above overlaps the plan kernel (programmatic launch); the work list
     // is read below.
+    griddep_launch();  // a chained merge may place its CTAs
     griddep_wait();
+    if (tid == 0 && p.span != nullptr) atomicMin(p.span, (unsigned long long)globaltimer_ns());
 
     const WorkList &wl = p.wl;
 
@@ -699,6 +732,16 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             // ------------------------------------------------ S-CTA: softmax
             const uint32_t peer_pfull0 = ptx::mapa(bar(kBarPFull), 1);
             const uint32_t peer_msg0 = ptx::mapa(sbase + kOffMsgO, 1);
+            // fp8: P leaves as fp16 q = K * w, the O-CTA splits it into e4m3 planes.
+            // Per-tensor scale: w = p, K = kP8Scale.  Per-row scales s_t = 2^(e_t) *
+            // f_t (f_t in [1, 2)): the exponent joins the logit in the online softmax
+            // (y_t = z_t + e_t, so w_t = 2^(y_t - m) <= 2^3 whatever s_t) and the
+            // weight is w_t * f_t with K = kP8ScaleRows; the row sum adds w_t *
+            // 2^-e_t = p_t.  Either way q <= 256 < 448.  K enters through the
+            // exponent (2^(y - m + log2 K)), so the row sum is K times the true one:
+            // K cancels in O = sum(q c) / sum, and the LSE subtracts log2 K.
+            const bool rows_scaled = kFp8 && p.kv_scales != nullptr;
+            const float p8log2k = rows_scaled ? kP8Log2ScaleRows : kP8Log2Scale;
             ItemCursor cur = items_begin<kSched>(wl, cid, ncl);
             Item it;
             int i;
@@ -743,6 +786,24 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         }
                         ptx::tc_fence_before();
                         ptx::mbar_arrive(bar(kBarSEmpty + sb));
+                        // fp8, per-row scales: r becomes y = sl2 * s * (Q8 . C8) + e (the log2
+                        // domain, sl2 applied here), the tail masked below
+                        const float *kvs = nullptr;
+                        float sl2_eff = sl2;
+                        if constexpr (kFp8) {
+                            if (rows_scaled) {
+                                kvs = p.kv_scales + it.row0 + t0;
+                                const int nv = min(kTS, it.len - t0);
+#pragma unroll
+                                for (int k = 0; k < kTS; ++k) {
+                                    if (k < nv) {
+                                        const float sc = __ldg(kvs + k);
+                                        r[k] = u32_of(fmaf(f32_of(r[k]) * sc, sl2, (float)scale_exp(sc)));
+                                    }
+                                }
+                                sl2_eff = 1.f;
+                            }
+                        }
 
                         // Row max of the raw logits (scale > 0 commutes with max), with
                         // masked tail columns at -inf; 8 independent chains.
@@ -759,8 +820,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                         for (int k = 8; k < kTS; ++k) m8[k & 7] = fmaxf(m8[k & 7], f32_of(r[k]));
                         const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                                               fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * sl2;
-                        if (mx > m_used + (kFp8 ? kRescaleLog2Fp8 : kRescaleLog2)) {
+                                               fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * sl2_eff;
+                        if (mx > m_used + (kFp8 ? (rows_scaled ? kRescaleLog2Fp8Rows : kRescaleLog2Fp8) : kRescaleLog2)) {
                             alpha = (m_used == -INFINITY) ? 0.f : ptx::ex2(m_used - mx);
                             m_used = mx;
                         }
@@ -768,12 +829,37 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         // (a row that has seen nothing yet keeps m_used = -inf: its p are 0)
                         const float neg_m = (kMtp && m_used == -INFINITY) ? 0.f : -m_used;
                         float s4[4] = {0.f, 0.f, 0.f, 0.f};
+                        if constexpr (kFp8) {
+                            // the per-row branch outside the unrolled loops (two copies)
+                            const float nmk = neg_m + p8log2k;
+                            if (kvs != nullptr) {
 #pragma unroll
-                        for (int k = 0; k < kTS; k += 2) {
-                            const float p0 = ptx::ex2(fmaf(f32_of(r[k]), sl2, neg_m));
-                            const float p1 = ptx::ex2(fmaf(f32_of(r[k + 1]), sl2, neg_m));
-                            s4[(k >> 1) & 3] += p0 + p1;
-                            pk[k >> 1] = pack2<kBf16>(p0, p1);
+                                for (int k = 0; k < kTS; k += 2) {
+                                    const float p0 = ptx::ex2(f32_of(r[k]) + nmk);
+                                    const float p1 = ptx::ex2(f32_of(r[k + 1]) + nmk);
+                                    // row sum of w * 2^-e; GEMM2 weight w * mantissa
+                                    const float sc0 = k < valid ? __ldg(kvs + k) : 1.f;
+                                    const float sc1 = k + 1 < valid ? __ldg(kvs + k + 1) : 1.f;
+                                    s4[(k >> 1) & 3] += p0 * scale_pow2_inv(sc0) + p1 * scale_pow2_inv(sc1);
+                                    pk[k >> 1] = pack2<false>(p0 * scale_mant(sc0), p1 * scale_mant(sc1));
+                                }
+                            } else {
+#pragma unroll
+                                for (int k = 0; k < kTS; k += 2) {
+                                    const float p0 = ptx::ex2(fmaf(f32_of(r[k]), sl2, nmk));
+                                    const float p1 = ptx::ex2(fmaf(f32_of(r[k + 1]), sl2, nmk));
+                                    s4[(k >> 1) & 3] += p0 + p1;
+                                    pk[k >> 1] = pack2<false>(p0, p1);
+                                }
+                            }
+                        } else {
+#pragma unroll
+                            for (int k = 0; k < kTS; k += 2) {
+                                const float p0 = ptx::ex2(fmaf(f32_of(r[k]), sl2, neg_m));
+                                const float p1 = ptx::ex2(fmaf(f32_of(r[k + 1]), sl2, neg_m));
+                                s4[(k >> 1) & 3] += p0 + p1;
+                                pk[k >> 1] = pack2<kBf16>(p0, p1);
+                            }
                         }
                         l_run = l_run * alpha + ((s4[0] + s4[1]) + (s4[2] + s4[3]));
                         // the peer's message slot is free once GEMM2 of S tile jt-3 finished
@@ -826,6 +912,15 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             auto gemm2_done = [&](uint32_t x) -> bool {
                 return ptx::mbar_wait(bar(kBarMmaDone + x % kMsgSlots), (x / kMsgSlots) & 1, kErrWaitMma);
             };
+            // fp8: O = (P8 . C8) * o_scale / l, o_scale = kv_scale per tensor, 1 with
+            // per-row scales (host); the weights' factor K is in l as well, and the
+            // LSE subtracts log2 K
+            float o_scale = 0.f, lse_k = 0.f;
+            const bool rows_scaled = kFp8 && p.kv_scales != nullptr;
+            if constexpr (kFp8) {
+                o_scale = p.o_scale;
+                lse_k = rows_scaled ? kP8Log2ScaleRows : kP8Log2Scale;
+            }
             ItemCursor cur = items_begin<kSched>(wl, cid, ncl);
             Item it;
             int i;
@@ -843,7 +938,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         P8Row pr;
                         p8_read(msg, h, pr);
                         ptx::named_barrier(2, 128);
-                        p8_write(const_cast<uint8_t *>(msg), h, pr);
+                        if (rows_scaled) p8_write<true>(const_cast<uint8_t *>(msg), h, pr);
+                        else p8_write<false>(const_cast<uint8_t *>(msg), h, pr);
                         ptx::fence_proxy_async_smem();
                     }
                     const float alpha = reinterpret_cast<const float *>(msg + kMsgAlpha)[h];
@@ -880,8 +976,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         item_range<kSched>(wl, it.b, ni0, ni1);
                         const bool single = ni1 - ni0 == 1;
                         float inv_l = l_fin > 0.f ? 1.f / l_fin : 0.f;
-                        if constexpr (kFp8) inv_l *= p.o_scale;
-                        const float lse = l_fin > 0.f ? (m_fin + __log2f(l_fin)) * kLn2 : -INFINITY;
+                        if constexpr (kFp8) inv_l *= o_scale;
+                        const float lse = l_fin > 0.f ? (m_fin + __log2f(l_fin) - lse_k) * kLn2 : -INFINITY;
                         // 16-bit output: fp16 from fp16 inputs, bf16 from bf16 inputs
                         const bool f16 = (single ? p.out_kind : p.part_kind) != kOutF32;
                         const size_t row_bytes = (size_t)kDV * (f16 ? 2 : 4);

@@ -177,7 +177,8 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar, uint32_t parity) {
 // after kWaitLimitNs records `err` and returns false.  The spin itself is just
 // try_wait; the global timer is read only every 256 misses.
 template <bool kCluster = false>
-__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int err) {
+__device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int err,
+                                          uint64_t limit_ns = kWaitLimitNs) {
     if (mbar_try_wait<kCluster>(bar, parity)) return true;
     uint64_t t0 = 0;
     for (uint32_t n = 1;; ++n) {
@@ -189,7 +190,7 @@ __device__ __forceinline__ bool mbar_wait(uint32_t bar, uint32_t parity, int err
             const uint64_t t = globaltimer_ns();
             if (t0 == 0) {
                 t0 = t;
-            } else if (t - t0 > kWaitLimitNs) {
+            } else if (t - t0 > limit_ns) {
                 set_device_error(err);
                 return false;
             }

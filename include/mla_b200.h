@@ -94,8 +94,9 @@ MLA_B200_API int mla_b200_set_kernel_timing(void *ev_start, void *ev_stop);
 /* Device-side span of the main tensor-core decode kernel (no reference
  * counterpart).  While set on the calling host thread, the k-th later launch
  * of that kernel (k counting from 0, wrapping after `slots`) records, in
- * span[2k] and span[2k+1], the %globaltimer (ns) of its first CTA's start
- * (atomic min) and of its last CTA's end (atomic max); the caller initialises
+ * span[2k] and span[2k+1], the %globaltimer (ns) at which its first CTA
+ * starts work (after its set-up and the wait for the preceding kernel; atomic
+ * min) and at which its last CTA ends (atomic max); the caller initialises
  * each pair to {UINT64_MAX, 0} before the launch runs.  The span excludes the
  * launch latency that an event pair around the launch includes.  `span` is a
  * device array of 2 * slots uint64; NULL (or slots <= 0) turns it off.  Under
@@ -243,10 +244,25 @@ MLA_B200_API int mla_b200_decode_mtp_bf16(const void *query, const void *cache,
  * with the layout of mla_b200_decode_batched_f16's cache (dense or packed) and
  * one per-tensor scale: C = cache * kv_scale.  query is fp16.  GEMM1 runs on
  * the fp8 tensor-core path with Q* split into two e4m3 planes (hi + lo, per-row
- * power-of-two scaling), GEMM2 on widened fp16 C_N tiles; accumulation and
- * softmax state are fp32.  out_dtype MLA_B200_OUT_F16 or MLA_B200_OUT_F32;
+ * power-of-two scaling); GEMM2 too, with P split into e4m3 hi + lo planes by
+ * the softmax; accumulation and softmax state are fp32.  out_dtype MLA_B200_OUT_F16 or MLA_B200_OUT_F32;
  * num_heads <= 128.  Workspace: mla_b200_workspace_size_fp8 (it adds the
  * e4m3 Q* planes, 2 x batch x num_heads x 576 bytes). */
+/* The same with one dequantisation scale per cache row instead of one per
+ * tensor: C[t] = cache[t] * kv_scales[t], kv_scales [total_tokens] fp32 on the
+ * device, indexed like the cache rows (a per-page or per-tile scale is that
+ * value repeated over the block's rows); scales must be positive normal
+ * floats.  A scale multiplies its column's logit, and its power of two joins the
+ * online softmax's exponent; within one 96-row tile the P weights of rows with
+ * small scales sit lower by the tile's scale spread, so scales that span more
+ * than ~2^5 inside a tile lose P precision (e4m3 subnormals).  Workspace:
+ * mla_b200_workspace_size_fp8. */
+MLA_B200_API int mla_b200_decode_batched_fp8_scaled(const void *query, const void *cache,
+                                                   const float *kv_scales, const int32_t *cu_seqlens,
+                                                   int batch, int num_heads, long long total_tokens,
+                                                   int max_seq_len, float softmax_scale, int num_splits,
+                                                   void *out, int out_dtype, float *out_lse,
+                                                   void *workspace, size_t workspace_bytes, void *stream);
 MLA_B200_API size_t mla_b200_workspace_size_fp8(int batch, int num_heads, long long total_tokens,
                                                 int max_seq_len, int num_splits);
 MLA_B200_API int mla_b200_decode_batched_fp8(const void *query, const void *cache, float kv_scale,
@@ -374,6 +390,15 @@ MLA_B200_API int mla_b200_get_device_error(int *code, void *stream);
  * (csrc/mla_decode_splitk_fwd.cuh:965-985, csrc/mla_decode_fused_fwd_sm89.cu:
  * 43-60): a caller can name the failure without the library printing. */
 MLA_B200_API int mla_b200_last_cuda_error(void);
+
+/* Self test of the bounded waits (no reference counterpart): launches one
+ * thread that waits, through the same wait loop every kernel here uses, on an
+ * mbarrier phase that nothing completes, with a limit of limit_ns (at most
+ * 100 ms).  The wait gives up, records code 6 in the device error word and
+ * returns; the kernel then writes 1 to the device int *done (2 would mean the
+ * wait completed).  Read the word with mla_b200_get_device_error afterwards:
+ * MLA_B200_ERR_DEVICE_TIMEOUT with code 6, and the context stays usable. */
+MLA_B200_API int mla_b200_selftest_wait_timeout(unsigned long long limit_ns, int *done, void *stream);
 
 #ifdef __cplusplus
 } /* extern "C" */

@@ -506,6 +506,58 @@ def test_fp8_batches_and_long(mla, b, nh, n):
     _no_device_error(mla)
 
 
+def _fp8_row_scaled_inputs(lens, nh, seed, block):
+    """e4m3 cache with one scale per row, constant over blocks of `block` rows
+    (a per-tile / per-page scaling) and spread over 2^-2 .. 2^2.6 (a 2^4.6
+    span, inside the documented ~2^5 per-tile envelope)."""
+    g = torch.Generator().manual_seed(seed)
+    q = (torch.randn(len(lens), nh, 576, generator=g) / np.sqrt(192)).half()
+    total = sum(lens)
+    nb = -(-total // block)
+    sblk = torch.pow(2.0, torch.randint(-2, 3, (nb,), generator=g).float()) * \
+        (1 + 0.5 * torch.rand(nb, generator=g))
+    scales = sblk.repeat_interleave(block)[:total].contiguous()
+    c = (torch.randn(total, 576, generator=g) / scales[:, None]).to(torch.float8_e4m3fn)
+    deq = c.float() * scales[:, None]
+    return q, c, scales, deq
+
+
+@pytest.mark.parametrize("block", [32, 96, 1])
+@pytest.mark.parametrize("num_splits", [-1, 2])
+def test_fp8_row_scales_varlen(mla, block, num_splits):
+    """Per-tile (32 or 96 rows) and per-row scales on a packed varlen batch."""
+    lens = [7, 96, 130, 1000, 2500, 0, 64]
+    q, c, scales, deq = _fp8_row_scaled_inputs(lens, 128, seed=64 + block, block=block)
+    cu = torch.tensor([0] + list(np.cumsum(lens)), dtype=torch.int32)
+    out = mla.mla_decode_batched(q.cuda(), c.cuda(), cu.cuda(), max_seq_len=max(lens), softmax_scale=1.0,
+                                 num_splits=num_splits, out_dtype=torch.float32, kv_scale=scales.cuda())
+    torch.cuda.synchronize()
+    lo = 0
+    for i, n in enumerate(lens):
+        if n == 0:
+            assert torch.count_nonzero(out[i]).item() == 0
+        else:
+            ref = oracle.mla_decode_oracle(_np(q[i]), deq[lo:lo + n].numpy(), 1.0, threads=8)
+            assert_close_parity(_np(out[i]), ref, what=f"fp8 row scales block={block} b={i} n={n}")
+        lo += n
+    _no_device_error(mla)
+
+
+def test_fp8_row_scales_dense_long(mla):
+    b, nh, n = 2, 128, 9000
+    q, c, scales, deq = _fp8_row_scaled_inputs([n] * b, nh, seed=69, block=64)
+    out16, lse = mla.mla_decode_batched(q.cuda(), c.view(b, n, 576).cuda(), softmax_scale=1.0, return_lse=True,
+                                        kv_scale=scales.view(b, n).cuda())
+    torch.cuda.synchronize()
+    for i in range(b):
+        rows = deq[i * n:(i + 1) * n].numpy()
+        ref = oracle.mla_decode_oracle(_np(q[i]), rows, 1.0, threads=8)
+        assert_close_parity(_np(out16[i]), ref, what=f"fp8 row scales dense b={i}")
+        _, ref_lse = oracle.lse_partial_oracle(_np(q[i]), rows, 1.0)
+        np.testing.assert_allclose(_np(lse[i]), ref_lse, atol=2e-3, rtol=0)
+    _no_device_error(mla)
+
+
 # ---------------------------------------------------------------------------
 # Multi-token (draft) decode: draft token i of k sees the first L - (k-1-i)
 # tokens of its sequence; the oracle runs each (sequence, token) separately.
