@@ -48,11 +48,11 @@ int cuda_failure(cudaError_t e) {
 
 // Opts a tensor-core kernel instantiation (both schedules) into its dynamic
 // shared memory.
-template <bool kBf16, bool kPaged, bool kFp8 = false, bool kMtp = false>
+template <bool kBf16, bool kPaged, bool kFp8 = false, bool kMtp = false, bool kRows = false>
 bool set_tc_smem() {
-    return cudaFuncSetAttribute(tc::tc_decode_kernel<kSchedChunked, kBf16, kPaged, kFp8, kMtp>,
+    return cudaFuncSetAttribute(tc::tc_decode_kernel<kSchedChunked, kBf16, kPaged, kFp8, kMtp, kRows>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmemBytes) == cudaSuccess &&
-           cudaFuncSetAttribute(tc::tc_decode_kernel<kSchedBalanced, kBf16, kPaged, kFp8, kMtp>,
+           cudaFuncSetAttribute(tc::tc_decode_kernel<kSchedBalanced, kBf16, kPaged, kFp8, kMtp, kRows>,
                                 cudaFuncAttributeMaxDynamicSharedMemorySize, tc::kSmemBytes) == cudaSuccess;
 }
 
@@ -96,7 +96,8 @@ int current_device(int *dev_out, DevInfo *info_out) {
     if (d.tc_clusters == 0) {
         if (!set_tc_smem<false, false>() || !set_tc_smem<true, false>() ||
             !set_tc_smem<false, true>() || !set_tc_smem<true, true>() ||
-            !set_tc_smem<false, false, true>() || !set_tc_smem<false, false, false, true>() ||
+            !set_tc_smem<false, false, true>() || !set_tc_smem<false, false, true, false, true>() ||
+            !set_tc_smem<false, false, false, true>() ||
             !set_tc_smem<true, false, false, true>()) {
             return cuda_failure(cudaGetLastError());
         }
@@ -370,9 +371,9 @@ struct TcMaps {
     CUtensorMap cmap_s, cmap_o, qmap;
 };
 
-template <int kSched, bool kBf16, bool kPaged, bool kFp8 = false, bool kMtp = false>
+template <int kSched, bool kBf16, bool kPaged, bool kFp8 = false, bool kMtp = false, bool kRows = false>
 void launch_tc(int clusters, const TcMaps &m, const tc::TcParams &tp, cudaStream_t stream, bool after_plan) {
-    launch_dependent(tc::tc_decode_kernel<kSched, kBf16, kPaged, kFp8, kMtp>, dim3(2 * clusters),
+    launch_dependent(tc::tc_decode_kernel<kSched, kBf16, kPaged, kFp8, kMtp, kRows>, dim3(2 * clusters),
                      dim3(tc::kThreads), tc::kSmemBytes, stream, after_plan, m.cmap_s, m.cmap_o, m.qmap, tp);
 }
 
@@ -512,7 +513,7 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
                 if (st == MLA_B200_OK) st = make_tmap_576(&qmap, q, qrows, 128, kBf16);
                 if (st != MLA_B200_OK) return st;
             }
-            tc::TcParams tp;
+            tc::TcParams tp{};
             tp.wl = wl;
             tp.num_heads = num_heads;
             tp.scale_log2 = scale * kLog2e;
@@ -541,6 +542,7 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
             }
             tp.span = next_span();
             tp.kv_scales = f8 != nullptr ? f8->kv_scales : nullptr;
+            tp.chain = chain ? 1 : 0;
             tc_direct = true;
             const int clusters = balanced ? bal_clusters : std::min(info.tc_clusters, wl.max_items);
             timing_mark(t_ev_start, stream);
@@ -549,8 +551,15 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
                 else launch_tc<kSchedChunked, kBf16, false, false, true>(clusters, maps, tp, stream, planned || chain);
             } else if (f8 != nullptr) {
                 if constexpr (!kBf16) {  // (fp8 runs with fp16 Q*; the prep kernel precedes)
-                    if (balanced) launch_tc<kSchedBalanced, false, false, true>(clusters, maps, tp, stream, true);
-                    else launch_tc<kSchedChunked, false, false, true>(clusters, maps, tp, stream, true);
+                    // per-row scales: their own instantiation (the per-row code in the
+                    // per-tensor kernel cost it ~10 %)
+                    if (f8->kv_scales != nullptr) {
+                        if (balanced) launch_tc<kSchedBalanced, false, false, true, false, true>(clusters, maps, tp, stream, true);
+                        else launch_tc<kSchedChunked, false, false, true, false, true>(clusters, maps, tp, stream, true);
+                    } else {
+                        if (balanced) launch_tc<kSchedBalanced, false, false, true>(clusters, maps, tp, stream, true);
+                        else launch_tc<kSchedChunked, false, false, true>(clusters, maps, tp, stream, true);
+                    }
                 }
             } else if (pg != nullptr) {
                 if (balanced) launch_tc<kSchedBalanced, kBf16, true>(clusters, maps, tp, stream, planned || chain);

@@ -103,8 +103,12 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(
     item_range(wl, b, i0, i1);
     if (skip_single && i1 - i0 == 1) return;
 
-    float mx = -INFINITY;
-    for (int i = i0 + tid; i < i1; i += kCombineThreads) mx = fmaxf(mx, part_lse[(size_t)i * lse_stride + h]);
+    // this thread's first split's LSE stays in a register for the weights below
+    // (one L2 round trip fewer for up to kCombineThreads splits)
+    const float my_lse = i0 + tid < i1 ? part_lse[(size_t)(i0 + tid) * lse_stride + h] : -INFINITY;
+    float mx = my_lse;
+    for (int i = i0 + tid + kCombineThreads; i < i1; i += kCombineThreads)
+        mx = fmaxf(mx, part_lse[(size_t)i * lse_stride + h]);
     mx = warp_max(mx);
     if (lane == 0) red[warp] = mx;
     __syncthreads();
@@ -121,7 +125,7 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(
             const int n = min(kCombineChunk, i1 - c0);
             __syncthreads();
             for (int k = tid; k < n; k += kCombineThreads) {
-                const float lse = part_lse[(size_t)(c0 + k) * lse_stride + h];
+                const float lse = (c0 == i0 && k == tid) ? my_lse : part_lse[(size_t)(c0 + k) * lse_stride + h];
                 w_s[k] = lse == -INFINITY ? 0.f : __expf(lse - mx);
             }
             __syncthreads();

@@ -49,11 +49,11 @@ constexpr float kLn2 = 0.6931471805599453f;
 //    varlen: cost0_b = cost_off[b] (prefix computed by plan_balanced_kernel),
 //            quota = ceil(cost_off[B] / nworkers), derived on the device.
 // ---------------------------------------------------------------------------
-// Fixed cost of one work item, in 96-row tiles: its Q load (n_h x 1152 B) and
-// its partial write (n_h x 1024 B; one SM writes ~45 GB/s) both scale with the
-// head count.  2 tiles at 128 heads (measured: 3 or 4 moved nothing), 1 for 64
-// heads or fewer, where a split costs little.
-__host__ __device__ constexpr int item_cost_for(int num_heads) { return 1 + num_heads / 128; }
+// Fixed cost of one work item, in 96-row tiles: its Q load (always a 128-row
+// box, 144 KB, whatever the head count), pipeline fill and its partial write
+// (n_h x 1024 B; one SM writes ~45 GB/s).  2 tiles (measured at 128 heads: 3 or
+// 4 moved nothing; at 16 heads, cfg4, 1 tile was 1-3.5 % slower).
+__host__ __device__ constexpr int item_cost_for(int /*num_heads*/) { return 2; }
 
 // Programmatic dependent launch.  A kernel launched with the programmatic
 // stream-serialization attribute may start while its predecessor in the stream

@@ -194,6 +194,7 @@ struct TcParams {
     };
     float *out_lse;    // [batch, num_heads] or null
     unsigned long long *span;  // or null: {first CTA start, last CTA end} %globaltimer of this launch
+    int chain;                 // the merge after this launch is a programmatic dependent
     const float *kv_scales;    // fp8 cache: per cache row dequantisation scale (or null: per tensor)
     // Paged cache (kPaged): the maps address the page pool as rows
     // [num_pages * page_size, 576]; token t of sequence b lives in pool row
@@ -350,9 +351,11 @@ struct Ring {
 // sees the sequence's first len - (k - 1 - i) tokens (its own KV being the
 // cache's last k rows).  kFp8: the cache is e4m3 (cmap_s:
 // 64-byte K-blocks, box 3 x 96 rows, SW64; cmap_o: (128 B, rows, 4) box of one
-// [32 x 512 B] tile, unswizzled) and qmap addresses Q8 [2 x B * n_h, 576] e4m3
-// (hi plane, then lo plane), box 64 x 128, SW64.
-template <int kSched, bool kBf16, bool kPaged, bool kFp8, bool kMtp = false>
+// [32 x 512 B] tile, SW128) and qmap addresses Q8 [2 x B * n_h, 576] e4m3
+// (hi plane, then lo plane), box 64 x 128, SW64.  kRows (with kFp8): one
+// dequantisation scale per cache row, p.kv_scales; a separate instantiation
+// because the per-row code slowed the per-tensor kernel by ~10 %.
+template <int kSched, bool kBf16, bool kPaged, bool kFp8, bool kMtp = false, bool kRows = false>
 __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     tc_decode_kernel(const __grid_constant__ CUtensorMap cmap_s,
                      const __grid_constant__ CUtensorMap cmap_o,
@@ -408,9 +411,11 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     const uint32_t tmem = *reinterpret_cast<volatile uint32_t *>(smem + kOffSlot);
     // Set-up above overlaps the plan kernel (programmatic launch); the work list
     // is read below.
-    griddep_launch();  // a chained merge may place its CTAs
+    if (p.chain) griddep_launch();  // the chained merge may place its CTAs
     griddep_wait();
-    if (tid == 0 && p.span != nullptr) atomicMin(p.span, (unsigned long long)globaltimer_ns());
+    // (the span is published at the end: the atomics here, and the unconditional
+    // trigger, measured 1-3 % slower on batches)
+    const unsigned long long t_start = globaltimer_ns();
 
     const WorkList &wl = p.wl;
 
@@ -740,7 +745,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             // 2^-e_t = p_t.  Either way q <= 256 < 448.  K enters through the
             // exponent (2^(y - m + log2 K)), so the row sum is K times the true one:
             // K cancels in O = sum(q c) / sum, and the LSE subtracts log2 K.
-            const bool rows_scaled = kFp8 && p.kv_scales != nullptr;
+            constexpr bool rows_scaled = kFp8 && kRows;
             const float p8log2k = rows_scaled ? kP8Log2ScaleRows : kP8Log2Scale;
             ItemCursor cur = items_begin<kSched>(wl, cid, ncl);
             Item it;
@@ -791,7 +796,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         const float *kvs = nullptr;
                         float sl2_eff = sl2;
                         if constexpr (kFp8) {
-                            if (rows_scaled) {
+                            if constexpr (rows_scaled) {
                                 kvs = p.kv_scales + it.row0 + t0;
                                 const int nv = min(kTS, it.len - t0);
 #pragma unroll
@@ -832,7 +837,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         if constexpr (kFp8) {
                             // the per-row branch outside the unrolled loops (two copies)
                             const float nmk = neg_m + p8log2k;
-                            if (kvs != nullptr) {
+                            if constexpr (rows_scaled) {
 #pragma unroll
                                 for (int k = 0; k < kTS; k += 2) {
                                     const float p0 = ptx::ex2(f32_of(r[k]) + nmk);
@@ -916,7 +921,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             // per-row scales (host); the weights' factor K is in l as well, and the
             // LSE subtracts log2 K
             float o_scale = 0.f, lse_k = 0.f;
-            const bool rows_scaled = kFp8 && p.kv_scales != nullptr;
+            constexpr bool rows_scaled = kFp8 && kRows;
             if constexpr (kFp8) {
                 o_scale = p.o_scale;
                 lse_k = rows_scaled ? kP8Log2ScaleRows : kP8Log2Scale;
@@ -938,7 +943,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         P8Row pr;
                         p8_read(msg, h, pr);
                         ptx::named_barrier(2, 128);
-                        if (rows_scaled) p8_write<true>(const_cast<uint8_t *>(msg), h, pr);
+                        if constexpr (rows_scaled) p8_write<true>(const_cast<uint8_t *>(msg), h, pr);
                         else p8_write<false>(const_cast<uint8_t *>(msg), h, pr);
                         ptx::fence_proxy_async_smem();
                     }
@@ -1058,7 +1063,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         ptx::tc_fence_after();
         ptx::tmem_dealloc(tmem, kTmemCols);
     }
-    if (tid == 0 && p.span != nullptr) atomicMax(p.span + 1, (unsigned long long)globaltimer_ns());
+    if (tid == 0 && p.span != nullptr) {
+        atomicMin(p.span, t_start);
+        atomicMax(p.span + 1, (unsigned long long)globaltimer_ns());
+    }
 }
 
 }  // namespace tc
