@@ -71,6 +71,14 @@ SIGNATURES = {
     "mla_b200_get_device_error": (_c_int, [ctypes.POINTER(_c_int), _vp]),
     "mla_b200_last_cuda_error": (_c_int, []),
     "mla_b200_selftest_wait_timeout": (_c_int, [ctypes.c_ulonglong, _vp, _vp]),
+    "mla_b200_exchange_bytes": (_c_size, [_c_int, _c_ll]),
+    "mla_b200_exchange_alloc": (_c_int, [_c_int, _c_ll, ctypes.POINTER(_vp)]),
+    "mla_b200_exchange_free": (_c_int, [_vp]),
+    "mla_b200_ipc_handle": (_c_int, [_vp, _vp]),
+    "mla_b200_ipc_open": (_c_int, [_vp, ctypes.POINTER(_vp)]),
+    "mla_b200_ipc_close": (_c_int, [_vp]),
+    "mla_b200_exchange_put_f32": (_c_int, [_vp, _c_ll, ctypes.POINTER(_vp), _c_int, _c_int, _vp]),
+    "mla_b200_exchange_merge_f32": (_c_int, [_vp, _c_int, _c_ll, _vp, _c_int, _vp, ctypes.c_ulonglong, _vp]),
 }
 
 _lib: ctypes.CDLL | None = None

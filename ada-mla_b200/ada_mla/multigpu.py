@@ -12,7 +12,10 @@ layer scales the same decode across the G GPUs of a node, one process per GPU:
   into a packed exchange buffer (O normalized, then LSE, fp32); one
   ``all_gather_into_tensor`` of ``n_h x (512 + 1)`` floats per sequence gives
   every rank all G partials, which the LSE-merge kernel reads in place and
-  reduces to the exact result (``KvSplitDecoder``).
+  reduces to the exact result (``KvSplitDecoder``).  With ``exchange="p2p"``
+  the all-gather is replaced by this library's own kernels over NVLink peer
+  memory (``PeerExchange``: CUDA IPC mappings, plain stores into every rank's
+  buffer, release / acquire flags at system scope, bounded waits).
 
 The per-rank decode and the merge are injectable so that the host logic
 (partitioning, packing, the collective, unpacking) can be exercised by CPU
@@ -124,6 +127,88 @@ def _cuda_merge(packed: torch.Tensor, parts: int, rows: int, stride: int, out_dt
     return out, lse
 
 
+class PeerExchange:
+    """The split-KV step's exchange over NVLink peer memory, instead of an NCCL
+    all-gather: every rank owns one exchange buffer (mla_b200_exchange_alloc),
+    maps every other rank's through CUDA IPC (handles swapped once with
+    ``all_gather_object``), stores its packed (O, LSE) straight into every
+    rank's buffer (``put``) and merges the G parts in its own buffer after a
+    bounded wait on the other ranks' flags (``merge``).  Both are stream-ordered
+    kernels, so the step captures in a CUDA graph.  Set up and ``close()`` on
+    every rank together (both end with a barrier)."""
+
+    WAIT_LIMIT_NS = 1_000_000_000  # a peer that has not published within 1 s is an error
+
+    def __init__(self, rows: int, group: dist.ProcessGroup | None = None):
+        import ctypes
+
+        from ada_mla import capi
+
+        self.rows = rows
+        self.group = group
+        self.world = dist.get_world_size(group) if dist.is_initialized() else 1
+        self.rank = dist.get_rank(group) if dist.is_initialized() else 0
+        lib = capi.lib()
+        own = ctypes.c_void_p()
+        capi._check("mla_b200_exchange_alloc", lib.mla_b200_exchange_alloc(self.world, rows, ctypes.byref(own)))
+        self.own = own.value
+        handle = ctypes.create_string_buffer(64)
+        capi._check("mla_b200_ipc_handle", lib.mla_b200_ipc_handle(self.own, handle))
+        handles = [None] * self.world
+        if self.world > 1:
+            dist.all_gather_object(handles, handle.raw, group=group)
+        else:
+            handles[0] = handle.raw
+        ptrs, self._opened = [], []
+        for g, h in enumerate(handles):
+            if g == self.rank:
+                ptrs.append(self.own)
+                continue
+            p = ctypes.c_void_p()
+            capi._check("mla_b200_ipc_open", lib.mla_b200_ipc_open(ctypes.create_string_buffer(h, 64), ctypes.byref(p)))
+            ptrs.append(p.value)
+            self._opened.append(p.value)
+        self._peer_array = (ctypes.c_void_p * self.world)(*ptrs)  # host array of device pointers
+        if self.world > 1:
+            dist.barrier(group=group)  # every mapping exists before the first put
+
+    def put(self, packed: torch.Tensor) -> None:
+        """packed: this rank's [packed_stride(rows)] fp32 (O then LSE)."""
+        from ada_mla import capi
+
+        capi._check("mla_b200_exchange_put_f32", capi.lib().mla_b200_exchange_put_f32(
+            packed.data_ptr(), self.rows, self._peer_array, self.rank, self.world,
+            torch.cuda.current_stream().cuda_stream))
+
+    def merge(self, out_dtype: torch.dtype = torch.float16, device=None):
+        """The merged [rows, 512] output and its [rows] LSE, on this rank."""
+        from ada_mla import capi
+
+        out = torch.empty((self.rows, HEAD_DIM_V), dtype=torch.float32 if out_dtype == torch.float32
+                          else torch.float16, device=device)
+        lse = torch.empty((self.rows,), dtype=torch.float32, device=device)
+        capi._check("mla_b200_exchange_merge_f32", capi.lib().mla_b200_exchange_merge_f32(
+            self.own, self.world, self.rows, out.data_ptr(),
+            capi.OUT_F32 if out_dtype == torch.float32 else capi.OUT_F16, lse.data_ptr(),
+            self.WAIT_LIMIT_NS, torch.cuda.current_stream().cuda_stream))
+        return out, lse
+
+    def close(self) -> None:
+        from ada_mla import capi
+
+        if self.own is None:
+            return
+        torch.cuda.synchronize()
+        lib = capi.lib()
+        for p in self._opened:
+            lib.mla_b200_ipc_close(p)
+        self._opened = []
+        if self.world > 1:
+            dist.barrier(group=self.group)  # no peer maps the buffer any more
+        lib.mla_b200_exchange_free(self.own)
+        self.own = None
+
+
 @dataclass
 class KvSplitDecoder:
     """KV-length-split decode across the ranks of ``group``.
@@ -137,18 +222,36 @@ class KvSplitDecoder:
     writes in place; ``merge(packed [G * stride], G, rows, stride, out_dtype) ->
     (out [rows, 512], lse [rows])``.  Both default to the CUDA kernels and are
     injectable (the CPU tests run the host logic on gloo ranks).
+
+    ``exchange="p2p"`` replaces the all-gather and the merge by ``PeerExchange``:
+    the packed partial goes straight into every rank's buffer over NVLink and is
+    merged there (CUDA only; ``close()`` releases the mappings on every rank).
     """
 
     group: dist.ProcessGroup | None = None
     local_decode: Callable | None = None
     merge: Callable | None = None
     make_workspace: Callable | None = None
+    exchange: str = "nccl"
 
     def __post_init__(self):
         self.local_decode = self.local_decode or _cuda_partial
         self.merge = self.merge or _cuda_merge
         self.make_workspace = self.make_workspace or _cuda_workspace
         self._bufs: dict = {}
+        self._peers: dict = {}
+        if self.exchange not in ("nccl", "p2p"):
+            raise ValueError(f"exchange must be 'nccl' or 'p2p', not {self.exchange!r}")
+
+    def _peer_exchange(self, rows: int) -> PeerExchange:
+        if rows not in self._peers:
+            self._peers[rows] = PeerExchange(rows, self.group)
+        return self._peers[rows]
+
+    def close(self) -> None:
+        for ex in self._peers.values():
+            ex.close()
+        self._peers = {}
 
     @property
     def world(self) -> int:
@@ -204,35 +307,55 @@ class KvSplitDecoder:
         Returns O* [B, n_h, 512] on every rank."""
         b, nh = query.shape[0], query.shape[1]
         stride, send, recv = self._local(query, cache_slice, softmax_scale)
-        self._gather(recv, send)
-        out, out_lse = self.merge(recv, self.world, b * nh, stride, out_dtype)
+        if self.exchange == "p2p":
+            ex = self._peer_exchange(b * nh)
+            ex.put(send)
+            out, out_lse = ex.merge(out_dtype, device=query.device)
+        else:
+            self._gather(recv, send)
+            out, out_lse = self.merge(recv, self.world, b * nh, stride, out_dtype)
         out = out.reshape(b, nh, HEAD_DIM_V)
         return (out, out_lse.reshape(b, nh)) if return_lse else out
 
     def stage_times_us(self, query: torch.Tensor, cache_slice: torch.Tensor, softmax_scale: float,
                        reps: int = 20) -> dict:
-        """Device time of each stage (local decode, all-gather, merge), each run
-        `reps` times back to back between CUDA events on this rank's stream.
+        """Device time of each stage (local decode, all-gather, merge): each stage
+        captured `reps` times in a CUDA graph, one replay between CUDA events on
+        this rank's stream (launch overhead excluded, as in the timed step).
         Every rank must call it (the all-gather stage is collective)."""
         b, nh = query.shape[0], query.shape[1]
         stride, send, recv = self._local(query, cache_slice, softmax_scale)
         times = {}
-        stages = {
-            "local_decode": lambda: self._local(query, cache_slice, softmax_scale),
-            "all_gather": lambda: self._gather(recv, send),
-            "merge": lambda: self.merge(recv, self.world, b * nh, stride, torch.float16),
-        }
+        if self.exchange == "p2p":
+            ex = self._peer_exchange(b * nh)
+            stages = {
+                "local_decode": lambda: self._local(query, cache_slice, softmax_scale),
+                "p2p_put_and_merge": lambda: (ex.put(send), ex.merge(torch.float16, device=query.device)),
+            }
+        else:
+            stages = {
+                "local_decode": lambda: self._local(query, cache_slice, softmax_scale),
+                "all_gather": lambda: self._gather(recv, send),
+                "merge": lambda: self.merge(recv, self.world, b * nh, stride, torch.float16),
+            }
         for name, fn in stages.items():
             fn()
+            torch.cuda.synchronize()
+            side = torch.cuda.Stream()
+            side.wait_stream(torch.cuda.current_stream())
+            graph = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(graph, stream=side):
+                for _ in range(reps):
+                    fn()
             torch.cuda.synchronize()
             self._barrier()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record()
-            for _ in range(reps):
-                fn()
+            graph.replay()
             e1.record()
             torch.cuda.synchronize()
             times[name] = e0.elapsed_time(e1) * 1e3 / reps
+            del graph
         return times
 
 

@@ -7,6 +7,7 @@
 
 #include <algorithm>
 #include <atomic>
+#include <cstring>
 #include <mutex>
 #include <type_traits>
 #include <utility>
@@ -17,6 +18,7 @@
 #include "mla_combine.cuh"
 #include "mla_fp8.cuh"
 #include "mla_common.cuh"
+#include "mla_exchange.cuh"
 #include "mla_proj.cuh"
 #include "mla_simt.cuh"
 #include "mla_tc.cuh"
@@ -519,10 +521,13 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
             tp.scale_log2 = scale * kLog2e;
             tp.part_o = L.part_o;
             tp.part_lse = L.part_lse;
-            // 16-bit partials for 16-bit output (fp16, or bf16 for bf16: its data may
-            // exceed the fp16 range), fp32 partials for fp32 output
-            tp.part_kind = out_dtype == MLA_B200_OUT_F16 ? tc::kOutF16
-                           : out_dtype == MLA_B200_OUT_BF16 ? tc::kOutBF16 : tc::kOutF32;
+            // 16-bit partials: fp16 for fp16 inputs (whatever the output type: a
+            // normalized partial fits fp16 and its 2^-11 rounding is far inside the
+            // error bar, and the epilogue and merge move half the bytes), bf16 for bf16
+            // output; bf16 inputs with fp32 output keep fp32 partials (bf16's 2^-8
+            // rounding would show at fp32 output precision)
+            tp.part_kind = out_dtype == MLA_B200_OUT_BF16 ? tc::kOutBF16
+                           : (out_dtype == MLA_B200_OUT_F16 || !kBf16) ? tc::kOutF16 : tc::kOutF32;
             tp.out = out;
             tp.out_kind = out_dtype == MLA_B200_OUT_F16 ? tc::kOutF16
                           : out_dtype == MLA_B200_OUT_BF16 ? tc::kOutBF16 : tc::kOutF32;
@@ -582,8 +587,8 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     const long long rows = (long long)batch * num_heads;
     const unsigned cgrid = (unsigned)rows;
     const int skip = tc_direct ? 1 : 0;
-    // The tcgen05 kernel keeps 16-bit partials for 16-bit output (fp16 or bf16); the
-    // SIMT kernel's are fp32.
+    // The tcgen05 kernel keeps fp16 partials for fp16 inputs and bf16 partials for
+    // bf16 output (fp32 for bf16 inputs with fp32 output); the SIMT kernel's are fp32.
     // Batches merge row-parallel (a warp per row, few splits each); a few long
     // sequences merge split-parallel (a block per row, many splits).
     if (batch >= 8) {
@@ -601,6 +606,9 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
         else if (out_dtype == MLA_B200_OUT_F16)
             launch_dependent(combine_rows_kernel<__half, float>, rgrid, rblock, 0, stream, chain, po, L.part_lse,
                              wl, num_heads, static_cast<__half *>(out), out_lse, skip);
+        else if (tc_direct && !kBf16)
+            launch_dependent(combine_rows_kernel<float, __half>, rgrid, rblock, 0, stream, chain, ph, L.part_lse,
+                             wl, num_heads, static_cast<float *>(out), out_lse, skip);
         else
             launch_dependent(combine_rows_kernel<float, float>, rgrid, rblock, 0, stream, chain, po, L.part_lse,
                              wl, num_heads, static_cast<float *>(out), out_lse, skip);
@@ -620,6 +628,9 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     else if (out_dtype == MLA_B200_OUT_F16)
         launch_dependent(combine_kernel<__half, float>, dim3(cgrid), cblock, 0, stream, chain, po, L.part_lse,
                          wl, num_heads, rows, static_cast<__half *>(out), out_lse, skip, ps, ls);
+    else if (tc_direct && !kBf16)
+        launch_dependent(combine_kernel<float, __half>, dim3(cgrid), cblock, 0, stream, chain, ph, L.part_lse,
+                         wl, num_heads, rows, static_cast<float *>(out), out_lse, skip, ps, ls);
     else
         launch_dependent(combine_kernel<float, float>, dim3(cgrid), cblock, 0, stream, chain, po, L.part_lse,
                          wl, num_heads, rows, static_cast<float *>(out), out_lse, skip, ps, ls);
@@ -1205,6 +1216,111 @@ int mla_b200_combine_packed_f32(const float *parts, int num_parts, long long row
         combine_kernel<float, float><<<cgrid, kCombineThreads, 0, s>>>(
             parts, lse0, wl, (int)rows, rows, static_cast<float *>(out), out_lse, 0,
             (size_t)part_stride, (size_t)part_stride);
+    return launch_status();
+}
+
+// ---------------------------------------------------------------------------
+// Cross-GPU exchange over peer memory (mla_exchange.cuh).
+// ---------------------------------------------------------------------------
+size_t mla_b200_exchange_bytes(int world, long long rows) {
+    if (world <= 0 || world > xchg::kMaxPeers || rows < 0) return 0;
+    return xchg::buffer_bytes(world, rows);
+}
+
+int mla_b200_exchange_alloc(int world, long long rows, void **buf) {
+    if (buf == nullptr || world <= 0 || world > xchg::kMaxPeers || rows <= 0 || rows >= (1LL << 31))
+        return MLA_B200_ERR_INVALID_ARG;
+    *buf = nullptr;
+    int dev;
+    DevInfo info;
+    int st = current_device(&dev, &info);
+    if (st != MLA_B200_OK) return st;
+    void *p = nullptr;
+    const size_t bytes = xchg::buffer_bytes(world, rows);
+    cudaError_t e = cudaMalloc(&p, bytes);
+    if (e != cudaSuccess) return cuda_failure(e);
+    e = cudaMemset(p, 0, bytes);
+    if (e != cudaSuccess) {
+        cudaFree(p);
+        return cuda_failure(e);
+    }
+    *buf = p;
+    return MLA_B200_OK;
+}
+
+int mla_b200_exchange_free(void *buf) {
+    if (buf == nullptr) return MLA_B200_OK;
+    const cudaError_t e = cudaFree(buf);
+    return e == cudaSuccess ? MLA_B200_OK : cuda_failure(e);
+}
+
+int mla_b200_ipc_handle(const void *buf, void *handle_64_bytes) {
+    if (buf == nullptr || handle_64_bytes == nullptr) return MLA_B200_ERR_INVALID_ARG;
+    static_assert(sizeof(cudaIpcMemHandle_t) == 64, "IPC handle size");
+    cudaIpcMemHandle_t h;
+    const cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void *>(buf));
+    if (e != cudaSuccess) return cuda_failure(e);
+    std::memcpy(handle_64_bytes, &h, sizeof(h));
+    return MLA_B200_OK;
+}
+
+int mla_b200_ipc_open(const void *handle_64_bytes, void **peer_buf) {
+    if (handle_64_bytes == nullptr || peer_buf == nullptr) return MLA_B200_ERR_INVALID_ARG;
+    *peer_buf = nullptr;
+    cudaIpcMemHandle_t h;
+    std::memcpy(&h, handle_64_bytes, sizeof(h));
+    const cudaError_t e = cudaIpcOpenMemHandle(peer_buf, h, cudaIpcMemLazyEnablePeerAccess);
+    return e == cudaSuccess ? MLA_B200_OK : cuda_failure(e);
+}
+
+int mla_b200_ipc_close(void *peer_buf) {
+    if (peer_buf == nullptr) return MLA_B200_OK;
+    const cudaError_t e = cudaIpcCloseMemHandle(peer_buf);
+    return e == cudaSuccess ? MLA_B200_OK : cuda_failure(e);
+}
+
+int mla_b200_exchange_put_f32(const float *part, long long rows, void *const *peer_bufs, int rank, int world,
+                              void *stream) {
+    if (world <= 0 || world > xchg::kMaxPeers || rank < 0 || rank >= world || rows <= 0 || rows >= (1LL << 31))
+        return MLA_B200_ERR_INVALID_ARG;
+    if (part == nullptr || peer_bufs == nullptr || !aligned(part, 16)) return MLA_B200_ERR_INVALID_ARG;
+    xchg::Peers peers = {};
+    for (int g = 0; g < world; ++g) {
+        if (peer_bufs[g] == nullptr || !aligned(peer_bufs[g], 256)) return MLA_B200_ERR_INVALID_ARG;
+        peers.buf[g] = static_cast<uint8_t *>(peer_bufs[g]);
+    }
+    int dev;
+    DevInfo info;
+    int st = current_device(&dev, &info);
+    if (st != MLA_B200_OK) return st;
+    const long long stride = xchg::stride_floats(rows);
+    const long long n4 = stride / 4;
+    const unsigned grid = (unsigned)std::min<long long>(info.sms, cdiv(n4, 256));
+    xchg::exchange_put_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
+        reinterpret_cast<const float4 *>(part), n4, peers, rank, world, stride);
+    return launch_status();
+}
+
+int mla_b200_exchange_merge_f32(const void *own_buf, int world, long long rows, void *out, int out_dtype,
+                                float *out_lse, unsigned long long wait_limit_ns, void *stream) {
+    if (world <= 0 || world > xchg::kMaxPeers || rows <= 0 || rows >= (1LL << 31)) return MLA_B200_ERR_INVALID_ARG;
+    if (own_buf == nullptr || out == nullptr || !aligned(own_buf, 256) || !aligned(out, 16))
+        return MLA_B200_ERR_INVALID_ARG;
+    if (out_dtype != MLA_B200_OUT_F16 && out_dtype != MLA_B200_OUT_F32) return MLA_B200_ERR_INVALID_ARG;
+    if (wait_limit_ns == 0 || wait_limit_ns > 60000000000ull) return MLA_B200_ERR_INVALID_ARG;
+    int dev;
+    DevInfo info;
+    int st = current_device(&dev, &info);
+    if (st != MLA_B200_OK) return st;
+    const long long stride = xchg::stride_floats(rows);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    const uint8_t *own = static_cast<const uint8_t *>(own_buf);
+    if (out_dtype == MLA_B200_OUT_F16)
+        xchg::exchange_merge_kernel<__half><<<(unsigned)rows, 128, 0, s>>>(own, world, rows, stride, wait_limit_ns,
+                                                                           static_cast<__half *>(out), out_lse);
+    else
+        xchg::exchange_merge_kernel<float><<<(unsigned)rows, 128, 0, s>>>(own, world, rows, stride, wait_limit_ns,
+                                                                          static_cast<float *>(out), out_lse);
     return launch_status();
 }
 

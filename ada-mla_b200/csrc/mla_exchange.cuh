@@ -1,0 +1,145 @@
+// mla_exchange.cuh -- the KV-split decode's cross-GPU exchange over NVLink peer
+// memory, replacing an NCCL all-gather of the ranks' (O, LSE) partials.
+//
+// One process per GPU.  Every rank owns one exchange buffer (cudaMalloc, zeroed),
+// mapped into every other rank's address space through CUDA IPC:
+//
+//   header [256 B]: flags[kMaxPeers] (u64: the last epoch rank g published into
+//                   this buffer), epoch (u64: this rank's last published epoch),
+//                   done (u32: blocks of the running put kernel that finished)
+//   data:           [2 parities][world][stride] fp32, stride = rows * 513
+//                   rounded up to 4 floats (O [rows, 512] normalized, then LSE)
+//
+// exchange_put_kernel (rank r, epoch e = its previous epoch + 1): every block
+// copies its share of r's packed (O, LSE) into part r of parity e & 1 of every
+// rank's buffer (own included) with plain stores over NVLink, fences at system
+// scope and counts itself done; the last block publishes e in r's own header
+// and stores e (release, system scope) into flags[r] of every rank's buffer.
+//
+// exchange_merge_kernel (rank r, epoch e read from its own header, written by
+// its put kernel just before in stream order): thread 0 of every block waits,
+// bounded by limit_ns, until flags[g] >= e for every g (acquire, system scope),
+// then the block LSE-merges its row over the G parts of parity e & 1.
+//
+// Two parities make the reuse safe: rank A writes epoch e + 2 into B's parity
+// (e & 1) only after its own merge of e + 1, which waited for B's flag e + 1,
+// which B stored after its merge of e finished (stream order on B).
+// No TMA, no multicast: plain loads and stores to peer memory.
+#pragma once
+
+#include "mla_common.cuh"
+
+namespace mla {
+namespace xchg {
+
+constexpr int kMaxPeers = 16;
+constexpr int kHeaderBytes = 256;
+constexpr int kOffEpoch = kMaxPeers * 8;   // 128
+constexpr int kOffDone = kOffEpoch + 8;    // 136
+static_assert(kOffDone + 4 <= kHeaderBytes, "exchange header");
+
+__host__ __device__ constexpr long long stride_floats(long long rows) { return (rows * (kDV + 1) + 3) / 4 * 4; }
+
+__host__ __device__ constexpr size_t buffer_bytes(int world, long long rows) {
+    return (size_t)kHeaderBytes + 2ull * (size_t)world * (size_t)stride_floats(rows) * sizeof(float);
+}
+
+struct Peers {
+    uint8_t *buf[kMaxPeers];  // every rank's exchange buffer as mapped in this process (own included)
+};
+
+__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
+    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
+    unsigned long long v;
+    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
+    return v;
+}
+
+// part: this rank's packed (O, LSE), stride floats (16-byte aligned).
+__global__ void __launch_bounds__(256) exchange_put_kernel(const float4 *__restrict__ part, long long n4,
+                                                           Peers peers, int rank, int world, long long stride) {
+    uint8_t *own = peers.buf[rank];
+    // every block reads the previous epoch before any block can count itself done
+    const unsigned long long e = *reinterpret_cast<volatile unsigned long long *>(own + kOffEpoch) + 1;
+    const size_t off = ((size_t)(e & 1) * (size_t)world + (size_t)rank) * (size_t)stride;  // floats
+    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
+        const float4 v = part[i];
+        for (int g = 0; g < world; ++g)
+            reinterpret_cast<float4 *>(reinterpret_cast<float *>(peers.buf[g] + kHeaderBytes) + off)[i] = v;
+    }
+    __threadfence_system();  // this thread's stores, visible to every GPU
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        unsigned int *done = reinterpret_cast<unsigned int *>(own + kOffDone);
+        if (atomicAdd(done, 1u) == gridDim.x - 1) {  // the last block: every block's data is out
+            *done = 0u;
+            *reinterpret_cast<volatile unsigned long long *>(own + kOffEpoch) = e;
+            __threadfence_system();
+            for (int g = 0; g < world; ++g)
+                st_release_sys(reinterpret_cast<unsigned long long *>(peers.buf[g]) + rank, e);
+        }
+    }
+}
+
+// One block of 128 threads per row; thread t owns columns [4 t, 4 t + 4).
+template <typename OutT>
+__global__ void __launch_bounds__(128) exchange_merge_kernel(const uint8_t *own, int world, long long rows,
+                                                             long long stride, unsigned long long limit_ns,
+                                                             OutT *__restrict__ out, float *__restrict__ out_lse) {
+    __shared__ int ok_s;
+    const long long row = blockIdx.x;
+    const unsigned long long e = *reinterpret_cast<const volatile unsigned long long *>(own + kOffEpoch);
+    if (threadIdx.x == 0) {
+        const unsigned long long *flags = reinterpret_cast<const unsigned long long *>(own);
+        int ok = 1;
+        uint64_t t0 = 0;
+        for (int g = 0; g < world && ok; ++g) {
+            for (uint32_t n = 0; ld_acquire_sys(flags + g) < e; ++n) {
+                if ((n & 255u) == 255u) {
+                    const uint64_t t = globaltimer_ns();
+                    if (t0 == 0) t0 = t;
+                    else if (t - t0 > limit_ns) { set_device_error(kErrWaitPeer); ok = 0; break; }
+                }
+            }
+        }
+        ok_s = ok;
+    }
+    __syncthreads();
+    if (!ok_s) return;
+    const float *data = reinterpret_cast<const float *>(own + kHeaderBytes) + (size_t)(e & 1) * (size_t)world * (size_t)stride;
+    float mx = -INFINITY;
+    for (int g = 0; g < world; ++g) mx = fmaxf(mx, __ldcg(data + (size_t)g * stride + (size_t)rows * kDV + row));
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float wsum = 0.f;
+    if (mx != -INFINITY) {
+        for (int g = 0; g < world; ++g) {
+            const float *p = data + (size_t)g * stride;
+            const float lse = __ldcg(p + (size_t)rows * kDV + row);
+            const float w = lse == -INFINITY ? 0.f : __expf(lse - mx);
+            const float4 v = __ldcg(reinterpret_cast<const float4 *>(p + (size_t)row * kDV) + threadIdx.x);
+            wsum += w;
+            acc.x = fmaf(w, v.x, acc.x);
+            acc.y = fmaf(w, v.y, acc.y);
+            acc.z = fmaf(w, v.z, acc.z);
+            acc.w = fmaf(w, v.w, acc.w);
+        }
+    }
+    const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+    OutT *dst = out + (size_t)row * kDV + threadIdx.x * 4;
+    if constexpr (sizeof(OutT) == 4) {
+        *reinterpret_cast<float4 *>(dst) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+    } else {
+        const __half2 a = __floats2half2_rn(acc.x * inv, acc.y * inv), b = __floats2half2_rn(acc.z * inv, acc.w * inv);
+        uint2 u;
+        u.x = *reinterpret_cast<const uint32_t *>(&a);
+        u.y = *reinterpret_cast<const uint32_t *>(&b);
+        *reinterpret_cast<uint2 *>(dst) = u;
+    }
+    if (out_lse != nullptr && threadIdx.x == 0) out_lse[row] = wsum > 0.f ? mx + __logf(wsum) : -INFINITY;
+}
+
+}  // namespace xchg
+}  // namespace mla

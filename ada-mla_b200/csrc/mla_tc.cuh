@@ -369,6 +369,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
+    if (tid == 0 && p.span != nullptr) atomicMin(p.span, (unsigned long long)globaltimer_ns());
     const uint32_t role = ptx::cluster_ctarank();  // 0 = S-CTA, 1 = O-CTA
     const int cid = (int)ptx::cluster_id_x();
     const int ncl = (int)ptx::nclusters_x();
@@ -413,9 +414,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // is read below.
     if (p.chain) griddep_launch();  // the chained merge may place its CTAs
     griddep_wait();
-    // (the span is published at the end: the atomics here, and the unconditional
-    // trigger, measured 1-3 % slower on batches)
-    const unsigned long long t_start = globaltimer_ns();
 
     const WorkList &wl = p.wl;
 
@@ -794,7 +792,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         // fp8, per-row scales: r becomes y = sl2 * s * (Q8 . C8) + e (the log2
                         // domain, sl2 applied here), the tail masked below
                         const float *kvs = nullptr;
-                        float sl2_eff = sl2;
                         if constexpr (kFp8) {
                             if constexpr (rows_scaled) {
                                 kvs = p.kv_scales + it.row0 + t0;
@@ -806,7 +803,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                                         r[k] = u32_of(fmaf(f32_of(r[k]) * sc, sl2, (float)scale_exp(sc)));
                                     }
                                 }
-                                sl2_eff = 1.f;
                             }
                         }
 
@@ -825,7 +821,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 #pragma unroll
                         for (int k = 8; k < kTS; ++k) m8[k & 7] = fmaxf(m8[k & 7], f32_of(r[k]));
                         const float mx = fmaxf(fmaxf(fmaxf(m8[0], m8[1]), fmaxf(m8[2], m8[3])),
-                                               fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * sl2_eff;
+                                               fmaxf(fmaxf(m8[4], m8[5]), fmaxf(m8[6], m8[7]))) * (rows_scaled ? 1.f : sl2);
                         if (mx > m_used + (kFp8 ? (rows_scaled ? kRescaleLog2Fp8Rows : kRescaleLog2Fp8) : kRescaleLog2)) {
                             alpha = (m_used == -INFINITY) ? 0.f : ptx::ex2(m_used - mx);
                             m_used = mx;
@@ -920,12 +916,8 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
             // fp8: O = (P8 . C8) * o_scale / l, o_scale = kv_scale per tensor, 1 with
             // per-row scales (host); the weights' factor K is in l as well, and the
             // LSE subtracts log2 K
-            float o_scale = 0.f, lse_k = 0.f;
             constexpr bool rows_scaled = kFp8 && kRows;
-            if constexpr (kFp8) {
-                o_scale = p.o_scale;
-                lse_k = rows_scaled ? kP8Log2ScaleRows : kP8Log2Scale;
-            }
+            constexpr float lse_k = rows_scaled ? kP8Log2ScaleRows : kP8Log2Scale;
             ItemCursor cur = items_begin<kSched>(wl, cid, ncl);
             Item it;
             int i;
@@ -981,8 +973,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
                         item_range<kSched>(wl, it.b, ni0, ni1);
                         const bool single = ni1 - ni0 == 1;
                         float inv_l = l_fin > 0.f ? 1.f / l_fin : 0.f;
-                        if constexpr (kFp8) inv_l *= o_scale;
-                        const float lse = l_fin > 0.f ? (m_fin + __log2f(l_fin) - lse_k) * kLn2 : -INFINITY;
+                        if constexpr (kFp8) inv_l *= p.o_scale;
+                        float lse = l_fin > 0.f ? (m_fin + __log2f(l_fin)) * kLn2 : -INFINITY;
+                        if constexpr (kFp8) lse -= lse_k * kLn2;
                         // 16-bit output: fp16 from fp16 inputs, bf16 from bf16 inputs
                         const bool f16 = (single ? p.out_kind : p.part_kind) != kOutF32;
                         const size_t row_bytes = (size_t)kDV * (f16 ? 2 : 4);
@@ -1063,10 +1056,7 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         ptx::tc_fence_after();
         ptx::tmem_dealloc(tmem, kTmemCols);
     }
-    if (tid == 0 && p.span != nullptr) {
-        atomicMin(p.span, t_start);
-        atomicMax(p.span + 1, (unsigned long long)globaltimer_ns());
-    }
+    if (tid == 0 && p.span != nullptr) atomicMax(p.span + 1, (unsigned long long)globaltimer_ns());
 }
 
 }  // namespace tc

@@ -718,9 +718,11 @@ def _graph_of(fn, steps):
     return graph
 
 
-def kv_split_line(cfg: int, steps: int, rank: int, world: int, local: int) -> dict:
+def kv_split_line(cfg: int, steps: int, rank: int, world: int, local: int, exchange: str = "p2p") -> dict:
     """One sequence's KV length split over the ranks: local decode of the rank's
-    slice into a packed (O, LSE) buffer, one NCCL all-gather, LSE merge."""
+    slice into a packed (O, LSE) buffer, then the exchange: "p2p" = this
+    library's put + merge kernels over NVLink peer memory, "nccl" = one NCCL
+    all-gather and the LSE merge."""
     import torch
 
     from ada_mla import multigpu
@@ -729,7 +731,7 @@ def kv_split_line(cfg: int, steps: int, rank: int, world: int, local: int) -> di
     dev = torch.device("cuda", local)
     wl = make_workload(cfg, seed=0, device=dev)
     n = wl.max_seq_len
-    dec = multigpu.KvSplitDecoder()
+    dec = multigpu.KvSplitDecoder(exchange=exchange)
     lo, hi = dec.bounds(n)
     slice_bytes = max(1, (hi - lo) * wl.batch * HEAD_DIM_K * 2)
     ring = _ring_len(slice_bytes, dev)
@@ -744,8 +746,11 @@ def kv_split_line(cfg: int, steps: int, rank: int, world: int, local: int) -> di
     ms, clocks = timed_replay(graph, steps, world, local)
     del graph
     stages = dec.stage_times_us(wl.query, slices[0], 1.0, reps=20)
+    dec.close()
+    how = ("put of (O, LSE) into every rank's buffer over NVLink peer memory + merge" if exchange == "p2p"
+           else "NCCL all-gather of (O, LSE) + LSE merge")
     return {"workload": f"cfg{cfg}: B={wl.batch} n_h={wl.num_heads} N={n}, KV length split over "
-                        f"{world} GPU(s): local decode + all-gather of (O, LSE) + LSE merge",
+                        f"{world} GPU(s): local decode + {how}", "exchange": exchange,
             "scaling": "strong", "us_per_step": ms * 1e3,
             "value": wl.cache_bytes / (ms * 1e-3) / 1e9, "unit": UNIT,
             "stages_us_rank0": stages, "clocks_sm_mhz": clocks.get("sm_mhz")}
@@ -789,7 +794,9 @@ def multi_gpu_lines(args, rank, world, local) -> dict:
 
     out = {}
     steps = max(10, min(args.steps, 50))
-    out["cfg3_kv_split"] = kv_split_line(3, steps, rank, world, local)
+    out["cfg3_kv_split"] = kv_split_line(3, steps, rank, world, local, "p2p")
+    torch.cuda.empty_cache()
+    out["cfg3_kv_split_nccl"] = kv_split_line(3, steps, rank, world, local, "nccl")
     torch.cuda.empty_cache()
     out["cfg2_sharded"] = sharded_line(2, steps, rank, world, local)
     torch.cuda.empty_cache()
@@ -802,7 +809,9 @@ def run_kv(args):
     import torch
 
     torch.cuda.set_device(local)
-    line = kv_split_line(args.config, args.steps, rank, world, local)
+    line = kv_split_line(args.config, args.steps, rank, world, local, "p2p")
+    torch.cuda.empty_cache()
+    line["nccl_exchange"] = kv_split_line(args.config, args.steps, rank, world, local, "nccl")
     if rank == 0:
         line.update({"metric": METRIC, "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
                      "ms_per_step": line["us_per_step"] / 1e3, "higher_is_better": True,

@@ -95,8 +95,9 @@ MLA_B200_API int mla_b200_set_kernel_timing(void *ev_start, void *ev_stop);
  * counterpart).  While set on the calling host thread, the k-th later launch
  * of that kernel (k counting from 0, wrapping after `slots`) records, in
  * span[2k] and span[2k+1], the %globaltimer (ns) at which its first CTA
- * starts work (after its set-up and the wait for the preceding kernel; atomic
- * min) and at which its last CTA ends (atomic max); the caller initialises
+ * starts (atomic min; under a programmatic launch chain a CTA may start while
+ * the preceding kernel still runs, and that overlap counts) and at which its
+ * last CTA ends (atomic max); the caller initialises
  * each pair to {UINT64_MAX, 0} before the launch runs.  The span excludes the
  * launch latency that an event pair around the launch includes.  `span` is a
  * device array of 2 * slots uint64; NULL (or slots <= 0) turns it off.  Under
@@ -373,6 +374,46 @@ MLA_B200_API int mla_b200_combine_f32(const float *part_o, const float *part_lse
 MLA_B200_API int mla_b200_combine_packed_f32(const float *parts, int num_parts, long long rows,
                                              long long part_stride, void *out, int out_dtype,
                                              float *out_lse, void *stream);
+
+/* ------------------------------------------------------------------------ */
+/* Cross-GPU exchange over NVLink peer memory (no reference counterpart: the   */
+/* reference runs on one GPU).  One process per GPU; replaces the all-gather   */
+/* of the split-KV step: each rank's packed (O, LSE) [rows * 513 fp32] is      */
+/* stored straight into every rank's exchange buffer, then merged there.       */
+/* ------------------------------------------------------------------------ */
+
+/* Bytes of one rank's exchange buffer for `world` ranks (<= 16) and `rows`
+ * (sequences x heads) rows: a 256-byte header of flags, then two parities of
+ * [world][stride] fp32, stride = rows * 513 rounded up to 4. */
+MLA_B200_API size_t mla_b200_exchange_bytes(int world, long long rows);
+
+/* cudaMalloc + zero of one exchange buffer on the current device (free with
+ * mla_b200_exchange_free, after every peer closed its mapping). */
+MLA_B200_API int mla_b200_exchange_alloc(int world, long long rows, void **buf);
+MLA_B200_API int mla_b200_exchange_free(void *buf);
+
+/* CUDA IPC: the 64-byte handle of an exchange buffer, and its mapping in
+ * another process (peer access enabled lazily); close before the owner frees. */
+MLA_B200_API int mla_b200_ipc_handle(const void *buf, void *handle_64_bytes);
+MLA_B200_API int mla_b200_ipc_open(const void *handle_64_bytes, void **peer_buf);
+MLA_B200_API int mla_b200_ipc_close(void *peer_buf);
+
+/* Publish this rank's packed (O, LSE) `part` (rows * 513 fp32, 16-byte
+ * aligned) into part `rank` of every rank's buffer: peer_bufs is a HOST array
+ * of `world` device pointers (every rank's buffer as mapped in this process,
+ * this rank's own at index `rank`).  Stream-ordered, graph-capturable; every
+ * rank calls it once per step, in the same order as its merge. */
+MLA_B200_API int mla_b200_exchange_put_f32(const float *part, long long rows, void *const *peer_bufs,
+                                           int rank, int world, void *stream);
+
+/* Wait until every rank published the step this rank last put, then
+ * LSE-merge the `world` parts into out [rows, 512] (MLA_B200_OUT_F16 or _F32)
+ * and out_lse [rows] (or null).  The wait is bounded by wait_limit_ns (at most
+ * 60 s): on expiry the rows are left unwritten and mla_b200_get_device_error
+ * reports MLA_B200_ERR_DEVICE_TIMEOUT (code 4, a peer wait). */
+MLA_B200_API int mla_b200_exchange_merge_f32(const void *own_buf, int world, long long rows, void *out,
+                                             int out_dtype, float *out_lse,
+                                             unsigned long long wait_limit_ns, void *stream);
 
 /* ------------------------------------------------------------------------ */
 /* Device error word                                                         */

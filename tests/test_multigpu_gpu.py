@@ -38,15 +38,21 @@ def _worker(rank, world, port, mode, results):
                             device_id=torch.device("cuda", rank))
     try:
         g = torch.Generator().manual_seed(11)
-        if mode == "kv":
+        if mode in ("kv", "kv_p2p"):
             b, nh, n = 1, 128, 5000
             q = (torch.randn(b, nh, 576, generator=g) / 192 ** 0.5).half()
             c = torch.randn(b, n, 576, generator=g).half()
-            dec = multigpu.KvSplitDecoder()
+            dec = multigpu.KvSplitDecoder(exchange="p2p" if mode == "kv_p2p" else "nccl")
             lo, hi = dec.bounds(n)
-            out = dec(q.cuda(), c[:, lo:hi].contiguous().cuda(), 1.0)
+            qd, cd = q.cuda(), c[:, lo:hi].contiguous().cuda()
+            outs = [dec(qd, cd, 1.0) for _ in range(3)]  # three steps: both exchange parities
+            torch.cuda.synchronize()
             ref = oracle.mla_decode_oracle(q[0].float().numpy(), c[0].float().numpy(), 1.0, threads=4)
-            d = np.abs(out[0].float().cpu().numpy() - ref)
+            d = np.abs(outs[-1][0].float().cpu().numpy() - ref)
+            assert all(torch.equal(o, outs[0]) for o in outs), "every step gives the same result"
+            from ada_mla import capi
+            assert capi.get_device_error() == 0
+            dec.close()
         else:
             bl, nh, n = 2, 128, 700
             qs = (torch.randn(world, bl, nh, 576, generator=g) / 192 ** 0.5).half()
@@ -63,7 +69,7 @@ def _worker(rank, world, port, mode, results):
 
 
 @needs_two
-@pytest.mark.parametrize("mode", ["kv", "shard"])
+@pytest.mark.parametrize("mode", ["kv", "kv_p2p", "shard"])
 def test_two_gpu_decode(mode):
     import torch.multiprocessing as mp
 
