@@ -61,8 +61,6 @@ __device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long
 // part: this rank's packed (O, LSE), stride floats (16-byte aligned).
 __global__ void __launch_bounds__(256) exchange_put_kernel(const float4 *__restrict__ part, long long n4,
                                                            Peers peers, int rank, int world, long long stride) {
-    griddep_launch();  // the merge may place its blocks (they wait below the trigger)
-    griddep_wait();    // the packed partial is complete (launched as a programmatic dependent)
     uint8_t *own = peers.buf[rank];
     // every block reads the previous epoch before any block can count itself done
     const unsigned long long e = *reinterpret_cast<volatile unsigned long long *>(own + kOffEpoch) + 1;
@@ -95,8 +93,6 @@ __global__ void __launch_bounds__(128) exchange_merge_kernel(const uint8_t *own,
                                                              long long stride, unsigned long long limit_ns,
                                                              OutT *__restrict__ out, float *__restrict__ out_lse) {
     __shared__ int ok_s;
-    griddep_launch();
-    griddep_wait();  // this rank's put kernel (the predecessor) has published its epoch
     const long long row = blockIdx.x;
     const unsigned long long e = *reinterpret_cast<const volatile unsigned long long *>(own + kOffEpoch);
     if (threadIdx.x == 0) {
