@@ -131,14 +131,16 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(
             __syncthreads();
             for (int k = 0; k < n; ++k) wsum += w_s[k];
             const uint4 *src = reinterpret_cast<const uint4 *>(part_o + (size_t)c0 * part_stride + (size_t)h * kDV) + col;
-            // up to 8 splits' loads in flight per thread (predicated at the end)
-            for (int k = g; k < n; k += 8 * kGroups) {
-                uint4 u[8];
+            // up to kInflight splits' loads in flight per thread (predicated at the end):
+            // 96 splits in one round of L2 latency
+            constexpr int kInflight = 12;
+            for (int k = g; k < n; k += kInflight * kGroups) {
+                uint4 u[kInflight];
 #pragma unroll
-                for (int j = 0; j < 8; ++j)
+                for (int j = 0; j < kInflight; ++j)
                     if (k + j * kGroups < n) u[j] = __ldg(src + (size_t)(k + j * kGroups) * step);
 #pragma unroll
-                for (int j = 0; j < 8; ++j) {
+                for (int j = 0; j < kInflight; ++j) {
                     if (k + j * kGroups < n) {
                         float v[kVec];
                         unpack_part<PartT>(u[j], v);
