@@ -131,9 +131,9 @@ __global__ void __launch_bounds__(kCombineThreads) combine_kernel(
             __syncthreads();
             for (int k = 0; k < n; ++k) wsum += w_s[k];
             const uint4 *src = reinterpret_cast<const uint4 *>(part_o + (size_t)c0 * part_stride + (size_t)h * kDV) + col;
-            // up to kInflight splits' loads in flight per thread (predicated at the end):
-            // 96 splits in one round of L2 latency
-            constexpr int kInflight = 12;
+            // up to kInflight splits' loads in flight per thread (predicated at the end;
+            // 12 measured no different on cfg3's 72 splits and 0.25 us slower on cfg1)
+            constexpr int kInflight = 8;
             for (int k = g; k < n; k += kInflight * kGroups) {
                 uint4 u[kInflight];
 #pragma unroll
