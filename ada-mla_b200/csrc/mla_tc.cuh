@@ -369,7 +369,6 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5, lane = tid & 31;
-    if (tid == 0 && p.span != nullptr) atomicMin(p.span, (unsigned long long)globaltimer_ns());
     const uint32_t role = ptx::cluster_ctarank();  // 0 = S-CTA, 1 = O-CTA
     const int cid = (int)ptx::cluster_id_x();
     const int ncl = (int)ptx::nclusters_x();
@@ -414,6 +413,9 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
     // is read below.
     if (p.chain) griddep_launch();  // the chained merge may place its CTAs
     griddep_wait();
+    // the span starts when work can start (a chained launch may have started
+    // early and waited above); it is published at teardown
+    const unsigned long long t_start = globaltimer_ns();
 
     const WorkList &wl = p.wl;
 
@@ -1056,7 +1058,10 @@ __global__ void __cluster_dims__(2, 1, 1) __launch_bounds__(kThreads, 1)
         ptx::tc_fence_after();
         ptx::tmem_dealloc(tmem, kTmemCols);
     }
-    if (tid == 0 && p.span != nullptr) atomicMax(p.span + 1, (unsigned long long)globaltimer_ns());
+    if (tid == 0 && p.span != nullptr) {
+        atomicMin(p.span, t_start);
+        atomicMax(p.span + 1, (unsigned long long)globaltimer_ns());
+    }
 }
 
 }  // namespace tc

@@ -95,9 +95,8 @@ MLA_B200_API int mla_b200_set_kernel_timing(void *ev_start, void *ev_stop);
  * counterpart).  While set on the calling host thread, the k-th later launch
  * of that kernel (k counting from 0, wrapping after `slots`) records, in
  * span[2k] and span[2k+1], the %globaltimer (ns) at which its first CTA
- * starts (atomic min; under a programmatic launch chain a CTA may start while
- * the preceding kernel still runs, and that overlap counts) and at which its
- * last CTA ends (atomic max); the caller initialises
+ * starts work (after its set-up and the wait for the preceding kernel; atomic
+ * min) and at which its last CTA ends (atomic max); the caller initialises
  * each pair to {UINT64_MAX, 0} before the launch runs.  The span excludes the
  * launch latency that an event pair around the launch includes.  `span` is a
  * device array of 2 * slots uint64; NULL (or slots <= 0) turns it off.  Under
