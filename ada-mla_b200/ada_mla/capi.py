@@ -79,6 +79,8 @@ SIGNATURES = {
     "mla_b200_ipc_close": (_c_int, [_vp]),
     "mla_b200_exchange_put_f32": (_c_int, [_vp, _c_ll, ctypes.POINTER(_vp), _c_int, _c_int, _vp]),
     "mla_b200_exchange_merge_f32": (_c_int, [_vp, _c_int, _c_ll, _vp, _c_int, _vp, ctypes.c_ulonglong, _vp]),
+    "mla_b200_exchange_f32": (_c_int, [_vp, _c_ll, ctypes.POINTER(_vp), _c_int, _c_int, _vp, _c_int, _vp,
+                                       ctypes.c_ulonglong, _vp]),
 }
 
 _lib: ctypes.CDLL | None = None

@@ -193,6 +193,24 @@ class PeerExchange:
             self.WAIT_LIMIT_NS, torch.cuda.current_stream().cuda_stream))
         return out, lse
 
+    def exchange(self, packed: torch.Tensor, out_dtype: torch.dtype = torch.float16, device=None):
+        """put + merge as one kernel (mla_b200_exchange_f32) when its blocks fit
+        the device at once, else the two kernels; returns (out, lse)."""
+        from ada_mla import capi
+
+        out = torch.empty((self.rows, HEAD_DIM_V), dtype=torch.float32 if out_dtype == torch.float32
+                          else torch.float16, device=device)
+        lse = torch.empty((self.rows,), dtype=torch.float32, device=device)
+        st = capi.lib().mla_b200_exchange_f32(
+            packed.data_ptr(), self.rows, self._peer_array, self.rank, self.world, out.data_ptr(),
+            capi.OUT_F32 if out_dtype == torch.float32 else capi.OUT_F16, lse.data_ptr(),
+            self.WAIT_LIMIT_NS, torch.cuda.current_stream().cuda_stream)
+        if st == capi.ERR_UNSUPPORTED:
+            self.put(packed)
+            return self.merge(out_dtype, device=device)
+        capi._check("mla_b200_exchange_f32", st)
+        return out, lse
+
     def close(self) -> None:
         from ada_mla import capi
 
@@ -308,9 +326,7 @@ class KvSplitDecoder:
         b, nh = query.shape[0], query.shape[1]
         stride, send, recv = self._local(query, cache_slice, softmax_scale)
         if self.exchange == "p2p":
-            ex = self._peer_exchange(b * nh)
-            ex.put(send)
-            out, out_lse = ex.merge(out_dtype, device=query.device)
+            out, out_lse = self._peer_exchange(b * nh).exchange(send, out_dtype, device=query.device)
         else:
             self._gather(recv, send)
             out, out_lse = self.merge(recv, self.world, b * nh, stride, out_dtype)
@@ -330,7 +346,7 @@ class KvSplitDecoder:
             ex = self._peer_exchange(b * nh)
             stages = {
                 "local_decode": lambda: self._local(query, cache_slice, softmax_scale),
-                "p2p_put_and_merge": lambda: (ex.put(send), ex.merge(torch.float16, device=query.device)),
+                "p2p_exchange": lambda: ex.exchange(send, torch.float16, device=query.device),
             }
         else:
             stages = {

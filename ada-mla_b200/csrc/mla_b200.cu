@@ -1303,6 +1303,43 @@ int mla_b200_exchange_put_f32(const float *part, long long rows, void *const *pe
     return launch_status();
 }
 
+int mla_b200_exchange_f32(const float *part, long long rows, void *const *peer_bufs, int rank, int world, void *out,
+                          int out_dtype, float *out_lse, unsigned long long wait_limit_ns, void *stream) {
+    if (world <= 0 || world > xchg::kMaxPeers || rank < 0 || rank >= world || rows <= 0 || rows >= (1LL << 31))
+        return MLA_B200_ERR_INVALID_ARG;
+    if (part == nullptr || peer_bufs == nullptr || out == nullptr || !aligned(part, 16) || !aligned(out, 16))
+        return MLA_B200_ERR_INVALID_ARG;
+    if (out_dtype != MLA_B200_OUT_F16 && out_dtype != MLA_B200_OUT_F32) return MLA_B200_ERR_INVALID_ARG;
+    if (wait_limit_ns == 0 || wait_limit_ns > 60000000000ull) return MLA_B200_ERR_INVALID_ARG;
+    xchg::Peers peers = {};
+    for (int g = 0; g < world; ++g) {
+        if (peer_bufs[g] == nullptr || !aligned(peer_bufs[g], 256)) return MLA_B200_ERR_INVALID_ARG;
+        peers.buf[g] = static_cast<uint8_t *>(peer_bufs[g]);
+    }
+    int dev;
+    DevInfo info;
+    int st = current_device(&dev, &info);
+    if (st != MLA_B200_OK) return st;
+    // every block must be resident at once (they wait on each other)
+    int per_sm = 0;
+    const cudaError_t oe = out_dtype == MLA_B200_OUT_F16
+        ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, xchg::exchange_fused_kernel<__half>, 128, 0)
+        : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, xchg::exchange_fused_kernel<float>, 128, 0);
+    if (oe != cudaSuccess) return cuda_failure(oe);
+    if (rows > (long long)per_sm * info.sms) return MLA_B200_ERR_UNSUPPORTED;
+    const long long stride = xchg::stride_floats(rows);
+    cudaStream_t s = static_cast<cudaStream_t>(stream);
+    if (out_dtype == MLA_B200_OUT_F16)
+        xchg::exchange_fused_kernel<__half><<<(unsigned)rows, 128, 0, s>>>(part, rows, peers, rank, world, stride,
+                                                                           wait_limit_ns, static_cast<__half *>(out),
+                                                                           out_lse);
+    else
+        xchg::exchange_fused_kernel<float><<<(unsigned)rows, 128, 0, s>>>(part, rows, peers, rank, world, stride,
+                                                                          wait_limit_ns, static_cast<float *>(out),
+                                                                          out_lse);
+    return launch_status();
+}
+
 int mla_b200_exchange_merge_f32(const void *own_buf, int world, long long rows, void *out, int out_dtype,
                                 float *out_lse, unsigned long long wait_limit_ns, void *stream) {
     if (world <= 0 || world > xchg::kMaxPeers || rows <= 0 || rows >= (1LL << 31)) return MLA_B200_ERR_INVALID_ARG;

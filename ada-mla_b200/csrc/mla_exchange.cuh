@@ -21,6 +21,10 @@
 // bounded by limit_ns, until flags[g] >= e for every g (acquire, system scope),
 // then the block LSE-merges its row over the G parts of parity e & 1.
 //
+// exchange_fused_kernel does both in one launch (block = row: put the row,
+// count done, wait for every flag, merge the row) when all its blocks fit on
+// the device at once.
+//
 // Two parities make the reuse safe: rank A writes epoch e + 2 into B's parity
 // (e & 1) only after its own merge of e + 1, which waited for B's flag e + 1,
 // which B stored after its merge of e finished (stream order on B).
@@ -87,32 +91,11 @@ __global__ void __launch_bounds__(256) exchange_put_kernel(const float4 *__restr
     }
 }
 
-// One block of 128 threads per row; thread t owns columns [4 t, 4 t + 4).
+// Block-wide LSE merge of row `row` over the `world` parts at `data` (parity
+// base of a buffer's data region); 128 threads, thread t owns columns [4 t, 4 t + 4).
 template <typename OutT>
-__global__ void __launch_bounds__(128) exchange_merge_kernel(const uint8_t *own, int world, long long rows,
-                                                             long long stride, unsigned long long limit_ns,
-                                                             OutT *__restrict__ out, float *__restrict__ out_lse) {
-    __shared__ int ok_s;
-    const long long row = blockIdx.x;
-    const unsigned long long e = *reinterpret_cast<const volatile unsigned long long *>(own + kOffEpoch);
-    if (threadIdx.x == 0) {
-        const unsigned long long *flags = reinterpret_cast<const unsigned long long *>(own);
-        int ok = 1;
-        uint64_t t0 = 0;
-        for (int g = 0; g < world && ok; ++g) {
-            for (uint32_t n = 0; ld_acquire_sys(flags + g) < e; ++n) {
-                if ((n & 255u) == 255u) {
-                    const uint64_t t = globaltimer_ns();
-                    if (t0 == 0) t0 = t;
-                    else if (t - t0 > limit_ns) { set_device_error(kErrWaitPeer); ok = 0; break; }
-                }
-            }
-        }
-        ok_s = ok;
-    }
-    __syncthreads();
-    if (!ok_s) return;
-    const float *data = reinterpret_cast<const float *>(own + kHeaderBytes) + (size_t)(e & 1) * (size_t)world * (size_t)stride;
+__device__ __forceinline__ void merge_row(const float *data, int world, long long rows, long long stride,
+                                          long long row, OutT *__restrict__ out, float *__restrict__ out_lse) {
     float mx = -INFINITY;
     for (int g = 0; g < world; ++g) mx = fmaxf(mx, __ldcg(data + (size_t)g * stride + (size_t)rows * kDV + row));
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
@@ -142,6 +125,94 @@ __global__ void __launch_bounds__(128) exchange_merge_kernel(const uint8_t *own,
         *reinterpret_cast<uint2 *>(dst) = u;
     }
     if (out_lse != nullptr && threadIdx.x == 0) out_lse[row] = wsum > 0.f ? mx + __logf(wsum) : -INFINITY;
+}
+
+// One block of 128 threads per row; thread t owns columns [4 t, 4 t + 4).
+template <typename OutT>
+__global__ void __launch_bounds__(128) exchange_merge_kernel(const uint8_t *own, int world, long long rows,
+                                                             long long stride, unsigned long long limit_ns,
+                                                             OutT *__restrict__ out, float *__restrict__ out_lse) {
+    __shared__ int ok_s;
+    const long long row = blockIdx.x;
+    const unsigned long long e = *reinterpret_cast<const volatile unsigned long long *>(own + kOffEpoch);
+    if (threadIdx.x == 0) {
+        const unsigned long long *flags = reinterpret_cast<const unsigned long long *>(own);
+        int ok = 1;
+        uint64_t t0 = 0;
+        for (int g = 0; g < world && ok; ++g) {
+            for (uint32_t n = 0; ld_acquire_sys(flags + g) < e; ++n) {
+                if ((n & 255u) == 255u) {
+                    const uint64_t t = globaltimer_ns();
+                    if (t0 == 0) t0 = t;
+                    else if (t - t0 > limit_ns) { set_device_error(kErrWaitPeer); ok = 0; break; }
+                }
+            }
+        }
+        ok_s = ok;
+    }
+    __syncthreads();
+    if (!ok_s) return;
+    merge_row(reinterpret_cast<const float *>(own + kHeaderBytes) + (size_t)(e & 1) * (size_t)world * (size_t)stride,
+              world, rows, stride, row, out, out_lse);
+}
+
+// The whole exchange in one kernel: block `row` stores its row of this rank's
+// packed (O, LSE) into every rank's buffer, the blocks count themselves done
+// and the last one publishes the epoch (as exchange_put_kernel), then every
+// block waits for every rank's flag and merges its row (as
+// exchange_merge_kernel).  The blocks wait on each other through the done
+// count, so all of them must be resident at once: the host launches it only
+// when the grid fits the device's occupancy (else put + merge); a block that
+// waits in vain (another kernel holding SMs) gives up after limit_ns with the
+// peer-wait code, like the merge.
+template <typename OutT>
+__global__ void __launch_bounds__(128) exchange_fused_kernel(const float *__restrict__ part, long long rows,
+                                                             Peers peers, int rank, int world, long long stride,
+                                                             unsigned long long limit_ns, OutT *__restrict__ out,
+                                                             float *__restrict__ out_lse) {
+    __shared__ int ok_s;
+    const long long row = blockIdx.x;
+    uint8_t *own = peers.buf[rank];
+    const unsigned long long e = *reinterpret_cast<volatile unsigned long long *>(own + kOffEpoch) + 1;
+    const size_t base = (size_t)(e & 1) * (size_t)world * (size_t)stride;  // floats: this epoch's parity
+    const size_t mine = base + (size_t)rank * (size_t)stride;
+    {
+        const float4 v = reinterpret_cast<const float4 *>(part + (size_t)row * kDV)[threadIdx.x];
+        const float lse = part[(size_t)rows * kDV + row];
+        for (int g = 0; g < world; ++g) {
+            float *d = reinterpret_cast<float *>(peers.buf[g] + kHeaderBytes) + mine;
+            reinterpret_cast<float4 *>(d + (size_t)row * kDV)[threadIdx.x] = v;
+            if (threadIdx.x == 0) d[(size_t)rows * kDV + row] = lse;
+        }
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        __threadfence_system();
+        unsigned int *done = reinterpret_cast<unsigned int *>(own + kOffDone);
+        if (atomicAdd(done, 1u) == gridDim.x - 1) {
+            *done = 0u;
+            *reinterpret_cast<volatile unsigned long long *>(own + kOffEpoch) = e;
+            __threadfence_system();
+            for (int g = 0; g < world; ++g)
+                st_release_sys(reinterpret_cast<unsigned long long *>(peers.buf[g]) + rank, e);
+        }
+        const unsigned long long *flags = reinterpret_cast<const unsigned long long *>(own);
+        int ok = 1;
+        uint64_t t0 = 0;
+        for (int g = 0; g < world && ok; ++g) {
+            for (uint32_t n = 0; ld_acquire_sys(flags + g) < e; ++n) {
+                if ((n & 255u) == 255u) {
+                    const uint64_t t = globaltimer_ns();
+                    if (t0 == 0) t0 = t;
+                    else if (t - t0 > limit_ns) { set_device_error(kErrWaitPeer); ok = 0; break; }
+                }
+            }
+        }
+        ok_s = ok;
+    }
+    __syncthreads();
+    if (!ok_s) return;
+    merge_row(reinterpret_cast<const float *>(own + kHeaderBytes) + base, world, rows, stride, row, out, out_lse);
 }
 
 }  // namespace xchg

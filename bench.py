@@ -747,7 +747,8 @@ def kv_split_line(cfg: int, steps: int, rank: int, world: int, local: int, excha
     del graph
     stages = dec.stage_times_us(wl.query, slices[0], 1.0, reps=20)
     dec.close()
-    how = ("put of (O, LSE) into every rank's buffer over NVLink peer memory + merge" if exchange == "p2p"
+    how = ("one exchange kernel: (O, LSE) stored into every rank's buffer over NVLink peer memory, then merged"
+           if exchange == "p2p"
            else "NCCL all-gather of (O, LSE) + LSE merge")
     return {"workload": f"cfg{cfg}: B={wl.batch} n_h={wl.num_heads} N={n}, KV length split over "
                         f"{world} GPU(s): local decode + {how}", "exchange": exchange,

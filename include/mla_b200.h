@@ -414,6 +414,16 @@ MLA_B200_API int mla_b200_exchange_merge_f32(const void *own_buf, int world, lon
                                              int out_dtype, float *out_lse,
                                              unsigned long long wait_limit_ns, void *stream);
 
+/* Put and merge in one kernel launch (one block per row): the same result as
+ * mla_b200_exchange_put_f32 followed by mla_b200_exchange_merge_f32, one launch
+ * fewer.  Its blocks wait on each other, so all `rows` blocks must be resident
+ * at once: MLA_B200_ERR_UNSUPPORTED when they do not fit the device (use put +
+ * merge then).  A block kept from running by other work on the device makes
+ * the wait run out (device error code 4, rows left unwritten). */
+MLA_B200_API int mla_b200_exchange_f32(const float *part, long long rows, void *const *peer_bufs, int rank,
+                                       int world, void *out, int out_dtype, float *out_lse,
+                                       unsigned long long wait_limit_ns, void *stream);
+
 /* ------------------------------------------------------------------------ */
 /* Device error word                                                         */
 /* ------------------------------------------------------------------------ */

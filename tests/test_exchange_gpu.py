@@ -55,6 +55,58 @@ def test_single_rank_put_merge_steps():
         ex.close()
 
 
+def test_single_rank_fused_exchange_matches_put_merge():
+    """The one-kernel exchange (mla_b200_exchange_f32) against the numpy merge,
+    steps alternating with put + merge on the same buffer (the epochs and
+    parities stay in step between the two forms)."""
+    from ada_mla import capi
+    from ada_mla.multigpu import PeerExchange
+
+    rows = 136
+    ex = PeerExchange(rows)
+    try:
+        g = torch.Generator().manual_seed(5)
+        for step in range(5):
+            parts, _ = _packed(rows, 1, g)
+            if step % 2 == 0:
+                out, lse = ex.exchange(parts[0].cuda(), torch.float32, device="cuda")
+            else:
+                ex.put(parts[0].cuda())
+                out, lse = ex.merge(torch.float32, device="cuda")
+            torch.cuda.synchronize()
+            ref_o, ref_lse = _np_merge(parts, rows)
+            np.testing.assert_allclose(out.cpu().numpy(), ref_o, rtol=0, atol=1e-5, err_msg=f"step {step}")
+            np.testing.assert_allclose(lse.cpu().numpy(), ref_lse, rtol=0, atol=1e-5)
+        assert capi.get_device_error() == 0
+    finally:
+        ex.close()
+
+
+def test_fused_exchange_wait_runs_out_when_a_peer_never_publishes():
+    from ada_mla import capi
+
+    lib = capi.lib()
+    rows, world = 8, 2
+    buf = ctypes.c_void_p()
+    assert lib.mla_b200_exchange_alloc(world, rows, ctypes.byref(buf)) == capi.OK
+    try:
+        parts, _ = _packed(rows, 1, torch.Generator().manual_seed(6))
+        part = parts[0].cuda()
+        s = torch.cuda.current_stream().cuda_stream
+        peers = (ctypes.c_void_p * world)(buf.value, buf.value)
+        out = torch.full((rows, 512), 7.0, device="cuda")
+        assert lib.mla_b200_exchange_f32(part.data_ptr(), rows, peers, 0, world, out.data_ptr(), capi.OUT_F32,
+                                         None, 2_000_000, s) == capi.OK
+        torch.cuda.synchronize()
+        code = ctypes.c_int(0)
+        assert lib.mla_b200_get_device_error(ctypes.byref(code), s) == capi.ERR_DEVICE_TIMEOUT
+        assert code.value == 4
+        assert bool((out == 7.0).all())
+    finally:
+        torch.cuda.synchronize()
+        lib.mla_b200_exchange_free(buf.value)
+
+
 def test_merge_wait_runs_out_when_a_peer_never_publishes():
     """A two-rank buffer whose rank 1 never puts: rank 0's merge gives up after
     its 2 ms limit with the peer-wait code, and leaves out untouched."""
