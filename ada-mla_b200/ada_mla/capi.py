@@ -81,6 +81,9 @@ SIGNATURES = {
     "mla_b200_exchange_merge_f32": (_c_int, [_vp, _c_int, _c_ll, _vp, _c_int, _vp, ctypes.c_ulonglong, _vp]),
     "mla_b200_exchange_f32": (_c_int, [_vp, _c_ll, ctypes.POINTER(_vp), _c_int, _c_int, _vp, _c_int, _vp,
                                        ctypes.c_ulonglong, _vp]),
+    "mla_b200_decode_exchange_f16": (_c_int, [_vp, _vp, _vp, _c_int, _c_int, _c_ll, _c_int, _c_float, _c_int,
+                                              ctypes.POINTER(_vp), _c_int, _c_int, _vp, _vp, _c_int, _vp,
+                                              ctypes.c_ulonglong, _vp, _c_size, _vp]),
 }
 
 _lib: ctypes.CDLL | None = None

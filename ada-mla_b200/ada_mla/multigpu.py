@@ -211,6 +211,30 @@ class PeerExchange:
         capi._check("mla_b200_exchange_f32", st)
         return out, lse
 
+    def decode_exchange(self, query: torch.Tensor, cache_slice: torch.Tensor, softmax_scale: float,
+                        workspace: torch.Tensor, direct: torch.Tensor, out_dtype: torch.dtype = torch.float16):
+        """This rank's decode of its dense KV slice and the whole exchange, the
+        slice's split merge included, in one decode launch and ONE exchange
+        kernel (mla_b200_decode_exchange_f16); ``direct`` is [packed_stride(rows)]
+        fp32 scratch.  Returns (out, lse), or None when the exchange kernel's rows
+        do not fit the device at once (nothing was launched then)."""
+        from ada_mla import capi
+
+        b, nh, n = query.shape[0], query.shape[1], cache_slice.shape[1]
+        out = torch.empty((self.rows, HEAD_DIM_V), dtype=torch.float32 if out_dtype == torch.float32
+                          else torch.float16, device=query.device)
+        lse = torch.empty((self.rows,), dtype=torch.float32, device=query.device)
+        st = capi.lib().mla_b200_decode_exchange_f16(
+            query.data_ptr(), cache_slice.data_ptr(), None, b, nh, b * n, n, float(softmax_scale), -1,
+            self._peer_array, self.rank, self.world, direct.data_ptr(), out.data_ptr(),
+            capi.OUT_F32 if out_dtype == torch.float32 else capi.OUT_F16, lse.data_ptr(),
+            self.WAIT_LIMIT_NS, workspace.data_ptr(), workspace.numel(),
+            torch.cuda.current_stream().cuda_stream)
+        if st == capi.ERR_UNSUPPORTED:
+            return None
+        capi._check("mla_b200_decode_exchange_f16", st)
+        return out, lse
+
     def close(self) -> None:
         from ada_mla import capi
 
@@ -244,6 +268,9 @@ class KvSplitDecoder:
     ``exchange="p2p"`` replaces the all-gather and the merge by ``PeerExchange``:
     the packed partial goes straight into every rank's buffer over NVLink and is
     merged there (CUDA only; ``close()`` releases the mappings on every rank).
+    With the default CUDA decode, fp16 inputs and a non-empty slice, the slice's
+    own split merge joins that kernel too (``PeerExchange.decode_exchange``;
+    ``fuse=False`` keeps it a kernel of its own).
     """
 
     group: dist.ProcessGroup | None = None
@@ -251,6 +278,7 @@ class KvSplitDecoder:
     merge: Callable | None = None
     make_workspace: Callable | None = None
     exchange: str = "nccl"
+    fuse: bool = True  # p2p: the slice's split merge joins the exchange kernel where it applies
 
     def __post_init__(self):
         self.local_decode = self.local_decode or _cuda_partial
@@ -258,6 +286,7 @@ class KvSplitDecoder:
         self.make_workspace = self.make_workspace or _cuda_workspace
         self._bufs: dict = {}
         self._peers: dict = {}
+        self._fused_ok: dict = {}  # (B, n_h) -> the one-kernel exchange fits the device
         if self.exchange not in ("nccl", "p2p"):
             raise ValueError(f"exchange must be 'nccl' or 'p2p', not {self.exchange!r}")
 
@@ -318,12 +347,31 @@ class KvSplitDecoder:
             lse.fill_(float("-inf"))
         return stride, send, recv
 
+    def _fused(self, query: torch.Tensor, cache_slice: torch.Tensor, softmax_scale: float,
+               out_dtype: torch.dtype):
+        """The decode + one-kernel exchange of ``PeerExchange.decode_exchange``
+        where it applies, else None."""
+        if (self.exchange != "p2p" or not self.fuse or self.local_decode is not _cuda_partial
+                or query.dtype != torch.float16 or cache_slice.shape[1] == 0
+                or not self._fused_ok.get(tuple(query.shape[:2]), True)):
+            return None
+        b, nh = query.shape[0], query.shape[1]
+        _, send, _, ws = self._buffers(query, cache_slice)
+        res = self._peer_exchange(b * nh).decode_exchange(query, cache_slice, softmax_scale, ws, send, out_dtype)
+        self._fused_ok[(b, nh)] = res is not None
+        return res
+
     def __call__(self, query: torch.Tensor, cache_slice: torch.Tensor, softmax_scale: float,
                  out_dtype: torch.dtype = torch.float16, return_lse: bool = False):
         """query [B, n_h, 576] (identical on every rank); cache_slice
         [B, N_r, 576] = this rank's rows of a dense cache (N_r may be 0).
         Returns O* [B, n_h, 512] on every rank."""
         b, nh = query.shape[0], query.shape[1]
+        fused = self._fused(query, cache_slice, softmax_scale, out_dtype)
+        if fused is not None:
+            out, out_lse = fused
+            out = out.reshape(b, nh, HEAD_DIM_V)
+            return (out, out_lse.reshape(b, nh)) if return_lse else out
         stride, send, recv = self._local(query, cache_slice, softmax_scale)
         if self.exchange == "p2p":
             out, out_lse = self._peer_exchange(b * nh).exchange(send, out_dtype, device=query.device)
@@ -335,10 +383,12 @@ class KvSplitDecoder:
 
     def stage_times_us(self, query: torch.Tensor, cache_slice: torch.Tensor, softmax_scale: float,
                        reps: int = 20) -> dict:
-        """Device time of each stage (local decode, all-gather, merge): each stage
-        captured `reps` times in a CUDA graph, one replay between CUDA events on
-        this rank's stream (launch overhead excluded, as in the timed step).
-        Every rank must call it (the all-gather stage is collective)."""
+        """Device time of each stage (local decode, all-gather, merge; p2p: local
+        decode, exchange, and decode + exchange as one step where fused): each
+        stage captured `reps` times in a CUDA graph, one replay between CUDA
+        events on this rank's stream (launch overhead excluded, as in the timed
+        step), after one untimed run of the stage that aligns the ranks on the
+        device.  Every rank must call it (the exchange stages are collective)."""
         b, nh = query.shape[0], query.shape[1]
         stride, send, recv = self._local(query, cache_slice, softmax_scale)
         times = {}
@@ -348,6 +398,8 @@ class KvSplitDecoder:
                 "local_decode": lambda: self._local(query, cache_slice, softmax_scale),
                 "p2p_exchange": lambda: ex.exchange(send, torch.float16, device=query.device),
             }
+            if self._fused(query, cache_slice, softmax_scale, torch.float16) is not None:
+                stages["decode_exchange"] = lambda: self._fused(query, cache_slice, softmax_scale, torch.float16)
         else:
             stages = {
                 "local_decode": lambda: self._local(query, cache_slice, softmax_scale),
@@ -366,6 +418,7 @@ class KvSplitDecoder:
             torch.cuda.synchronize()
             self._barrier()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            fn()  # a collective stage completes on every rank together: the events start aligned
             e0.record()
             graph.replay()
             e1.record()

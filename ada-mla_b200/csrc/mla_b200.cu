@@ -339,6 +339,16 @@ struct MtpArgs {
     int heads;
 };
 
+// The split-KV multi-GPU step's exchange, fused into the decode's merge
+// (xchg::exchange_combine_kernel): the decode writes single-item rows as fp32
+// (O, LSE) into `direct` (the packed layout, O [rows, 512] then LSE [rows]).
+struct XchgArgs {
+    xchg::Peers peers;
+    int rank, world;
+    unsigned long long limit_ns;
+    float *direct;
+};
+
 struct PagedArgs {
     const int32_t *block_table;
     const int32_t *seq_lens;
@@ -388,7 +398,8 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
                      int num_heads, long long total_tokens, int max_seq_len, float scale,
                      int num_splits, void *out, int out_dtype, float *out_lse, void *workspace,
                      size_t workspace_bytes, cudaStream_t stream, const PagedArgs *pg = nullptr,
-                     const Fp8Args *f8 = nullptr, const MtpArgs *mtp = nullptr, int group = 1) {
+                     const Fp8Args *f8 = nullptr, const MtpArgs *mtp = nullptr, int group = 1,
+                     const XchgArgs *xa = nullptr) {
     int dev;
     DevInfo info;
     int st = current_device(&dev, &info);
@@ -411,6 +422,21 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     if (virt && (!tc_path || pg != nullptr || f8 != nullptr || mtp != nullptr || batch % group != 0))
         return MLA_B200_ERR_UNSUPPORTED;
     const long long plan_total = virt ? total_tokens * group : total_tokens;
+    if (xa != nullptr) {
+        // fp16 inputs on the tensor-core kernel only (fp16 partials, fp32 direct
+        // rows), and every block of the exchange kernel resident at once (they
+        // wait on each other); checked before anything is launched
+        if (!tc_path || kBf16 || pg != nullptr || f8 != nullptr || mtp != nullptr || virt)
+            return MLA_B200_ERR_UNSUPPORTED;
+        int per_sm = 0;
+        const cudaError_t oe = out_dtype == MLA_B200_OUT_F16
+            ? cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                  &per_sm, xchg::exchange_combine_kernel<__half, __half>, kCombineThreads, 0)
+            : cudaOccupancyMaxActiveBlocksPerMultiprocessor(
+                  &per_sm, xchg::exchange_combine_kernel<__half, float>, kCombineThreads, 0);
+        if (oe != cudaSuccess) return cuda_failure(oe);
+        if ((long long)batch * num_heads > (long long)per_sm * info.sms) return MLA_B200_ERR_UNSUPPORTED;
+    }
     // (A single sequence splits evenly in the chunked schedule already.)
     const bool balanced = tc_path && num_splits <= 0 && batch > 1;
     int chunk = chunk_for(batch, plan_total, max_seq_len, num_splits, info.sms, num_heads);
@@ -532,6 +558,11 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
             tp.out_kind = out_dtype == MLA_B200_OUT_F16 ? tc::kOutF16
                           : out_dtype == MLA_B200_OUT_BF16 ? tc::kOutBF16 : tc::kOutF32;
             tp.out_lse = out_lse;
+            if (xa != nullptr) {  // single-item rows go to the exchange's direct buffer
+                tp.out = xa->direct;
+                tp.out_kind = tc::kOutF32;
+                tp.out_lse = xa->direct + (size_t)batch * num_heads * kDV;
+            }
             tp.max_blocks = pg != nullptr ? pg->max_blocks : 0;
             if (mtp != nullptr) tp.mtp = (mtp->tokens << 16) | mtp->heads;
             if (f8 != nullptr) {
@@ -582,9 +613,22 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
             timing_mark(t_ev_stop, stream);
         }
     }
+    const long long rows = (long long)batch * num_heads;
+    if (xa != nullptr) {
+        // local merge + exchange + cross-GPU merge in one plain launch (its blocks
+        // spin on the other ranks' flags, so none may start before the decode ends)
+        const xchg::XchgRows xr = {xa->peers, xa->rank, xa->world, xchg::stride_floats(rows), xa->limit_ns};
+        const __half *ph = reinterpret_cast<const __half *>(L.part_o);
+        if (out_dtype == MLA_B200_OUT_F16)
+            xchg::exchange_combine_kernel<__half, __half><<<(unsigned)rows, kCombineThreads, 0, stream>>>(
+                ph, L.part_lse, wl, num_heads, rows, xa->direct, xr, static_cast<__half *>(out), out_lse);
+        else
+            xchg::exchange_combine_kernel<__half, float><<<(unsigned)rows, kCombineThreads, 0, stream>>>(
+                ph, L.part_lse, wl, num_heads, rows, xa->direct, xr, static_cast<float *>(out), out_lse);
+        return launch_status();
+    }
     // A dense batch decoded as one item per sequence is complete already.
     if (tc_direct && !planned && (balanced ? !bal_split : wl.cps == 1)) return launch_status();
-    const long long rows = (long long)batch * num_heads;
     const unsigned cgrid = (unsigned)rows;
     const int skip = tc_direct ? 1 : 0;
     // The tcgen05 kernel keeps fp16 partials for fp16 inputs and bf16 partials for
@@ -1338,6 +1382,40 @@ int mla_b200_exchange_f32(const float *part, long long rows, void *const *peer_b
                                                                           wait_limit_ns, static_cast<float *>(out),
                                                                           out_lse);
     return launch_status();
+}
+
+int mla_b200_decode_exchange_f16(const void *query, const void *cache, const int32_t *cu_seqlens, int batch,
+                                 int num_heads, long long total_tokens, int max_seq_len, float softmax_scale,
+                                 int num_splits, void *const *peer_bufs, int rank, int world, float *direct,
+                                 void *out, int out_dtype, float *out_lse, unsigned long long wait_limit_ns,
+                                 void *workspace, size_t workspace_bytes, void *stream) {
+    if (batch <= 0 || num_heads <= 0 || total_tokens < 0 || max_seq_len < 0) return MLA_B200_ERR_INVALID_ARG;
+    if (query == nullptr || out == nullptr || direct == nullptr || peer_bufs == nullptr)
+        return MLA_B200_ERR_INVALID_ARG;
+    if (total_tokens > 0 && cache == nullptr) return MLA_B200_ERR_INVALID_ARG;
+    if (out_dtype != MLA_B200_OUT_F16 && out_dtype != MLA_B200_OUT_F32) return MLA_B200_ERR_INVALID_ARG;
+    if (!(softmax_scale > 0.f) || !isfinite(softmax_scale)) return MLA_B200_ERR_INVALID_ARG;
+    if (!aligned(query, 16) || !aligned(cache, 16) || !aligned(out, 16) || !aligned(direct, 16) ||
+        !aligned(out_lse, 4))
+        return MLA_B200_ERR_INVALID_ARG;
+    if (cu_seqlens == nullptr && (long long)batch * max_seq_len != total_tokens) return MLA_B200_ERR_INVALID_ARG;
+    if (cu_seqlens != nullptr && max_seq_len == 0 && total_tokens > 0) return MLA_B200_ERR_INVALID_ARG;
+    if (world <= 0 || world > xchg::kMaxPeers || rank < 0 || rank >= world) return MLA_B200_ERR_INVALID_ARG;
+    if (wait_limit_ns == 0 || wait_limit_ns > 60000000000ull) return MLA_B200_ERR_INVALID_ARG;
+    if (total_tokens >= (1LL << 31) || (long long)batch * num_heads >= (1LL << 31)) return MLA_B200_ERR_UNSUPPORTED;
+    XchgArgs xa = {};
+    for (int g = 0; g < world; ++g) {
+        if (peer_bufs[g] == nullptr || !aligned(peer_bufs[g], 256)) return MLA_B200_ERR_INVALID_ARG;
+        xa.peers.buf[g] = static_cast<uint8_t *>(peer_bufs[g]);
+    }
+    xa.rank = rank;
+    xa.world = world;
+    xa.limit_ns = wait_limit_ns;
+    xa.direct = direct;
+    return run_split_decode<__half>(static_cast<const __half *>(query), static_cast<const __half *>(cache),
+                                    cu_seqlens, batch, num_heads, total_tokens, max_seq_len, softmax_scale,
+                                    num_splits, out, out_dtype, out_lse, workspace, workspace_bytes,
+                                    static_cast<cudaStream_t>(stream), nullptr, nullptr, nullptr, 1, &xa);
 }
 
 int mla_b200_exchange_merge_f32(const void *own_buf, int world, long long rows, void *out, int out_dtype,

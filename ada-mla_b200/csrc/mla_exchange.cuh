@@ -23,7 +23,8 @@
 //
 // exchange_fused_kernel does both in one launch (block = row: put the row,
 // count done, wait for every flag, merge the row) when all its blocks fit on
-// the device at once.
+// the device at once.  exchange_combine_kernel also merges the rank's own
+// split-KV partials first, so the decode's merge kernel drops out of the step.
 //
 // Two parities make the reuse safe: rank A writes epoch e + 2 into B's parity
 // (e & 1) only after its own merge of e + 1, which waited for B's flag e + 1,
@@ -31,6 +32,7 @@
 // No TMA, no multicast: plain loads and stores to peer memory.
 #pragma once
 
+#include "mla_combine.cuh"
 #include "mla_common.cuh"
 
 namespace mla {
@@ -212,6 +214,155 @@ __global__ void __launch_bounds__(128) exchange_fused_kernel(const float *__rest
     }
     __syncthreads();
     if (!ok_s) return;
+    merge_row(reinterpret_cast<const float *>(own + kHeaderBytes) + base, world, rows, stride, row, out, out_lse);
+}
+
+// Where exchange_combine_kernel stores and waits: every rank's buffer, this
+// rank's index, the part stride and the wait's limit.
+struct XchgRows {
+    Peers peers;
+    int rank, world;
+    long long stride;  // floats per part (stride_floats(rows))
+    unsigned long long limit_ns;
+};
+
+// The local LSE merge of a decode's split partials fused with the exchange:
+// block = row (b, h) of this rank's KV slice.  It merges the row's partials
+// as combine_kernel does (or, for a sequence decoded as a single item, takes
+// the (O, LSE) the decode kernel wrote straight into `direct`), stores the
+// merged row and its LSE into every rank's buffer, counts itself done (the
+// last block publishes the epoch), waits for every rank's flag and merges the
+// G parts of its row into `out`.  One launch for the local merge, the
+// exchange and the cross-GPU merge.  Like exchange_fused_kernel its blocks wait
+// on each other: the host launches it only when the grid fits the device.
+template <typename PartT, typename OutT>
+__global__ void __launch_bounds__(kCombineThreads) exchange_combine_kernel(
+    const PartT *__restrict__ part_o, const float *__restrict__ part_lse, WorkList wl, int num_heads,
+    long long rows, const float *__restrict__ direct, XchgRows xr, OutT *__restrict__ out,
+    float *__restrict__ out_lse) {
+    const Peers &peers = xr.peers;
+    const int rank = xr.rank, world = xr.world;
+    const long long stride = xr.stride;
+    constexpr int kVec = 16 / (int)sizeof(PartT);    // partial elements per thread
+    constexpr int kTpr = kDV / kVec;                 // threads covering one row
+    constexpr int kGroups = kCombineThreads / kTpr;  // split groups
+    __shared__ float w_s[kCombineChunk];
+    __shared__ float red[kCombineThreads / 32];
+    __shared__ __align__(16) float acc_s[kGroups][kDV];
+    __shared__ float lse_s;
+    __shared__ int ok_s;
+    const long long row = blockIdx.x;
+    const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+    const int b = (int)(row / num_heads);
+    const int h = (int)(row - (long long)b * num_heads);
+    uint8_t *own = peers.buf[rank];
+    const unsigned long long e = *reinterpret_cast<volatile unsigned long long *>(own + kOffEpoch) + 1;
+    const size_t base = (size_t)(e & 1) * (size_t)world * (size_t)stride;
+    const size_t mine = base + (size_t)rank * (size_t)stride;
+    int i0, i1;
+    item_range(wl, b, i0, i1);
+
+    if (i1 - i0 == 1) {
+        // the decode kernel finished this row itself: (O, LSE) are in `direct`
+        if (tid < kDV / 4)
+            reinterpret_cast<float4 *>(acc_s[0])[tid] = reinterpret_cast<const float4 *>(direct + (size_t)row * kDV)[tid];
+        if (tid == 0) lse_s = direct[(size_t)rows * kDV + row];
+    } else {
+        const int col = tid % kTpr, g = tid / kTpr;
+        float mx = -INFINITY;
+        for (int i = i0 + tid; i < i1; i += kCombineThreads) mx = fmaxf(mx, part_lse[(size_t)i * num_heads + h]);
+        mx = warp_max(mx);
+        if (lane == 0) red[warp] = mx;
+        __syncthreads();
+#pragma unroll
+        for (int w = 0; w < kCombineThreads / 32; ++w) mx = fmaxf(mx, red[w]);
+        float acc[kVec];
+#pragma unroll
+        for (int j = 0; j < kVec; ++j) acc[j] = 0.f;
+        float wsum = 0.f;  // identical in every thread (same weights, same order)
+        if (mx != -INFINITY) {
+            const size_t step = (size_t)num_heads * kDV / kVec;  // one split, in 16-byte vectors
+            for (int c0 = i0; c0 < i1; c0 += kCombineChunk) {
+                const int n = min(kCombineChunk, i1 - c0);
+                __syncthreads();
+                for (int k = tid; k < n; k += kCombineThreads) {
+                    const float lse = part_lse[(size_t)(c0 + k) * num_heads + h];
+                    w_s[k] = lse == -INFINITY ? 0.f : __expf(lse - mx);
+                }
+                __syncthreads();
+                for (int k = 0; k < n; ++k) wsum += w_s[k];
+                const uint4 *src =
+                    reinterpret_cast<const uint4 *>(part_o + (size_t)c0 * num_heads * kDV + (size_t)h * kDV) + col;
+                for (int k = g; k < n; k += 8 * kGroups) {
+                    uint4 u[8];
+#pragma unroll
+                    for (int j = 0; j < 8; ++j)
+                        if (k + j * kGroups < n) u[j] = __ldg(src + (size_t)(k + j * kGroups) * step);
+#pragma unroll
+                    for (int j = 0; j < 8; ++j) {
+                        if (k + j * kGroups < n) {
+                            float v[kVec];
+                            unpack_part<PartT>(u[j], v);
+                            const float w = w_s[k + j * kGroups];
+#pragma unroll
+                            for (int q = 0; q < kVec; ++q) acc[q] = fmaf(w, v[q], acc[q]);
+                        }
+                    }
+                }
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < kVec; ++q) acc_s[g][col * kVec + q] = acc[q];
+        __syncthreads();
+        if (g == 0) {
+            const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+#pragma unroll
+            for (int q = 0; q < kVec; ++q) {
+                float t = acc_s[0][col * kVec + q];
+#pragma unroll
+                for (int o = 1; o < kGroups; ++o) t += acc_s[o][col * kVec + q];
+                acc_s[0][col * kVec + q] = t * inv;
+            }
+            if (tid == 0) lse_s = wsum > 0.f ? mx + __logf(wsum) : -INFINITY;
+        }
+    }
+    __syncthreads();
+    // the merged row into part `rank` of every rank's buffer
+    if (tid < kDV / 4) {
+        const float4 v = reinterpret_cast<const float4 *>(acc_s[0])[tid];
+        for (int q = 0; q < world; ++q) {
+            float *d = reinterpret_cast<float *>(peers.buf[q] + kHeaderBytes) + mine;
+            reinterpret_cast<float4 *>(d + (size_t)row * kDV)[tid] = v;
+            if (tid == 0) d[(size_t)rows * kDV + row] = lse_s;
+        }
+    }
+    __syncthreads();
+    if (tid == 0) {
+        __threadfence_system();
+        unsigned int *done = reinterpret_cast<unsigned int *>(own + kOffDone);
+        if (atomicAdd(done, 1u) == gridDim.x - 1) {
+            *done = 0u;
+            *reinterpret_cast<volatile unsigned long long *>(own + kOffEpoch) = e;
+            __threadfence_system();
+            for (int q = 0; q < world; ++q)
+                st_release_sys(reinterpret_cast<unsigned long long *>(peers.buf[q]) + rank, e);
+        }
+        const unsigned long long *flags = reinterpret_cast<const unsigned long long *>(own);
+        int ok = 1;
+        uint64_t t0 = 0;
+        for (int q = 0; q < world && ok; ++q) {
+            for (uint32_t n = 0; ld_acquire_sys(flags + q) < e; ++n) {
+                if ((n & 255u) == 255u) {
+                    const uint64_t t = globaltimer_ns();
+                    if (t0 == 0) t0 = t;
+                    else if (t - t0 > xr.limit_ns) { set_device_error(kErrWaitPeer); ok = 0; break; }
+                }
+            }
+        }
+        ok_s = ok;
+    }
+    __syncthreads();
+    if (!ok_s || tid >= kDV / 4) return;
     merge_row(reinterpret_cast<const float *>(own + kHeaderBytes) + base, world, rows, stride, row, out, out_lse);
 }
 

@@ -250,10 +250,14 @@ def max_over_ranks(x: float, world: int) -> float:
     return float(t.item())
 
 
-def timed_replay(graph, steps: int, world: int, local: int):
+def timed_replay(graph, steps: int, world: int, local: int, align=None):
     """Times ONE replay of `graph` (exactly `steps` steps) with CUDA events,
     bracketed by a barrier and a synchronize; returns (ms per step, max over
-    ranks, clocks sampled by NVML while that replay runs)."""
+    ranks, clocks sampled by NVML while that replay runs).  `align`: one
+    untimed step of a cross-rank exchange, enqueued before the start event so
+    that every rank's events start when that exchange completes on all ranks
+    (otherwise the first timed exchange waits out the ranks' host skew after
+    the barrier, charged to the earliest rank)."""
     import torch
 
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -261,6 +265,8 @@ def timed_replay(graph, steps: int, world: int, local: int):
     barrier(world)
     torch.cuda.synchronize()
     with sampler:
+        if align is not None:
+            align()
         ev0.record()
         graph.replay()
         ev1.record()
@@ -720,9 +726,9 @@ def _graph_of(fn, steps):
 
 def kv_split_line(cfg: int, steps: int, rank: int, world: int, local: int, exchange: str = "p2p") -> dict:
     """One sequence's KV length split over the ranks: local decode of the rank's
-    slice into a packed (O, LSE) buffer, then the exchange: "p2p" = this
-    library's put + merge kernels over NVLink peer memory, "nccl" = one NCCL
-    all-gather and the LSE merge."""
+    slice, then the exchange: "p2p" = this library's exchange kernel over NVLink
+    peer memory (the slice's split merge fused in), "nccl" = the slice's merge
+    into a packed (O, LSE) buffer, one NCCL all-gather and the LSE merge."""
     import torch
 
     from ada_mla import multigpu
@@ -743,12 +749,12 @@ def kv_split_line(cfg: int, steps: int, rank: int, world: int, local: int, excha
         it[0] += 1
 
     graph = _graph_of(fn, steps)
-    ms, clocks = timed_replay(graph, steps, world, local)
+    ms, clocks = timed_replay(graph, steps, world, local, align=fn)
     del graph
     stages = dec.stage_times_us(wl.query, slices[0], 1.0, reps=20)
     dec.close()
-    how = ("one exchange kernel: (O, LSE) stored into every rank's buffer over NVLink peer memory, then merged"
-           if exchange == "p2p"
+    how = ("one exchange kernel: the slice's split merge, (O, LSE) stored into every rank's buffer over "
+           "NVLink peer memory, then merged" if exchange == "p2p"
            else "NCCL all-gather of (O, LSE) + LSE merge")
     return {"workload": f"cfg{cfg}: B={wl.batch} n_h={wl.num_heads} N={n}, KV length split over "
                         f"{world} GPU(s): local decode + {how}", "exchange": exchange,

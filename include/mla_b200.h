@@ -424,6 +424,24 @@ MLA_B200_API int mla_b200_exchange_f32(const float *part, long long rows, void *
                                        int world, void *out, int out_dtype, float *out_lse,
                                        unsigned long long wait_limit_ns, void *stream);
 
+/* One rank's whole split-KV step: the decode of this rank's KV slice (the
+ * arguments of mla_b200_decode_batched_f16) followed by ONE kernel that merges
+ * the slice's split partials, publishes the merged (O, LSE) into every rank's
+ * buffer and LSE-merges the `world` parts into out / out_lse, as
+ * mla_b200_exchange_f32 does.  `direct` is rows * 513 fp32 scratch (16-byte
+ * aligned) where the decode stores sequences it finishes as one work item.
+ * The same result as mla_b200_decode_batched_f16 (OUT_F32 with LSE) followed
+ * by mla_b200_exchange_f32, one launch fewer.  MLA_B200_ERR_UNSUPPORTED (before
+ * anything is launched) when the exchange kernel's rows do not fit the device
+ * at once or n_h > 128; a wait that runs out: device error code 4. */
+MLA_B200_API int mla_b200_decode_exchange_f16(const void *query, const void *cache, const int32_t *cu_seqlens,
+                                              int batch, int num_heads, long long total_tokens,
+                                              int max_seq_len, float softmax_scale, int num_splits,
+                                              void *const *peer_bufs, int rank, int world, float *direct,
+                                              void *out, int out_dtype, float *out_lse,
+                                              unsigned long long wait_limit_ns, void *workspace,
+                                              size_t workspace_bytes, void *stream);
+
 /* ------------------------------------------------------------------------ */
 /* Device error word                                                         */
 /* ------------------------------------------------------------------------ */

@@ -1,10 +1,11 @@
 """The peer-memory exchange kernels of the split-KV multi-GPU step
-(mla_b200_exchange_put_f32 / _merge_f32) on one GPU: a single rank's buffer
-goes through put + merge for several steps (both parities of the buffer), the
-merged output against a numpy LSE merge of the same packed partials; and a
-peer that never publishes makes the merge's bounded wait run out (a flag that
-nothing sets: no fault), report the peer-wait code and leave the rows alone.
-The two-rank path runs in tests/test_multigpu_gpu.py."""
+(mla_b200_exchange_put_f32 / _merge_f32 / _f32, mla_b200_decode_exchange_f16)
+on one GPU: a single rank's buffer goes through put + merge for several steps
+(both parities of the buffer), the merged output against a numpy LSE merge of
+the same packed partials; the decode with its merge fused into the exchange
+against the plain decode; and a peer that never publishes makes the bounded
+wait run out (a flag that nothing sets: no fault), report the peer-wait code
+and leave the rows alone.  The two-rank path runs in tests/test_multigpu_gpu.py."""
 import ctypes
 
 import numpy as np
@@ -148,3 +149,73 @@ def test_exchange_rejects_bad_arguments():
     z = torch.zeros(16, device="cuda")
     assert lib.mla_b200_exchange_merge_f32(z.data_ptr(), 1, 8, z.data_ptr(), capi.OUT_F32, None, 0, s) \
         == capi.ERR_INVALID_ARG
+
+
+def _plain_decode(q, c, scale, out_fp32):
+    """mla_b200_decode_batched_f16 on a dense batch: (out, lse)."""
+    from ada_mla import capi
+
+    b, nh, n = q.shape[0], q.shape[1], c.shape[1]
+    ws = torch.empty(max(256, capi.workspace_size(b, nh, b * n, n, -1)), dtype=torch.uint8, device="cuda")
+    out = torch.empty(b * nh, 512, dtype=torch.float32 if out_fp32 else torch.float16, device="cuda")
+    lse = torch.empty(b * nh, device="cuda")
+    assert capi.lib().mla_b200_decode_batched_f16(
+        q.data_ptr(), c.data_ptr(), None, b, nh, b * n, n, scale, -1, out.data_ptr(),
+        capi.OUT_F32 if out_fp32 else capi.OUT_F16, lse.data_ptr(), ws.data_ptr(), ws.numel(),
+        torch.cuda.current_stream().cuda_stream) == capi.OK
+    return out, lse
+
+
+@pytest.mark.parametrize("b,nh,n,out_fp32", [
+    (1, 128, 5000, False),  # one long sequence: many splits per row
+    (100, 2, 192, False),   # a batch on the balanced schedule: single-item rows and split rows
+    (2, 64, 777, True),     # fp32 output
+])
+def test_decode_exchange_single_rank_matches_decode(b, nh, n, out_fp32):
+    """mla_b200_decode_exchange_f16 with one rank (its own buffer the only peer)
+    over several steps: the decode's split merge, the put and the merge of one
+    part give the plain decode's output, and its LSE."""
+    from ada_mla import capi
+    from ada_mla.multigpu import PeerExchange, packed_stride
+
+    g = torch.Generator().manual_seed(b * 1000 + n)
+    q = (torch.randn(b, nh, 576, generator=g) / 192 ** 0.5).half().cuda()
+    c = torch.randn(b, n, 576, generator=g).half().cuda()
+    scale = 1.0 / 192 ** 0.5
+    ref_o, ref_lse = _plain_decode(q, c, scale, out_fp32)
+    rows = b * nh
+    ex = PeerExchange(rows)
+    try:
+        ws = torch.empty(max(256, capi.workspace_size(b, nh, b * n, n, -1)), dtype=torch.uint8, device="cuda")
+        direct = torch.empty(packed_stride(rows), device="cuda")
+        for step in range(3):
+            res = ex.decode_exchange(q, c, scale, ws, direct, torch.float32 if out_fp32 else torch.float16)
+            assert res is not None
+            out, lse = res
+            torch.cuda.synchronize()
+            d = (out.float() - ref_o.float()).abs()
+            assert float(d.max()) <= (1e-6 if out_fp32 else 1e-3), (step, float(d.max()))
+            assert float((lse - ref_lse).abs().max()) <= 1e-5, step
+        assert capi.get_device_error() == 0
+    finally:
+        ex.close()
+
+
+def test_decode_exchange_rejects_rows_that_do_not_fit():
+    """More rows than the exchange kernel can hold resident at once: refused
+    before anything is launched (the caller falls back to decode + exchange)."""
+    from ada_mla import capi
+    from ada_mla.multigpu import PeerExchange, packed_stride
+
+    b, nh, n = 19, 128, 96  # 2432 rows: more than 148 SMs x 4 blocks of 512 threads
+    q = torch.zeros(b, nh, 576, dtype=torch.float16, device="cuda")
+    c = torch.zeros(b, n, 576, dtype=torch.float16, device="cuda")
+    ex = PeerExchange(b * nh)
+    try:
+        ws = torch.empty(max(256, capi.workspace_size(b, nh, b * n, n, -1)), dtype=torch.uint8, device="cuda")
+        direct = torch.full((packed_stride(b * nh),), 5.0, device="cuda")
+        assert ex.decode_exchange(q, c, 0.1, ws, direct) is None
+        torch.cuda.synchronize()
+        assert bool((direct == 5.0).all()), "nothing ran"
+    finally:
+        ex.close()

@@ -1,6 +1,7 @@
-"""Multi-GPU decode over NCCL (needs >= 2 GPUs; skipped otherwise): the
-KV-length split with its all-gather + LSE merge, and sequence sharding, both
-against the CPU oracle."""
+"""Multi-GPU decode (needs >= 2 GPUs; skipped otherwise): the KV-length split
+with its NCCL all-gather + LSE merge or its peer-memory exchange (the slice's
+merge fused into the exchange kernel or not, and one rank fused while the other
+is not), and sequence sharding, all against the CPU oracle."""
 import os
 import socket
 
@@ -38,15 +39,21 @@ def _worker(rank, world, port, mode, results):
                             device_id=torch.device("cuda", rank))
     try:
         g = torch.Generator().manual_seed(11)
-        if mode in ("kv", "kv_p2p"):
-            b, nh, n = 1, 128, 5000
+        if mode.startswith("kv"):
+            # kv_p2p: decode + one exchange kernel (the slice's merge fused in);
+            # kv_p2p_unfused: decode, merge, exchange kernel; kv_p2p_empty: rank 1's
+            # slice is empty, so it takes the unfused kernels while rank 0 fuses
+            b, nh, n = 1, 128, 90 if mode == "kv_p2p_empty" else 5000
             q = (torch.randn(b, nh, 576, generator=g) / 192 ** 0.5).half()
             c = torch.randn(b, n, 576, generator=g).half()
-            dec = multigpu.KvSplitDecoder(exchange="p2p" if mode == "kv_p2p" else "nccl")
+            dec = multigpu.KvSplitDecoder(exchange="nccl" if mode == "kv" else "p2p",
+                                          fuse=mode != "kv_p2p_unfused")
             lo, hi = dec.bounds(n)
             qd, cd = q.cuda(), c[:, lo:hi].contiguous().cuda()
             outs = [dec(qd, cd, 1.0) for _ in range(3)]  # three steps: both exchange parities
             torch.cuda.synchronize()
+            fused = dec._fused_ok.get((b, nh), False)
+            assert fused == (mode == "kv_p2p" or (mode == "kv_p2p_empty" and rank == 0)), (mode, rank, fused)
             ref = oracle.mla_decode_oracle(q[0].float().numpy(), c[0].float().numpy(), 1.0, threads=4)
             d = np.abs(outs[-1][0].float().cpu().numpy() - ref)
             assert all(torch.equal(o, outs[0]) for o in outs), "every step gives the same result"
@@ -69,7 +76,7 @@ def _worker(rank, world, port, mode, results):
 
 
 @needs_two
-@pytest.mark.parametrize("mode", ["kv", "kv_p2p", "shard"])
+@pytest.mark.parametrize("mode", ["kv", "kv_p2p", "kv_p2p_unfused", "kv_p2p_empty", "shard"])
 def test_two_gpu_decode(mode):
     import torch.multiprocessing as mp
 
