@@ -617,14 +617,14 @@ int run_split_decode(const T *q, const T *cache, const int32_t *cu_seqlens, int 
     if (xa != nullptr) {
         // local merge + exchange + cross-GPU merge in one plain launch (its blocks
         // spin on the other ranks' flags, so none may start before the decode ends)
-        const xchg::XchgRows xr = {xa->peers, xa->rank, xa->world, xchg::stride_floats(rows), xa->limit_ns};
+        const xchg::XchgRows xr = {xa->peers, xa->rank, xa->world, rows, xchg::stride_words(rows), xa->limit_ns};
         const __half *ph = reinterpret_cast<const __half *>(L.part_o);
         if (out_dtype == MLA_B200_OUT_F16)
             xchg::exchange_combine_kernel<__half, __half><<<(unsigned)rows, kCombineThreads, 0, stream>>>(
-                ph, L.part_lse, wl, num_heads, rows, xa->direct, xr, static_cast<__half *>(out), out_lse);
+                ph, L.part_lse, wl, num_heads, xa->direct, xr, static_cast<__half *>(out), out_lse);
         else
             xchg::exchange_combine_kernel<__half, float><<<(unsigned)rows, kCombineThreads, 0, stream>>>(
-                ph, L.part_lse, wl, num_heads, rows, xa->direct, xr, static_cast<float *>(out), out_lse);
+                ph, L.part_lse, wl, num_heads, xa->direct, xr, static_cast<float *>(out), out_lse);
         return launch_status();
     }
     // A dense batch decoded as one item per sequence is complete already.
@@ -1337,13 +1337,10 @@ int mla_b200_exchange_put_f32(const float *part, long long rows, void *const *pe
     DevInfo info;
     int st = current_device(&dev, &info);
     if (st != MLA_B200_OK) return st;
-    const long long stride = xchg::stride_floats(rows);
-    const long long n4 = stride / 4;
-    const unsigned grid = (unsigned)std::min<long long>(info.sms, cdiv(n4, 256));
+    const xchg::XchgRows xr = {peers, rank, world, rows, xchg::stride_words(rows), 0};
     // (plain launches: chaining put and merge as programmatic dependents measured
     // slower on the whole 2-GPU step, 83 vs 61 us)
-    xchg::exchange_put_kernel<<<grid, 256, 0, static_cast<cudaStream_t>(stream)>>>(
-        reinterpret_cast<const float4 *>(part), n4, peers, rank, world, stride);
+    xchg::exchange_put_kernel<<<(unsigned)rows, 128, 0, static_cast<cudaStream_t>(stream)>>>(part, xr);
     return launch_status();
 }
 
@@ -1371,16 +1368,12 @@ int mla_b200_exchange_f32(const float *part, long long rows, void *const *peer_b
         : cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, xchg::exchange_fused_kernel<float>, 128, 0);
     if (oe != cudaSuccess) return cuda_failure(oe);
     if (rows > (long long)per_sm * info.sms) return MLA_B200_ERR_UNSUPPORTED;
-    const long long stride = xchg::stride_floats(rows);
+    const xchg::XchgRows xr = {peers, rank, world, rows, xchg::stride_words(rows), wait_limit_ns};
     cudaStream_t s = static_cast<cudaStream_t>(stream);
     if (out_dtype == MLA_B200_OUT_F16)
-        xchg::exchange_fused_kernel<__half><<<(unsigned)rows, 128, 0, s>>>(part, rows, peers, rank, world, stride,
-                                                                           wait_limit_ns, static_cast<__half *>(out),
-                                                                           out_lse);
+        xchg::exchange_fused_kernel<__half><<<(unsigned)rows, 128, 0, s>>>(part, xr, static_cast<__half *>(out), out_lse);
     else
-        xchg::exchange_fused_kernel<float><<<(unsigned)rows, 128, 0, s>>>(part, rows, peers, rank, world, stride,
-                                                                          wait_limit_ns, static_cast<float *>(out),
-                                                                          out_lse);
+        xchg::exchange_fused_kernel<float><<<(unsigned)rows, 128, 0, s>>>(part, xr, static_cast<float *>(out), out_lse);
     return launch_status();
 }
 
@@ -1429,15 +1422,19 @@ int mla_b200_exchange_merge_f32(const void *own_buf, int world, long long rows, 
     DevInfo info;
     int st = current_device(&dev, &info);
     if (st != MLA_B200_OK) return st;
-    const long long stride = xchg::stride_floats(rows);
+    // the merge reads only this rank's own buffer: it stands at index 0
+    xchg::XchgRows xr = {};
+    xr.peers.buf[0] = static_cast<uint8_t *>(const_cast<void *>(own_buf));
+    xr.rank = 0;
+    xr.world = world;
+    xr.rows = rows;
+    xr.stride = xchg::stride_words(rows);
+    xr.limit_ns = wait_limit_ns;
     cudaStream_t s = static_cast<cudaStream_t>(stream);
-    const uint8_t *own = static_cast<const uint8_t *>(own_buf);
     if (out_dtype == MLA_B200_OUT_F16)
-        xchg::exchange_merge_kernel<__half><<<(unsigned)rows, 128, 0, s>>>(own, world, rows, stride, wait_limit_ns,
-                                                                           static_cast<__half *>(out), out_lse);
+        xchg::exchange_merge_kernel<__half><<<(unsigned)rows, 128, 0, s>>>(xr, static_cast<__half *>(out), out_lse);
     else
-        xchg::exchange_merge_kernel<float><<<(unsigned)rows, 128, 0, s>>>(own, world, rows, stride, wait_limit_ns,
-                                                                          static_cast<float *>(out), out_lse);
+        xchg::exchange_merge_kernel<float><<<(unsigned)rows, 128, 0, s>>>(xr, static_cast<float *>(out), out_lse);
     return launch_status();
 }
 

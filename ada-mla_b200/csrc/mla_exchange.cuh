@@ -4,31 +4,30 @@
 // One process per GPU.  Every rank owns one exchange buffer (cudaMalloc, zeroed),
 // mapped into every other rank's address space through CUDA IPC:
 //
-//   header [256 B]: flags[kMaxPeers] (u64: the last epoch rank g published into
-//                   this buffer), epoch (u64: this rank's last published epoch),
-//                   done (u32: blocks of the running put kernel that finished)
-//   data:           [2 parities][world][stride] fp32, stride = rows * 513
-//                   rounded up to 4 floats (O [rows, 512] normalized, then LSE)
+//   header: epoch[rows] (u32: how many steps this rank has published for each
+//           row), padded to a multiple of 256 bytes
+//   data:   [2 parities][world parts][stride words]; one part = O [rows, 512]
+//           then LSE [rows], each value one 8-byte word (epoch << 32 | fp32 bits)
 //
-// exchange_put_kernel (rank r, epoch e = its previous epoch + 1): every block
-// copies its share of r's packed (O, LSE) into part r of parity e & 1 of every
-// rank's buffer (own included) with plain stores over NVLink, fences at system
-// scope and counts itself done; the last block publishes e in r's own header
-// and stores e (release, system scope) into flags[r] of every rank's buffer.
+// Flags live in the data: every 8-byte word carries the epoch of the step that
+// wrote it, and an aligned 8-byte store is seen whole or not at all.  A rank
+// stores row r of its packed (O, LSE) as such words into its part of every
+// rank's buffer (parity e & 1 for epoch e); a reader polls the words of its own
+// buffer (volatile loads, bounded by limit_ns) until each carries e, and then
+// LSE-merges the G parts.  No fence, no counter, no block waits for another
+// block of its own grid; the cost is twice the bytes on NVLink (4 KB per row
+// per peer instead of 2 KB).
 //
-// exchange_merge_kernel (rank r, epoch e read from its own header, written by
-// its put kernel just before in stream order): thread 0 of every block waits,
-// bounded by limit_ns, until flags[g] >= e for every g (acquire, system scope),
-// then the block LSE-merges its row over the G parts of parity e & 1.
+// Kernels (block = row, 128 threads own 4 columns each, unless noted):
+//   exchange_put_kernel     epoch[r] += 1, then the stores
+//   exchange_merge_kernel   waits for epoch[r] in every part, merges
+//   exchange_fused_kernel   both, one launch
+//   exchange_combine_kernel (512 threads) merges the rank's own split-KV
+//                           partials of the row first, then as the fused one
 //
-// exchange_fused_kernel does both in one launch (block = row: put the row,
-// count done, wait for every flag, merge the row) when all its blocks fit on
-// the device at once.  exchange_combine_kernel also merges the rank's own
-// split-KV partials first, so the decode's merge kernel drops out of the step.
-//
-// Two parities make the reuse safe: rank A writes epoch e + 2 into B's parity
-// (e & 1) only after its own merge of e + 1, which waited for B's flag e + 1,
-// which B stored after its merge of e finished (stream order on B).
+// Two parities make the reuse safe: rank A writes row r of epoch e + 2 into B's
+// parity e & 1 only after its merge of e + 1 saw B's row r of e + 1, which B
+// stored after its kernel of step e (the one reading that parity) had ended.
 // No TMA, no multicast: plain loads and stores to peer memory.
 #pragma once
 
@@ -39,210 +38,213 @@ namespace mla {
 namespace xchg {
 
 constexpr int kMaxPeers = 16;
-constexpr int kHeaderBytes = 256;
-constexpr int kOffEpoch = kMaxPeers * 8;   // 128
-constexpr int kOffDone = kOffEpoch + 8;    // 136
-static_assert(kOffDone + 4 <= kHeaderBytes, "exchange header");
 
-__host__ __device__ constexpr long long stride_floats(long long rows) { return (rows * (kDV + 1) + 3) / 4 * 4; }
+// header bytes: a u32 step count per row, padded to 256 bytes
+__host__ __device__ constexpr size_t header_bytes(long long rows) { return ((size_t)rows * 4 + 255) / 256 * 256; }
+
+// 8-byte words per part: O [rows, 512] then LSE [rows], rounded up to an even
+// count so that every part's O rows start on a 16-byte boundary
+__host__ __device__ constexpr long long stride_words(long long rows) { return (rows * (kDV + 1) + 1) / 2 * 2; }
 
 __host__ __device__ constexpr size_t buffer_bytes(int world, long long rows) {
-    return (size_t)kHeaderBytes + 2ull * (size_t)world * (size_t)stride_floats(rows) * sizeof(float);
+    return header_bytes(rows) + 2ull * (size_t)world * (size_t)stride_words(rows) * 8;
 }
 
 struct Peers {
     uint8_t *buf[kMaxPeers];  // every rank's exchange buffer as mapped in this process (own included)
 };
 
-__device__ __forceinline__ void st_release_sys(unsigned long long *p, unsigned long long v) {
-    asm volatile("st.release.sys.global.u64 [%0], %1;" ::"l"(p), "l"(v) : "memory");
-}
-
-__device__ __forceinline__ unsigned long long ld_acquire_sys(const unsigned long long *p) {
-    unsigned long long v;
-    asm volatile("ld.acquire.sys.global.u64 %0, [%1];" : "=l"(v) : "l"(p) : "memory");
-    return v;
-}
-
-// part: this rank's packed (O, LSE), stride floats (16-byte aligned).
-__global__ void __launch_bounds__(256) exchange_put_kernel(const float4 *__restrict__ part, long long n4,
-                                                           Peers peers, int rank, int world, long long stride) {
-    uint8_t *own = peers.buf[rank];
-    // every block reads the previous epoch before any block can count itself done
-    const unsigned long long e = *reinterpret_cast<volatile unsigned long long *>(own + kOffEpoch) + 1;
-    const size_t off = ((size_t)(e & 1) * (size_t)world + (size_t)rank) * (size_t)stride;  // floats
-    for (long long i = (long long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long long)gridDim.x * blockDim.x) {
-        const float4 v = part[i];
-        for (int g = 0; g < world; ++g)
-            reinterpret_cast<float4 *>(reinterpret_cast<float *>(peers.buf[g] + kHeaderBytes) + off)[i] = v;
-    }
-    // The block's stores happen before thread 0's system-scope fence (bar.sync,
-    // then the fence's cumulativity): one fence per block, not per thread (a
-    // system fence waits for the thread's stores to be acknowledged over NVLink).
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence_system();
-        unsigned int *done = reinterpret_cast<unsigned int *>(own + kOffDone);
-        if (atomicAdd(done, 1u) == gridDim.x - 1) {  // the last block: every block's data is out
-            *done = 0u;
-            *reinterpret_cast<volatile unsigned long long *>(own + kOffEpoch) = e;
-            __threadfence_system();
-            for (int g = 0; g < world; ++g)
-                st_release_sys(reinterpret_cast<unsigned long long *>(peers.buf[g]) + rank, e);
-        }
-    }
-}
-
-// Block-wide LSE merge of row `row` over the `world` parts at `data` (parity
-// base of a buffer's data region); 128 threads, thread t owns columns [4 t, 4 t + 4).
-template <typename OutT>
-__device__ __forceinline__ void merge_row(const float *data, int world, long long rows, long long stride,
-                                          long long row, OutT *__restrict__ out, float *__restrict__ out_lse) {
-    float mx = -INFINITY;
-    for (int g = 0; g < world; ++g) mx = fmaxf(mx, __ldcg(data + (size_t)g * stride + (size_t)rows * kDV + row));
-    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-    float wsum = 0.f;
-    if (mx != -INFINITY) {
-        for (int g = 0; g < world; ++g) {
-            const float *p = data + (size_t)g * stride;
-            const float lse = __ldcg(p + (size_t)rows * kDV + row);
-            const float w = lse == -INFINITY ? 0.f : __expf(lse - mx);
-            const float4 v = __ldcg(reinterpret_cast<const float4 *>(p + (size_t)row * kDV) + threadIdx.x);
-            wsum += w;
-            acc.x = fmaf(w, v.x, acc.x);
-            acc.y = fmaf(w, v.y, acc.y);
-            acc.z = fmaf(w, v.z, acc.z);
-            acc.w = fmaf(w, v.w, acc.w);
-        }
-    }
-    const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
-    OutT *dst = out + (size_t)row * kDV + threadIdx.x * 4;
-    if constexpr (sizeof(OutT) == 4) {
-        *reinterpret_cast<float4 *>(dst) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
-    } else {
-        const __half2 a = __floats2half2_rn(acc.x * inv, acc.y * inv), b = __floats2half2_rn(acc.z * inv, acc.w * inv);
-        uint2 u;
-        u.x = *reinterpret_cast<const uint32_t *>(&a);
-        u.y = *reinterpret_cast<const uint32_t *>(&b);
-        *reinterpret_cast<uint2 *>(dst) = u;
-    }
-    if (out_lse != nullptr && threadIdx.x == 0) out_lse[row] = wsum > 0.f ? mx + __logf(wsum) : -INFINITY;
-}
-
-// One block of 128 threads per row; thread t owns columns [4 t, 4 t + 4).
-template <typename OutT>
-__global__ void __launch_bounds__(128) exchange_merge_kernel(const uint8_t *own, int world, long long rows,
-                                                             long long stride, unsigned long long limit_ns,
-                                                             OutT *__restrict__ out, float *__restrict__ out_lse) {
-    __shared__ int ok_s;
-    const long long row = blockIdx.x;
-    const unsigned long long e = *reinterpret_cast<const volatile unsigned long long *>(own + kOffEpoch);
-    if (threadIdx.x == 0) {
-        const unsigned long long *flags = reinterpret_cast<const unsigned long long *>(own);
-        int ok = 1;
-        uint64_t t0 = 0;
-        for (int g = 0; g < world && ok; ++g) {
-            for (uint32_t n = 0; ld_acquire_sys(flags + g) < e; ++n) {
-                if ((n & 255u) == 255u) {
-                    const uint64_t t = globaltimer_ns();
-                    if (t0 == 0) t0 = t;
-                    else if (t - t0 > limit_ns) { set_device_error(kErrWaitPeer); ok = 0; break; }
-                }
-            }
-        }
-        ok_s = ok;
-    }
-    __syncthreads();
-    if (!ok_s) return;
-    merge_row(reinterpret_cast<const float *>(own + kHeaderBytes) + (size_t)(e & 1) * (size_t)world * (size_t)stride,
-              world, rows, stride, row, out, out_lse);
-}
-
-// The whole exchange in one kernel: block `row` stores its row of this rank's
-// packed (O, LSE) into every rank's buffer, the blocks count themselves done
-// and the last one publishes the epoch (as exchange_put_kernel), then every
-// block waits for every rank's flag and merges its row (as
-// exchange_merge_kernel).  The blocks wait on each other through the done
-// count, so all of them must be resident at once: the host launches it only
-// when the grid fits the device's occupancy (else put + merge); a block that
-// waits in vain (another kernel holding SMs) gives up after limit_ns with the
-// peer-wait code, like the merge.
-template <typename OutT>
-__global__ void __launch_bounds__(128) exchange_fused_kernel(const float *__restrict__ part, long long rows,
-                                                             Peers peers, int rank, int world, long long stride,
-                                                             unsigned long long limit_ns, OutT *__restrict__ out,
-                                                             float *__restrict__ out_lse) {
-    __shared__ int ok_s;
-    const long long row = blockIdx.x;
-    uint8_t *own = peers.buf[rank];
-    const unsigned long long e = *reinterpret_cast<volatile unsigned long long *>(own + kOffEpoch) + 1;
-    const size_t base = (size_t)(e & 1) * (size_t)world * (size_t)stride;  // floats: this epoch's parity
-    const size_t mine = base + (size_t)rank * (size_t)stride;
-    {
-        const float4 v = reinterpret_cast<const float4 *>(part + (size_t)row * kDV)[threadIdx.x];
-        const float lse = part[(size_t)rows * kDV + row];
-        for (int g = 0; g < world; ++g) {
-            float *d = reinterpret_cast<float *>(peers.buf[g] + kHeaderBytes) + mine;
-            reinterpret_cast<float4 *>(d + (size_t)row * kDV)[threadIdx.x] = v;
-            if (threadIdx.x == 0) d[(size_t)rows * kDV + row] = lse;
-        }
-    }
-    __syncthreads();
-    if (threadIdx.x == 0) {
-        __threadfence_system();
-        unsigned int *done = reinterpret_cast<unsigned int *>(own + kOffDone);
-        if (atomicAdd(done, 1u) == gridDim.x - 1) {
-            *done = 0u;
-            *reinterpret_cast<volatile unsigned long long *>(own + kOffEpoch) = e;
-            __threadfence_system();
-            for (int g = 0; g < world; ++g)
-                st_release_sys(reinterpret_cast<unsigned long long *>(peers.buf[g]) + rank, e);
-        }
-        const unsigned long long *flags = reinterpret_cast<const unsigned long long *>(own);
-        int ok = 1;
-        uint64_t t0 = 0;
-        for (int g = 0; g < world && ok; ++g) {
-            for (uint32_t n = 0; ld_acquire_sys(flags + g) < e; ++n) {
-                if ((n & 255u) == 255u) {
-                    const uint64_t t = globaltimer_ns();
-                    if (t0 == 0) t0 = t;
-                    else if (t - t0 > limit_ns) { set_device_error(kErrWaitPeer); ok = 0; break; }
-                }
-            }
-        }
-        ok_s = ok;
-    }
-    __syncthreads();
-    if (!ok_s) return;
-    merge_row(reinterpret_cast<const float *>(own + kHeaderBytes) + base, world, rows, stride, row, out, out_lse);
-}
-
-// Where exchange_combine_kernel stores and waits: every rank's buffer, this
-// rank's index, the part stride and the wait's limit.
+// Where the exchange kernels store and wait: every rank's buffer, this rank's
+// index, rows per part, the part stride and the wait's limit.
 struct XchgRows {
     Peers peers;
     int rank, world;
-    long long stride;  // floats per part (stride_floats(rows))
+    long long rows;
+    long long stride;  // stride_words(rows)
     unsigned long long limit_ns;
 };
+
+__device__ __forceinline__ unsigned long long *data_of(uint8_t *buf, long long rows) {
+    return reinterpret_cast<unsigned long long *>(buf + header_bytes(rows));
+}
+
+__device__ __forceinline__ unsigned long long word_of(float v, uint32_t e) {
+    return ((unsigned long long)e << 32) | __float_as_uint(v);
+}
+
+__device__ __forceinline__ void st_words2(unsigned long long *p, unsigned long long a, unsigned long long b) {
+    asm volatile("st.volatile.global.v2.u64 [%0], {%1, %2};" ::"l"(p), "l"(a), "l"(b) : "memory");
+}
+
+__device__ __forceinline__ void st_word(unsigned long long *p, unsigned long long a) {
+    asm volatile("st.volatile.global.u64 [%0], %1;" ::"l"(p), "l"(a) : "memory");
+}
+
+__device__ __forceinline__ void ld_words2(const unsigned long long *p, unsigned long long &a, unsigned long long &b) {
+    asm volatile("ld.volatile.global.v2.u64 {%0, %1}, [%2];" : "=l"(a), "=l"(b) : "l"(p) : "memory");
+}
+
+__device__ __forceinline__ unsigned long long ld_word(const unsigned long long *p) {
+    unsigned long long a;
+    asm volatile("ld.volatile.global.u64 %0, [%1];" : "=l"(a) : "l"(p) : "memory");
+    return a;
+}
+
+__device__ __forceinline__ bool has_epoch(unsigned long long w, uint32_t e) { return (uint32_t)(w >> 32) == e; }
+
+// Bounded poll step: false once more than limit_ns passed since the first call
+// that had to wait (t0 = 0 before it).
+__device__ __forceinline__ bool still_waiting(uint32_t n, uint64_t &t0, unsigned long long limit_ns) {
+    if ((n & 63u) != 63u) return true;
+    const uint64_t t = globaltimer_ns();
+    if (t0 == 0) t0 = t;
+    return t - t0 <= limit_ns;
+}
+
+// Thread t (< 128) stores columns [4 t, 4 t + 4) of row `row` (v) and, thread 0,
+// its LSE, as epoch-e words into part `rank` of every rank's buffer.
+__device__ __forceinline__ void put_row(const XchgRows &xr, long long row, uint32_t e, float4 v, float lse) {
+    const size_t base = ((size_t)(e & 1) * (size_t)xr.world + (size_t)xr.rank) * (size_t)xr.stride;
+    const int t = threadIdx.x;
+    const unsigned long long w0 = word_of(v.x, e), w1 = word_of(v.y, e), w2 = word_of(v.z, e), w3 = word_of(v.w, e);
+    const unsigned long long wl = word_of(lse, e);
+    for (int q = 0; q < xr.world; ++q) {
+        unsigned long long *d = data_of(xr.peers.buf[q], xr.rows) + base;
+        unsigned long long *o = d + (size_t)row * kDV + 4 * t;
+        st_words2(o, w0, w1);
+        st_words2(o + 2, w2, w3);
+        if (t == 0) st_word(d + (size_t)xr.rows * kDV + row, wl);
+    }
+}
+
+// Block-wide: waits (bounded) until every part of row `row` in this rank's own
+// buffer carries epoch e, then LSE-merges the parts into out / out_lse.  Every
+// thread of the block calls it (barriers inside); threads 0..127 own 4 columns
+// each.  Returns false, with nothing written and the peer-wait code recorded,
+// when a wait ran out.
+template <typename OutT>
+__device__ bool merge_row(const XchgRows &xr, long long row, uint32_t e, OutT *__restrict__ out,
+                          float *__restrict__ out_lse) {
+    __shared__ float lse_s[kMaxPeers];
+    const int t = threadIdx.x;
+    const int world = xr.world;
+    const unsigned long long *d =
+        data_of(xr.peers.buf[xr.rank], xr.rows) + (size_t)(e & 1) * (size_t)world * (size_t)xr.stride;
+    bool ok = true;
+    uint64_t t0 = 0;
+    if (t < world) {
+        const unsigned long long *p = d + (size_t)t * xr.stride + (size_t)xr.rows * kDV + row;
+        unsigned long long w = ld_word(p);
+        for (uint32_t n = 0; ok && !has_epoch(w, e); ++n) {
+            ok = still_waiting(n, t0, xr.limit_ns);
+            w = ld_word(p);
+        }
+        lse_s[t] = __uint_as_float((uint32_t)w);
+    }
+    if (__syncthreads_or(!ok)) {
+        if (t == 0) set_device_error(kErrWaitPeer);
+        return false;
+    }
+    float mx = -INFINITY;
+    for (int g = 0; g < world; ++g) mx = fmaxf(mx, lse_s[g]);
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    float wsum = 0.f;
+    if (t < kDV / 4) {
+        for (int g = 0; g < world && ok; ++g) {
+            const unsigned long long *p = d + (size_t)g * xr.stride + (size_t)row * kDV + 4 * t;
+            unsigned long long a, b, c, f;
+            ld_words2(p, a, b);
+            ld_words2(p + 2, c, f);
+            for (uint32_t n = 0; ok && !(has_epoch(a, e) && has_epoch(b, e) && has_epoch(c, e) && has_epoch(f, e)); ++n) {
+                ok = still_waiting(n, t0, xr.limit_ns);
+                ld_words2(p, a, b);
+                ld_words2(p + 2, c, f);
+            }
+            const float lse = lse_s[g];
+            const float w = (mx == -INFINITY || lse == -INFINITY) ? 0.f : __expf(lse - mx);
+            wsum += w;
+            acc.x = fmaf(w, __uint_as_float((uint32_t)a), acc.x);
+            acc.y = fmaf(w, __uint_as_float((uint32_t)b), acc.y);
+            acc.z = fmaf(w, __uint_as_float((uint32_t)c), acc.z);
+            acc.w = fmaf(w, __uint_as_float((uint32_t)f), acc.w);
+        }
+    }
+    if (__syncthreads_or(!ok)) {
+        if (t == 0) set_device_error(kErrWaitPeer);
+        return false;
+    }
+    if (t < kDV / 4) {
+        const float inv = wsum > 0.f ? 1.f / wsum : 0.f;
+        OutT *dst = out + (size_t)row * kDV + t * 4;
+        if constexpr (sizeof(OutT) == 4) {
+            *reinterpret_cast<float4 *>(dst) = make_float4(acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv);
+        } else {
+            const __half2 a = __floats2half2_rn(acc.x * inv, acc.y * inv), b = __floats2half2_rn(acc.z * inv, acc.w * inv);
+            uint2 u;
+            u.x = *reinterpret_cast<const uint32_t *>(&a);
+            u.y = *reinterpret_cast<const uint32_t *>(&b);
+            *reinterpret_cast<uint2 *>(dst) = u;
+        }
+        if (out_lse != nullptr && t == 0) out_lse[row] = wsum > 0.f ? mx + __logf(wsum) : -INFINITY;
+    }
+    return true;
+}
+
+// This rank's step count for `row` (own header), advanced by one when `advance`;
+// returns the step's epoch.  Block-wide (one barrier).
+__device__ __forceinline__ uint32_t row_epoch(const XchgRows &xr, long long row, bool advance) {
+    __shared__ uint32_t e_s;
+    uint32_t *ep = reinterpret_cast<uint32_t *>(xr.peers.buf[xr.rank]) + row;
+    if (threadIdx.x == 0) {
+        const uint32_t e = *ep + (advance ? 1u : 0u);
+        if (advance) *ep = e;  // read again only by this row's block of the next kernel
+        e_s = e;
+    }
+    __syncthreads();
+    return e_s;
+}
+
+// part: this rank's packed (O [rows, 512], LSE [rows]) fp32, 16-byte aligned.
+__global__ void __launch_bounds__(128) exchange_put_kernel(const float *__restrict__ part, XchgRows xr) {
+    const long long row = blockIdx.x;
+    const uint32_t e = row_epoch(xr, row, true);
+    const float4 v = reinterpret_cast<const float4 *>(part + (size_t)row * kDV)[threadIdx.x];
+    put_row(xr, row, e, v, part[(size_t)xr.rows * kDV + row]);
+}
+
+// The merge after exchange_put_kernel (which advanced the epoch).
+template <typename OutT>
+__global__ void __launch_bounds__(128) exchange_merge_kernel(XchgRows xr, OutT *__restrict__ out,
+                                                             float *__restrict__ out_lse) {
+    const long long row = blockIdx.x;
+    const uint32_t e = row_epoch(xr, row, false);
+    merge_row(xr, row, e, out, out_lse);
+}
+
+// put + merge in one launch.  Blocks wait only on the same row's blocks of the
+// other ranks; the host still launches it only when the whole grid fits the
+// device at once, so that no rank's block r waits behind its own waiting blocks.
+template <typename OutT>
+__global__ void __launch_bounds__(128) exchange_fused_kernel(const float *__restrict__ part, XchgRows xr,
+                                                             OutT *__restrict__ out, float *__restrict__ out_lse) {
+    const long long row = blockIdx.x;
+    const uint32_t e = row_epoch(xr, row, true);
+    const float4 v = reinterpret_cast<const float4 *>(part + (size_t)row * kDV)[threadIdx.x];
+    put_row(xr, row, e, v, part[(size_t)xr.rows * kDV + row]);
+    merge_row(xr, row, e, out, out_lse);
+}
 
 // The local LSE merge of a decode's split partials fused with the exchange:
 // block = row (b, h) of this rank's KV slice.  It merges the row's partials
 // as combine_kernel does (or, for a sequence decoded as a single item, takes
 // the (O, LSE) the decode kernel wrote straight into `direct`), stores the
-// merged row and its LSE into every rank's buffer, counts itself done (the
-// last block publishes the epoch), waits for every rank's flag and merges the
-// G parts of its row into `out`.  One launch for the local merge, the
-// exchange and the cross-GPU merge.  Like exchange_fused_kernel its blocks wait
-// on each other: the host launches it only when the grid fits the device.
+// merged row into every rank's buffer and merges the G parts of its row into
+// `out`: one launch for the local merge, the exchange and the cross-GPU merge.
+// Launched, like exchange_fused_kernel, only when the grid fits the device.
 template <typename PartT, typename OutT>
 __global__ void __launch_bounds__(kCombineThreads) exchange_combine_kernel(
     const PartT *__restrict__ part_o, const float *__restrict__ part_lse, WorkList wl, int num_heads,
-    long long rows, const float *__restrict__ direct, XchgRows xr, OutT *__restrict__ out,
-    float *__restrict__ out_lse) {
-    const Peers &peers = xr.peers;
-    const int rank = xr.rank, world = xr.world;
-    const long long stride = xr.stride;
+    const float *__restrict__ direct, XchgRows xr, OutT *__restrict__ out, float *__restrict__ out_lse) {
     constexpr int kVec = 16 / (int)sizeof(PartT);    // partial elements per thread
     constexpr int kTpr = kDV / kVec;                 // threads covering one row
     constexpr int kGroups = kCombineThreads / kTpr;  // split groups
@@ -250,15 +252,11 @@ __global__ void __launch_bounds__(kCombineThreads) exchange_combine_kernel(
     __shared__ float red[kCombineThreads / 32];
     __shared__ __align__(16) float acc_s[kGroups][kDV];
     __shared__ float lse_s;
-    __shared__ int ok_s;
     const long long row = blockIdx.x;
+    const long long rows = xr.rows;
     const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
     const int b = (int)(row / num_heads);
     const int h = (int)(row - (long long)b * num_heads);
-    uint8_t *own = peers.buf[rank];
-    const unsigned long long e = *reinterpret_cast<volatile unsigned long long *>(own + kOffEpoch) + 1;
-    const size_t base = (size_t)(e & 1) * (size_t)world * (size_t)stride;
-    const size_t mine = base + (size_t)rank * (size_t)stride;
     int i0, i1;
     item_range(wl, b, i0, i1);
 
@@ -326,44 +324,9 @@ __global__ void __launch_bounds__(kCombineThreads) exchange_combine_kernel(
             if (tid == 0) lse_s = wsum > 0.f ? mx + __logf(wsum) : -INFINITY;
         }
     }
-    __syncthreads();
-    // the merged row into part `rank` of every rank's buffer
-    if (tid < kDV / 4) {
-        const float4 v = reinterpret_cast<const float4 *>(acc_s[0])[tid];
-        for (int q = 0; q < world; ++q) {
-            float *d = reinterpret_cast<float *>(peers.buf[q] + kHeaderBytes) + mine;
-            reinterpret_cast<float4 *>(d + (size_t)row * kDV)[tid] = v;
-            if (tid == 0) d[(size_t)rows * kDV + row] = lse_s;
-        }
-    }
-    __syncthreads();
-    if (tid == 0) {
-        __threadfence_system();
-        unsigned int *done = reinterpret_cast<unsigned int *>(own + kOffDone);
-        if (atomicAdd(done, 1u) == gridDim.x - 1) {
-            *done = 0u;
-            *reinterpret_cast<volatile unsigned long long *>(own + kOffEpoch) = e;
-            __threadfence_system();
-            for (int q = 0; q < world; ++q)
-                st_release_sys(reinterpret_cast<unsigned long long *>(peers.buf[q]) + rank, e);
-        }
-        const unsigned long long *flags = reinterpret_cast<const unsigned long long *>(own);
-        int ok = 1;
-        uint64_t t0 = 0;
-        for (int q = 0; q < world && ok; ++q) {
-            for (uint32_t n = 0; ld_acquire_sys(flags + q) < e; ++n) {
-                if ((n & 255u) == 255u) {
-                    const uint64_t t = globaltimer_ns();
-                    if (t0 == 0) t0 = t;
-                    else if (t - t0 > xr.limit_ns) { set_device_error(kErrWaitPeer); ok = 0; break; }
-                }
-            }
-        }
-        ok_s = ok;
-    }
-    __syncthreads();
-    if (!ok_s || tid >= kDV / 4) return;
-    merge_row(reinterpret_cast<const float *>(own + kHeaderBytes) + base, world, rows, stride, row, out, out_lse);
+    const uint32_t e = row_epoch(xr, row, true);  // (its barrier publishes acc_s and lse_s)
+    if (tid < kDV / 4) put_row(xr, row, e, reinterpret_cast<const float4 *>(acc_s[0])[tid], lse_s);
+    merge_row(xr, row, e, out, out_lse);
 }
 
 }  // namespace xchg

@@ -382,8 +382,10 @@ MLA_B200_API int mla_b200_combine_packed_f32(const float *parts, int num_parts, 
 /* ------------------------------------------------------------------------ */
 
 /* Bytes of one rank's exchange buffer for `world` ranks (<= 16) and `rows`
- * (sequences x heads) rows: a 256-byte header of flags, then two parities of
- * [world][stride] fp32, stride = rows * 513 rounded up to 4. */
+ * (sequences x heads) rows: a header of one u32 step count per row (padded to
+ * 256 bytes), then two parities of [world][stride] 8-byte words, stride =
+ * rows * 513 rounded up to even; each word is one fp32 value with the epoch of
+ * the step that stored it in its upper half (readers poll for the epoch). */
 MLA_B200_API size_t mla_b200_exchange_bytes(int world, long long rows);
 
 /* cudaMalloc + zero of one exchange buffer on the current device (free with

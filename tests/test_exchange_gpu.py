@@ -144,7 +144,8 @@ def test_exchange_rejects_bad_arguments():
     buf = ctypes.c_void_p()
     assert lib.mla_b200_exchange_alloc(0, 8, ctypes.byref(buf)) == capi.ERR_INVALID_ARG
     assert lib.mla_b200_exchange_alloc(17, 8, ctypes.byref(buf)) == capi.ERR_INVALID_ARG
-    assert lib.mla_b200_exchange_bytes(2, 8) == 256 + 2 * 2 * (8 * 513) * 4
+    assert lib.mla_b200_exchange_bytes(2, 8) == 256 + 2 * 2 * (8 * 513) * 8  # header, 2 parities x 2 parts
+    assert lib.mla_b200_exchange_bytes(1, 65) == 512 + 2 * (65 * 513 + 1) * 8  # stride rounded up to even
     s = torch.cuda.current_stream().cuda_stream
     z = torch.zeros(16, device="cuda")
     assert lib.mla_b200_exchange_merge_f32(z.data_ptr(), 1, 8, z.data_ptr(), capi.OUT_F32, None, 0, s) \
