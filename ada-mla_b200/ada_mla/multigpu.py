@@ -15,7 +15,8 @@ layer scales the same decode across the G GPUs of a node, one process per GPU:
   reduces to the exact result (``KvSplitDecoder``).  With ``exchange="p2p"``
   the all-gather is replaced by this library's own kernels over NVLink peer
   memory (``PeerExchange``: CUDA IPC mappings, plain stores into every rank's
-  buffer, release / acquire flags at system scope, bounded waits).
+  buffer of 8-byte words that each carry the step's epoch, readers polling their
+  own buffer with bounded waits).
 
 The per-rank decode and the merge are injectable so that the host logic
 (partitioning, packing, the collective, unpacking) can be exercised by CPU
@@ -132,8 +133,8 @@ class PeerExchange:
     all-gather: every rank owns one exchange buffer (mla_b200_exchange_alloc),
     maps every other rank's through CUDA IPC (handles swapped once with
     ``all_gather_object``), stores its packed (O, LSE) straight into every
-    rank's buffer (``put``) and merges the G parts in its own buffer after a
-    bounded wait on the other ranks' flags (``merge``).  Both are stream-ordered
+    rank's buffer (``put``) and merges the G parts in its own buffer once their
+    words carry this step's epoch (``merge``, a bounded wait).  Both are stream-ordered
     kernels, so the step captures in a CUDA graph.  Set up and ``close()`` on
     every rank together (both end with a barrier)."""
 
