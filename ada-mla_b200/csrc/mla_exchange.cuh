@@ -6,8 +6,8 @@
 //
 //   header: epoch[rows] (u32: how many steps this rank has published for each
 //           row), padded to a multiple of 256 bytes
-//   data:   [2 parities][world parts][stride words]; one part = O [rows, 512]
-//           then LSE [rows], each value one 8-byte word (epoch << 32 | fp32 bits)
+//   data:   [2 parities][world parts][stride words]; one part = O [rows, 512
+//           words] then LSE [rows words], 8-byte words (epoch << 32 | payload)
 //
 // Flags live in the data: every 8-byte word carries the epoch of the step that
 // wrote it, and an aligned 8-byte store is seen whole or not at all.  A rank
@@ -15,13 +15,16 @@
 // rank's buffer (parity e & 1 for epoch e); a reader polls the words of its own
 // buffer (volatile loads, bounded by limit_ns) until each carries e, and then
 // LSE-merges the G parts.  No fence, no counter, no block waits for another
-// block of its own grid; the cost is twice the bytes on NVLink (4 KB per row
-// per peer instead of 2 KB).
+// block of its own grid.  O words hold one fp32 value (4 KB per row per peer:
+// twice the bytes of the values) or, in the one-launch kernels with fp16
+// output, two fp16 values (2 KB; the merged output is fp16 anyway); the LSE word
+// is always fp32.  put + merge always use fp32 words, and every rank of a step
+// takes the same form (same rows, same device), so the formats never mix.
 //
 // Kernels (block = row, 128 threads own 4 columns each, unless noted):
-//   exchange_put_kernel     epoch[r] += 1, then the stores
-//   exchange_merge_kernel   waits for epoch[r] in every part, merges
-//   exchange_fused_kernel   both, one launch
+//   exchange_put_kernel     epoch[r] += 1, then the stores (fp32 words)
+//   exchange_merge_kernel   waits for epoch[r] in every part, merges (fp32 words)
+//   exchange_fused_kernel   both, one launch (fp16 words for fp16 output)
 //   exchange_combine_kernel (512 threads) merges the rank's own split-KV
 //                           partials of the row first, then as the fused one
 //
@@ -101,28 +104,71 @@ __device__ __forceinline__ bool still_waiting(uint32_t n, uint64_t &t0, unsigned
     return t - t0 <= limit_ns;
 }
 
+__device__ __forceinline__ unsigned long long word_of_half2(float a, float b, uint32_t e) {
+    const __half2 h = __floats2half2_rn(a, b);
+    return ((unsigned long long)e << 32) | *reinterpret_cast<const uint32_t *>(&h);
+}
+
 // Thread t (< 128) stores columns [4 t, 4 t + 4) of row `row` (v) and, thread 0,
-// its LSE, as epoch-e words into part `rank` of every rank's buffer.
+// its LSE, as epoch-e words into part `rank` of every rank's buffer.  Row r's O
+// words start at word r * 512 (fp32 words: 512 of them; fp16 words: 256).
+template <bool kHalf>
 __device__ __forceinline__ void put_row(const XchgRows &xr, long long row, uint32_t e, float4 v, float lse) {
     const size_t base = ((size_t)(e & 1) * (size_t)xr.world + (size_t)xr.rank) * (size_t)xr.stride;
     const int t = threadIdx.x;
-    const unsigned long long w0 = word_of(v.x, e), w1 = word_of(v.y, e), w2 = word_of(v.z, e), w3 = word_of(v.w, e);
     const unsigned long long wl = word_of(lse, e);
-    for (int q = 0; q < xr.world; ++q) {
-        unsigned long long *d = data_of(xr.peers.buf[q], xr.rows) + base;
-        unsigned long long *o = d + (size_t)row * kDV + 4 * t;
-        st_words2(o, w0, w1);
-        st_words2(o + 2, w2, w3);
-        if (t == 0) st_word(d + (size_t)xr.rows * kDV + row, wl);
+    if constexpr (kHalf) {
+        const unsigned long long w0 = word_of_half2(v.x, v.y, e), w1 = word_of_half2(v.z, v.w, e);
+        for (int q = 0; q < xr.world; ++q) {
+            unsigned long long *d = data_of(xr.peers.buf[q], xr.rows) + base;
+            st_words2(d + (size_t)row * kDV + 2 * t, w0, w1);
+            if (t == 0) st_word(d + (size_t)xr.rows * kDV + row, wl);
+        }
+    } else {
+        const unsigned long long w0 = word_of(v.x, e), w1 = word_of(v.y, e), w2 = word_of(v.z, e), w3 = word_of(v.w, e);
+        for (int q = 0; q < xr.world; ++q) {
+            unsigned long long *d = data_of(xr.peers.buf[q], xr.rows) + base;
+            unsigned long long *o = d + (size_t)row * kDV + 4 * t;
+            st_words2(o, w0, w1);
+            st_words2(o + 2, w2, w3);
+            if (t == 0) st_word(d + (size_t)xr.rows * kDV + row, wl);
+        }
     }
+}
+
+// Thread t's words of one part's row (fp32 words: 4, fp16 words: 2), the test
+// that they all carry epoch e, and their values.
+template <bool kHalf>
+__device__ __forceinline__ void load_part(const unsigned long long *p, unsigned long long (&w)[4]) {
+    ld_words2(p, w[0], w[1]);
+    if constexpr (!kHalf) ld_words2(p + 2, w[2], w[3]);
+}
+
+template <bool kHalf>
+__device__ __forceinline__ bool part_ready(const unsigned long long (&w)[4], uint32_t e) {
+    if constexpr (kHalf) return has_epoch(w[0], e) && has_epoch(w[1], e);
+    return has_epoch(w[0], e) && has_epoch(w[1], e) && has_epoch(w[2], e) && has_epoch(w[3], e);
+}
+
+template <bool kHalf>
+__device__ __forceinline__ float4 part_values(const unsigned long long (&w)[4]) {
+    if constexpr (kHalf) {
+        const uint32_t a = (uint32_t)w[0], b = (uint32_t)w[1];
+        const float2 x = __half22float2(*reinterpret_cast<const __half2 *>(&a));
+        const float2 y = __half22float2(*reinterpret_cast<const __half2 *>(&b));
+        return make_float4(x.x, x.y, y.x, y.y);
+    }
+    return make_float4(__uint_as_float((uint32_t)w[0]), __uint_as_float((uint32_t)w[1]),
+                       __uint_as_float((uint32_t)w[2]), __uint_as_float((uint32_t)w[3]));
 }
 
 // Block-wide: waits (bounded) until every part of row `row` in this rank's own
 // buffer carries epoch e, then LSE-merges the parts into out / out_lse.  Every
 // thread of the block calls it (barriers inside); threads 0..127 own 4 columns
-// each.  Returns false, with nothing written and the peer-wait code recorded,
-// when a wait ran out.
-template <typename OutT>
+// each and load four parts' words before testing any (one round trip to L2 per
+// four parts, not per part).  Returns false, with nothing written and the
+// peer-wait code recorded, when a wait ran out.
+template <bool kHalf, typename OutT>
 __device__ bool merge_row(const XchgRows &xr, long long row, uint32_t e, OutT *__restrict__ out,
                           float *__restrict__ out_lse) {
     __shared__ float lse_s[kMaxPeers];
@@ -150,23 +196,30 @@ __device__ bool merge_row(const XchgRows &xr, long long row, uint32_t e, OutT *_
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     float wsum = 0.f;
     if (t < kDV / 4) {
-        for (int g = 0; g < world && ok; ++g) {
-            const unsigned long long *p = d + (size_t)g * xr.stride + (size_t)row * kDV + 4 * t;
-            unsigned long long a, b, c, f;
-            ld_words2(p, a, b);
-            ld_words2(p + 2, c, f);
-            for (uint32_t n = 0; ok && !(has_epoch(a, e) && has_epoch(b, e) && has_epoch(c, e) && has_epoch(f, e)); ++n) {
-                ok = still_waiting(n, t0, xr.limit_ns);
-                ld_words2(p, a, b);
-                ld_words2(p + 2, c, f);
+        const size_t col = (size_t)row * kDV + (kHalf ? 2 : 4) * t;
+        for (int g0 = 0; g0 < world && ok; g0 += 4) {
+            unsigned long long w[4][4];
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+                if (g0 + j < world) load_part<kHalf>(d + (size_t)(g0 + j) * xr.stride + col, w[j]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+                if (g0 + j < world && ok) {
+                    const unsigned long long *p = d + (size_t)(g0 + j) * xr.stride + col;
+                    for (uint32_t n = 0; ok && !part_ready<kHalf>(w[j], e); ++n) {
+                        ok = still_waiting(n, t0, xr.limit_ns);
+                        load_part<kHalf>(p, w[j]);
+                    }
+                    const float lse = lse_s[g0 + j];
+                    const float wt = (mx == -INFINITY || lse == -INFINITY) ? 0.f : __expf(lse - mx);
+                    const float4 v = part_values<kHalf>(w[j]);
+                    wsum += wt;
+                    acc.x = fmaf(wt, v.x, acc.x);
+                    acc.y = fmaf(wt, v.y, acc.y);
+                    acc.z = fmaf(wt, v.z, acc.z);
+                    acc.w = fmaf(wt, v.w, acc.w);
+                }
             }
-            const float lse = lse_s[g];
-            const float w = (mx == -INFINITY || lse == -INFINITY) ? 0.f : __expf(lse - mx);
-            wsum += w;
-            acc.x = fmaf(w, __uint_as_float((uint32_t)a), acc.x);
-            acc.y = fmaf(w, __uint_as_float((uint32_t)b), acc.y);
-            acc.z = fmaf(w, __uint_as_float((uint32_t)c), acc.z);
-            acc.w = fmaf(w, __uint_as_float((uint32_t)f), acc.w);
         }
     }
     if (__syncthreads_or(!ok)) {
@@ -209,7 +262,7 @@ __global__ void __launch_bounds__(128) exchange_put_kernel(const float *__restri
     const long long row = blockIdx.x;
     const uint32_t e = row_epoch(xr, row, true);
     const float4 v = reinterpret_cast<const float4 *>(part + (size_t)row * kDV)[threadIdx.x];
-    put_row(xr, row, e, v, part[(size_t)xr.rows * kDV + row]);
+    put_row<false>(xr, row, e, v, part[(size_t)xr.rows * kDV + row]);
 }
 
 // The merge after exchange_put_kernel (which advanced the epoch).
@@ -218,7 +271,7 @@ __global__ void __launch_bounds__(128) exchange_merge_kernel(XchgRows xr, OutT *
                                                              float *__restrict__ out_lse) {
     const long long row = blockIdx.x;
     const uint32_t e = row_epoch(xr, row, false);
-    merge_row(xr, row, e, out, out_lse);
+    merge_row<false>(xr, row, e, out, out_lse);
 }
 
 // put + merge in one launch.  Blocks wait only on the same row's blocks of the
@@ -229,9 +282,10 @@ __global__ void __launch_bounds__(128) exchange_fused_kernel(const float *__rest
                                                              OutT *__restrict__ out, float *__restrict__ out_lse) {
     const long long row = blockIdx.x;
     const uint32_t e = row_epoch(xr, row, true);
+    constexpr bool kHalf = sizeof(OutT) == 2;
     const float4 v = reinterpret_cast<const float4 *>(part + (size_t)row * kDV)[threadIdx.x];
-    put_row(xr, row, e, v, part[(size_t)xr.rows * kDV + row]);
-    merge_row(xr, row, e, out, out_lse);
+    put_row<kHalf>(xr, row, e, v, part[(size_t)xr.rows * kDV + row]);
+    merge_row<kHalf>(xr, row, e, out, out_lse);
 }
 
 // The local LSE merge of a decode's split partials fused with the exchange:
@@ -324,9 +378,10 @@ __global__ void __launch_bounds__(kCombineThreads) exchange_combine_kernel(
             if (tid == 0) lse_s = wsum > 0.f ? mx + __logf(wsum) : -INFINITY;
         }
     }
+    constexpr bool kHalf = sizeof(OutT) == 2;
     const uint32_t e = row_epoch(xr, row, true);  // (its barrier publishes acc_s and lse_s)
-    if (tid < kDV / 4) put_row(xr, row, e, reinterpret_cast<const float4 *>(acc_s[0])[tid], lse_s);
-    merge_row(xr, row, e, out, out_lse);
+    if (tid < kDV / 4) put_row<kHalf>(xr, row, e, reinterpret_cast<const float4 *>(acc_s[0])[tid], lse_s);
+    merge_row<kHalf>(xr, row, e, out, out_lse);
 }
 
 }  // namespace xchg
