@@ -19,7 +19,10 @@
 // twice the bytes of the values) or, in the one-launch kernels with fp16
 // output, two fp16 values (2 KB; the merged output is fp16 anyway); the LSE word
 // is always fp32.  put + merge always use fp32 words, and every rank of a step
-// takes the same form (same rows, same device), so the formats never mix.
+// takes the same form (same rows, same device).  The top bit of a word's epoch
+// half names its payload format (set: fp16 pairs), so ranks that disagree on
+// it (different output types) wait in vain and report code 4 instead of
+// reading each other's words in the wrong format.
 //
 // Kernels (block = row, 128 threads own 4 columns each, unless noted):
 //   exchange_put_kernel     epoch[r] += 1, then the stores (fp32 words)
@@ -95,6 +98,12 @@ __device__ __forceinline__ unsigned long long ld_word(const unsigned long long *
 
 __device__ __forceinline__ bool has_epoch(unsigned long long w, uint32_t e) { return (uint32_t)(w >> 32) == e; }
 
+// The epoch half of a word: 31 bits of epoch, the top bit set for fp16 payload.
+template <bool kHalf>
+__device__ __forceinline__ uint32_t word_tag(uint32_t e) {
+    return kHalf ? (e | 0x80000000u) : (e & 0x7fffffffu);
+}
+
 // Bounded poll step: false once more than limit_ns passed since the first call
 // that had to wait (t0 = 0 before it).
 __device__ __forceinline__ bool still_waiting(uint32_t n, uint64_t &t0, unsigned long long limit_ns) {
@@ -116,16 +125,18 @@ template <bool kHalf>
 __device__ __forceinline__ void put_row(const XchgRows &xr, long long row, uint32_t e, float4 v, float lse) {
     const size_t base = ((size_t)(e & 1) * (size_t)xr.world + (size_t)xr.rank) * (size_t)xr.stride;
     const int t = threadIdx.x;
-    const unsigned long long wl = word_of(lse, e);
+    const uint32_t tag = word_tag<kHalf>(e);
+    const unsigned long long wl = word_of(lse, tag);
     if constexpr (kHalf) {
-        const unsigned long long w0 = word_of_half2(v.x, v.y, e), w1 = word_of_half2(v.z, v.w, e);
+        const unsigned long long w0 = word_of_half2(v.x, v.y, tag), w1 = word_of_half2(v.z, v.w, tag);
         for (int q = 0; q < xr.world; ++q) {
             unsigned long long *d = data_of(xr.peers.buf[q], xr.rows) + base;
             st_words2(d + (size_t)row * kDV + 2 * t, w0, w1);
             if (t == 0) st_word(d + (size_t)xr.rows * kDV + row, wl);
         }
     } else {
-        const unsigned long long w0 = word_of(v.x, e), w1 = word_of(v.y, e), w2 = word_of(v.z, e), w3 = word_of(v.w, e);
+        const unsigned long long w0 = word_of(v.x, tag), w1 = word_of(v.y, tag), w2 = word_of(v.z, tag),
+                                 w3 = word_of(v.w, tag);
         for (int q = 0; q < xr.world; ++q) {
             unsigned long long *d = data_of(xr.peers.buf[q], xr.rows) + base;
             unsigned long long *o = d + (size_t)row * kDV + 4 * t;
@@ -176,12 +187,13 @@ __device__ bool merge_row(const XchgRows &xr, long long row, uint32_t e, OutT *_
     const int world = xr.world;
     const unsigned long long *d =
         data_of(xr.peers.buf[xr.rank], xr.rows) + (size_t)(e & 1) * (size_t)world * (size_t)xr.stride;
+    const uint32_t tag = word_tag<kHalf>(e);
     bool ok = true;
     uint64_t t0 = 0;
     if (t < world) {
         const unsigned long long *p = d + (size_t)t * xr.stride + (size_t)xr.rows * kDV + row;
         unsigned long long w = ld_word(p);
-        for (uint32_t n = 0; ok && !has_epoch(w, e); ++n) {
+        for (uint32_t n = 0; ok && !has_epoch(w, tag); ++n) {
             ok = still_waiting(n, t0, xr.limit_ns);
             w = ld_word(p);
         }
@@ -206,7 +218,7 @@ __device__ bool merge_row(const XchgRows &xr, long long row, uint32_t e, OutT *_
             for (int j = 0; j < 4; ++j) {
                 if (g0 + j < world && ok) {
                     const unsigned long long *p = d + (size_t)(g0 + j) * xr.stride + col;
-                    for (uint32_t n = 0; ok && !part_ready<kHalf>(w[j], e); ++n) {
+                    for (uint32_t n = 0; ok && !part_ready<kHalf>(w[j], tag); ++n) {
                         ok = still_waiting(n, t0, xr.limit_ns);
                         load_part<kHalf>(p, w[j]);
                     }

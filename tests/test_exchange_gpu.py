@@ -220,3 +220,41 @@ def test_decode_exchange_rejects_rows_that_do_not_fit():
         assert bool((direct == 5.0).all()), "nothing ran"
     finally:
         ex.close()
+
+
+def test_ranks_that_disagree_on_the_word_format_time_out():
+    """Two ranks' buffers in one process: "rank 1" exchanges with fp32 output
+    (fp32 payload words) and "rank 0" with fp16 output (fp16 payload words).
+    Rank 0 must not read rank 1's words as fp16 pairs: the format bit in each
+    word's epoch half keeps them from matching, its wait runs out (code 4) and
+    its rows stay untouched.  (Rank 1's own wait runs out first: rank 0 has not
+    put yet when it runs.)"""
+    from ada_mla import capi
+
+    lib = capi.lib()
+    rows, world = 8, 2
+    bufs = [ctypes.c_void_p(), ctypes.c_void_p()]
+    for b in bufs:
+        assert lib.mla_b200_exchange_alloc(world, rows, ctypes.byref(b)) == capi.OK
+    try:
+        parts, _ = _packed(rows, 1, torch.Generator().manual_seed(8))
+        part = parts[0].cuda()
+        s = torch.cuda.current_stream().cuda_stream
+        peers = (ctypes.c_void_p * world)(bufs[0].value, bufs[1].value)
+        code = ctypes.c_int(0)
+        out1 = torch.full((rows, 512), 7.0, device="cuda")
+        assert lib.mla_b200_exchange_f32(part.data_ptr(), rows, peers, 1, world, out1.data_ptr(), capi.OUT_F32,
+                                         None, 2_000_000, s) == capi.OK
+        torch.cuda.synchronize()
+        assert lib.mla_b200_get_device_error(ctypes.byref(code), s) == capi.ERR_DEVICE_TIMEOUT
+        out0 = torch.full((rows, 512), 7.0, dtype=torch.float16, device="cuda")
+        assert lib.mla_b200_exchange_f32(part.data_ptr(), rows, peers, 0, world, out0.data_ptr(), capi.OUT_F16,
+                                         None, 2_000_000, s) == capi.OK
+        torch.cuda.synchronize()
+        assert lib.mla_b200_get_device_error(ctypes.byref(code), s) == capi.ERR_DEVICE_TIMEOUT
+        assert code.value == 4
+        assert bool((out0 == 7.0).all()), "no row merged from words of the other format"
+    finally:
+        torch.cuda.synchronize()
+        for b in bufs:
+            lib.mla_b200_exchange_free(b.value)
